@@ -1,0 +1,46 @@
+// Block-table-indexed GQA decode attention with split-K (flash-decoding).
+//
+// Replaces emitServingPagedKVAttention (KVCacheMetalEmitter.cpp:312-406),
+// emitPagedKVAttention (:210-310) and emitKVAttention (:119-208): causal
+// decode attention for one query token per row, scale 1/sqrt(D), softmax in
+// fp32, context rounded to fp16. The reference is MHA only; here query head h
+// reads KV head h / (Hq / Hkv) (grouped-query attention).
+//
+// KV layout in HBM: a pool of pages [page][Hkv][page_size][D] (fp16), the
+// serving layout of emitServingPagedCacheAppend
+// (DecoderLLMMetalEmitter.cpp:314-373). A contiguous per-sequence cache
+// [B][H][capacity][D] is the special case page_size = capacity with block
+// table row b = {b}.
+#pragma once
+
+#include "common.cuh"
+
+namespace tmc {
+
+struct AttentionParams {
+  const __half *q;      // [rows, Hq, D], row stride q_stride elements
+  long long q_stride;
+  __half *out;          // [rows, Hq, D], row stride out_stride elements
+  long long out_stride;
+  const __half *k_pool;  // [pool_pages, Hkv, page_size, D]
+  const __half *v_pool;
+  const int *block_table;  // [table rows, table_stride]
+  int table_stride;
+  const int *table_rows;   // [rows] block-table row of each query row
+  const int *positions;    // [rows] query position; keys [0, position] are attended
+  int rows, hq, hkv, head_dim, page_size, pool_pages, capacity;
+  float scale;
+  int max_splits;  // grid.x; splits actually used <= max_splits
+  int min_chunk;   // positions per split at least this many
+  float *ws_acc;   // [rows, hkv, max_splits, G, D]
+  float *ws_ml;    // [rows, hkv, max_splits, G, 2]
+  unsigned int *counters;  // [rows, hkv], zero between launches
+  TmcDeviceStatus *status;
+};
+
+// Workspace bytes needed for a launch with these dimensions.
+size_t attention_workspace_bytes(int rows, int hq, int hkv, int head_dim, int max_splits);
+
+cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool pdl);
+
+}  // namespace tmc

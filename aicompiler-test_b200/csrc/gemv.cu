@@ -1,0 +1,456 @@
+// Decode GEMV family for sm_100a (see gemv.cuh for the op list).
+//
+// Design (HBM-bound, arithmetic intensity ~1 flop/byte at M=1):
+//  * one CTA = 8 warps; a warp owns a group of R=2 consecutive weight rows
+//    and streams both rows with 16-byte `ld.global.nc.L1::no_allocate` loads,
+//    U chunks per row in flight per lane (R*U*16 B = 256 B per lane);
+//  * the grid is one wave (SMs x resident CTAs); row groups are dealt to
+//    warps with the global warp id `warp * gridDim.x + blockIdx.x`, so every
+//    CTA (hence every SM) gets the same number of rows to within one;
+//  * the activation vector(s) are staged once per CTA in shared memory after
+//    the fused prologue (RMSNorm / embedding gather), read back conflict-free;
+//  * warp-shuffle reduction, then a scalar fused epilogue by lane 0;
+//  * programmatic dependent launch: the CTA prefetches its first rows into L2
+//    before griddepcontrol.wait, so weight streaming overlaps the tail of the
+//    previous kernel in the decode graph.
+#include "gemv.cuh"
+
+#include <mutex>
+#include <unordered_map>
+
+namespace tmc {
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+template <typename XS>
+struct XLoad;
+template <>
+struct XLoad<float> {
+  static __device__ __forceinline__ void get(const float *row, int c, float (&v)[8]) {
+    const float4 a = reinterpret_cast<const float4 *>(row)[2 * c];
+    const float4 b = reinterpret_cast<const float4 *>(row)[2 * c + 1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+  static __device__ __forceinline__ float cvt(float v) { return v; }
+};
+template <>
+struct XLoad<__half> {
+  static __device__ __forceinline__ void get(const __half *row, int c, float (&v)[8]) {
+    const uint4 u = reinterpret_cast<const uint4 *>(row)[c];
+    float2 f;
+    f = half2_bits_to_float2(u.x); v[0] = f.x; v[1] = f.y;
+    f = half2_bits_to_float2(u.y); v[2] = f.x; v[3] = f.y;
+    f = half2_bits_to_float2(u.z); v[4] = f.x; v[5] = f.y;
+    f = half2_bits_to_float2(u.w); v[6] = f.x; v[7] = f.y;
+  }
+};
+
+template <typename XS>
+__device__ __forceinline__ XS to_xs(float v);
+template <>
+__device__ __forceinline__ float to_xs<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __half to_xs<__half>(float v) { return __float2half_rn(v); }
+
+__device__ __forceinline__ float dot8(const uint4 w, const float (&x)[8], float acc) {
+  float2 a = half2_bits_to_float2(w.x);
+  acc = fmaf(a.x, x[0], acc); acc = fmaf(a.y, x[1], acc);
+  a = half2_bits_to_float2(w.y);
+  acc = fmaf(a.x, x[2], acc); acc = fmaf(a.y, x[3], acc);
+  a = half2_bits_to_float2(w.z);
+  acc = fmaf(a.x, x[4], acc); acc = fmaf(a.y, x[5], acc);
+  a = half2_bits_to_float2(w.w);
+  acc = fmaf(a.x, x[6], acc); acc = fmaf(a.y, x[7], acc);
+  return acc;
+}
+
+// Stage the M activation rows (after the fused prologue) into shared memory.
+// K is a multiple of 8 (checked on the host).
+template <typename XS, int M>
+__device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
+  const int K = p.K;
+  const int nvec = K >> 3;
+  for (int m = 0; m < M; ++m) {
+    XS *dst = xs + (size_t)m * K;
+    if (m >= p.M) {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = to_xs<XS>(0.0f);
+      continue;
+    }
+    const int pro = p.prologue;
+    if (pro == kProF32 || pro == kProF32Norm) {
+      const float *src = static_cast<const float *>(p.x) + (size_t)m * p.x_stride;
+      float inv = 1.0f;
+      if (pro == kProF32Norm) {
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+          const float v = src[i];
+          ss = fmaf(v, v, ss);
+        }
+        ss = block_sum(ss, red);
+        inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+      }
+      const float *g = static_cast<const float *>(p.gamma);
+      for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        float v = src[i];
+        if (pro == kProF32Norm) v = __fmul_rn(__fmul_rn(v, inv), g[i]);
+        dst[i] = to_xs<XS>(v);
+      }
+    } else {
+      // fp16 sources: plain, RMSNorm, or embedding gather + RMSNorm.
+      const __half *src = nullptr;
+      if (pro == kProEmbedNorm) {
+        const int tok = p.tokens[m];
+        if (tok < 0 || tok >= p.vocab) {
+          if (threadIdx.x == 0 && blockIdx.x == 0)
+            report_status(p.status, kStatusTokenRange, kWhereEmbedding, tok, m);
+        } else {
+          src = p.embedding + (size_t)tok * K;
+        }
+      } else {
+        src = static_cast<const __half *>(p.x) + (size_t)m * p.x_stride;
+      }
+      const bool norm = (pro == kProF16Norm || pro == kProEmbedNorm);
+      float inv = 1.0f;
+      if (norm) {
+        float ss = 0.0f;
+        if (src != nullptr) {
+          for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+            float f[8];
+            XLoad<__half>::get(src, v, f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+          }
+        }
+        ss = block_sum(ss, red);
+        inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+      }
+      const __half *g = static_cast<const __half *>(p.gamma);
+      const bool write_h = (pro == kProEmbedNorm) && blockIdx.x == 0 && p.h_out != nullptr;
+      for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        float f[8];
+        if (src != nullptr) {
+          XLoad<__half>::get(src, v, f);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = 0.0f;
+        }
+        if (write_h) {
+          uint4 raw = src != nullptr ? reinterpret_cast<const uint4 *>(src)[v] : make_uint4(0, 0, 0, 0);
+          reinterpret_cast<uint4 *>(p.h_out + (size_t)m * K)[v] = raw;
+        }
+        if (norm) {
+          float gv[8];
+          XLoad<__half>::get(g, v, gv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = round_half(__fmul_rn(__fmul_rn(f[j], inv), gv[j]));
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[v * 8 + j] = to_xs<XS>(f[j]);
+      }
+    }
+  }
+}
+
+template <int R, int M>
+__device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&acc)[R][M],
+                                         int lane, unsigned long long (&best)[M]) {
+  const int epi = p.epilogue;
+  if (epi == kEpiArgmax) {
+    // Every lane holds the full sums; all lanes track the key identically.
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = row0 + r;
+      if (row >= p.N) continue;
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        if (m >= p.M) continue;
+        const float v = round_half(acc[r][m]);
+        if (lane == 0 && p.y_f32 != nullptr) p.y_f32[(size_t)m * p.y_stride + row] = v;
+        const unsigned long long key = argmax_key(v, p.vocab_offset + row);
+        best[m] = key > best[m] ? key : best[m];
+      }
+    }
+    return;
+  }
+  if (lane != 0) return;
+  if (epi == kEpiSwiGLU) {
+    // rows (row0, row0+1) = (gate_i, up_i) with i = row0 / 2
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (m >= p.M) continue;
+      const float g = round_half(acc[0][m]);
+      const float u = round_half(acc[R - 1][m]);
+      const float a = round_half(g / (1.0f + expf(-g)));
+      p.y_f16[(size_t)m * p.y_stride + (row0 >> 1)] = __float2half_rn(__fmul_rn(a, u));
+    }
+    return;
+  }
+  if (epi == kEpiQKV) {
+    // (row0, row0+1) is an interleaved RoPE pair inside one head.
+    const int D = p.head_dim;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (m >= p.M) continue;
+      float e = round_half(acc[0][m]);
+      float o = round_half(acc[R - 1][m]);
+      const int pos = p.positions[m];
+      if (pos < 0 || pos >= p.capacity) {
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        continue;
+      }
+      if (row0 < p.q_rows + p.kv_rows) {
+        const int pair = (row0 % D) >> 1;
+        const float c = p.rope_cos[(size_t)pos * (D >> 1) + pair];
+        const float s = p.rope_sin[(size_t)pos * (D >> 1) + pair];
+        const float re = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
+        const float ro = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
+        e = re;
+        o = ro;
+      }
+      if (row0 < p.q_rows) {
+        __half2 hv = __floats2half2_rn(e, o);
+        *reinterpret_cast<__half2 *>(p.y_f16 + (size_t)m * p.y_stride + row0) = hv;
+        continue;
+      }
+      int local = row0 - p.q_rows;
+      __half *pool = p.k_pool;
+      if (local >= p.kv_rows) {
+        local -= p.kv_rows;
+        pool = p.v_pool;
+      }
+      const int kvh = local / D, d = local % D;
+      const int lp = pos / p.page_size, off = pos % p.page_size;
+      if (lp >= p.table_stride) {
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        continue;
+      }
+      const int page = p.block_table[(size_t)p.table_rows[m] * p.table_stride + lp];
+      if (page < 0) {
+        report_status(p.status, kStatusPageMissing, kWhereAppend, lp, m);
+        continue;
+      }
+      if (page >= p.pool_pages) {
+        report_status(p.status, kStatusPageRange, kWhereAppend, page, m);
+        continue;
+      }
+      const int hkv = p.kv_rows / D;
+      const size_t addr = (((size_t)page * hkv + kvh) * p.page_size + off) * D + d;
+      *reinterpret_cast<__half2 *>(pool + addr) = __floats2half2_rn(e, o);
+    }
+    return;
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int row = row0 + r;
+    if (row >= p.N) continue;
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      if (m >= p.M) continue;
+      const size_t idx = (size_t)m * p.y_stride + row;
+      const float v = acc[r][m];
+      if (epi == kEpiF32 || epi == kEpiF32Partial) {
+        p.y_f32[idx] = v;
+      } else if (epi == kEpiF16) {
+        p.y_f16[idx] = __float2half_rn(v);
+      } else if (epi == kEpiResidual) {
+        p.y_f16[idx] = __float2half_rn(__fadd_rn(__half2float(p.residual[idx]), round_half(v)));
+      }
+    }
+  }
+}
+
+template <typename XS, int M, int R, int U>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  XS *xs = reinterpret_cast<XS *>(smem_raw);
+  __shared__ float red[32];
+  __shared__ unsigned long long warp_best[kWarps][M];
+  __shared__ int is_last;
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int total_w = kWarps * gridDim.x;
+  const int gw = warp * gridDim.x + blockIdx.x;
+  const int ngroups = (p.N + R - 1) / R;
+  const int nchunks = p.K >> 3;
+
+  // Weights never change: warm L2 with the first row group before waiting on
+  // the producer of x.
+  if (gw < ngroups) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = gw * R + r;
+      if (row < p.N) {
+        const uint4 *wr = reinterpret_cast<const uint4 *>(p.W + (size_t)row * p.K);
+        for (int c = lane; c < nchunks && c < 32 * U; c += 32) prefetch_l2(wr + c);
+      }
+    }
+  }
+  pdl_wait();
+  stage_x<XS, M>(p, xs, red);
+  __syncthreads();
+  pdl_launch_dependents();
+
+  unsigned long long best[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) best[m] = 0ull;
+
+  for (int g = gw; g < ngroups; g += total_w) {
+    const int row0 = g * R;
+    float acc[R][M];
+    const uint4 *wr[R];
+    bool rv[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      rv[r] = row0 + r < p.N;
+      wr[r] = reinterpret_cast<const uint4 *>(p.W + (size_t)(rv[r] ? row0 + r : row0) * p.K);
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
+    }
+    for (int c0 = 0; c0 < nchunks; c0 += 32 * U) {
+      uint4 w[R][U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32 + lane;
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+          w[r][u] = (c < nchunks && rv[r]) ? ldg_stream(wr[r] + c) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < nchunks) {
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            float xv[8];
+            XLoad<XS>::get(xs + (size_t)m * p.K, c, xv);
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[r][u], xv, acc[r][m]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+    epilogue<R, M>(p, row0, acc, lane, best);
+  }
+
+  if (p.epilogue == kEpiArgmax) {
+    if (lane == 0) {
+#pragma unroll
+      for (int m = 0; m < M; ++m) warp_best[warp][m] = best[m];
+    }
+    __syncthreads();
+    if (threadIdx.x < M && threadIdx.x < p.M) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kWarps; ++w) b = warp_best[w][threadIdx.x] > b ? warp_best[w][threadIdx.x] : b;
+      if (b != 0ull) atomicMax(p.argmax_keys + threadIdx.x, b);
+    }
+    if (p.next_tokens == nullptr) return;  // cross-rank reduction finalises
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int prev = atomicAdd(p.argmax_counter, 1u);
+      is_last = (prev == gridDim.x - 1) ? 1 : 0;
+    }
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      if (threadIdx.x < p.M) {
+        const unsigned long long key = atomicExch(p.argmax_keys + threadIdx.x, 0ull);
+        const int tok = argmax_key_index(key);
+        p.next_tokens[threadIdx.x] = tok;
+        if (p.feed_tokens != nullptr) p.feed_tokens[threadIdx.x] = tok;
+        if (p.feed_positions != nullptr) p.feed_positions[threadIdx.x] += 1;
+      }
+      if (threadIdx.x == 0) atomicExch(p.argmax_counter, 0u);
+    }
+  }
+}
+
+template <typename XS, int M, int R, int U>
+cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
+  auto kernel = gemv_kernel<XS, M, R, U>;
+  const size_t smem = (size_t)M * p.K * sizeof(XS);
+  // Occupancy depends on the dynamic shared memory; cache it per (device, smem).
+  static std::mutex mu;
+  static std::unordered_map<long long, int> occ_cache;
+  static size_t configured_smem = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  int occ = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem > 48 * 1024 && smem > configured_smem) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      configured_smem = smem;
+    }
+    const long long key = (static_cast<long long>(dev) << 40) | static_cast<long long>(smem);
+    auto it = occ_cache.find(key);
+    if (it != occ_cache.end()) {
+      occ = it->second;
+    } else {
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kThreads, smem);
+      if (e != cudaSuccess) return e;
+      if (occ < 1) occ = 1;
+      occ_cache[key] = occ;
+    }
+  }
+  const int ngroups = (p.N + R - 1) / R;
+  int grid = (ngroups + kWarps - 1) / kWarps;
+  const int wave = occ * num_sms;
+  if (grid > wave) grid = wave;
+  if (grid < 1) grid = 1;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, p);
+}
+
+}  // namespace
+
+cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
+  if (p.K <= 0 || (p.K & 7) != 0 || p.N <= 0 || p.M <= 0 || p.M > 8) return cudaErrorInvalidValue;
+  if ((p.epilogue == kEpiQKV || p.epilogue == kEpiSwiGLU) && (p.N & 1)) return cudaErrorInvalidValue;
+  const bool f32_in = (p.prologue == kProF32 || p.prologue == kProF32Norm);
+  const size_t k = static_cast<size_t>(p.K);
+  // fp32 staging keeps un-rounded fp32 activations exact (C1 graph); fp16 staging
+  // is exact for the decoder's fp16-rounded activations and halves shared memory.
+  if (p.M == 1) {
+    if (f32_in || k * 4 <= 64 * 1024) return launch_instance<float, 1, 2, 8>(p, stream, pdl, num_sms);
+    return launch_instance<__half, 1, 2, 8>(p, stream, pdl, num_sms);
+  }
+  if (p.M == 2) {
+    if (k * 2 * 4 <= 112 * 1024) return launch_instance<float, 2, 2, 8>(p, stream, pdl, num_sms);
+    if (f32_in) return cudaErrorInvalidValue;
+    return launch_instance<__half, 2, 2, 8>(p, stream, pdl, num_sms);
+  }
+  if (p.M <= 4) {
+    if (f32_in && k * 4 * 4 <= 200 * 1024) return launch_instance<float, 4, 2, 4>(p, stream, pdl, num_sms);
+    if (f32_in || k * 4 * 2 > 200 * 1024) return cudaErrorInvalidValue;
+    return launch_instance<__half, 4, 2, 4>(p, stream, pdl, num_sms);
+  }
+  if (f32_in || k * 8 * 2 > 200 * 1024) return cudaErrorInvalidValue;
+  return launch_instance<__half, 8, 2, 4>(p, stream, pdl, num_sms);
+}
+
+}  // namespace tmc

@@ -1,0 +1,85 @@
+// Decode GEMV family: y[m, n] = sum_k x[m, k] * W[n, k] with fp16 W (row-major
+// [N, K]), fp32 accumulation, an optional fused prologue on x (RMSNorm,
+// embedding gather) and a fused epilogue (store, residual add, RoPE + KV-cache
+// append, SwiGLU, LM-head argmax).
+//
+// This replaces the reference's Metal emitters for the decode linear layers:
+// emitDecodeGEMV / emitLinearBaseline (DecodeGEMVMetalEmitter.cpp:18-132),
+// emitDecoderQKVFusion (DecoderLLMMetalEmitter.cpp:538-602),
+// emitDecoderGatedMLP (:479-536), emitLinearResidual (:604-621),
+// emitLMHeadPartialArgmax/FinalArgmax (:700-753) and the RMSNorm prologue of
+// emitDecoderRMSNorm (:63-108).
+#pragma once
+
+#include "common.cuh"
+
+namespace tmc {
+
+enum GemvPrologue : int {
+  kProF32 = 0,        // xs = x (fp32 input)
+  kProF32Norm = 1,    // xs = x * rsqrt(mean(x^2)+eps) * gamma, all fp32 (C1 graph)
+  kProF16 = 2,        // xs = x (fp16 input)
+  kProF16Norm = 3,    // xs = half(x * inv * gamma)   (decoder RMSNorm, fp16 storage)
+  kProEmbedNorm = 4,  // x = embedding[token[m]]; CTA 0 stores x to h_out; then kProF16Norm
+};
+
+enum GemvEpilogue : int {
+  kEpiF32 = 0,       // y_f32[m, n] = acc
+  kEpiF16 = 1,       // y_f16[m, n] = half(acc)
+  kEpiResidual = 2,  // y_f16[m, n] = half(residual[m, n] + half(acc))   (in place allowed)
+  kEpiQKV = 3,       // rows = [q | k | v]; RoPE on q,k; q -> y_f16; k,v -> paged cache
+  kEpiSwiGLU = 4,    // rows interleaved (gate_i, up_i) -> y_f16[m, i] = half(half(silu(g)) * u)
+  kEpiArgmax = 5,    // LM head: logits (fp16-rounded) -> y_f32 (optional) + argmax token
+  kEpiF32Partial = 6 // y_f32[m, n] = acc (row-parallel partial sum, reduced across ranks)
+};
+
+struct GemvParams {
+  const __half *W;  // [N, K]
+  int N, K, M;
+  // ---- prologue ----
+  int prologue;
+  const void *x;       // [M, x_stride] (fp32 or fp16 per prologue)
+  long long x_stride;  // elements
+  const void *gamma;   // [K] fp32 (kProF32Norm) or fp16 (kProF16Norm/kProEmbedNorm)
+  float eps;
+  const __half *embedding;  // [vocab, K]
+  const int *tokens;        // [M]
+  int vocab;
+  __half *h_out;            // [M, K] embedding write-back (residual stream)
+  // ---- epilogue ----
+  int epilogue;
+  float *y_f32;
+  __half *y_f16;
+  long long y_stride;      // elements between output rows
+  const __half *residual;  // [M, y_stride] (kEpiResidual)
+  // QKV / cache append
+  int q_rows;            // Hq_local * D
+  int kv_rows;           // Hkv_local * D
+  int head_dim;
+  const float *rope_cos;  // [capacity, D/2]
+  const float *rope_sin;
+  const int *positions;   // [M] position of the row's token
+  const int *table_rows;  // [M] block-table row of the row's sequence
+  const int *block_table; // [rows, table_stride]
+  int table_stride;       // max logical pages per sequence
+  int page_size;
+  int pool_pages;
+  int capacity;           // max position + 1
+  __half *k_pool;         // [pages, Hkv_local, page_size, D]
+  __half *v_pool;
+  // argmax
+  unsigned long long *argmax_keys;  // [M] (zero before launch; the last CTA resets)
+  unsigned int *argmax_counter;     // [1]
+  int *next_tokens;                 // [M]
+  int *feed_tokens;                 // [M] optional: next step's input tokens
+  int *feed_positions;              // [M] optional: positions += 1 (greedy loop)
+  int vocab_offset;                 // global index of local row 0 (vocab-parallel head)
+  TmcDeviceStatus *status;
+};
+
+// Host-side launcher; returns a cudaError_t. Chooses the template instance
+// from (M, K) and the grid from the device occupancy.
+cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl,
+                        int num_sms);
+
+}  // namespace tmc

@@ -1,0 +1,19 @@
+#pragma once
+
+#include "common.cuh"
+
+namespace tmc {
+
+cudaError_t launch_fill_normal_f16(__half *dst, size_t count, uint64_t seed, float mean,
+                                   float stddev, cudaStream_t stream);
+cudaError_t launch_fill_uniform_f32(float *dst, size_t count, uint64_t seed, float lo, float hi,
+                                    cudaStream_t stream);
+// Tokens from packed argmax keys (see argmax_key in common.cuh); resets keys.
+cudaError_t launch_argmax_finalize(unsigned long long *keys, int rows, int *next_tokens,
+                                   int *feed_tokens, int *feed_positions, cudaStream_t stream,
+                                   bool pdl);
+// h = half(h + half(partial)) for a reduced row-parallel projection.
+cudaError_t launch_add_residual_f32(__half *h, const float *partial, int n, cudaStream_t stream,
+                                    bool pdl);
+
+}  // namespace tmc

@@ -1,0 +1,83 @@
+// oracle/ref_driver.cpp -- TEST INFRASTRUCTURE ONLY.
+//
+// A thin extern "C" driver around the reference's own CPU oracle
+// (tensor::validation::evaluateGraph, reference src/validation/GraphReference.cpp:98,
+// with analyze(), src/analyzer/GraphAnalyzer.cpp:278), compiled from the
+// reference sources where they lie (oracle/Makefile) into oracle/_ref/.
+// It is used to pin the C restatement in oracle/graph_ref.c and to time the
+// reference's CPU path; the product never links it.
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+#include "analyzer/GraphAnalyzer.hpp"
+#include "validation/GraphReference.hpp"
+
+using namespace tensor;
+
+namespace {
+thread_local std::string g_error;
+}
+
+extern "C" {
+
+const char *ref_last_error() { return g_error.c_str(); }
+
+// The C1 graph of the scope table: RMSNorm(x, gamma) -> MatMul with a
+// Transpose(W) view, everything fp32 (W holds fp16-rounded values because
+// TensorIR MatMul requires matching dtypes, GraphAnalyzer.cpp:74).
+// y receives the fp64 "precise" outputs of evaluateGraph.
+int ref_rmsnorm_matmul(const float *x, const float *gamma, const float *w, long rows, long k,
+                       long n, float eps, double *y) {
+  try {
+    TensorGraph graph;
+    const auto xi = graph.addInput("x", TensorType{{std::size_t(rows), std::size_t(k)}, DType::Float32});
+    const auto gi = graph.addInput("gamma", TensorType{{std::size_t(k)}, DType::Float32});
+    const auto wi = graph.addInput("weight", TensorType{{std::size_t(n), std::size_t(k)}, DType::Float32});
+    const auto normed = graph.addNode(OpType::RMSNorm, {xi, gi}, RMSNormAttributes{eps, -1});
+    const auto wt = graph.addNode(OpType::Transpose, {wi}, TransposeAttributes{0, 1});
+    const auto out = graph.addNode(OpType::MatMul, {normed, wt});
+    graph.outputs = {out};
+    const auto analyzed = analyzer::analyze(graph);
+    GraphInputs inputs;
+    inputs[xi] = std::vector<float>(x, x + rows * k);
+    inputs[gi] = std::vector<float>(gamma, gamma + k);
+    inputs[wi] = std::vector<float>(w, w + n * k);
+    const auto result = validation::evaluateGraph(analyzed, inputs);
+    const auto &o = result.outputs.at(0);
+    std::memcpy(y, o.data(), o.size() * sizeof(double));
+    return 0;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+// RMSNorm graph alone (the graph-suite RMSNorm cases, tensor_graph_examples.cpp:79-123),
+// dtype 0 = fp16 storage, 1 = fp32.
+int ref_rmsnorm(const float *x, const float *gamma, long rows, long width, float eps, int dtype,
+                double *y) {
+  try {
+    const DType dt = dtype == 0 ? DType::Float16 : DType::Float32;
+    TensorGraph graph;
+    const auto xi = graph.addInput("x", TensorType{{std::size_t(rows), std::size_t(width)}, dt});
+    const auto gi = graph.addInput("gamma", TensorType{{std::size_t(width)}, dt});
+    const auto out = graph.addNode(OpType::RMSNorm, {xi, gi}, RMSNormAttributes{eps, -1});
+    graph.outputs = {out};
+    const auto analyzed = analyzer::analyze(graph);
+    GraphInputs inputs;
+    inputs[xi] = std::vector<float>(x, x + rows * width);
+    inputs[gi] = std::vector<float>(gamma, gamma + width);
+    const auto result = validation::evaluateGraph(analyzed, inputs);
+    const auto &o = result.outputs.at(0);
+    std::memcpy(y, o.data(), o.size() * sizeof(double));
+    return 0;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
+}  // extern "C"

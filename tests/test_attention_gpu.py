@@ -1,0 +1,107 @@
+"""Paged GQA decode attention on the GPU vs the CPU oracle (fp64 restatement of
+emitServingPagedKVAttention, reference KVCacheMetalEmitter.cpp:312-406, plus the
+GQA head map). Tolerance: max |gpu - ref| <= 2e-3 x RMS(ref) per case, after
+the reference's storage rounding of the context to fp16."""
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+
+
+def make_case(seed, rows, hq, hkv, d, page_size, lengths, pool_pages=None, share_table=False):
+    rng = np.random.default_rng(seed)
+    max_len = max(lengths)
+    stride = (max_len + page_size - 1) // page_size
+    need = sum((l + page_size - 1) // page_size for l in lengths)
+    pool_pages = pool_pages or max(need + 3, 8)
+    perm = rng.permutation(pool_pages).astype(np.int32)
+    table = np.full((rows, stride), -1, dtype=np.int32)
+    off = 0
+    for r, l in enumerate(lengths):
+        n = (l + page_size - 1) // page_size
+        table[r, :n] = perm[off:off + n]
+        off += n
+    k_pool = rng.standard_normal((pool_pages, hkv, page_size, d)).astype(np.float16)
+    v_pool = rng.standard_normal((pool_pages, hkv, page_size, d)).astype(np.float16)
+    q = rng.standard_normal((rows, hq, d)).astype(np.float16)
+    positions = np.array([l - 1 for l in lengths], dtype=np.int32)
+    table_rows = np.arange(rows, dtype=np.int32)
+    return q, k_pool, v_pool, table, table_rows, positions
+
+
+def run_attention(rt, q, k_pool, v_pool, table, table_rows, positions, hkv, page_size, capacity,
+                  max_splits=8, min_chunk=32):
+    import tmc_cuda
+    rows, hq, d = q.shape
+    ws_bytes = tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, max_splits)
+    qb, kb, vb = rt.upload(q), rt.upload(k_pool), rt.upload(v_pool)
+    tb, trb, pb = rt.upload(table), rt.upload(table_rows), rt.upload(positions)
+    out = rt.buffer(q.size, tmc_cuda.F16)
+    ws = rt.buffer(max(ws_bytes // 4, 1), tmc_cuda.F32)
+    counters = rt.upload(np.zeros(rows * hkv, dtype=np.int32))
+    tmc_cuda.paged_attention_f16(rt, qb, out, kb, vb, tb, table.shape[1], trb, pb, rows, hq, hkv, d,
+                                 page_size, k_pool.shape[0], capacity, max_splits, min_chunk, ws,
+                                 counters)
+    rt.synchronize()
+    assert np.all(counters.read_raw() == 0), "split tickets must be left at zero"
+    return out.read().reshape(rows, hq, d)
+
+
+def check(got, ref):
+    ref16 = oracle.round_f16(ref.astype(np.float32)).reshape(ref.shape)
+    rms = float(np.sqrt(np.mean(ref ** 2)))
+    err = float(np.max(np.abs(got.astype(np.float64) - ref16)))
+    assert err <= 2e-3 * rms, (err, rms)
+
+
+CASES = [
+    # (rows, hq, hkv, d, page, lengths)
+    (1, 32, 8, 128, 16, [1]),
+    (1, 32, 8, 128, 16, [1152]),
+    (3, 32, 8, 128, 16, [17, 16, 300]),
+    (4, 16, 16, 64, 2048, [513, 520, 576, 1]),   # contiguous MHA (C2 shape): one page per row
+    (2, 4, 4, 16, 4, [9, 32]),                   # reference defaults: head_dim 16, page 4
+    (2, 8, 2, 32, 8, [100, 7]),
+    (2, 16, 2, 128, 16, [2000, 65]),             # G = 8
+    (2, 4, 2, 64, 16, [64, 1000]),               # G = 2
+]
+
+
+@pytest.mark.parametrize("rows,hq,hkv,d,page,lengths", CASES)
+@pytest.mark.parametrize("splits", [(1, 64), (16, 32)])
+def test_paged_attention_matches_oracle(rt, rows, hq, hkv, d, page, lengths, splits):
+    q, kp, vp, table, trows, pos = make_case(rows * 7 + d, rows, hq, hkv, d, page, lengths)
+    capacity = table.shape[1] * page
+    ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
+                                 table, trows, pos, hkv, page)
+    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, page, capacity, *splits)
+    check(got, ref)
+
+
+def test_paged_attention_c4_subset(rt):
+    # C4 shapes (32q/8kv x 128, 16-token pages, random pages of a large pool)
+    # on 8 sequences with contexts drawn from U[128, 8192].
+    from oracle import workloads
+    ctx, table, positions, q = workloads.c4_inputs(seed=0, seqs=8, pool_pages=4608)
+    rng = np.random.default_rng(1)
+    kp = rng.standard_normal((4608, 8, 16, 128)).astype(np.float16)
+    vp = rng.standard_normal((4608, 8, 16, 128)).astype(np.float16)
+    trows = np.arange(8, dtype=np.int32)
+    ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
+                                 table, trows, positions, 8, 16)
+    got = run_attention(rt, q, kp, vp, table, trows, positions, 8, 16, 8192, 32, 256)
+    check(got, ref)
+
+
+def test_missing_page_reports_device_status(rt):
+    import tmc_cuda
+    q, kp, vp, table, trows, pos = make_case(3, 1, 4, 4, 16, 4, [20])
+    table[0, 2] = -1
+    with pytest.raises(tmc_cuda.TmcError) as err:
+        run_attention(rt, q, kp, vp, table, trows, pos, 4, 4, table.shape[1] * 4)
+    assert err.value.code == tmc_cuda.ERR_DEVICE_STATUS
+    assert "no physical page" in err.value.message
+    rt.synchronize()  # the status block was consumed; the context is still usable

@@ -1,0 +1,101 @@
+"""C1 parity: fused RMSNorm -> GEMV on the GPU vs the reference CPU path.
+
+Tolerance: max |gpu - ref| <= 2e-3 x RMS(ref); the
+reference graph suite's own fp32 tolerance (atol 1e-5, rtol 1e-4,
+apps/tensor_graph_examples.cpp:55-58) is checked as well.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle, workloads
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def run_c1(rt, x, gamma, w, eps=1e-5):
+    import tmc_cuda
+    rows, k = x.shape
+    n = w.shape[0]
+    xb = rt.upload(x.astype(np.float32))
+    gb = rt.upload(gamma.astype(np.float32))
+    wb = rt.upload(w.astype(np.float16))
+    yb = rt.buffer(rows * n, tmc_cuda.F32)
+    tmc_cuda.rmsnorm_gemv_f32(rt, xb, gb, wb, yb, rows, k, n, eps)
+    rt.synchronize()
+    return yb.read().reshape(rows, n)
+
+
+def assert_close(y, ref):
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2)))
+    err = float(np.max(np.abs(y.astype(np.float64) - ref)))
+    assert err <= 2e-3 * rms, (err, rms)
+    ok, worst, bad, first = oracle.compare(y, ref, 1e-5, 1e-4)
+    assert ok, (worst, bad, first)
+
+
+def test_c1_full_size_matches_reference_golden(rt):
+    x, gamma, w = workloads.c1_inputs(seed=0)
+    g = np.load(os.path.join(GOLDEN, "c1_full.npz"))
+    y = run_c1(rt, x, gamma, w)
+    assert_close(y, g["y"])
+
+
+@pytest.mark.parametrize("kind", ["pattern", "seeded"])
+@pytest.mark.parametrize("rows", [1, 3])
+def test_c1_small_matches_reference_golden(rt, kind, rows):
+    g = np.load(os.path.join(GOLDEN, "c1_small.npz"))
+    x, gamma, w, ref = (g[f"{kind}{rows}_{n}"] for n in ("x", "gamma", "w", "y"))
+    y = run_c1(rt, x, gamma, w.astype(np.float16))
+    assert_close(y, ref)
+
+
+@pytest.mark.parametrize("rows,k,n", [(1, 8, 1), (1, 24, 7), (2, 4104, 4097), (4, 2816, 1024),
+                                      (1, 14336, 515), (3, 1024, 130)])
+def test_c1_ragged_shapes_match_oracle(rt, rows, k, n):
+    x, gamma, w = workloads.c1_inputs(seed=rows * 1000 + n, k=k, n=n, rows=rows)
+    ref = oracle.rmsnorm_matmul(x, gamma, w.astype(np.float32))
+    assert_close(run_c1(rt, x, gamma, w), ref)
+
+
+def test_c1_zero_and_tiny_rows(rt):
+    # The graph suite's RMSNorm edge rows: all-zero and x1e-4 (eps-dominated).
+    k, n = 4096, 256
+    x, gamma, w = workloads.c1_inputs(seed=5, k=k, n=n, rows=3)
+    x[0] = 0.0
+    x[1] *= np.float32(1e-4)
+    ref = oracle.rmsnorm_matmul(x, gamma, w.astype(np.float32))
+    y = run_c1(rt, x, gamma, w)
+    assert np.all(y[0] == 0.0)
+    np.testing.assert_allclose(y[1:], ref[1:], rtol=1e-4, atol=1e-5)
+
+
+def test_c1_is_deterministic(rt):
+    x, gamma, w = workloads.c1_inputs(seed=11, k=4096, n=4096)
+    a = run_c1(rt, x, gamma, w)
+    b = run_c1(rt, x, gamma, w)
+    assert np.array_equal(a, b)
+
+
+def test_gemv_f16_matches_oracle(rt):
+    import tmc_cuda
+    rng = np.random.default_rng(4)
+    for rows, k, n in [(1, 4096, 1024), (2, 14336, 4096), (5, 1024, 2816), (8, 4096, 64)]:
+        x = rng.standard_normal((rows, k)).astype(np.float16)
+        w = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+        ref = oracle.gemv(x.astype(np.float32), w.astype(np.float32))
+        xb, wb = rt.upload(x), rt.upload(w)
+        y16 = rt.buffer(rows * n, tmc_cuda.F16)
+        y32 = rt.buffer(rows * n, tmc_cuda.F32)
+        tmc_cuda.gemv_f16(rt, xb, wb, y16, rows, k, n)
+        tmc_cuda.gemv_f16(rt, xb, wb, y32, rows, k, n)
+        rt.synchronize()
+        got32 = y32.read().reshape(rows, n)
+        rms = np.sqrt(np.mean(ref ** 2))
+        assert np.max(np.abs(got32 - ref)) <= 2e-3 * rms
+        # fp16 output is the storage rounding of the fp32 result
+        got16 = y16.read().reshape(rows, n)
+        assert np.max(np.abs(got16 - oracle.round_f16(got32).reshape(rows, n))) <= 2e-3 * rms
