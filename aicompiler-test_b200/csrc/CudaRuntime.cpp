@@ -295,7 +295,7 @@ SequencePreparationResult CudaRuntime::prepareSequence(
   }
   DeviceGuard guard(device_);
   cudaGraph_t graph = nullptr;
-  cudaError_t e = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal);
+  cudaError_t e = cudaStreamBeginCapture(stream_, cudaStreamCaptureModeRelaxed);
   if (e != cudaSuccess) {
     result.errorMessage = cudaMessage("cudaStreamBeginCapture", e);
     return result;

@@ -5,7 +5,18 @@
 
 #include <string>
 
+#include <memory>
+
 #include "CudaRuntime.hpp"
+
+// Opaque handle types of include/tmc_cuda.h.
+struct tmc_runtime {
+  std::unique_ptr<tensor::cuda::CudaRuntime> rt;
+};
+struct tmc_buffer {
+  tensor::cuda::BufferHandle buf;
+  tensor::cuda::CudaRuntime *rt;
+};
 
 namespace tmc_api {
 

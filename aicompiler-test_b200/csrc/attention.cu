@@ -252,7 +252,12 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
 #pragma unroll
       for (int e = 0; e < E; ++e) acc[e] *= r;
       const float *pr = sS + pg * T;
-      for (int lp = 0; lp < T; ++lp) {
+      // Rows past the chunk end (and rows whose page was missing) were never
+      // written this tile: skip them rather than multiply stale data by zero.
+      const int nt = min(T, end - (begin + t * T));
+      const int *valid = sValid + stage * T;
+      for (int lp = 0; lp < nt; ++lp) {
+        if (!valid[lp]) continue;
         const float w = pr[lp];
         const __half *vr = v + (size_t)lp * D + pd;
         if (E % 2 == 0) {

@@ -1,5 +1,6 @@
 // extern "C" boundary: runtime, buffers and kernel entry points
 // (declarations and reference citations in include/tmc_cuda.h).
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -15,13 +16,6 @@ using tensor::cuda::BufferHandle;
 using tensor::cuda::CudaRuntime;
 using tensor::cuda::ElementType;
 
-struct tmc_runtime {
-  std::unique_ptr<CudaRuntime> rt;
-};
-struct tmc_buffer {
-  BufferHandle buf;
-  CudaRuntime *rt;
-};
 
 namespace tmc_api {
 
@@ -94,7 +88,7 @@ int tmc_cuda_device_info(int device, tmc_device_info *out) {
   cudaError_t e = cudaGetDeviceProperties(&prop, device);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
   std::memset(out, 0, sizeof(*out));
-  std::strncpy(out->name, prop.name, sizeof(out->name) - 1);
+  std::snprintf(out->name, sizeof(out->name), "%s", prop.name);
   out->compute_major = prop.major;
   out->compute_minor = prop.minor;
   out->multiprocessor_count = prop.multiProcessorCount;
@@ -111,6 +105,8 @@ int tmc_runtime_create(int device, tmc_runtime **out) {
   *out = nullptr;
   auto rt = std::make_unique<CudaRuntime>(device);
   if (!rt->isAvailable()) return fail(TMC_ERR_UNAVAILABLE, rt->initializationError());
+  // One runtime per device and thread: kernels launch on the current device.
+  cudaSetDevice(device);
   *out = new tmc_runtime{std::move(rt)};
   return ok();
 }

@@ -1,0 +1,257 @@
+// extern "C" boundary of the decoder executor (declarations and reference
+// citations in include/tmc_cuda.h).
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include <nccl.h>
+
+#include "CudaRuntime.hpp"
+#include "DecoderExecutor.hpp"
+#include "NcclCollective.hpp"
+#include "api_util.hpp"
+#include "tmc_cuda.h"
+
+using tensor::runtime::DecoderConfig;
+using tensor::runtime::DecoderExecutor;
+using namespace tmc_api;
+
+struct tmc_decoder {
+  std::unique_ptr<DecoderExecutor> ex;
+  int device = 0;
+};
+
+namespace {
+
+int status_of(const std::string &e) {
+  if (e.rfind("device status", 0) == 0) return TMC_ERR_DEVICE_STATUS;
+  if (e.find("exhausted") != std::string::npos) return TMC_ERR_OUT_OF_MEMORY;
+  if (e.find("cuda") != std::string::npos || e.find("Cuda") != std::string::npos) return TMC_ERR_CUDA;
+  return TMC_ERR_INVALID;
+}
+
+int done(const std::string &e) { return e.empty() ? ok() : fail(status_of(e), e); }
+
+bool bind(tmc_decoder *d) {
+  if (d == nullptr || !d->ex) return false;
+  int cur = -1;
+  if (cudaGetDevice(&cur) == cudaSuccess && cur != d->device) cudaSetDevice(d->device);
+  return true;
+}
+
+}  // namespace
+
+extern "C" {
+
+int tmc_decoder_create(tmc_runtime *rt, const tmc_decoder_config *c, tmc_decoder **out) {
+  if (rt == nullptr || c == nullptr || out == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  *out = nullptr;
+  cudaSetDevice(rt->rt->device());
+  DecoderConfig cfg;
+  cfg.hidden = c->hidden_size;
+  cfg.heads = c->heads;
+  cfg.kvHeads = c->kv_heads > 0 ? c->kv_heads : c->heads;
+  cfg.headDim = c->head_dim > 0 ? c->head_dim : (c->heads > 0 ? c->hidden_size / c->heads : 0);
+  cfg.intermediate = c->intermediate_size;
+  cfg.vocab = c->vocab_size;
+  cfg.layers = c->layers;
+  cfg.capacity = c->capacity;
+  cfg.epsilon = c->epsilon;
+  cfg.ropeTheta = c->rope_theta > 0.0 ? c->rope_theta : 10000.0;
+  cfg.maxRows = c->max_rows > 0 ? c->max_rows : 8;
+  cfg.maxSlots = c->max_slots > 0 ? c->max_slots : 1;
+  cfg.pageSize = c->page_size;
+  cfg.poolPages = c->pool_pages;
+  cfg.tpRank = c->tp_rank;
+  cfg.tpSize = c->tp_size > 0 ? c->tp_size : 1;
+  cfg.useGraphs = c->use_graphs != 0;
+  cfg.usePDL = c->use_pdl != 0;
+  std::string err;
+  auto ex = DecoderExecutor::create(*rt->rt, cfg, &err);
+  if (!ex) return fail(err.find("cudaMalloc") != std::string::npos ? TMC_ERR_OUT_OF_MEMORY : TMC_ERR_INVALID, err);
+  *out = new tmc_decoder{std::move(ex), rt->rt->device()};
+  return ok();
+}
+
+void tmc_decoder_destroy(tmc_decoder *dec) {
+  if (dec) {
+    bind(dec);
+    delete dec;
+  }
+}
+
+int tmc_decoder_load_weight(tmc_decoder *dec, const char *name, const float *values, size_t count) {
+  if (!bind(dec) || name == nullptr || values == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  return done(dec->ex->loadWeight(name, values, count));
+}
+
+int tmc_decoder_load_weight_f16(tmc_decoder *dec, const char *name, const uint16_t *bits, size_t count) {
+  if (!bind(dec) || name == nullptr || bits == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  return done(dec->ex->loadWeightF16(name, bits, count));
+}
+
+int tmc_decoder_read_weight(tmc_decoder *dec, const char *name, float *out, size_t count) {
+  if (!bind(dec) || name == nullptr || out == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  std::vector<float> v;
+  auto e = dec->ex->readWeight(name, &v);
+  if (!e.empty()) return done(e);
+  if (v.size() != count) return fail(TMC_ERR_INVALID, "count does not match the rank-local weight size " + std::to_string(v.size()));
+  std::memcpy(out, v.data(), count * sizeof(float));
+  return ok();
+}
+
+int tmc_decoder_init_random(tmc_decoder *dec, uint64_t seed, float stddev) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->initRandom(seed, stddev));
+}
+
+int tmc_decoder_prefill(tmc_decoder *dec, int slot, const int32_t *tokens, int count, float *logits,
+                        int32_t *next_token) {
+  if (!bind(dec) || tokens == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  return done(dec->ex->prefill(slot, tokens, count, logits, next_token));
+}
+
+int tmc_decoder_decode(tmc_decoder *dec, const int32_t *slots, const int32_t *tokens, int rows, float *logits,
+                       int32_t *next_tokens) {
+  if (!bind(dec) || slots == nullptr || tokens == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  return done(dec->ex->decode(slots, tokens, rows, logits, next_tokens));
+}
+
+int tmc_decoder_generate(tmc_decoder *dec, const int32_t *slots, const int32_t *tokens, int rows, int steps,
+                         int32_t *tokens_out, double *gpu_us) {
+  if (!bind(dec) || slots == nullptr || tokens == nullptr || tokens_out == nullptr)
+    return fail(TMC_ERR_INVALID, "null argument");
+  tensor::runtime::StepTiming t;
+  auto e = dec->ex->generate(slots, tokens, rows, steps, tokens_out, &t);
+  if (gpu_us) *gpu_us = t.gpuUs;
+  return done(e);
+}
+
+size_t tmc_decoder_current_length(tmc_decoder *dec, int slot) {
+  if (!bind(dec)) return 0;
+  return dec->ex->currentLength(slot);
+}
+
+int tmc_decoder_read_kv(tmc_decoder *dec, int layer, int slot, float *key, float *value, size_t count) {
+  if (!bind(dec) || key == nullptr || value == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  std::vector<float> k, v;
+  auto e = dec->ex->readKV(layer, slot, &k, &v);
+  if (!e.empty()) return done(e);
+  if (k.size() != count) return fail(TMC_ERR_INVALID, "count must be local_kv_heads*length*head_dim = " + std::to_string(k.size()));
+  std::memcpy(key, k.data(), count * sizeof(float));
+  std::memcpy(value, v.data(), count * sizeof(float));
+  return ok();
+}
+
+int tmc_decoder_restore_kv(tmc_decoder *dec, int slot, size_t length, const float *keys, const float *values) {
+  if (!bind(dec) || keys == nullptr || values == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  const auto &c = dec->ex->config();
+  const size_t per = (size_t)dec->ex->localKVHeads() * length * c.headDim;
+  std::vector<std::vector<float>> k(c.layers), v(c.layers);
+  for (int l = 0; l < c.layers; ++l) {
+    k[l].assign(keys + l * per, keys + (l + 1) * per);
+    v[l].assign(values + l * per, values + (l + 1) * per);
+  }
+  return done(dec->ex->restoreKV(slot, length, k, v));
+}
+
+int tmc_decoder_block_table(tmc_decoder *dec, int slot, int32_t *out, size_t capacity, size_t *count) {
+  if (!bind(dec) || count == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  const auto t = dec->ex->blockTable(slot);
+  *count = t.size();
+  if (out != nullptr) std::memcpy(out, t.data(), std::min(capacity, t.size()) * sizeof(int32_t));
+  return ok();
+}
+
+int tmc_decoder_stage_length(tmc_decoder *dec, int slot, size_t length) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->stageLength(slot, length));
+}
+
+int tmc_decoder_commit_length(tmc_decoder *dec, int slot, size_t length) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->commitLength(slot, length));
+}
+
+int tmc_decoder_rollback_length(tmc_decoder *dec, int slot, size_t length) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->rollbackLength(slot, length));
+}
+
+int tmc_decoder_release(tmc_decoder *dec, int slot) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->releaseSlot(slot));
+}
+
+int tmc_decoder_storage(tmc_decoder *dec, size_t *model_bytes, size_t *kv_bytes, size_t *activation_bytes) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  if (model_bytes) *model_bytes = dec->ex->modelStorageBytes();
+  if (kv_bytes) *kv_bytes = dec->ex->kvStorageBytes();
+  if (activation_bytes) *activation_bytes = dec->ex->activationStorageBytes();
+  return ok();
+}
+
+int tmc_decoder_local_dims(tmc_decoder *dec, int *heads, int *kv_heads, int *intermediate, int *vocab,
+                           int *vocab_offset) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  if (heads) *heads = dec->ex->localHeads();
+  if (kv_heads) *kv_heads = dec->ex->localKVHeads();
+  if (intermediate) *intermediate = dec->ex->localIntermediate();
+  if (vocab) *vocab = dec->ex->localVocab();
+  if (vocab_offset) *vocab_offset = dec->ex->vocabOffset();
+  return ok();
+}
+
+int tmc_decoder_pool_stats(tmc_decoder *dec, size_t *capacity, size_t *used, size_t *peak, size_t *allocations,
+                           size_t *releases) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  auto &p = dec->ex->pagePool();
+  if (capacity) *capacity = p.capacityPages();
+  if (used) *used = p.usedPages();
+  if (peak) *peak = p.peakUsedPages();
+  if (allocations) *allocations = p.allocationCount();
+  if (releases) *releases = p.releaseCount();
+  return ok();
+}
+
+int tmc_decoder_inject_page_failures(tmc_decoder *dec, size_t n) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  dec->ex->pagePool().failNextAllocations(n);
+  return ok();
+}
+
+int tmc_decoder_kernels_per_step(tmc_decoder *dec, int rows) {
+  if (!bind(dec)) return -1;
+  return dec->ex->kernelsPerStep(rows);
+}
+
+double tmc_decoder_step_bytes(tmc_decoder *dec, int rows, const int32_t *context_lengths) {
+  if (!bind(dec) || context_lengths == nullptr) return 0.0;
+  std::vector<int> ctx(context_lengths, context_lengths + rows);
+  return dec->ex->stepAlgorithmicBytes(rows, ctx);
+}
+
+int tmc_decoder_profile_kernel(tmc_decoder *dec, int kind, int rows, int rounds, double *avg_us,
+                               double *bytes_per_launch, int *launches_per_step) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->profileKernel(kind, rows, rounds, avg_us, bytes_per_launch, launches_per_step));
+}
+
+int tmc_nccl_unique_id(uint8_t *id, size_t nbytes) {
+  if (id == nullptr || nbytes < NCCL_UNIQUE_ID_BYTES) return fail(TMC_ERR_INVALID, "id buffer too small");
+  auto e = tensor::runtime::ncclUniqueIdBytes(id);
+  return e.empty() ? ok() : fail(TMC_ERR_UNAVAILABLE, e);
+}
+
+int tmc_decoder_attach_nccl(tmc_decoder *dec, const uint8_t *id, size_t nbytes, int world, int rank) {
+  if (!bind(dec) || id == nullptr || nbytes < NCCL_UNIQUE_ID_BYTES) return fail(TMC_ERR_INVALID, "bad argument");
+  const auto &c = dec->ex->config();
+  if (world != c.tpSize || rank != c.tpRank) return fail(TMC_ERR_INVALID, "world/rank must match the decoder's tensor-parallel config");
+  std::string err;
+  auto coll = tensor::runtime::NcclCollective::create(id, world, rank, &err);
+  if (!coll) return fail(TMC_ERR_UNAVAILABLE, err);
+  return done(dec->ex->setCollective(coll));
+}
+
+}  // extern "C"

@@ -59,6 +59,21 @@ __device__ __forceinline__ float to_xs<float>(float v) { return v; }
 template <>
 __device__ __forceinline__ __half to_xs<__half>(float v) { return __float2half_rn(v); }
 
+// Vectorised store of 8 staged values (16 or 32 bytes).
+__device__ __forceinline__ void store8(float *dst, const float (&f)[8]) {
+  reinterpret_cast<float4 *>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+  reinterpret_cast<float4 *>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+}
+__device__ __forceinline__ void store8(__half *dst, const float (&f)[8]) {
+  uint4 u;
+  __half2 h;
+  h = __floats2half2_rn(f[0], f[1]); u.x = *reinterpret_cast<uint32_t *>(&h);
+  h = __floats2half2_rn(f[2], f[3]); u.y = *reinterpret_cast<uint32_t *>(&h);
+  h = __floats2half2_rn(f[4], f[5]); u.z = *reinterpret_cast<uint32_t *>(&h);
+  h = __floats2half2_rn(f[6], f[7]); u.w = *reinterpret_cast<uint32_t *>(&h);
+  *reinterpret_cast<uint4 *>(dst) = u;
+}
+
 __device__ __forceinline__ float dot8(const uint4 w, const float (&x)[8], float acc) {
   float2 a = half2_bits_to_float2(w.x);
   acc = fmaf(a.x, x[0], acc); acc = fmaf(a.y, x[1], acc);
@@ -85,26 +100,79 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
     }
     const int pro = p.prologue;
     if (pro == kProF32 || pro == kProF32Norm) {
-      const float *src = static_cast<const float *>(p.x) + (size_t)m * p.x_stride;
-      float inv = 1.0f;
-      if (pro == kProF32Norm) {
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-          const float v = src[i];
-          ss = fmaf(v, v, ss);
-        }
-        ss = block_sum(ss, red);
-        inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+      // One vectorised pass from global memory into shared memory (sum of
+      // squares on the way), then normalise in place.
+      const float4 *src = reinterpret_cast<const float4 *>(static_cast<const float *>(p.x) +
+                                                           (size_t)m * p.x_stride);
+      float ss = 0.0f;
+#pragma unroll 4
+      for (int v = threadIdx.x; v < K / 4; v += blockDim.x) {
+        const float4 f = src[v];
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+        ss = fmaf(f.z, f.z, ss);
+        ss = fmaf(f.w, f.w, ss);
+        dst[4 * v + 0] = to_xs<XS>(f.x);
+        dst[4 * v + 1] = to_xs<XS>(f.y);
+        dst[4 * v + 2] = to_xs<XS>(f.z);
+        dst[4 * v + 3] = to_xs<XS>(f.w);
       }
-      const float *g = static_cast<const float *>(p.gamma);
-      for (int i = threadIdx.x; i < K; i += blockDim.x) {
-        float v = src[i];
-        if (pro == kProF32Norm) v = __fmul_rn(__fmul_rn(v, inv), g[i]);
-        dst[i] = to_xs<XS>(v);
+      if (pro == kProF32Norm) {
+        ss = block_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+        const float4 *g = static_cast<const float4 *>(p.gamma);
+#pragma unroll 4
+        for (int v = threadIdx.x; v < K / 4; v += blockDim.x) {
+          const float4 gv = g[v];
+          // each thread rewrites exactly the elements it wrote above
+          dst[4 * v + 0] = to_xs<XS>(__fmul_rn(__fmul_rn(static_cast<float>(dst[4 * v + 0]), inv), gv.x));
+          dst[4 * v + 1] = to_xs<XS>(__fmul_rn(__fmul_rn(static_cast<float>(dst[4 * v + 1]), inv), gv.y));
+          dst[4 * v + 2] = to_xs<XS>(__fmul_rn(__fmul_rn(static_cast<float>(dst[4 * v + 2]), inv), gv.z));
+          dst[4 * v + 3] = to_xs<XS>(__fmul_rn(__fmul_rn(static_cast<float>(dst[4 * v + 3]), inv), gv.w));
+        }
       }
     } else {
       // fp16 sources: plain, RMSNorm, or embedding gather + RMSNorm.
       const __half *src = nullptr;
+      if (pro == kProResidualNorm) {
+        // x = half(h + half(partial)): the residual add after a cross-rank
+        // reduction, fused into the consumer's prologue. Staged into dst first.
+        const __half *hrow = static_cast<const __half *>(p.x) + (size_t)m * p.x_stride;
+        const float *prow = p.partial + (size_t)m * K;
+        const bool write_back = blockIdx.x == 0 && p.h_out != nullptr;
+        float ss = 0.0f;
+        for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+          float hv[8], f[8];
+          XLoad<__half>::get(hrow, v, hv);
+          const float4 a = reinterpret_cast<const float4 *>(prow)[2 * v];
+          const float4 b = reinterpret_cast<const float4 *>(prow)[2 * v + 1];
+          const float pv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            f[j] = round_half(__fadd_rn(hv[j], round_half(pv[j])));
+            ss = fmaf(f[j], f[j], ss);
+          }
+          store8(dst + v * 8, f);
+          if (write_back) {
+            __half tmp[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) tmp[j] = __float2half_rn(f[j]);
+            reinterpret_cast<uint4 *>(p.h_out + (size_t)m * K)[v] = *reinterpret_cast<uint4 *>(tmp);
+          }
+        }
+        ss = block_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+        const __half *g = static_cast<const __half *>(p.gamma);
+        for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+          float gv[8], xv[8];
+          XLoad<__half>::get(g, v, gv);
+          XLoad<XS>::get(dst, v, xv);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) xv[j] = round_half(__fmul_rn(__fmul_rn(xv[j], inv), gv[j]));
+          store8(dst + v * 8, xv);
+        }
+        continue;
+      }
       if (pro == kProEmbedNorm) {
         const int tok = p.tokens[m];
         if (tok < 0 || tok >= p.vocab) {
@@ -117,42 +185,37 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
         src = static_cast<const __half *>(p.x) + (size_t)m * p.x_stride;
       }
       const bool norm = (pro == kProF16Norm || pro == kProEmbedNorm);
-      float inv = 1.0f;
-      if (norm) {
-        float ss = 0.0f;
-        if (src != nullptr) {
-          for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-            float f[8];
-            XLoad<__half>::get(src, v, f);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
-          }
-        }
-        ss = block_sum(ss, red);
-        inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
-      }
-      const __half *g = static_cast<const __half *>(p.gamma);
       const bool write_h = (pro == kProEmbedNorm) && blockIdx.x == 0 && p.h_out != nullptr;
+      // Pass 1: global -> shared (raw values; exact in XS), sum of squares.
+      float ss = 0.0f;
+#pragma unroll 2
       for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        const uint4 raw = src != nullptr ? reinterpret_cast<const uint4 *>(src)[v] : make_uint4(0, 0, 0, 0);
+        if (write_h) reinterpret_cast<uint4 *>(p.h_out + (size_t)m * K)[v] = raw;
         float f[8];
-        if (src != nullptr) {
-          XLoad<__half>::get(src, v, f);
-        } else {
+        float2 t;
+        t = half2_bits_to_float2(raw.x); f[0] = t.x; f[1] = t.y;
+        t = half2_bits_to_float2(raw.y); f[2] = t.x; f[3] = t.y;
+        t = half2_bits_to_float2(raw.z); f[4] = t.x; f[5] = t.y;
+        t = half2_bits_to_float2(raw.w); f[6] = t.x; f[7] = t.y;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) f[j] = 0.0f;
-        }
-        if (write_h) {
-          uint4 raw = src != nullptr ? reinterpret_cast<const uint4 *>(src)[v] : make_uint4(0, 0, 0, 0);
-          reinterpret_cast<uint4 *>(p.h_out + (size_t)m * K)[v] = raw;
-        }
-        if (norm) {
-          float gv[8];
+        for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+        store8(dst + v * 8, f);
+      }
+      if (norm) {
+        ss = block_sum(ss, red);
+        const float inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
+        const __half *g = static_cast<const __half *>(p.gamma);
+        // Pass 2 (same elements per thread): half(x * inv * gamma).
+#pragma unroll 2
+        for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+          float gv[8], xv[8];
           XLoad<__half>::get(g, v, gv);
+          XLoad<XS>::get(dst, v, xv);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) f[j] = round_half(__fmul_rn(__fmul_rn(f[j], inv), gv[j]));
+          for (int j = 0; j < 8; ++j) xv[j] = round_half(__fmul_rn(__fmul_rn(xv[j], inv), gv[j]));
+          store8(dst + v * 8, xv);
         }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dst[v * 8 + j] = to_xs<XS>(f[j]);
       }
     }
   }
@@ -280,15 +343,35 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   const int ngroups = (p.N + R - 1) / R;
   const int nchunks = p.K >> 3;
 
-  // Weights never change: warm L2 with the first row group before waiting on
-  // the producer of x.
-  if (gw < ngroups) {
+  // Load a batch of U 16-byte chunks of each of the R rows of group g,
+  // starting at chunk c0, into registers.
+  auto load_batch = [&](int g, int c0, uint4 (&w)[R][U]) {
+    const int row0 = g * R;
 #pragma unroll
     for (int r = 0; r < R; ++r) {
-      const int row = gw * R + r;
+      const bool rv = row0 + r < p.N;
+      const uint4 *wr = reinterpret_cast<const uint4 *>(p.W + (size_t)(rv ? row0 + r : row0) * p.K);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32 + lane;
+        w[r][u] = (c < nchunks && rv) ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+
+  // Weights never change: the first batch is loaded into registers (and the
+  // rest of the first group warmed in L2) before waiting on the producer of x,
+  // so HBM latency overlaps the previous kernel's tail and the prologue.
+  uint4 w[R][U];
+  int g = gw, c0 = 0;
+  if (g < ngroups) {
+    load_batch(g, 0, w);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int row = g * R + r;
       if (row < p.N) {
         const uint4 *wr = reinterpret_cast<const uint4 *>(p.W + (size_t)row * p.K);
-        for (int c = lane; c < nchunks && c < 32 * U; c += 32) prefetch_l2(wr + c);
+        for (int c = 32 * U + lane; c < nchunks && c < 4 * 32 * U; c += 32) prefetch_l2(wr + c);
       }
     }
   }
@@ -301,46 +384,47 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
 #pragma unroll
   for (int m = 0; m < M; ++m) best[m] = 0ull;
 
-  for (int g = gw; g < ngroups; g += total_w) {
-    const int row0 = g * R;
-    float acc[R][M];
-    const uint4 *wr[R];
-    bool rv[R];
+  float acc[R][M];
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      rv[r] = row0 + r < p.N;
-      wr[r] = reinterpret_cast<const uint4 *>(p.W + (size_t)(rv[r] ? row0 + r : row0) * p.K);
+  for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
-    }
-    for (int c0 = 0; c0 < nchunks; c0 += 32 * U) {
-      uint4 w[R][U];
+    for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
+
+  while (g < ngroups) {
+    // Consume the batch held in w.
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int c = c0 + u * 32 + lane;
+    for (int u = 0; u < U; ++u) {
+      const int c = c0 + u * 32 + lane;
+      if (c < nchunks) {
 #pragma unroll
-        for (int r = 0; r < R; ++r)
-          w[r][u] = (c < nchunks && rv[r]) ? ldg_stream(wr[r] + c) : make_uint4(0, 0, 0, 0);
-      }
+        for (int m = 0; m < M; ++m) {
+          float xv[8];
+          XLoad<XS>::get(xs + (size_t)m * p.K, c, xv);
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int c = c0 + u * 32 + lane;
-        if (c < nchunks) {
-#pragma unroll
-          for (int m = 0; m < M; ++m) {
-            float xv[8];
-            XLoad<XS>::get(xs + (size_t)m * p.K, c, xv);
-#pragma unroll
-            for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[r][u], xv, acc[r][m]);
-          }
+          for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[r][u], xv, acc[r][m]);
         }
       }
     }
+    // Issue the next batch before reducing / running the epilogue.
+    int ng = g, nc = c0 + 32 * U;
+    if (nc >= nchunks) {
+      nc = 0;
+      ng += total_w;
+    }
+    if (ng < ngroups) load_batch(ng, nc, w);
+    if (nc == 0) {
 #pragma unroll
-    for (int r = 0; r < R; ++r)
+      for (int r = 0; r < R; ++r)
 #pragma unroll
-      for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
-    epilogue<R, M>(p, row0, acc, lane, best);
+        for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+      epilogue<R, M>(p, g * R, acc, lane, best);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
+    }
+    g = ng;
+    c0 = nc;
   }
 
   if (p.epilogue == kEpiArgmax) {
@@ -364,14 +448,20 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     __syncthreads();
     if (is_last) {
       __threadfence();
+      const unsigned int step = p.history != nullptr ? *p.history_counter : 0u;
       if (threadIdx.x < p.M) {
         const unsigned long long key = atomicExch(p.argmax_keys + threadIdx.x, 0ull);
         const int tok = argmax_key_index(key);
         p.next_tokens[threadIdx.x] = tok;
         if (p.feed_tokens != nullptr) p.feed_tokens[threadIdx.x] = tok;
         if (p.feed_positions != nullptr) p.feed_positions[threadIdx.x] += 1;
+        if (p.history != nullptr) p.history[(size_t)step * p.M + threadIdx.x] = tok;
       }
-      if (threadIdx.x == 0) atomicExch(p.argmax_counter, 0u);
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        if (p.history != nullptr) *p.history_counter = step + 1;
+        atomicExch(p.argmax_counter, 0u);
+      }
     }
   }
 }

@@ -21,6 +21,8 @@ enum GemvPrologue : int {
   kProF16 = 2,        // xs = x (fp16 input)
   kProF16Norm = 3,    // xs = half(x * inv * gamma)   (decoder RMSNorm, fp16 storage)
   kProEmbedNorm = 4,  // x = embedding[token[m]]; CTA 0 stores x to h_out; then kProF16Norm
+  kProResidualNorm = 5,  // x = half(h[m] + half(partial[m])) (reduced row-parallel output);
+                         // CTA 0 stores x to h_out; then kProF16Norm
 };
 
 enum GemvEpilogue : int {
@@ -45,7 +47,8 @@ struct GemvParams {
   const __half *embedding;  // [vocab, K]
   const int *tokens;        // [M]
   int vocab;
-  __half *h_out;            // [M, K] embedding write-back (residual stream)
+  __half *h_out;            // [M, K] residual-stream write-back (embedding / residual prologue)
+  const float *partial;     // [M, K] reduced fp32 projection (kProResidualNorm)
   // ---- epilogue ----
   int epilogue;
   float *y_f32;
@@ -73,6 +76,8 @@ struct GemvParams {
   int *next_tokens;                 // [M]
   int *feed_tokens;                 // [M] optional: next step's input tokens
   int *feed_positions;              // [M] optional: positions += 1 (greedy loop)
+  int *history;                     // optional [steps, M] generated tokens
+  unsigned int *history_counter;    // [1] steps recorded so far
   int vocab_offset;                 // global index of local row 0 (vocab-parallel head)
   TmcDeviceStatus *status;
 };

@@ -32,6 +32,35 @@ __global__ void fill_normal_kernel(__half *dst, size_t count, uint64_t seed, flo
   }
 }
 
+// dst[r * dst_stride + c] = N(mean, std) drawn for the LOGICAL element
+// (logical_row0 + r) * logical_cols + logical_col0 + c, so a tensor-parallel
+// shard or an interleaved/fused layout receives exactly the values of the
+// unsharded tensor.
+__global__ void fill_normal_2d_kernel(__half *dst, int rows, int cols, long long dst_stride,
+                                      uint64_t seed, long long logical_row0, long long logical_cols,
+                                      long long logical_col0, float mean, float stddev) {
+  const long long total = (long long)rows * cols;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    const long long r = i / cols, c = i % cols;
+    const unsigned long long li =
+        (unsigned long long)((logical_row0 + r) * logical_cols + logical_col0 + c);
+    const uint64_t h = splitmix64(seed ^ splitmix64(li >> 1));
+    const float u1 = (static_cast<float>((h >> 40) & 0xffffffu) + 1.0f) * (1.0f / 16777216.0f);
+    const float u2 = static_cast<float>((h >> 8) & 0xffffffu) * (1.0f / 16777216.0f);
+    const float rr = sqrtf(-2.0f * logf(u1));
+    float sn, cs;
+    sincospif(2.0f * u2, &sn, &cs);
+    dst[r * dst_stride + c] = __float2half_rn(mean + stddev * rr * ((li & 1) ? sn : cs));
+  }
+}
+
+__global__ void fill_value_f16_kernel(__half *dst, size_t count, float value) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count;
+       i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = __float2half_rn(value);
+}
+
 __global__ void fill_uniform_f32_kernel(float *dst, size_t count, uint64_t seed, float lo,
                                         float hi) {
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count;
@@ -44,9 +73,11 @@ __global__ void fill_uniform_f32_kernel(float *dst, size_t count, uint64_t seed,
 
 // Resolve packed argmax keys (after a cross-rank max) into token ids and reset.
 __global__ void argmax_finalize_kernel(unsigned long long *keys, int rows, int *next_tokens,
-                                       int *feed_tokens, int *feed_positions) {
+                                       int *feed_tokens, int *feed_positions, int *history,
+                                       unsigned int *history_counter) {
   pdl_wait();
   const int m = threadIdx.x;
+  const unsigned int step = history != nullptr ? *history_counter : 0u;
   if (m < rows) {
     const unsigned long long key = keys[m];
     keys[m] = 0ull;
@@ -54,7 +85,10 @@ __global__ void argmax_finalize_kernel(unsigned long long *keys, int rows, int *
     next_tokens[m] = tok;
     if (feed_tokens != nullptr) feed_tokens[m] = tok;
     if (feed_positions != nullptr) feed_positions[m] += 1;
+    if (history != nullptr) history[(size_t)step * rows + m] = tok;
   }
+  __syncthreads();
+  if (m == 0 && history != nullptr) *history_counter = step + 1;
 }
 
 __global__ void add_residual_f32_kernel(__half *h, const float *partial, int n) {
@@ -77,6 +111,27 @@ cudaError_t launch_fill_normal_f16(__half *dst, size_t count, uint64_t seed, flo
   return cudaGetLastError();
 }
 
+cudaError_t launch_fill_normal_2d(__half *dst, int rows, int cols, long long dst_stride,
+                                  uint64_t seed, long long logical_row0, long long logical_cols,
+                                  long long logical_col0, float mean, float stddev,
+                                  cudaStream_t stream) {
+  const long long total = (long long)rows * cols;
+  if (total <= 0) return cudaSuccess;
+  long long blocks = (total + 255) / 256;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  fill_normal_2d_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(
+      dst, rows, cols, dst_stride, seed, logical_row0, logical_cols, logical_col0, mean, stddev);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_fill_value_f16(__half *dst, size_t count, float value, cudaStream_t stream) {
+  if (count == 0) return cudaSuccess;
+  int blocks = static_cast<int>((count + 255) / 256);
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  fill_value_f16_kernel<<<blocks, 256, 0, stream>>>(dst, count, value);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_fill_uniform_f32(float *dst, size_t count, uint64_t seed, float lo, float hi,
                                     cudaStream_t stream) {
   if (count == 0) return cudaSuccess;
@@ -87,8 +142,8 @@ cudaError_t launch_fill_uniform_f32(float *dst, size_t count, uint64_t seed, flo
 }
 
 cudaError_t launch_argmax_finalize(unsigned long long *keys, int rows, int *next_tokens,
-                                   int *feed_tokens, int *feed_positions, cudaStream_t stream,
-                                   bool pdl) {
+                                   int *feed_tokens, int *feed_positions, int *history,
+                                   unsigned int *history_counter, cudaStream_t stream, bool pdl) {
   if (rows <= 0 || rows > 1024) return cudaErrorInvalidValue;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(1);
@@ -100,7 +155,7 @@ cudaError_t launch_argmax_finalize(unsigned long long *keys, int rows, int *next
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, argmax_finalize_kernel, keys, rows, next_tokens, feed_tokens,
-                            feed_positions);
+                            feed_positions, history, history_counter);
 }
 
 cudaError_t launch_add_residual_f32(__half *h, const float *partial, int n, cudaStream_t stream,

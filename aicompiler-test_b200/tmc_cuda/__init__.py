@@ -247,3 +247,210 @@ def paged_attention_f16(rt: Runtime, q: Buffer, out: Buffer, k_pool: Buffer, v_p
 
 def fill_normal_f16(rt: Runtime, buf: Buffer, seed: int, mean: float, std: float):
     check(lib.tmc_k_fill_normal_f16(buf.ptr, buf.count, seed, mean, std, rt.stream))
+
+
+# ---- decoder executor (tmc_decoder_*) ------------------------------------------------
+
+class DecoderConfig(ctypes.Structure):
+    _fields_ = [
+        ("hidden_size", c_int), ("heads", c_int), ("kv_heads", c_int), ("head_dim", c_int),
+        ("intermediate_size", c_int), ("vocab_size", c_int), ("layers", c_int),
+        ("capacity", c_int), ("epsilon", c_float), ("rope_theta", ctypes.c_double),
+        ("max_rows", c_int), ("max_slots", c_int), ("page_size", c_int), ("pool_pages", c_int),
+        ("tp_rank", c_int), ("tp_size", c_int), ("use_graphs", c_int), ("use_pdl", c_int),
+    ]
+
+
+_I32P = POINTER(c_int32)
+_sig("tmc_decoder_create", c_int, c_void_p, POINTER(DecoderConfig), POINTER(c_void_p))
+_sig("tmc_decoder_destroy", None, c_void_p)
+_sig("tmc_decoder_load_weight", c_int, c_void_p, c_char_p, POINTER(c_float), c_size_t)
+_sig("tmc_decoder_load_weight_f16", c_int, c_void_p, c_char_p, c_void_p, c_size_t)
+_sig("tmc_decoder_read_weight", c_int, c_void_p, c_char_p, POINTER(c_float), c_size_t)
+_sig("tmc_decoder_init_random", c_int, c_void_p, c_uint64, c_float)
+_sig("tmc_decoder_prefill", c_int, c_void_p, c_int, _I32P, c_int, POINTER(c_float), _I32P)
+_sig("tmc_decoder_decode", c_int, c_void_p, _I32P, _I32P, c_int, POINTER(c_float), _I32P)
+_sig("tmc_decoder_generate", c_int, c_void_p, _I32P, _I32P, c_int, c_int, _I32P,
+     POINTER(ctypes.c_double))
+_sig("tmc_decoder_current_length", c_size_t, c_void_p, c_int)
+_sig("tmc_decoder_read_kv", c_int, c_void_p, c_int, c_int, POINTER(c_float), POINTER(c_float), c_size_t)
+_sig("tmc_decoder_restore_kv", c_int, c_void_p, c_int, c_size_t, POINTER(c_float), POINTER(c_float))
+_sig("tmc_decoder_block_table", c_int, c_void_p, c_int, _I32P, c_size_t, POINTER(c_size_t))
+_sig("tmc_decoder_stage_length", c_int, c_void_p, c_int, c_size_t)
+_sig("tmc_decoder_commit_length", c_int, c_void_p, c_int, c_size_t)
+_sig("tmc_decoder_rollback_length", c_int, c_void_p, c_int, c_size_t)
+_sig("tmc_decoder_release", c_int, c_void_p, c_int)
+_sig("tmc_decoder_storage", c_int, c_void_p, POINTER(c_size_t), POINTER(c_size_t), POINTER(c_size_t))
+_sig("tmc_decoder_local_dims", c_int, c_void_p, POINTER(c_int), POINTER(c_int), POINTER(c_int),
+     POINTER(c_int), POINTER(c_int))
+_sig("tmc_decoder_pool_stats", c_int, c_void_p, POINTER(c_size_t), POINTER(c_size_t),
+     POINTER(c_size_t), POINTER(c_size_t), POINTER(c_size_t))
+_sig("tmc_decoder_inject_page_failures", c_int, c_void_p, c_size_t)
+_sig("tmc_decoder_kernels_per_step", c_int, c_void_p, c_int)
+_sig("tmc_decoder_step_bytes", ctypes.c_double, c_void_p, c_int, _I32P)
+_sig("tmc_decoder_profile_kernel", c_int, c_void_p, c_int, c_int, c_int, POINTER(ctypes.c_double),
+     POINTER(ctypes.c_double), POINTER(c_int))
+_sig("tmc_nccl_unique_id", c_int, ctypes.c_char_p, c_size_t)
+_sig("tmc_decoder_attach_nccl", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_int, c_int)
+
+
+def _i32(a):
+    return np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))
+
+
+class Decoder:
+    """Decoder executor (reference CompiledDecoderLLM, DecoderLLMExecutor.hpp:46-102)."""
+
+    def __init__(self, runtime: Runtime, hidden, heads, intermediate, vocab, layers, capacity,
+                 kv_heads=None, head_dim=None, epsilon=1e-5, rope_theta=10000.0, max_rows=8,
+                 max_slots=1, page_size=0, pool_pages=0, tp_rank=0, tp_size=1, use_graphs=True,
+                 use_pdl=True):
+        self.runtime = runtime
+        cfg = DecoderConfig(hidden, heads, kv_heads or heads, head_dim or hidden // heads,
+                            intermediate, vocab, layers, capacity, epsilon, rope_theta, max_rows,
+                            max_slots, page_size, pool_pages, tp_rank, tp_size, int(use_graphs),
+                            int(use_pdl))
+        self.cfg = cfg
+        h = c_void_p()
+        check(lib.tmc_decoder_create(runtime.handle, ctypes.byref(cfg), ctypes.byref(h)))
+        self.handle = h
+        dims = [c_int() for _ in range(5)]
+        check(lib.tmc_decoder_local_dims(h, *[ctypes.byref(d) for d in dims]))
+        (self.local_heads, self.local_kv_heads, self.local_intermediate, self.local_vocab,
+         self.vocab_offset) = [d.value for d in dims]
+
+    def close(self):
+        if self.handle:
+            lib.tmc_decoder_destroy(self.handle)
+            self.handle = c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # weights
+    def load_weight(self, name: str, values):
+        values = np.asarray(values)
+        if values.dtype == np.float16:
+            v = np.ascontiguousarray(values.reshape(-1))
+            check(lib.tmc_decoder_load_weight_f16(self.handle, name.encode(), v.ctypes.data_as(c_void_p), v.size))
+        else:
+            v = np.ascontiguousarray(values.reshape(-1), dtype=np.float32)
+            check(lib.tmc_decoder_load_weight(self.handle, name.encode(), _fptr(v), v.size))
+
+    def load_weights(self, weights: dict):
+        for name, value in weights.items():
+            self.load_weight(name, value)
+
+    def read_weight(self, name: str, count: int) -> np.ndarray:
+        out = np.empty(count, dtype=np.float32)
+        check(lib.tmc_decoder_read_weight(self.handle, name.encode(), _fptr(out), count))
+        return out
+
+    def init_random(self, seed: int, std: float = 0.02):
+        check(lib.tmc_decoder_init_random(self.handle, seed, std))
+
+    # execution
+    def prefill(self, tokens, slot=0, logits=True):
+        t = _i32(tokens)
+        out = np.empty((t.size, self.local_vocab), dtype=np.float32) if logits else None
+        nxt = np.zeros(1, dtype=np.int32)
+        check(lib.tmc_decoder_prefill(self.handle, slot, t.ctypes.data_as(_I32P), t.size,
+                                      _fptr(out) if logits else None, nxt.ctypes.data_as(_I32P)))
+        return out, int(nxt[0])
+
+    def decode(self, tokens, slots=None, logits=True):
+        t = _i32(tokens)
+        s = _i32(slots if slots is not None else range(t.size))
+        out = np.empty((t.size, self.local_vocab), dtype=np.float32) if logits else None
+        nxt = np.zeros(t.size, dtype=np.int32)
+        check(lib.tmc_decoder_decode(self.handle, s.ctypes.data_as(_I32P), t.ctypes.data_as(_I32P), t.size,
+                                     _fptr(out) if logits else None, nxt.ctypes.data_as(_I32P)))
+        return out, nxt
+
+    def generate(self, tokens, steps, slots=None):
+        t = _i32(tokens)
+        s = _i32(slots if slots is not None else range(t.size))
+        out = np.zeros((steps, t.size), dtype=np.int32)
+        us = ctypes.c_double(0.0)
+        check(lib.tmc_decoder_generate(self.handle, s.ctypes.data_as(_I32P), t.ctypes.data_as(_I32P), t.size,
+                                       steps, out.ctypes.data_as(_I32P), ctypes.byref(us)))
+        return out, us.value
+
+    # KV state
+    def length(self, slot=0) -> int:
+        return int(lib.tmc_decoder_current_length(self.handle, slot))
+
+    def read_kv(self, layer, slot=0):
+        n = self.local_kv_heads * self.length(slot) * self.cfg.head_dim
+        k = np.empty(n, np.float32)
+        v = np.empty(n, np.float32)
+        check(lib.tmc_decoder_read_kv(self.handle, layer, slot, _fptr(k), _fptr(v), n))
+        shape = (self.local_kv_heads, self.length(slot), self.cfg.head_dim)
+        return k.reshape(shape), v.reshape(shape)
+
+    def restore_kv(self, slot, keys, values):
+        keys = np.ascontiguousarray(keys, dtype=np.float32)
+        values = np.ascontiguousarray(values, dtype=np.float32)
+        length = keys.shape[2]
+        check(lib.tmc_decoder_restore_kv(self.handle, slot, length, _fptr(keys), _fptr(values)))
+
+    def block_table(self, slot=0):
+        n = c_size_t(0)
+        check(lib.tmc_decoder_block_table(self.handle, slot, None, 0, ctypes.byref(n)))
+        out = np.zeros(n.value, np.int32)
+        check(lib.tmc_decoder_block_table(self.handle, slot, out.ctypes.data_as(_I32P), n.value, ctypes.byref(n)))
+        return out
+
+    def stage(self, slot, length):
+        check(lib.tmc_decoder_stage_length(self.handle, slot, length))
+
+    def commit(self, slot, length):
+        check(lib.tmc_decoder_commit_length(self.handle, slot, length))
+
+    def rollback(self, slot, length):
+        check(lib.tmc_decoder_rollback_length(self.handle, slot, length))
+
+    def release(self, slot=0):
+        check(lib.tmc_decoder_release(self.handle, slot))
+
+    def storage(self):
+        a, b, c = c_size_t(), c_size_t(), c_size_t()
+        check(lib.tmc_decoder_storage(self.handle, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)))
+        return {"model": a.value, "kv": b.value, "activation": c.value}
+
+    def pool_stats(self):
+        vals = [c_size_t() for _ in range(5)]
+        check(lib.tmc_decoder_pool_stats(self.handle, *[ctypes.byref(v) for v in vals]))
+        return dict(zip(("capacity", "used", "peak", "allocations", "releases"), [v.value for v in vals]))
+
+    def inject_page_failures(self, n):
+        check(lib.tmc_decoder_inject_page_failures(self.handle, n))
+
+    def kernels_per_step(self, rows=1) -> int:
+        return int(lib.tmc_decoder_kernels_per_step(self.handle, rows))
+
+    def step_bytes(self, context_lengths) -> float:
+        c = _i32(context_lengths)
+        return float(lib.tmc_decoder_step_bytes(self.handle, c.size, c.ctypes.data_as(_I32P)))
+
+    KERNELS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head")
+
+    def profile_kernel(self, kind, rows=1, rounds=4):
+        """(mean launch us, algorithmic bytes per launch, launches per step)."""
+        k = self.KERNELS.index(kind) if isinstance(kind, str) else int(kind)
+        us, b, n = ctypes.c_double(), ctypes.c_double(), c_int()
+        check(lib.tmc_decoder_profile_kernel(self.handle, k, rows, rounds, ctypes.byref(us),
+                                             ctypes.byref(b), ctypes.byref(n)))
+        return us.value, b.value, n.value
+
+    def attach_nccl(self, unique_id: bytes, world: int, rank: int):
+        check(lib.tmc_decoder_attach_nccl(self.handle, unique_id, len(unique_id), world, rank))
+
+
+def nccl_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(128)
+    check(lib.tmc_nccl_unique_id(buf, 128))
+    return buf.raw

@@ -147,6 +147,116 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
 int tmc_k_fill_normal_f16(void *dst, size_t count, uint64_t seed, float mean, float stddev,
                           void *stream);
 
+
+/* ---- decoder executor ----------------------------------------------------
+ * tmc_decoder replaces tensor::runtime::CompiledDecoderLLM and
+ * compileDecoderLLM (DecoderLLMExecutor.hpp:46-101) for fp16 storage. One
+ * executor holds up to max_slots sequences (the reference holds one request per
+ * executor and shares KV pools between executors, ServingRuntime.cpp:569-618).
+ * Config fields follow DecoderLLMPlan / KVCachePlan (DecoderLLMPlan.hpp:9-22,
+ * KVCachePlan.hpp:9-22) and DecoderLLMCompileOptions (DecoderLLMExecutor.hpp:19-29),
+ * extended with kv_heads (grouped-query attention) and rope_theta. */
+typedef struct {
+  int hidden_size, heads, kv_heads, head_dim, intermediate_size, vocab_size, layers;
+  int capacity;      /* KVCachePlan::capacity: positions per sequence */
+  float epsilon;     /* DecoderLLMPlan::rmsNormEpsilon */
+  double rope_theta;
+  int max_rows;      /* tokens per step, 1..8 */
+  int max_slots;     /* sequences with KV state */
+  int page_size;     /* DecoderLLMCompileOptions::kvPageSize; 0 = contiguous */
+  int pool_pages;    /* 0 = max_slots * ceil(capacity / page_size) */
+  int tp_rank, tp_size;
+  int use_graphs, use_pdl;
+} tmc_decoder_config;
+
+typedef struct tmc_decoder tmc_decoder;
+
+/* compileDecoderLLM (DecoderLLMExecutor.hpp:99-101): allocate weights, KV pools
+ * and activations on the runtime's device. Weights start at zero (norms at 1). */
+int tmc_decoder_create(tmc_runtime *rt, const tmc_decoder_config *cfg, tmc_decoder **out);
+void tmc_decoder_destroy(tmc_decoder *dec);
+/* Weights by the reference manifest's logical names (export_decoder_llm.py:531-547):
+ * "embedding.weight", "final_norm.weight", "lm_head.weight", "rope.cosine",
+ * "rope.sine", "layer{i}.{input_norm,q,k,v,o,post_norm,gate,up,down}.weight".
+ * Values are the full logical tensor; each rank keeps its tensor-parallel shard.
+ * (DecoderLLMImporter.cpp:154-281 reads the same names.) */
+int tmc_decoder_load_weight(tmc_decoder *dec, const char *name, const float *values, size_t count);
+int tmc_decoder_load_weight_f16(tmc_decoder *dec, const char *name, const uint16_t *bits,
+                                size_t count);
+/* Rank-local window of a logical weight as floats (count must match it). */
+int tmc_decoder_read_weight(tmc_decoder *dec, const char *name, float *out, size_t count);
+/* Synthetic random init: every matrix ~N(0, stddev^2) from a counter-based
+ * generator indexed by the logical element, so shards agree with TP=1. */
+int tmc_decoder_init_random(tmc_decoder *dec, uint64_t seed, float stddev);
+/* CompiledDecoderLLM::prefill / prefillChunked (DecoderLLMExecutor.hpp:55-58):
+ * count tokens of one sequence in max_rows chunks. logits: NULL or
+ * [count, local_vocab] floats; next_token: NULL or the greedy token after the
+ * last position. */
+int tmc_decoder_prefill(tmc_decoder *dec, int slot, const int32_t *tokens, int count,
+                        float *logits, int32_t *next_token);
+/* CompiledDecoderLLM::decode (DecoderLLMExecutor.hpp:59-60) for `rows`
+ * sequences at once (distinct slots): stage length+1, run the step graph,
+ * commit. logits: NULL or [rows, local_vocab]; next_tokens: [rows]. */
+int tmc_decoder_decode(tmc_decoder *dec, const int32_t *slots, const int32_t *tokens, int rows,
+                       float *logits, int32_t *next_tokens);
+/* Greedy loop on the device: `steps` replays of the step graph, each feeding
+ * its argmax back (the apps' host loop, decoder_llm_main.cpp:135-162, without
+ * host round trips). tokens_out: [steps, rows]; gpu_us: optional event time. */
+int tmc_decoder_generate(tmc_decoder *dec, const int32_t *slots, const int32_t *tokens, int rows,
+                         int steps, int32_t *tokens_out, double *gpu_us);
+/* CompiledDecoderLLM::currentLength (DecoderLLMExecutor.hpp:62). */
+size_t tmc_decoder_current_length(tmc_decoder *dec, int slot);
+/* readKeyPrefix / readValuePrefix (DecoderLLMExecutor.hpp:63-64):
+ * [local_kv_heads, length, head_dim] floats each; count = that size. */
+int tmc_decoder_read_kv(tmc_decoder *dec, int layer, int slot, float *key, float *value,
+                        size_t count);
+/* restoreKVCache (DecoderLLMExecutor.hpp:83): keys/values are
+ * [layers, local_kv_heads, length, head_dim] for an empty slot. */
+int tmc_decoder_restore_kv(tmc_decoder *dec, int slot, size_t length, const float *keys,
+                           const float *values);
+/* kvBlockTable (DecoderLLMExecutor.hpp:79-80): allocated physical pages. */
+int tmc_decoder_block_table(tmc_decoder *dec, int slot, int32_t *out, size_t capacity,
+                            size_t *count);
+/* stageKVLength / commitKVLength / rollbackKVLength / releaseKVCache
+ * (DecoderLLMExecutor.hpp:81-86). */
+int tmc_decoder_stage_length(tmc_decoder *dec, int slot, size_t length);
+int tmc_decoder_commit_length(tmc_decoder *dec, int slot, size_t length);
+int tmc_decoder_rollback_length(tmc_decoder *dec, int slot, size_t length);
+int tmc_decoder_release(tmc_decoder *dec, int slot);
+/* modelStorageBytes / kvStorageBytes / activationStorageBytes (DecoderLLMExecutor.hpp:72-74). */
+int tmc_decoder_storage(tmc_decoder *dec, size_t *model_bytes, size_t *kv_bytes,
+                        size_t *activation_bytes);
+/* Rank-local sizes: heads, kv heads, intermediate, vocab slice and its offset. */
+int tmc_decoder_local_dims(tmc_decoder *dec, int *heads, int *kv_heads, int *intermediate,
+                           int *vocab, int *vocab_offset);
+/* KVPagePool counters (KVCacheState.hpp:28-35): capacity, used, peak,
+ * allocations, releases. */
+int tmc_decoder_pool_stats(tmc_decoder *dec, size_t *capacity, size_t *used, size_t *peak,
+                           size_t *allocations, size_t *releases);
+/* Host-side failure injection for tests: the next n page allocations fail. */
+int tmc_decoder_inject_page_failures(tmc_decoder *dec, size_t n);
+/* Kernel launches in one step and the step's algorithmic HBM bytes (weights +
+ * KV reads/appends for the given per-row context lengths). */
+int tmc_decoder_kernels_per_step(tmc_decoder *dec, int rows);
+double tmc_decoder_step_bytes(tmc_decoder *dec, int rows, const int32_t *context_lengths);
+
+/* Time one kernel kind of the decode step in isolation (kind: 0 QKV, 1
+ * attention, 2 O projection, 3 gate/up, 4 down, 5 LM head): a CUDA graph of
+ * `rounds` passes over every layer's launch with the real weights, replayed
+ * between CUDA events on the executor's stream. Outputs the mean launch
+ * duration, the algorithmic HBM bytes of one launch and launches per step.
+ * Call after a decode/generate so the step inputs are staged. */
+int tmc_decoder_profile_kernel(tmc_decoder *dec, int kind, int rows, int rounds, double *avg_us,
+                               double *bytes_per_launch, int *launches_per_step);
+
+/* ---- tensor parallelism (NCCL over NVLink; no reference counterpart: the
+ * reference is single-device, README.md:321) ----
+ * Rank 0 creates the id and shares it with the other ranks out of band
+ * (e.g. torch.distributed broadcast); every rank then attaches its executor. */
+int tmc_nccl_unique_id(uint8_t *id, size_t nbytes);
+int tmc_decoder_attach_nccl(tmc_decoder *dec, const uint8_t *id, size_t nbytes, int world,
+                            int rank);
+
 #ifdef __cplusplus
 }
 #endif
