@@ -1,7 +1,9 @@
 // CudaRuntime implementation (see CudaRuntime.hpp).
 #include "CudaRuntime.hpp"
 
+#include <algorithm>
 #include <chrono>
+#include <cstring>
 #include <cmath>
 #include <limits>
 #include <sstream>
@@ -166,7 +168,8 @@ CudaRuntime::CudaRuntime(int device) : device_(device) {
     return;
   }
   e = cudaMalloc(&status_, sizeof(tmc::TmcDeviceStatus));
-  if (e == cudaSuccess) e = cudaMemset(status_, 0, sizeof(tmc::TmcDeviceStatus));
+  if (e == cudaSuccess) e = cudaMemsetAsync(status_, 0, sizeof(tmc::TmcDeviceStatus), stream_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
   if (e != cudaSuccess) error_ = cudaMessage("status block", e);
 }
 
@@ -228,26 +231,21 @@ std::string CudaRuntime::writeBufferBytes(const BufferHandle &buffer, const void
     return "writeBufferBytes: write exceeds the buffer.";
   if (byteCount == 0) return {};
   DeviceGuard guard(device_);
-  cudaError_t e = cudaMemcpy(static_cast<char *>(buffer->data()) + byteOffset, bytes, byteCount,
-                             cudaMemcpyHostToDevice);
+  // Ordered on the runtime stream (kernels run there; the legacy default
+  // stream does not synchronise with a non-blocking stream), then completed
+  // before returning because `bytes` is caller-owned pageable memory.
+  cudaError_t e = cudaMemcpyAsync(static_cast<char *>(buffer->data()) + byteOffset, bytes, byteCount,
+                                  cudaMemcpyHostToDevice, stream_);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream_);
   return e == cudaSuccess ? std::string() : cudaMessage("cudaMemcpy H2D", e);
 }
 
 std::string CudaRuntime::fillSentinel(const BufferHandle &buffer) const {
   if (!buffer) return "fillSentinel: null buffer.";
   DeviceGuard guard(device_);
-  cudaError_t e;
-  switch (buffer->elementType()) {
-    case ElementType::Int32:
-      e = cudaMemset(buffer->data(), 0, buffer->byteCount());
-      break;
-    case ElementType::Float32:
-      e = cudaMemset(buffer->data(), 0xff, buffer->byteCount());  // 0xffffffff is a NaN
-      break;
-    default:
-      e = cudaMemset(buffer->data(), 0xff, buffer->byteCount());  // 0xffff is a NaN (fp16, bf16)
-      break;
-  }
+  // Integers 0; floating types all-ones bits, a NaN for fp32, fp16 and bf16.
+  const int pattern = buffer->elementType() == ElementType::Int32 ? 0 : 0xff;
+  cudaError_t e = cudaMemsetAsync(buffer->data(), pattern, buffer->byteCount(), stream_);
   return e == cudaSuccess ? std::string() : cudaMessage("cudaMemset", e);
 }
 
@@ -351,7 +349,7 @@ std::string CudaRuntime::consumeDeviceStatus() const {
   cudaError_t e = cudaMemcpy(&host, status_, sizeof(host), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cudaMessage("status readback", e);
   if (host.code == 0) return {};
-  cudaMemset(status_, 0, sizeof(host));
+  cudaMemsetAsync(status_, 0, sizeof(host), stream_);  // ordered before later kernels
   return describeDeviceStatus(host);
 }
 

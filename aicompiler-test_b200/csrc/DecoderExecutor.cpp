@@ -175,11 +175,12 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)R * hkvL_, I32, &attnCounters_, &activationBytes_)).empty()) return e;
   // Zero the state the kernels expect zero (int32 buffers were zero-filled by
   // createBuffer); residual-stream buffers start at zero too.
-  TMC_TRY(cudaMemset(argmaxKeys_->data(), 0, argmaxKeys_->byteCount()));
-  TMC_TRY(cudaMemset(h_->data(), 0, h_->byteCount()));
-  TMC_TRY(cudaMemset(hB_->data(), 0, hB_->byteCount()));
+  cudaStream_t s0 = rt_.stream();
+  TMC_TRY(cudaMemsetAsync(argmaxKeys_->data(), 0, argmaxKeys_->byteCount(), s0));
+  TMC_TRY(cudaMemsetAsync(h_->data(), 0, h_->byteCount(), s0));
+  TMC_TRY(cudaMemsetAsync(hB_->data(), 0, hB_->byteCount(), s0));
   // Block table: -1 = unmapped.
-  TMC_TRY(cudaMemset(blockTable_->data(), 0xff, blockTable_->byteCount()));
+  TMC_TRY(cudaMemsetAsync(blockTable_->data(), 0xff, blockTable_->byteCount(), s0));
   TMC_TRY(cudaMallocHost(&pinnedIO_, sizeof(std::int32_t) * 4 * R));
   // Norm weights default to 1 (nn.Parameter(torch.ones), decoder_llm.py:11).
   for (auto &L : layers_) {
@@ -503,11 +504,12 @@ std::string DecoderExecutor::restoreKV(int slot, std::size_t length,
             kb[dst] = cuda::floatToHalfBits(keys[l][src]);
             vb[dst] = cuda::floatToHalfBits(values[l][src]);
           }
-      cudaError_t ce = cudaMemcpy(static_cast<std::uint16_t *>(layers_[l].kPool->data()) + page * pageElems, kb.data(),
-                                  pageElems * 2, cudaMemcpyHostToDevice);
+      cudaError_t ce = cudaMemcpyAsync(static_cast<std::uint16_t *>(layers_[l].kPool->data()) + page * pageElems,
+                                       kb.data(), pageElems * 2, cudaMemcpyHostToDevice, rt_.stream());
       if (ce == cudaSuccess)
-        ce = cudaMemcpy(static_cast<std::uint16_t *>(layers_[l].vPool->data()) + page * pageElems, vb.data(),
-                        pageElems * 2, cudaMemcpyHostToDevice);
+        ce = cudaMemcpyAsync(static_cast<std::uint16_t *>(layers_[l].vPool->data()) + page * pageElems, vb.data(),
+                             pageElems * 2, cudaMemcpyHostToDevice, rt_.stream());
+      if (ce == cudaSuccess) ce = cudaStreamSynchronize(rt_.stream());
       if (ce != cudaSuccess) {
         (void)st.rollbackLength(0);
         return cudaText("restore copy", ce);
