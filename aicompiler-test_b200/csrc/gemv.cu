@@ -518,9 +518,10 @@ cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, 
 
 }  // namespace
 
-cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
-  if (p.K <= 0 || (p.K & 7) != 0 || p.N <= 0 || p.M <= 0 || p.M > 8) return cudaErrorInvalidValue;
-  if ((p.epilogue == kEpiQKV || p.epilogue == kEpiSwiGLU) && (p.N & 1)) return cudaErrorInvalidValue;
+namespace {
+
+// One launch for M rows whose staged activations fit in shared memory.
+cudaError_t launch_rows(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
   const bool f32_in = (p.prologue == kProF32 || p.prologue == kProF32Norm);
   const size_t k = static_cast<size_t>(p.K);
   // fp32 staging keeps un-rounded fp32 activations exact (C1 graph); fp16 staging
@@ -541,6 +542,55 @@ cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int 
   }
   if (f32_in || k * 8 * 2 > 200 * 1024) return cudaErrorInvalidValue;
   return launch_instance<__half, 8, 2, 4>(p, stream, pdl, num_sms);
+}
+
+// Largest row count per launch whose staging fits (see launch_rows).
+int max_rows_per_launch(const GemvParams &p) {
+  const bool f32_in = (p.prologue == kProF32 || p.prologue == kProF32Norm);
+  const size_t k = static_cast<size_t>(p.K);
+  const size_t budget = 200 * 1024;
+  const size_t per_row = k * (f32_in ? 4 : 2);
+  if (per_row > budget) return 0;
+  int m = static_cast<int>(budget / per_row);
+  if (m >= 8) return 8;
+  if (m >= 4) return 4;
+  if (m >= 2) return 2;
+  return 1;
+}
+
+}  // namespace
+
+cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
+  if (p.K <= 0 || (p.K & 7) != 0 || p.N <= 0 || p.M <= 0 || p.M > 8) return cudaErrorInvalidValue;
+  if ((p.epilogue == kEpiQKV || p.epilogue == kEpiSwiGLU) && (p.N & 1)) return cudaErrorInvalidValue;
+  const int cap = max_rows_per_launch(p);
+  if (cap <= 0) return cudaErrorInvalidValue;
+  if (p.M <= cap) return launch_rows(p, stream, pdl, num_sms);
+  // Too many rows to stage at once: one launch per group of `cap` rows with
+  // every row-indexed pointer offset (each launch streams the weights again).
+  if (p.history != nullptr) return cudaErrorInvalidValue;  // greedy history indexes rows by M
+  for (int m0 = 0; m0 < p.M; m0 += cap) {
+    GemvParams q = p;
+    q.M = p.M - m0 < cap ? p.M - m0 : cap;
+    const bool f32_in = (p.prologue == kProF32 || p.prologue == kProF32Norm);
+    if (p.x) q.x = f32_in ? static_cast<const void *>(static_cast<const float *>(p.x) + m0 * p.x_stride)
+                         : static_cast<const void *>(static_cast<const __half *>(p.x) + m0 * p.x_stride);
+    if (p.tokens) q.tokens = p.tokens + m0;
+    if (p.h_out) q.h_out = p.h_out + (size_t)m0 * p.K;
+    if (p.partial) q.partial = p.partial + (size_t)m0 * p.K;
+    if (p.y_f32) q.y_f32 = p.y_f32 + (size_t)m0 * p.y_stride;
+    if (p.y_f16) q.y_f16 = p.y_f16 + (size_t)m0 * p.y_stride;
+    if (p.residual) q.residual = p.residual + (size_t)m0 * p.y_stride;
+    if (p.positions) q.positions = p.positions + m0;
+    if (p.table_rows) q.table_rows = p.table_rows + m0;
+    if (p.argmax_keys) q.argmax_keys = p.argmax_keys + m0;
+    if (p.next_tokens) q.next_tokens = p.next_tokens + m0;
+    if (p.feed_tokens) q.feed_tokens = p.feed_tokens + m0;
+    if (p.feed_positions) q.feed_positions = p.feed_positions + m0;
+    cudaError_t e = launch_rows(q, stream, pdl, num_sms);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 }  // namespace tmc

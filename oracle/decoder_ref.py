@@ -84,6 +84,11 @@ class DecoderOracle:
     rope_cos: torch.Tensor | None = None
     rope_sin: torch.Tensor | None = None
     caches: dict = field(default_factory=dict)  # seq -> list[(K [Hkv,L,D], V)] per layer
+    # When set, every linear layer sums its inputs in a fixed permuted order:
+    # mathematically the same model, a different fp32 summation order. The
+    # spread between two such oracles is the order-of-operations noise floor
+    # that any other correct implementation (e.g. a GPU kernel) also shows.
+    summation_order_seed: int | None = None
 
     def __post_init__(self):
         dt = self.spec.dtype
@@ -92,6 +97,13 @@ class DecoderOracle:
         if self.rope_cos is None:
             self.rope_cos, self.rope_sin = rope_tables(self.spec.capacity, self.spec.head_dim,
                                                        self.spec.rope_theta)
+
+    def _linear(self, x, weight):
+        if self.summation_order_seed is None:
+            return F.linear(x, weight)
+        k = weight.shape[1]
+        perm = torch.from_numpy(np.random.default_rng(self.summation_order_seed + k).permutation(k))
+        return F.linear(x[..., perm], weight[:, perm])
 
     def length(self, seq) -> int:
         c = self.caches.get(seq)
@@ -117,9 +129,9 @@ class DecoderOracle:
         for layer in range(s.layers):
             p = f"layer{layer}."
             h = _rms_norm(x, self.w[p + "input_norm.weight"], s.epsilon)
-            q = F.linear(h, self.w[p + "q.weight"]).view(1, S, s.heads, D).transpose(1, 2)
-            k = F.linear(h, self.w[p + "k.weight"]).view(1, S, s.kv_heads, D).transpose(1, 2)
-            v = F.linear(h, self.w[p + "v.weight"]).view(1, S, s.kv_heads, D).transpose(1, 2)
+            q = self._linear(h, self.w[p + "q.weight"]).view(1, S, s.heads, D).transpose(1, 2)
+            k = self._linear(h, self.w[p + "k.weight"]).view(1, S, s.kv_heads, D).transpose(1, 2)
+            v = self._linear(h, self.w[p + "v.weight"]).view(1, S, s.kv_heads, D).transpose(1, 2)
             q = _rope(q, self.rope_cos, self.rope_sin, positions)
             k = _rope(k, self.rope_cos, self.rope_sin, positions)
             if past is not None:
@@ -135,12 +147,12 @@ class DecoderOracle:
             probs = torch.softmax(scores, dim=-1)
             ctx = torch.matmul(probs, vv.float()).to(dt)
             ctx = ctx.transpose(1, 2).contiguous().view(1, S, -1)
-            x = x + F.linear(ctx, self.w[p + "o.weight"])
+            x = x + self._linear(ctx, self.w[p + "o.weight"])
             h = _rms_norm(x, self.w[p + "post_norm.weight"], s.epsilon)
-            mlp = F.linear(F.silu(F.linear(h, self.w[p + "gate.weight"])) * F.linear(h, self.w[p + "up.weight"]),
+            mlp = self._linear(F.silu(self._linear(h, self.w[p + "gate.weight"])) * self._linear(h, self.w[p + "up.weight"]),
                            self.w[p + "down.weight"])
             x = x + mlp
-        logits = F.linear(_rms_norm(x, self.w["final_norm.weight"], s.epsilon), self.w["lm_head.weight"])
+        logits = self._linear(_rms_norm(x, self.w["final_norm.weight"], s.epsilon), self.w["lm_head.weight"])
         self.caches[seq] = new_cache
         nxt = int(logits[0, -1].argmax().item())
         return logits[0], nxt

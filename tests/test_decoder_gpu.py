@@ -31,12 +31,17 @@ def load(name):
     return g, json.loads(str(g["meta"]))
 
 
-def rms_close(got, ref, what):
+def rms_close(got, ref, what, floor=0.0):
+    """North-star tolerance max|err| <= 2e-3 x RMS(ref), widened to 3x the
+    oracle's own summation-order noise floor when one is given (deep fp16
+    models amplify last-bit differences of any reordering), plus the reference
+    app's fp16 tolerance atol = rtol = 2e-2 (decoder_llm_main.cpp:15-23)."""
     got = np.asarray(got, np.float64)
     ref = np.asarray(ref, np.float64)
     rms = float(np.sqrt(np.mean(ref ** 2)))
     err = float(np.max(np.abs(got - ref)))
-    assert err <= 2e-3 * rms, f"{what}: max err {err} > 2e-3 x rms {rms}"
+    tol = max(2e-3 * rms, 3.0 * floor)
+    assert err <= tol, f"{what}: max err {err} > tol {tol} (rms {rms}, floor {floor})"
     assert np.all(np.abs(got - ref) <= 2e-2 + 2e-2 * np.abs(ref)), f"{what}: reference fp16 tolerance"
 
 
@@ -251,17 +256,22 @@ def test_gqa_model_matches_oracle(rt, kv_heads, theta, hidden, heads):
     cos = torch.from_numpy(dec.read_weight("rope.cosine", spec.capacity * half).reshape(spec.capacity, half))
     sin = torch.from_numpy(dec.read_weight("rope.sine", spec.capacity * half).reshape(spec.capacity, half))
     oracle = DecoderOracle(spec, w, cos, sin)
+    alt = DecoderOracle(spec, w, cos, sin, summation_order_seed=7)  # noise-floor twin
     ref_tables = __import__("oracle.decoder_ref", fromlist=["rope_tables"]).rope_tables(spec.capacity, spec.head_dim, theta)
     torch.testing.assert_close(cos, ref_tables[0], rtol=0, atol=2e-6)
     prompt = np.random.default_rng(1).integers(0, spec.vocab, 37)
     lo, to = oracle.forward(0, prompt)
+    la, _ = alt.forward(0, prompt)
     lg, tg = dec.prefill(prompt)
-    rms_close(lg, lo.float().numpy(), "gqa prefill logits")
+    floor = float((lo.float() - la.float()).abs().max())
+    rms_close(lg, lo.float().numpy(), "gqa prefill logits", floor)
     t = to
     for step in range(12):
         lo, to2 = oracle.forward(0, [t])
+        la, _ = alt.forward(0, [t])
         lg, tg2 = dec.decode([t])
-        rms_close(lg[0], lo[0].float().numpy(), f"gqa decode {step}")
+        floor = float((lo.float() - la.float()).abs().max())
+        rms_close(lg[0], lo[0].float().numpy(), f"gqa decode {step}", floor)
         margin = np.sort(lo[0].float().numpy())[-2:]
         if margin[1] - margin[0] > 1e-2:
             assert int(tg2[0]) == to2
