@@ -13,8 +13,13 @@
 // (atomic ticket), so no second launch is needed.
 #include "attention.cuh"
 
+#include <cmath>
 #include <mutex>
+#include <string>
 #include <unordered_map>
+
+#include "api_util.hpp"
+#include "tmc_cuda.h"
 
 namespace tmc {
 namespace {
@@ -402,3 +407,102 @@ cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool
 }
 
 }  // namespace tmc
+
+// ---- allocation-free entry point ---------------------------------------------
+//
+// Some callers cannot allocate device memory when they call into this
+// library: a host that reserved all of its device memory up front for its own
+// pool, a runtime with a fixed memory plan that forbids allocation after
+// start-up, or code on a latency-critical path where cudaMalloc's implicit
+// device synchronisation is not acceptable. For them the split-K partials and
+// tickets of the attention kernel live in this fixed array instead of a
+// caller-provided workspace. Every GPU that loads the library holds the array
+// (8 MiB) until the process exits.
+namespace tmc {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_attention_scratch[kNoAllocScratchBytes];
+
+// Device address of the scratch array on the current device, resolved once per
+// device (host code cannot use the symbol itself: on the host it names a
+// stand-in, not device memory).
+cudaError_t attention_scratch_address(void **out) {
+  static std::mutex mu;
+  static std::unordered_map<int, void *> addresses;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = addresses.find(dev);
+  if (it == addresses.end()) {
+    void *ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_attention_scratch);
+    if (e != cudaSuccess) return e;
+    it = addresses.emplace(dev, ptr).first;
+  }
+  *out = it->second;
+  return cudaSuccess;
+}
+
+}  // namespace
+}  // namespace tmc
+
+extern "C" int tmc_k_paged_attention_f16_noalloc(
+    const void *q, void *out, const void *k_pool, const void *v_pool, const int32_t *block_table,
+    int table_stride, const int32_t *table_rows, const int32_t *positions, int rows, int hq, int hkv,
+    int d, int page_size, int pool_pages, int capacity, int max_splits, int min_chunk, void *status,
+    void *stream) {
+  using namespace tmc_api;
+  if (!q || !out || !k_pool || !v_pool || !block_table || !table_rows || !positions)
+    return fail(TMC_ERR_INVALID, "null pointer");
+  if (rows <= 0 || hq <= 0 || hkv <= 0 || d <= 0 || max_splits <= 0)
+    return fail(TMC_ERR_INVALID, "rows, heads, head_dim and max_splits must be positive");
+  // Scratch layout: split partials (acc, then m/l), then the tickets.
+  const size_t partials = tmc::attention_workspace_bytes(rows, hq, hkv, d, max_splits);
+  const size_t tickets_offset = (partials + 255) / 256 * 256;
+  const size_t needed = tickets_offset + (size_t)rows * hkv * sizeof(uint32_t);
+  if (needed > tmc::kNoAllocScratchBytes) {
+    return fail(TMC_ERR_UNSUPPORTED,
+                "paged attention (no-alloc): needs " + std::to_string(needed) +
+                    " bytes of scratch, the fixed limit is " + std::to_string(tmc::kNoAllocScratchBytes) +
+                    " (lower max_splits or rows, or use tmc_k_paged_attention_f16)");
+  }
+  void *scratch = nullptr;
+  cudaError_t e = tmc::attention_scratch_address(&scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(attention scratch)");
+  auto *base = static_cast<unsigned char *>(scratch);
+  auto *tickets = reinterpret_cast<unsigned int *>(base + tickets_offset);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents; the tickets must start at 0.
+  e = cudaMemsetAsync(tickets, 0, (size_t)rows * hkv * sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing attention scratch tickets");
+  tmc::AttentionParams p{};
+  p.q = static_cast<const __half *>(q);
+  p.q_stride = static_cast<long long>(hq) * d;
+  p.out = static_cast<__half *>(out);
+  p.out_stride = static_cast<long long>(hq) * d;
+  p.k_pool = static_cast<const __half *>(k_pool);
+  p.v_pool = static_cast<const __half *>(v_pool);
+  p.block_table = block_table;
+  p.table_stride = table_stride;
+  p.table_rows = table_rows;
+  p.positions = positions;
+  p.rows = rows;
+  p.hq = hq;
+  p.hkv = hkv;
+  p.head_dim = d;
+  p.page_size = page_size;
+  p.pool_pages = pool_pages;
+  p.capacity = capacity;
+  p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d)));
+  p.max_splits = max_splits;
+  p.min_chunk = min_chunk;
+  p.ws_acc = reinterpret_cast<float *>(base);
+  p.ws_ml = reinterpret_cast<float *>(base + (size_t)rows * hq * max_splits * d * sizeof(float));
+  p.counters = tickets;
+  p.status = static_cast<tmc::TmcDeviceStatus *>(status);
+  e = tmc::launch_attention(p, s, false);
+  if (e == cudaErrorInvalidValue) return fail(TMC_ERR_UNSUPPORTED, "attention: unsupported shape");
+  return e == cudaSuccess ? ok() : cuda_fail(e, "attention (no-alloc) launch");
+}

@@ -142,6 +142,31 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
                               int capacity, int max_splits, int min_chunk, void *workspace,
                               uint32_t *counters, void *status, void *stream);
 
+/* Allocation-free variant of tmc_k_paged_attention_f16, for callers that cannot
+ * allocate device memory at call time (a host that hands all device memory to
+ * its own pool up front, a runtime whose memory plan forbids allocation after
+ * start-up, or a latency-critical path that cannot afford cudaMalloc's implicit
+ * device synchronisation). This entry point has no counterpart in the
+ * reference. Same arguments and results as tmc_k_paged_attention_f16 minus the
+ * workspace and counters: the split partials and tickets live in one fixed
+ * 8 MiB device array that the library reserves on every GPU that loads it,
+ * until process exit. It calls no allocator.
+ * Limit: rows*hq*max_splits*(d+2)*4 bytes, rounded up to 256, plus rows*hkv*4
+ * bytes must fit in 8 MiB (8388608); larger requests fail with
+ * TMC_ERR_UNSUPPORTED before anything is launched (max_splits = 1 needs only
+ * the tickets). The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before
+ * any stream capture. All calls share the array and it keeps the previous
+ * call's contents; the tickets are cleared on `stream` before each launch, so
+ * calls that overlap on the GPU (e.g. on different streams) race and must be
+ * serialised by the caller. */
+int tmc_k_paged_attention_f16_noalloc(const void *q, void *out, const void *k_pool,
+                                      const void *v_pool, const int32_t *block_table,
+                                      int table_stride, const int32_t *table_rows,
+                                      const int32_t *positions, int rows, int hq, int hkv, int d,
+                                      int page_size, int pool_pages, int capacity, int max_splits,
+                                      int min_chunk, void *status, void *stream);
+
 /* Deterministic N(0, std^2) fp16 fill from a counter-based hash generator
  * (synthetic random-init weights without a host round trip). */
 int tmc_k_fill_normal_f16(void *dst, size_t count, uint64_t seed, float mean, float stddev,
