@@ -173,6 +173,8 @@ std::string DecoderExecutor::allocate() {
   const size_t wsBytes = tmc::attention_workspace_bytes(R, hqL_, hkvL_, D, maxSplits);
   if (!(e = make(wsBytes / 4 + 1, F32, &attnWorkspace_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)R * hkvL_, I32, &attnCounters_, &activationBytes_)).empty()) return e;
+  if (!(e = make((size_t)cfg_.layers * 6 * tmc::kGemvCounterWords, I32, &workCounters_, &activationBytes_)).empty())
+    return e;
   // Zero the state the kernels expect zero (int32 buffers were zero-filled by
   // createBuffer); residual-stream buffers start at zero too.
   cudaStream_t s0 = rt_.stream();
@@ -540,7 +542,7 @@ double DecoderExecutor::stepAlgorithmicBytes(int rows, const std::vector<int> &c
   return bytes;
 }
 
-std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
+std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bool distinct) {
   cudaStream_t s = rt_.stream();
   const bool pdl = cfg_.usePDL;
   const bool tp = cfg_.tpSize > 1;
@@ -599,6 +601,8 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
       p.k_pool = hp(L.kPool);
       p.v_pool = hp(L.vPool);
       p.status = status;
+      p.trace = traceSink(l, kind);
+      p.work_counter = workCounter(l, kind);
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("qkv gemv", e);
 
       return {};
@@ -626,10 +630,14 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
       a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
       a.max_splits = splits;
       a.min_chunk = 64;
+      // One row per sequence: only each row's newest K/V comes from the QKV
+      // kernel still running, older rows can be gathered before its completion.
+      a.early_mode = distinct ? 1 : 0;
       a.ws_acc = fp(attnWorkspace_);
       a.ws_ml = fp(attnWorkspace_) + (size_t)R * hqL_ * splits * D;
       a.counters = static_cast<unsigned int *>(attnCounters_->data());
       a.status = status;
+      a.trace = traceSink(l, kind);
       if ((e = tmc::launch_attention(a, s, pdl)) != cudaSuccess) return cudaText("attention", e);
 
       return {};
@@ -654,6 +662,8 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
         p.residual = hA;
       }
       p.status = status;
+      p.trace = traceSink(l, kind);
+      p.work_counter = workCounter(l, kind);
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("o gemv", e);
       if (tp && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (o): " + collective_->lastError();
@@ -683,6 +693,8 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
       p.y_f16 = hp(act_);
       p.y_stride = iL_;
       p.status = status;
+      p.trace = traceSink(l, kind);
+      p.work_counter = workCounter(l, kind);
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("gate/up gemv", e);
 
       return {};
@@ -707,6 +719,8 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
         p.residual = hA;
       }
       p.status = status;
+      p.trace = traceSink(l, kind);
+      p.work_counter = workCounter(l, kind);
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("down gemv", e);
       if (tp && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (down): " + collective_->lastError();
@@ -748,7 +762,9 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
         p.history_counter = static_cast<unsigned int *>(historyCounter_->data());
       }
     }
-    if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("lm head gemv", e);
+    p.trace = traceSink(0, kind);
+    p.work_counter = workCounter(0, kind);
+      if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("lm head gemv", e);
     if (tp) {
       if ((e = collective_->allReduceMaxU64(p.argmax_keys, R, s)) != cudaSuccess)
         return "allreduce (argmax): " + collective_->lastError();
@@ -767,15 +783,65 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed) {
   }
 }
 
-std::string DecoderExecutor::enqueueStep(int R, bool feed) {
+std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct) {
   const bool tp = cfg_.tpSize > 1;
   if (tp && !collective_) return "tensor parallelism needs a collective (setCollective).";
   for (int l = 0; l < cfg_.layers; ++l)
     for (int kind = kKernelQKV; kind <= kKernelDown; ++kind) {
-      auto e = enqueueKernel(kind, l, R, feed);
+      auto e = enqueueKernel(kind, l, R, feed, distinct);
       if (!e.empty()) return e;
     }
-  return enqueueKernel(kKernelLMHead, 0, R, feed);
+  return enqueueKernel(kKernelLMHead, 0, R, feed, distinct);
+}
+
+unsigned int *DecoderExecutor::workCounter(int layer, int kind) const {
+  return static_cast<unsigned int *>(workCounters_->data()) + (size_t)(layer * 6 + kind) * tmc::kGemvCounterWords;
+}
+
+tmc::TraceSink DecoderExecutor::traceSink(int layer, int kind) const {
+  tmc::TraceSink t{};
+  if (traceCapacity_ == 0) return t;
+  t.records = static_cast<tmc::TraceRecord *>(traceRecords_->data());
+  t.count = static_cast<unsigned int *>(traceCount_->data());
+  t.capacity = static_cast<unsigned int>(traceCapacity_);
+  t.tag = (static_cast<unsigned int>(layer) << 8) | static_cast<unsigned int>(kind);
+  return t;
+}
+
+std::string DecoderExecutor::setTrace(std::size_t capacity) {
+  auto e = rt_.synchronize();
+  if (!e.empty()) return e;
+  for (auto &kv : graphs_) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+  }
+  graphs_.clear();
+  traceCapacity_ = 0;
+  traceRecords_.reset();
+  traceCount_.reset();
+  if (capacity == 0) return {};
+  auto r = rt_.createBuffer(capacity * sizeof(tmc::TraceRecord) / 4, nullptr, ElementType::Int32);
+  if (!r.buffer) return r.errorMessage;
+  auto c = rt_.createBuffer(4, nullptr, ElementType::Int32);
+  if (!c.buffer) return c.errorMessage;
+  traceRecords_ = r.buffer;
+  traceCount_ = c.buffer;
+  traceCapacity_ = capacity;
+  return rt_.synchronize();
+}
+
+std::string DecoderExecutor::readTrace(std::vector<tmc::TraceRecord> *out) {
+  out->clear();
+  if (traceCapacity_ == 0) return "tracing is off";
+  auto e = rt_.synchronize();
+  if (!e.empty()) return e;
+  unsigned int n = 0;
+  TMC_TRY(cudaMemcpy(&n, traceCount_->data(), 4, cudaMemcpyDeviceToHost));
+  n = std::min<unsigned int>(n, static_cast<unsigned int>(traceCapacity_));
+  out->resize(n);
+  if (n) TMC_TRY(cudaMemcpy(out->data(), traceRecords_->data(), n * sizeof(tmc::TraceRecord), cudaMemcpyDeviceToHost));
+  TMC_TRY(cudaMemsetAsync(traceCount_->data(), 0, 4, rt_.stream()));
+  return rt_.synchronize();
 }
 
 std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *avgUs,
@@ -816,7 +882,7 @@ std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *
   TMC_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
   std::string err;
   for (int r = 0; r < rounds && err.empty(); ++r)
-    for (int l = 0; l < perRound && err.empty(); ++l) err = enqueueKernel(kind, l, R, false);
+    for (int l = 0; l < perRound && err.empty(); ++l) err = enqueueKernel(kind, l, R, false, true);
   cudaGraph_t graph = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(s, &graph);
   if (!err.empty() || ce != cudaSuccess) {
@@ -851,14 +917,14 @@ std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *
   return {};
 }
 
-std::string DecoderExecutor::launchStep(int R, bool feed) {
-  if (!cfg_.useGraphs) return enqueueStep(R, feed);
-  const auto key = std::make_pair(R, feed);
+std::string DecoderExecutor::launchStep(int R, bool feed, bool distinct) {
+  if (!cfg_.useGraphs) return enqueueStep(R, feed, distinct);
+  const int key = graphKey(R, feed, distinct);
   auto it = graphs_.find(key);
   if (it == graphs_.end()) {
     cudaStream_t s = rt_.stream();
     TMC_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
-    const std::string err = enqueueStep(R, feed);
+    const std::string err = enqueueStep(R, feed, distinct);
     cudaGraph_t graph = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (!err.empty() || ce != cudaSuccess) {
@@ -930,7 +996,7 @@ std::string DecoderExecutor::decode(const std::int32_t *slots, const std::int32_
   const auto c0 = std::chrono::steady_clock::now();
   err = uploadStepInputs(rows, tokens, positions.data(), tableRows.data());
   if (timing) cudaEventRecord(e0, rt_.stream());
-  if (err.empty()) err = launchStep(rows, false);
+  if (err.empty()) err = launchStep(rows, false, true);
   if (timing) cudaEventRecord(e1, rt_.stream());
   if (err.empty()) {
     cudaError_t ce = cudaMemcpyAsync(pinnedIO_ + 3 * cfg_.maxRows, nextTokens_->data(), sizeof(std::int32_t) * rows,
@@ -984,7 +1050,7 @@ std::string DecoderExecutor::prefill(int slot, const std::int32_t *tokens, int c
       cudaEventCreate(&e1);
       cudaEventRecord(e0, rt_.stream());
     }
-    if (err.empty()) err = launchStep(R, false);
+    if (err.empty()) err = launchStep(R, false, R == 1);
     if (timing) cudaEventRecord(e1, rt_.stream());
     if (err.empty() && logits) {
       cudaError_t ce = cudaMemcpyAsync(logits + (size_t)done * vL_, logits_->data(), sizeof(float) * R * vL_,
@@ -1057,13 +1123,13 @@ std::string DecoderExecutor::generate(const std::int32_t *slots, const std::int3
     if (ce != cudaSuccess) err = cudaText("history reset", ce);
   }
   // Build the graph before timing so capture cost is not counted.
-  if (err.empty() && cfg_.useGraphs && !graphs_.count({rows, true})) {
+  if (err.empty() && cfg_.useGraphs && !graphs_.count(graphKey(rows, true, true))) {
     err = rt_.synchronize();
     if (err.empty()) {
       cudaStream_t s = rt_.stream();
       cudaError_t ce = cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed);
       if (ce != cudaSuccess) err = cudaText("capture", ce);
-      std::string ee = err.empty() ? enqueueStep(rows, true) : err;
+      std::string ee = err.empty() ? enqueueStep(rows, true, true) : err;
       cudaGraph_t graph = nullptr;
       ce = cudaStreamEndCapture(s, &graph);
       if (!ee.empty() || ce != cudaSuccess) {
@@ -1078,13 +1144,13 @@ std::string DecoderExecutor::generate(const std::int32_t *slots, const std::int3
           cudaGraphDestroy(graph);
           err = cudaText("cudaGraphInstantiate", ce);
         } else {
-          graphs_.emplace(std::make_pair(rows, true), g);
+          graphs_.emplace(graphKey(rows, true, true), g);
         }
       }
     }
   }
   cudaEventRecord(e0, rt_.stream());
-  for (int i = 0; i < steps && err.empty(); ++i) err = launchStep(rows, true);
+  for (int i = 0; i < steps && err.empty(); ++i) err = launchStep(rows, true, true);
   cudaEventRecord(e1, rt_.stream());
   if (err.empty()) {
     cudaError_t ce = cudaMemcpyAsync(tokensOut, history_->data(), sizeof(std::int32_t) * steps * rows,

@@ -133,6 +133,14 @@ class DecoderExecutor {
   std::string profileKernel(int kind, int rows, int rounds, double *avgUs, double *bytesPerLaunch,
                             int *launchesPerStep);
 
+  // ---- tracing ----
+  // capacity > 0: every kernel of later steps appends per-CTA timeline records
+  // (tmc::TraceRecord; tag = ((layer << 8) | kind) << 32 | CTA); 0 turns it off.
+  // Step graphs are recaptured either way.
+  std::string setTrace(std::size_t capacity);
+  // Copy out and clear the records collected so far.
+  std::string readTrace(std::vector<tmc::TraceRecord> *out);
+
   // ---- KV state ----
   std::size_t currentLength(int slot) const;
   std::string stageLength(int slot, std::size_t length);
@@ -163,9 +171,12 @@ class DecoderExecutor {
  private:
   DecoderExecutor(cuda::CudaRuntime &runtime, const DecoderConfig &config);
   std::string allocate();
-  std::string enqueueStep(int rows, bool feed);
-  std::string enqueueKernel(int kind, int layer, int rows, bool feed);
-  std::string launchStep(int rows, bool feed);
+  // `distinct`: every row belongs to a different sequence (decode); prefill
+  // chunks put several rows of one sequence in a step.
+  std::string enqueueStep(int rows, bool feed, bool distinct);
+  std::string enqueueKernel(int kind, int layer, int rows, bool feed, bool distinct);
+  std::string launchStep(int rows, bool feed, bool distinct);
+  static int graphKey(int rows, bool feed, bool distinct) { return rows * 4 + (feed ? 2 : 0) + (distinct ? 1 : 0); }
   std::string uploadStepInputs(int rows, const std::int32_t *tokens, const std::int32_t *positions,
                                const std::int32_t *tableRows);
   std::string writeBlockRow(int slot, const std::vector<std::int32_t> &row);
@@ -195,9 +206,14 @@ class DecoderExecutor {
   cuda::BufferHandle blockTable_;   // int32 [maxSlots, maxPagesPerSeq]
   cuda::BufferHandle nextTokens_, argmaxKeys_, argmaxCounter_, history_, historyCounter_;
   cuda::BufferHandle attnWorkspace_, attnCounters_;
+  cuda::BufferHandle workCounters_;  // per launch site: tmc::kGemvCounterWords uints
+  unsigned int *workCounter(int layer, int kind) const;
   std::int32_t *pinnedIO_ = nullptr;   // host staging [3 * maxRows + maxRows]
   int historyCapacity_ = 0;
   std::vector<int> lastPositions_;  // positions of the last staged step (profiling)
+  cuda::BufferHandle traceRecords_, traceCount_;
+  std::size_t traceCapacity_ = 0;
+  tmc::TraceSink traceSink(int layer, int kind) const;
   bool ropeSet_ = false;
 
   std::shared_ptr<KVPagePool> pool_;
@@ -208,7 +224,7 @@ class DecoderExecutor {
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
   };
-  std::map<std::pair<int, bool>, Graph> graphs_;
+  std::map<int, Graph> graphs_;
 
   std::size_t modelBytes_ = 0, kvBytes_ = 0, activationBytes_ = 0;
 };

@@ -66,92 +66,135 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void ldmatrix_x2(uint32_t &r0, uint32_t &r1, const void *row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(row_addr)));
+}
+__device__ __forceinline__ void ldmatrix_x2_trans(uint32_t &r0, uint32_t &r1, const void *row_addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(smem_u32(row_addr)));
+}
+
+// D = A(16x16, fp16, row) * B(16x8, fp16, col) + C, fp32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
 template <int D, int G>
 struct Cfg {
-  static constexpr int T = (128 / G) > 64 ? 64 : (128 / G);  // positions per tile
-  static constexpr int E = (G * D / kThreads) > 1 ? (G * D / kThreads) : 1;  // outputs per thread
-  static constexpr int kChunks = D / 8;                       // 16-byte chunks per row
-  static constexpr size_t kStageBytes = (size_t)T * D * 2;    // one of K or V per stage
-  static constexpr size_t smem_bytes() {
-    return 4 * kStageBytes                 // sK[2], sV[2]
-           + (size_t)G * D * 4             // sQ
-           + (size_t)G * T * 4             // sS
-           + 3 * (size_t)G * 4 + 16        // sM, sL, sR (+pad)
-           + 2 * (size_t)T * 4             // sValid[2]
-           + 2 * 8 + 16;                   // bars
+  static constexpr int kWarpsPerCta = kThreads / 32;     // 4
+  static constexpr int kRowsPerWarp = 16;                // positions per warp per tile
+  static constexpr int T = kWarpsPerCta * kRowsPerWarp;  // 64 positions per tile
+  static constexpr int kRow = D + 8;                     // padded row (halves): conflict-free ldmatrix
+  static constexpr size_t kStageBytes = (size_t)T * kRow * 2;  // one of K or V per stage
+  static constexpr int kStages = 2;
+  static constexpr int kMaxSplits = 64;
+  static constexpr int kKSteps = D / 16;                 // QK^T k-steps
+  static constexpr int kDTiles = D / 8;                  // PV n-tiles
+  __host__ __device__ static constexpr size_t merge_bytes() { return (size_t)kWarpsPerCta * (G * D + 2 * G) * 4; }
+  __host__ __device__ static constexpr size_t smem_bytes() {
+    const size_t stages = (size_t)kStages * 2 * kStageBytes;
+    return (stages > merge_bytes() ? stages : merge_bytes())  // K/V ring, reused for the warp merge
+           + (size_t)kStages * T * 4                            // sValid
+           + (size_t)kMaxSplits * G * 4 * 2                     // combine weights (m then l)
+           + (size_t)2 * kStages * 8 + 32;                      // full/empty barriers (+align)
   }
 };
 
+// Grid (max_splits, Hkv, rows), 4 warps. A CTA owns one KV head of one query
+// row and a chunk of key positions; each warp runs flash-decoding on its own 16
+// positions of every 64-position tile with tensor-core MMAs (the G query heads
+// of the KV head fill rows of the 16-row A tile; unused rows are zero), keeps
+// its own online-softmax state, and the warps merge once at the end.
 template <int D, int G>
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionParams p) {
   using C = Cfg<D, G>;
-  constexpr int T = C::T, E = C::E;
+  constexpr int T = C::T, S = C::kStages, ROW = C::kRow;
+  static_assert(G <= 8 && D % 16 == 0, "attention tile shape");
   extern __shared__ __align__(128) unsigned char smem[];
   __half *sK = reinterpret_cast<__half *>(smem);
-  __half *sV = sK + 2 * T * D;
-  float *sQ = reinterpret_cast<float *>(sV + 2 * T * D);
-  float *sS = sQ + G * D;
-  float *sM = sS + G * T;
-  float *sL = sM + G;
-  float *sR = sL + G;
-  int *sValid = reinterpret_cast<int *>(sR + G + 4);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(sValid + 2 * T) + 15) & ~uintptr_t(15));
+  __half *sV = sK + S * T * ROW;
+  const size_t ring = (size_t)S * 2 * C::kStageBytes;
+  unsigned char *after = smem + (ring > C::merge_bytes() ? ring : C::merge_bytes());
+  int *sValid = reinterpret_cast<int *>(after);
+  float *sW = reinterpret_cast<float *>(sValid + S * T);  // [kMaxSplits * G] weights, then l
+  uint64_t *full = reinterpret_cast<uint64_t *>(
+      (reinterpret_cast<uintptr_t>(sW + 2 * C::kMaxSplits * G) + 15) & ~uintptr_t(15));
+  uint64_t *empty = full + S;
   __shared__ int is_last;
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates
+  const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
+  unsigned long long t_ready = 0ull;
 
-  pdl_wait();
-  pdl_launch_dependents();
-
+  // Positions, table rows and the block table are final before the kernel that
+  // produces q (and the newest K/V rows) starts: they are read, and the K/V rows
+  // of older positions gathered, before the programmatic-dependency wait.
   const int pos = p.positions[row];
   if (pos < 0 || pos >= p.capacity) {
     if (split == 0 && kvh == 0 && tid == 0)
       report_status(p.status, kStatusLengthRange, kWhereAttention, pos, row);
+    pdl_wait();
     return;
   }
   const int len = pos + 1;
   int nsplit = (len + p.min_chunk - 1) / p.min_chunk;
   if (nsplit > p.max_splits) nsplit = p.max_splits;
+  if (nsplit > C::kMaxSplits) nsplit = C::kMaxSplits;
   if (nsplit < 1) nsplit = 1;
   int chunk = (len + nsplit - 1) / nsplit;
   chunk = (chunk + T - 1) / T * T;
   const int active = (len + chunk - 1) / chunk;
-  if (split >= active) return;
+  if (split >= active) {
+    pdl_wait();
+    trace_emit(p.trace, t_entry, t_entry);
+    return;
+  }
   const int begin = split * chunk;
   const int end = min(len, begin + chunk);
   const int ntiles = (end - begin + T - 1) / T;
   const int *table = p.block_table + (size_t)p.table_rows[row] * p.table_stride;
+  // Positions below `fresh` are never written by the producer kernel.
+  const int fresh = p.early_mode == 2 ? end : (p.early_mode == 1 ? pos : begin);
 
-  // Query heads of this KV head -> fp32 shared memory.
-  for (int i = tid; i < G * D; i += kThreads) {
-    const int g = i / D, d = i % D;
-    sQ[i] = __half2float(p.q[(size_t)row * p.q_stride + (size_t)(kvh * G + g) * D + d]);
-  }
-  if (tid < G) {
-    sM[tid] = -INFINITY;
-    sL[tid] = 0.0f;
-  }
   if (tid == 0) {
-    mbar_init(&bars[0], 1);
-    mbar_init(&bars[1], 1);
+#pragma unroll
+    for (int st = 0; st < S; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], C::kWarpsPerCta);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  // Warp 0 gathers tile `t` into stage `t & 1`.
-  auto issue = [&](int t) {
-    const int stage = t & 1;
+  // Warp 0: mark tile t's valid rows and arm its barrier with their bytes.
+  auto arm = [&](int t) {
+    const int stage = t % S;
     const int p0 = begin + t * T;
-    int ok[(T + 31) / 32];
     int nvalid = 0;
 #pragma unroll
-    for (int j = 0; j < (T + 31) / 32; ++j) {
+    for (int j = 0; j < T / 32; ++j) {
       const int lp = lane + 32 * j;
       const int position = p0 + lp;
       int v = 0;
-      if (lp < T && position < end) {
+      if (position < end) {
         const int logical = position / p.page_size;
         const int page = logical < p.table_stride ? table[logical] : -1;
         if (page < 0) {
@@ -162,147 +205,233 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
           v = 1;
         }
       }
-      ok[j] = v;
-      if (lp < T) sValid[stage * T + lp] = v;
+      sValid[stage * T + lp] = v;
+      if (!v) {
+        // No copy lands in this row: zero its V (P = 0 there, and 0 * NaN
+        // from stale shared memory would poison the P.V product).
+        uint4 *vrow = reinterpret_cast<uint4 *>(sV + ((size_t)stage * T + lp) * ROW);
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) vrow[c] = make_uint4(0u, 0u, 0u, 0u);
+      }
       nvalid += __popc(__ballot_sync(0xffffffffu, v));
     }
-    __syncwarp();  // sValid writes of all lanes precede the arrive (release)
-    if (lane == 0) mbar_arrive_expect_tx(&bars[stage], static_cast<uint32_t>(nvalid) * D * 2 * 2);
     __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(nvalid) * D * 2 * 2);
+    __syncwarp();
+  };
+  // Warp 0: one bulk copy per valid row with position in [lo, hi) into the
+  // padded shared-memory rows.
+  auto copy = [&](int t, int lo, int hi) {
+    const int stage = t % S;
+    const int p0 = begin + t * T;
 #pragma unroll
-    for (int j = 0; j < (T + 31) / 32; ++j) {
+    for (int j = 0; j < T / 32; ++j) {
       const int lp = lane + 32 * j;
-      if (!ok[j]) continue;
       const int position = p0 + lp;
+      if (position < lo || position >= hi || position >= end || !sValid[stage * T + lp]) continue;
       const int page = table[position / p.page_size];
-      const size_t off =
-          (((size_t)page * p.hkv + kvh) * p.page_size + position % p.page_size) * D;
-      bulk_g2s(sK + ((size_t)stage * T + lp) * D, p.k_pool + off, D * 2, &bars[stage]);
-      bulk_g2s(sV + ((size_t)stage * T + lp) * D, p.v_pool + off, D * 2, &bars[stage]);
+      const size_t off = (((size_t)page * p.hkv + kvh) * p.page_size + position % p.page_size) * D;
+      bulk_g2s(sK + ((size_t)stage * T + lp) * ROW, p.k_pool + off, D * 2, &full[stage]);
+      bulk_g2s(sV + ((size_t)stage * T + lp) * ROW, p.v_pool + off, D * 2, &full[stage]);
     }
   };
 
+  const int first = ntiles < S ? ntiles : S;
   if (warp == 0) {
-    issue(0);
-    if (ntiles > 1) issue(1);
+    for (int t = 0; t < first; ++t) {
+      arm(t);
+      copy(t, begin, fresh);
+    }
   }
-
-  // PV ownership: head pg, features [pd, pd + E).
-  const int pg = tid / (D / E);
-  const int pd = (tid % (D / E)) * E;
-  const bool pv_active = pg < G;
-  float acc[E];
+  pdl_wait();
+  if (warp == 0) {
+    for (int t = 0; t < first; ++t) copy(t, fresh, end);
+  }
+  // Query A fragments: rows = the G query heads of this KV head (rows >= G are
+  // zero), columns = head dimensions; fp16 values are exact.
+  uint32_t qa[C::kKSteps][4];
+  {
+    const __half *q = p.q + (size_t)row * p.q_stride + (size_t)kvh * G * D;
 #pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+    for (int kk = 0; kk < C::kKSteps; ++kk) {
+      const int c0 = kk * 16 + 2 * tq;
+      if (gq < G) {
+        qa[kk][0] = *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0);
+        qa[kk][2] = *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0 + 8);
+      } else {
+        qa[kk][0] = 0u;
+        qa[kk][2] = 0u;
+      }
+      qa[kk][1] = 0u;  // rows 8..15: G <= 8
+      qa[kk][3] = 0u;
+    }
+  }
+  if (p.trace.records) t_ready = global_ns();
+
+  // Per-warp flash-decoding state for fragment rows gq (valid when gq < G).
+  float m_run = -INFINITY, l_run = 0.0f;
+  float acc[C::kDTiles][4];
+#pragma unroll
+  for (int i = 0; i < C::kDTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
 
   for (int t = 0; t < ntiles; ++t) {
-    const int stage = t & 1;
-    if (!mbar_wait(&bars[stage], (t >> 1) & 1)) {
-      if (tid == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
+    const int stage = t % S;
+    if (!mbar_wait(&full[stage], (t / S) & 1)) {
+      if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
       return;
     }
-    const __half *k = sK + (size_t)stage * T * D;
-    const __half *v = sV + (size_t)stage * T * D;
-    // Scores.
-    if (tid < G * T) {
-      const int g = tid / T, lp = tid % T;
-      float s = -INFINITY;
-      if (sValid[stage * T + lp]) {
-        const float *qg = sQ + g * D;
-        const uint4 *krow = reinterpret_cast<const uint4 *>(k + (size_t)lp * D);
-        float dot = 0.0f;
+    const int r0 = warp * 16;  // this warp's 16 rows of the tile
+    const int p0 = begin + t * T + r0;
+    const __half *k = sK + ((size_t)stage * T + r0) * ROW;
+    const __half *v = sV + ((size_t)stage * T + r0) * ROW;
+    const int *valid = sValid + stage * T + r0;
+    // Scores S[16 heads x 16 positions] as two n-tiles of 8 positions.
+    float sc[2][4];
 #pragma unroll
-        for (int cc = 0; cc < C::kChunks; ++cc) {
-          const int c = (cc + lp) % C::kChunks;
-          const uint4 u = krow[c];
-          const float4 qa = reinterpret_cast<const float4 *>(qg)[2 * c];
-          const float4 qb = reinterpret_cast<const float4 *>(qg)[2 * c + 1];
-          float2 f;
-          f = half2_bits_to_float2(u.x); dot = fmaf(qa.x, f.x, dot); dot = fmaf(qa.y, f.y, dot);
-          f = half2_bits_to_float2(u.y); dot = fmaf(qa.z, f.x, dot); dot = fmaf(qa.w, f.y, dot);
-          f = half2_bits_to_float2(u.z); dot = fmaf(qb.x, f.x, dot); dot = fmaf(qb.y, f.y, dot);
-          f = half2_bits_to_float2(u.w); dot = fmaf(qb.z, f.x, dot); dot = fmaf(qb.w, f.y, dot);
-        }
-        s = dot * p.scale;
-      }
-      sS[g * T + lp] = s;
-    }
-    __syncthreads();
-    // Online softmax update, one warp per head.
-    for (int g = warp; g < G; g += kThreads / 32) {
-      float mx = -INFINITY;
-      for (int lp = lane; lp < T; lp += 32) mx = fmaxf(mx, sS[g * T + lp]);
-      mx = warp_max(mx);
-      const float m_old = sM[g];
-      const float m_new = fmaxf(m_old, mx);
-      float sum = 0.0f;
-      for (int lp = lane; lp < T; lp += 32) {
-        const float s = sS[g * T + lp];
-        const float e = (s == -INFINITY) ? 0.0f : expf(s - m_new);
-        sS[g * T + lp] = e;
-        sum += e;
-      }
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        const float rescale = (m_old == -INFINITY) ? 0.0f : expf(m_old - m_new);
-        sR[g] = rescale;
-        sL[g] = sL[g] * rescale + sum;
-        sM[g] = m_new;
+    for (int nt = 0; nt < 2; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < C::kKSteps; ++kk) {
+        uint32_t b0, b1;
+        // matrices: rows = positions nt*8..+7, columns = dims kk*16..+7 and +8..+15
+        const __half *addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
+        ldmatrix_x2(b0, b1, addr);
+        mma_16816(sc[nt], qa[kk], b0, b1);
       }
     }
-    __syncthreads();
-    // P.V
-    if (pv_active) {
-      const float r = sR[pg];
+    // Scale, mask, online softmax (row gq owns c0/c1; c2/c3 are rows gq+8, unused).
+    float mx = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] *= r;
-      const float *pr = sS + pg * T;
-      // Rows past the chunk end (and rows whose page was missing) were never
-      // written this tile: skip them rather than multiply stale data by zero.
-      const int nt = min(T, end - (begin + t * T));
-      const int *valid = sValid + stage * T;
-      for (int lp = 0; lp < nt; ++lp) {
-        if (!valid[lp]) continue;
-        const float w = pr[lp];
-        const __half *vr = v + (size_t)lp * D + pd;
-        if (E % 2 == 0) {
+    for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-          for (int e = 0; e < E; e += 2) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(vr + e));
-            acc[e] = fmaf(w, f.x, acc[e]);
-            acc[e + 1] = fmaf(w, f.y, acc[e + 1]);
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < E; ++e) acc[e] = fmaf(w, __half2float(vr[e]), acc[e]);
-        }
+      for (int j = 0; j < 2; ++j) {
+        const int lp = nt * 8 + 2 * tq + j;
+        const bool ok = p0 + lp < end && valid[lp];
+        sc[nt][j] = ok ? sc[nt][j] * p.scale : -INFINITY;
+        mx = fmaxf(mx, sc[nt][j]);
       }
     }
-    __syncthreads();
-    if (warp == 0 && t + 2 < ntiles) issue(t + 2);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+    float psum = 0.0f;
+    float pr[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        pr[nt][j] = (sc[nt][j] == -INFINITY) ? 0.0f : expf(sc[nt][j] - m_new);
+        psum += pr[nt][j];
+      }
+    }
+    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+    l_run = l_run * rescale + psum;
+    m_run = m_new;
+    // P as the A operand (16 heads x 16 positions) in two fp16 parts, hi + lo,
+    // so the probabilities keep ~22 bits (the reference multiplies fp32
+    // probabilities by the values).
+    uint32_t pa[4], pl[4];
+    {
+      const __half2 h0 = __floats2half2_rn(pr[0][0], pr[0][1]);
+      const __half2 h1 = __floats2half2_rn(pr[1][0], pr[1][1]);
+      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+      pa[0] = *reinterpret_cast<const uint32_t *>(&h0);
+      pa[2] = *reinterpret_cast<const uint32_t *>(&h1);
+      pl[0] = pack_half2(pr[0][0] - f0.x, pr[0][1] - f0.y);
+      pl[2] = pack_half2(pr[1][0] - f1.x, pr[1][1] - f1.y);
+      pa[1] = pa[3] = pl[1] = pl[3] = 0u;
+    }
+    // O[16 x D] += P . V[16 positions x D].
+#pragma unroll
+    for (int dt = 0; dt < C::kDTiles; ++dt) {
+      acc[dt][0] *= rescale;
+      acc[dt][1] *= rescale;
+      uint32_t b0, b1;
+      // matrices (transposed on load): rows = positions 0..7 and 8..15, columns = dims dt*8..+7
+      const __half *addr = v + (size_t)(lane & 15) * ROW + dt * 8;
+      ldmatrix_x2_trans(b0, b1, addr);
+      mma_16816(acc[dt], pl, b0, b1);
+      mma_16816(acc[dt], pa, b0, b1);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[stage]);
+    if (warp == 0 && t + S < ntiles) {
+      // Every warp has finished this stage before it is refilled.
+      if (!mbar_wait(&empty[stage], (t / S) & 1)) {
+        if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
+        return;
+      }
+      arm(t + S);
+      copy(t + S, begin, end);
+    }
+  }
+  // Let the next kernel launch only now: its weight prefetch would otherwise
+  // queue ahead of this kernel's latency-critical loads.
+  pdl_launch_dependents();
+
+  // Merge the four warps' states (rows gq < G) in shared memory (the K/V ring
+  // is free now): per warp [G][D] accumulators, then m and l per head.
+  __syncthreads();
+  float *mrg = reinterpret_cast<float *>(smem);
+  float *mrg_ml = mrg + C::kWarpsPerCta * G * D;
+  if (gq < G) {
+#pragma unroll
+    for (int dt = 0; dt < C::kDTiles; ++dt) {
+      float *dst = mrg + ((size_t)warp * G + gq) * D + dt * 8 + 2 * tq;
+      dst[0] = acc[dt][0];
+      dst[1] = acc[dt][1];
+    }
+    if (tq == 0) {
+      mrg_ml[(warp * G + gq) * 2] = m_run;
+      mrg_ml[(warp * G + gq) * 2 + 1] = l_run;
+    }
+  }
+  __syncthreads();
+  // Thread -> (head hg, features [hd, hd + E)) over the merged result.
+  constexpr int E = (G * D / kThreads) > 1 ? (G * D / kThreads) : 1;
+  const int hg = tid / (D / E);
+  const int hd = (tid % (D / E)) * E;
+  const bool own = hg < G;
+  float m_cta = -INFINITY, l_cta = 0.0f, o_cta[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) o_cta[e] = 0.0f;
+  if (own) {
+#pragma unroll
+    for (int w = 0; w < C::kWarpsPerCta; ++w) m_cta = fmaxf(m_cta, mrg_ml[(w * G + hg) * 2]);
+#pragma unroll
+    for (int w = 0; w < C::kWarpsPerCta; ++w) {
+      const float mw = mrg_ml[(w * G + hg) * 2];
+      const float f = (mw == -INFINITY) ? 0.0f : expf(mw - m_cta);
+      l_cta += mrg_ml[(w * G + hg) * 2 + 1] * f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) o_cta[e] = fmaf(mrg[((size_t)w * G + hg) * D + hd + e], f, o_cta[e]);
+    }
   }
 
   const size_t head_base = ((size_t)row * p.hkv + kvh);
   if (active == 1) {
-    if (pv_active) {
-      const float inv = 1.0f / sL[pg];
-      __half *o = p.out + (size_t)row * p.out_stride + (size_t)(kvh * G + pg) * D + pd;
+    if (own) {
+      const float inv = 1.0f / l_cta;
+      __half *o = p.out + (size_t)row * p.out_stride + (size_t)(kvh * G + hg) * D + hd;
 #pragma unroll
-      for (int e = 0; e < E; ++e) o[e] = __float2half_rn(acc[e] * inv);
+      for (int e = 0; e < E; ++e) o[e] = __float2half_rn(o_cta[e] * inv);
     }
+    trace_emit(p.trace, t_entry, t_ready);
     return;
   }
   // Write this split's partial, then the last CTA of the (row, KV head) combines.
   {
     float *wa = p.ws_acc + ((head_base * p.max_splits + split) * G) * D;
-    if (pv_active) {
+    if (own) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) wa[(size_t)pg * D + pd + e] = acc[e];
-    }
-    if (tid < G) {
-      float *wm = p.ws_ml + ((head_base * p.max_splits + split) * G + tid) * 2;
-      wm[0] = sM[tid];
-      wm[1] = sL[tid];
+      for (int e = 0; e < E; ++e) wa[(size_t)hg * D + hd + e] = o_cta[e];
+      if (hd == 0) {
+        float *wm = p.ws_ml + ((head_base * p.max_splits + split) * G + hg) * 2;
+        wm[0] = m_cta;
+        wm[1] = l_cta;
+      }
     }
   }
   __threadfence();
@@ -312,33 +441,66 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
     is_last = (prev == static_cast<unsigned int>(active - 1)) ? 1 : 0;
   }
   __syncthreads();
-  if (!is_last) return;
+  if (!is_last) {
+    trace_emit(p.trace, t_entry, t_ready);
+    return;
+  }
   __threadfence();
-  if (pv_active) {
-    float mmax = -INFINITY;
-    for (int s = 0; s < active; ++s) {
-      const float *wm = p.ws_ml + ((head_base * p.max_splits + s) * G + pg) * 2;
-      mmax = fmaxf(mmax, __ldcg(wm));
-    }
+  // Combine: per (split, head) weights exp(m_s - M) / sum_s l_s exp(m_s - M)
+  // from one pass over the (m, l) pairs, then every thread sums its outputs
+  // over the splits with eight partial loads in flight.
+  const float2 *ml = reinterpret_cast<const float2 *>(p.ws_ml + (head_base * p.max_splits) * G * 2);
+  float *sWl = sW + C::kMaxSplits * G;
+  for (int i = tid; i < active * G; i += kThreads) {
+    const float2 v = __ldcg(ml + i);
+    sW[i] = v.x;
+    sWl[i] = v.y;
+  }
+  __syncthreads();
+  for (int g = warp; g < G; g += kThreads / 32) {
+    float mx = -INFINITY;
+    for (int sp = lane; sp < active; sp += 32) mx = fmaxf(mx, sW[sp * G + g]);
+    mx = warp_max(mx);
     float den = 0.0f;
+    for (int sp = lane; sp < active; sp += 32) {
+      const int i = sp * G + g;
+      const float ms = sW[i];
+      const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
+      den += sWl[i] * f;
+      sW[i] = f;
+    }
+    den = warp_sum(den);
+    const float inv = 1.0f / den;
+    for (int sp = lane; sp < active; sp += 32) sW[sp * G + g] *= inv;
+  }
+  __syncthreads();
+  if (own) {
     float out[E];
 #pragma unroll
     for (int e = 0; e < E; ++e) out[e] = 0.0f;
-    for (int s = 0; s < active; ++s) {
-      const float *wm = p.ws_ml + ((head_base * p.max_splits + s) * G + pg) * 2;
-      const float ms = __ldcg(wm), ls = __ldcg(wm + 1);
-      const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mmax);
-      den += ls * f;
-      const float *wa = p.ws_acc + ((head_base * p.max_splits + s) * G + pg) * D + pd;
+    const float *wa = p.ws_acc + (head_base * p.max_splits) * G * D + (size_t)hg * D + hd;
+    for (int s0 = 0; s0 < active; s0 += 8) {
+      float part[8][E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) out[e] = fmaf(__ldcg(wa + e), f, out[e]);
+      for (int j = 0; j < 8; ++j) {
+        const int sp = s0 + j;
+        const float *src = wa + (size_t)sp * G * D;
+#pragma unroll
+        for (int e = 0; e < E; ++e) part[j][e] = sp < active ? __ldcg(src + e) : 0.0f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float f = s0 + j < active ? sW[(s0 + j) * G + hg] : 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) out[e] = fmaf(part[j][e], f, out[e]);
+      }
     }
-    const float inv = 1.0f / den;
-    __half *o = p.out + (size_t)row * p.out_stride + (size_t)(kvh * G + pg) * D + pd;
+    __half *o = p.out + (size_t)row * p.out_stride + (size_t)(kvh * G + hg) * D + hd;
 #pragma unroll
-    for (int e = 0; e < E; ++e) o[e] = __float2half_rn(out[e] * inv);
+    for (int e = 0; e < E; ++e) o[e] = __float2half_rn(out[e]);
   }
   if (tid == 0) atomicExch(p.counters + head_base, 0u);
+  trace_emit(p.trace, t_entry, t_ready);
 }
 
 template <int D, int G>
@@ -498,6 +660,7 @@ extern "C" int tmc_k_paged_attention_f16_noalloc(
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d)));
   p.max_splits = max_splits;
   p.min_chunk = min_chunk;
+  p.early_mode = 2;  // standalone call: no kernel produces K/V concurrently
   p.ws_acc = reinterpret_cast<float *>(base);
   p.ws_ml = reinterpret_cast<float *>(base + (size_t)rows * hq * max_splits * d * sizeof(float));
   p.counters = tickets;

@@ -271,6 +271,7 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d)));
   p.max_splits = max_splits;
   p.min_chunk = min_chunk;
+  p.early_mode = 2;  // standalone call: no kernel produces K/V concurrently
   const size_t acc_bytes = (size_t)rows * hq * max_splits * d * 4;
   p.ws_acc = static_cast<float *>(workspace);
   p.ws_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + acc_bytes);

@@ -55,6 +55,44 @@ __device__ __forceinline__ void report_status(TmcDeviceStatus *s, int code, int 
   }
 }
 
+// ---- tracing ---------------------------------------------------------------------
+// Optional per-CTA timeline of a decode step: when a kernel's `trace` pointer
+// is set, thread 0 of every CTA appends one record (global nanosecond timer at
+// entry, after the programmatic-dependency wait, and at exit).
+struct TraceRecord {
+  unsigned long long tag;      // (kernel tag << 32) | CTA linear index
+  unsigned long long t_entry;
+  unsigned long long t_ready;  // after griddepcontrol.wait and the prologue
+  unsigned long long t_exit;
+};
+
+struct TraceSink {
+  TraceRecord *records;
+  unsigned int *count;
+  unsigned int capacity;
+  unsigned int tag;
+};
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void trace_emit(const TraceSink &sink, unsigned long long t_entry,
+                                           unsigned long long t_ready) {
+  if (sink.records == nullptr || threadIdx.x != 0) return;
+  const unsigned int i = atomicAdd(sink.count, 1u);
+  if (i >= sink.capacity) return;
+  const unsigned int cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  TraceRecord r;
+  r.tag = (static_cast<unsigned long long>(sink.tag) << 32) | cta;
+  r.t_entry = t_entry;
+  r.t_ready = t_ready;
+  r.t_exit = global_ns();
+  sink.records[i] = r;
+}
+
 // ---- programmatic dependent launch (PDL) -------------------------------------
 // Both are no-ops when the kernel was not launched with the programmatic
 // stream-serialization attribute.

@@ -1,5 +1,6 @@
 // extern "C" boundary of the decoder executor (declarations and reference
 // citations in include/tmc_cuda.h).
+#include <algorithm>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -236,6 +237,21 @@ int tmc_decoder_profile_kernel(tmc_decoder *dec, int kind, int rows, int rounds,
                                double *bytes_per_launch, int *launches_per_step) {
   if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
   return done(dec->ex->profileKernel(kind, rows, rounds, avg_us, bytes_per_launch, launches_per_step));
+}
+
+int tmc_decoder_set_trace(tmc_decoder *dec, size_t capacity) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->setTrace(capacity));
+}
+
+int tmc_decoder_read_trace(tmc_decoder *dec, uint64_t *out, size_t capacity, size_t *count) {
+  if (!bind(dec) || count == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  std::vector<tmc::TraceRecord> recs;
+  auto e = dec->ex->readTrace(&recs);
+  if (!e.empty()) return done(e);
+  *count = recs.size();
+  if (out != nullptr) std::memcpy(out, recs.data(), std::min(capacity, recs.size()) * sizeof(tmc::TraceRecord));
+  return ok();
 }
 
 int tmc_nccl_unique_id(uint8_t *id, size_t nbytes) {

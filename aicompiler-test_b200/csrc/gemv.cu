@@ -329,22 +329,32 @@ __device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&
   }
 }
 
-template <typename XS, int M, int R, int U>
+template <typename XS, int M, int R, int U, int KS>
 __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   XS *xs = reinterpret_cast<XS *>(smem_raw);
   __shared__ float red[32];
   __shared__ unsigned long long warp_best[kWarps][M];
+  __shared__ float team_part[kWarps][R * M];
+  __shared__ int team_next[kWarps][2];
   __shared__ int is_last;
 
+  // A team of KS warps shares each row group; warp `wt` of the team streams
+  // the K-slice [c_lo, c_hi) of the group's rows (partials reduced in shared
+  // memory). KS > 1 cuts each warp's chain of dependent load batches for
+  // short-N / long-K shapes.
+  constexpr int kTeams = kWarps / KS;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int total_w = kWarps * gridDim.x;
-  const int gw = warp * gridDim.x + blockIdx.x;
+  const int team = warp / KS, wt = warp % KS;
+  const int total_teams = kTeams * gridDim.x;
+  const int gt = team * gridDim.x + blockIdx.x;
   const int ngroups = (p.N + R - 1) / R;
   const int nchunks = p.K >> 3;
+  const int c_lo = (int)(((long long)nchunks * wt) / KS);
+  const int c_hi = (int)(((long long)nchunks * (wt + 1)) / KS);
 
   // Load a batch of U 16-byte chunks of each of the R rows of group g,
-  // starting at chunk c0, into registers.
+  // starting at chunk c0 (chunks at or past c_hi read as zero), into registers.
   auto load_batch = [&](int g, int c0, uint4 (&w)[R][U]) {
     const int row0 = g * R;
 #pragma unroll
@@ -354,31 +364,55 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int c = c0 + u * 32 + lane;
-        w[r][u] = (c < nchunks && rv) ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
+        w[r][u] = (c < c_hi && rv) ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
       }
     }
   };
 
   // Weights never change: the first batch is loaded into registers (and the
-  // rest of the first group warmed in L2) before waiting on the producer of x,
-  // so HBM latency overlaps the previous kernel's tail and the prologue.
+  // rest of this warp's slice of the first group warmed in L2) before waiting
+  // on the producer of x, so HBM latency overlaps the previous kernel's tail
+  // and the prologue.
+  const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
   uint4 w[R][U];
-  int g = gw, c0 = 0;
-  if (g < ngroups) {
-    load_batch(g, 0, w);
+  int g = gt, c0 = c_lo;
+  if (g < ngroups && c_lo < c_hi) {
+    load_batch(g, c_lo, w);
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       const int row = g * R + r;
       if (row < p.N) {
         const uint4 *wr = reinterpret_cast<const uint4 *>(p.W + (size_t)row * p.K);
-        for (int c = 32 * U + lane; c < nchunks && c < 4 * 32 * U; c += 32) prefetch_l2(wr + c);
+        for (int c = c_lo + 32 * U + lane; c < c_hi && c < c_lo + 4 * 32 * U; c += 32) prefetch_l2(wr + c);
       }
     }
   }
   pdl_wait();
+  // Dynamic scheduling: SMs do not get equal HBM bandwidth, so equal static
+  // shares finish at different times. Groups are split into kGemvPools
+  // interleaved pools (group = pool + kGemvPools * k) with one ticket counter
+  // each; a team keeps to the pool of its first group. Its first three groups
+  // are static; afterwards the team leader keeps one ticket in flight and
+  // publishes it a group later, so the atomic's round trip never stalls the
+  // weight stream. A group's arithmetic does not depend on the team that runs
+  // it, so results stay deterministic.
+  const bool dynamic = p.work_counter != nullptr && total_teams % kGemvPools == 0 &&
+                       ngroups > 3 * total_teams;
+  const bool leader = lane == 0 && wt == 0;
+  const int pool = gt % kGemvPools;
+  const int pool_base = 3 * (total_teams / kGemvPools);
+  unsigned int *ticket = p.work_counter + pool * kGemvPoolStride;
+  int g_next = gt + total_teams;
+  int slot = 0;
+  int pending = 0;
+  if (dynamic && leader) {
+    team_next[team][0] = gt + 2 * total_teams;
+    pending = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
+  }
   stage_x<XS, M>(p, xs, red);
   __syncthreads();
   pdl_launch_dependents();
+  const unsigned long long t_ready = p.trace.records ? global_ns() : 0ull;
 
   unsigned long long best[M];
 #pragma unroll
@@ -391,33 +425,73 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
 
   while (g < ngroups) {
-    // Consume the batch held in w.
+    // Consume the batch held in w (warps whose slice is empty skip).
+    if (c0 < c_hi) {
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u * 32 + lane;
-      if (c < nchunks) {
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + u * 32 + lane;
+        if (c < c_hi) {
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          float xv[8];
-          XLoad<XS>::get(xs + (size_t)m * p.K, c, xv);
+          for (int m = 0; m < M; ++m) {
+            float xv[8];
+            XLoad<XS>::get(xs + (size_t)m * p.K, c, xv);
 #pragma unroll
-          for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[r][u], xv, acc[r][m]);
+            for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[r][u], xv, acc[r][m]);
+          }
         }
       }
     }
     // Issue the next batch before reducing / running the epilogue.
     int ng = g, nc = c0 + 32 * U;
-    if (nc >= nchunks) {
-      nc = 0;
-      ng += total_w;
+    if (nc >= c_hi) {
+      nc = c_lo;
+      ng = g_next;
+      if (dynamic) {
+        // Written by the team leader one group ago (two team barriers, or a
+        // warp sync when KS == 1, separate that write from this read).
+        g_next = team_next[team][slot];
+        slot ^= 1;
+        if (KS == 1) __syncwarp();
+        if (leader) {
+          team_next[team][slot] = pending;
+          pending = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
+        }
+        if (KS == 1) __syncwarp();
+      } else {
+        g_next += total_teams;
+      }
     }
-    if (ng < ngroups) load_batch(ng, nc, w);
-    if (nc == 0) {
+    if (ng < ngroups && c_lo < c_hi) load_batch(ng, nc, w);
+    if (nc == c_lo) {
+      // Group finished by every warp of the team (all walk the same groups).
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
-      epilogue<R, M>(p, g * R, acc, lane, best);
+      if (KS > 1) {
+        if (lane == 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int m = 0; m < M; ++m) team_part[warp][r * M + m] = acc[r][m];
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(KS * 32) : "memory");
+        if (wt == 0) {
+#pragma unroll
+          for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int m = 0; m < M; ++m) {
+              float t = 0.0f;
+#pragma unroll
+              for (int k = 0; k < KS; ++k) t += team_part[team * KS + k][r * M + m];
+              acc[r][m] = t;
+            }
+          epilogue<R, M>(p, g * R, acc, lane, best);
+        }
+        asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(KS * 32) : "memory");
+      } else {
+        epilogue<R, M>(p, g * R, acc, lane, best);
+      }
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
@@ -427,7 +501,25 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     c0 = nc;
   }
 
-  if (p.epilogue == kEpiArgmax) {
+  if (dynamic) {
+    // The last CTA to finish resets the tickets for the next launch.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int done = atomicAdd(p.work_counter + kGemvPools * kGemvPoolStride, 1u);
+      if (done == gridDim.x - 1) {
+        for (int c = 0; c < kGemvPools; ++c) atomicExch(p.work_counter + c * kGemvPoolStride, 0u);
+        atomicExch(p.work_counter + kGemvPools * kGemvPoolStride, 0u);
+      }
+    }
+  }
+  if (p.epilogue != kEpiArgmax) {
+    if (p.trace.records) {
+      __syncthreads();  // record the CTA's last warp, not warp 0
+      trace_emit(p.trace, t_entry, t_ready);
+    }
+    return;
+  }
+  {
     if (lane == 0) {
 #pragma unroll
       for (int m = 0; m < M; ++m) warp_best[warp][m] = best[m];
@@ -438,7 +530,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       for (int w = 0; w < kWarps; ++w) b = warp_best[w][threadIdx.x] > b ? warp_best[w][threadIdx.x] : b;
       if (b != 0ull) atomicMax(p.argmax_keys + threadIdx.x, b);
     }
-    if (p.next_tokens == nullptr) return;  // cross-rank reduction finalises
+    if (p.next_tokens == nullptr) {  // cross-rank reduction finalises
+      trace_emit(p.trace, t_entry, t_ready);
+      return;
+    }
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -463,12 +558,13 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
         atomicExch(p.argmax_counter, 0u);
       }
     }
+    trace_emit(p.trace, t_entry, t_ready);
   }
 }
 
-template <typename XS, int M, int R, int U>
+template <typename XS, int M, int R, int U, int KS>
 cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
-  auto kernel = gemv_kernel<XS, M, R, U>;
+  auto kernel = gemv_kernel<XS, M, R, U, KS>;
   const size_t smem = (size_t)M * p.K * sizeof(XS);
   // Occupancy depends on the dynamic shared memory; cache it per (device, smem).
   static std::mutex mu;
@@ -498,9 +594,10 @@ cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, 
     }
   }
   const int ngroups = (p.N + R - 1) / R;
-  int grid = (ngroups + kWarps - 1) / kWarps;
+  int grid = (ngroups + kWarps / KS - 1) / (kWarps / KS);
   const int wave = occ * num_sms;
   if (grid > wave) grid = wave;
+  if (p.work_counter != nullptr && grid > kGemvPools) grid -= grid % kGemvPools;
   if (grid < 1) grid = 1;
 
   cudaLaunchConfig_t cfg = {};
@@ -520,6 +617,29 @@ cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, 
 
 namespace {
 
+// Warps per row group: split K across a team when a row is several load
+// batches long and there are too few row groups to keep every warp busy.
+template <int M, int R, int U>
+int choose_ks(const GemvParams &p, int num_sms) {
+  const int ngroups = (p.N + R - 1) / R;
+  const int batches = (p.K >> 3) / (32 * U);  // full load batches per row
+  const int warps = num_sms * 16;             // two resident CTAs of 8 warps per SM
+  if (batches < 2 || ngroups >= 4 * warps) return 1;
+  int ks = 1;
+  while (ks < 8 && ks * 2 <= batches + 1 && ngroups * ks < 4 * warps) ks *= 2;
+  return ks;
+}
+
+template <typename XS, int M, int R, int U>
+cudaError_t launch_ks(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
+  switch (choose_ks<M, R, U>(p, num_sms)) {
+    case 8: return launch_instance<XS, M, R, U, 8>(p, stream, pdl, num_sms);
+    case 4: return launch_instance<XS, M, R, U, 4>(p, stream, pdl, num_sms);
+    case 2: return launch_instance<XS, M, R, U, 2>(p, stream, pdl, num_sms);
+    default: return launch_instance<XS, M, R, U, 1>(p, stream, pdl, num_sms);
+  }
+}
+
 // One launch for M rows whose staged activations fit in shared memory.
 cudaError_t launch_rows(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
   const bool f32_in = (p.prologue == kProF32 || p.prologue == kProF32Norm);
@@ -527,21 +647,21 @@ cudaError_t launch_rows(const GemvParams &p, cudaStream_t stream, bool pdl, int 
   // fp32 staging keeps un-rounded fp32 activations exact (C1 graph); fp16 staging
   // is exact for the decoder's fp16-rounded activations and halves shared memory.
   if (p.M == 1) {
-    if (f32_in || k * 4 <= 64 * 1024) return launch_instance<float, 1, 2, 8>(p, stream, pdl, num_sms);
-    return launch_instance<__half, 1, 2, 8>(p, stream, pdl, num_sms);
+    if (f32_in || k * 4 <= 64 * 1024) return launch_ks<float, 1, 2, 8>(p, stream, pdl, num_sms);
+    return launch_ks<__half, 1, 2, 8>(p, stream, pdl, num_sms);
   }
   if (p.M == 2) {
-    if (k * 2 * 4 <= 112 * 1024) return launch_instance<float, 2, 2, 8>(p, stream, pdl, num_sms);
+    if (k * 2 * 4 <= 112 * 1024) return launch_ks<float, 2, 2, 8>(p, stream, pdl, num_sms);
     if (f32_in) return cudaErrorInvalidValue;
-    return launch_instance<__half, 2, 2, 8>(p, stream, pdl, num_sms);
+    return launch_ks<__half, 2, 2, 8>(p, stream, pdl, num_sms);
   }
   if (p.M <= 4) {
-    if (f32_in && k * 4 * 4 <= 200 * 1024) return launch_instance<float, 4, 2, 4>(p, stream, pdl, num_sms);
+    if (f32_in && k * 4 * 4 <= 200 * 1024) return launch_ks<float, 4, 2, 4>(p, stream, pdl, num_sms);
     if (f32_in || k * 4 * 2 > 200 * 1024) return cudaErrorInvalidValue;
-    return launch_instance<__half, 4, 2, 4>(p, stream, pdl, num_sms);
+    return launch_ks<__half, 4, 2, 4>(p, stream, pdl, num_sms);
   }
   if (f32_in || k * 8 * 2 > 200 * 1024) return cudaErrorInvalidValue;
-  return launch_instance<__half, 8, 2, 4>(p, stream, pdl, num_sms);
+  return launch_ks<__half, 8, 2, 4>(p, stream, pdl, num_sms);
 }
 
 // Largest row count per launch whose staging fits (see launch_rows).

@@ -80,7 +80,17 @@ struct GemvParams {
   unsigned int *history_counter;    // [1] steps recorded so far
   int vocab_offset;                 // global index of local row 0 (vocab-parallel head)
   TmcDeviceStatus *status;
+  TraceSink trace;                  // optional timeline (records == nullptr: off)
+  // Optional dynamic row-group scheduling: kGemvPools ticket counters, each on
+  // its own 128-byte line (stride kGemvPoolStride uints), then a CTA exit
+  // ticket; all zero before the launch and reset by the last CTA. Null: the
+  // static interleaved assignment.
+  unsigned int *work_counter;
 };
+
+constexpr int kGemvPools = 8;
+constexpr int kGemvPoolStride = 32;
+constexpr int kGemvCounterWords = (kGemvPools + 1) * kGemvPoolStride;
 
 // Host-side launcher; returns a cudaError_t. Chooses the template instance
 // from (M, K) and the grid from the device occupancy.

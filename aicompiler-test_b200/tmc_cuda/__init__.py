@@ -290,6 +290,8 @@ _sig("tmc_decoder_kernels_per_step", c_int, c_void_p, c_int)
 _sig("tmc_decoder_step_bytes", ctypes.c_double, c_void_p, c_int, _I32P)
 _sig("tmc_decoder_profile_kernel", c_int, c_void_p, c_int, c_int, c_int, POINTER(ctypes.c_double),
      POINTER(ctypes.c_double), POINTER(c_int))
+_sig("tmc_decoder_set_trace", c_int, c_void_p, c_size_t)
+_sig("tmc_decoder_read_trace", c_int, c_void_p, POINTER(ctypes.c_uint64), c_size_t, POINTER(c_size_t))
 _sig("tmc_nccl_unique_id", c_int, ctypes.c_char_p, c_size_t)
 _sig("tmc_decoder_attach_nccl", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_int, c_int)
 
@@ -445,6 +447,27 @@ class Decoder:
         check(lib.tmc_decoder_profile_kernel(self.handle, k, rows, rounds, ctypes.byref(us),
                                              ctypes.byref(b), ctypes.byref(n)))
         return us.value, b.value, n.value
+
+    def set_trace(self, capacity: int):
+        check(lib.tmc_decoder_set_trace(self.handle, capacity))
+        self._trace_cap = capacity
+
+    def read_trace(self) -> np.ndarray:
+        """Structured array (layer, kind, cta, t_entry, t_ready, t_exit) in ns."""
+        cap = getattr(self, "_trace_cap", 0)
+        buf = np.zeros((cap, 4), dtype=np.uint64)
+        n = c_size_t(0)
+        check(lib.tmc_decoder_read_trace(self.handle, buf.ctypes.data_as(POINTER(ctypes.c_uint64)), cap,
+                                         ctypes.byref(n)))
+        rec = buf[:min(n.value, cap)]
+        out = np.zeros(len(rec), dtype=[("layer", "i4"), ("kind", "i4"), ("cta", "i4"),
+                                        ("t_entry", "u8"), ("t_ready", "u8"), ("t_exit", "u8")])
+        tag = rec[:, 0] >> np.uint64(32)
+        out["layer"] = (tag >> np.uint64(8)).astype(np.int32)
+        out["kind"] = (tag & np.uint64(0xff)).astype(np.int32)
+        out["cta"] = (rec[:, 0] & np.uint64(0xffffffff)).astype(np.int32)
+        out["t_entry"], out["t_ready"], out["t_exit"] = rec[:, 1], rec[:, 2], rec[:, 3]
+        return out
 
     def attach_nccl(self, unique_id: bytes, world: int, rank: int):
         check(lib.tmc_decoder_attach_nccl(self.handle, unique_id, len(unique_id), world, rank))

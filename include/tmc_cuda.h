@@ -274,6 +274,17 @@ double tmc_decoder_step_bytes(tmc_decoder *dec, int rows, const int32_t *context
 int tmc_decoder_profile_kernel(tmc_decoder *dec, int kind, int rows, int rounds, double *avg_us,
                                double *bytes_per_launch, int *launches_per_step);
 
+/* Step timeline: capacity > 0 makes every kernel of later steps append one
+ * record per CTA (4 x uint64: tag = ((layer << 8) | kind) << 32 | CTA index,
+ * then global-timer nanoseconds at entry, after the dependency wait and
+ * prologue, and at exit); 0 turns it off. tmc_decoder_read_trace copies up to
+ * `capacity` records into `out` (4 uint64 each), reports how many were
+ * collected, and clears them. Tracing is a profiling aid with no reference
+ * counterpart (the reference records one GPU duration per command buffer,
+ * MetalRuntime.mm:253-258). */
+int tmc_decoder_set_trace(tmc_decoder *dec, size_t capacity);
+int tmc_decoder_read_trace(tmc_decoder *dec, uint64_t *out, size_t capacity, size_t *count);
+
 /* ---- tensor parallelism (NCCL over NVLink; no reference counterpart: the
  * reference is single-device, README.md:321) ----
  * Rank 0 creates the id and shares it with the other ranks out of band
