@@ -621,12 +621,14 @@ namespace {
 // batches long and there are too few row groups to keep every warp busy.
 template <int M, int R, int U>
 int choose_ks(const GemvParams &p, int num_sms) {
+  // The team reduction makes a team's warps wait for their slowest member at
+  // every group (barrier stalls dominate a K-split down projection), so K is
+  // split only when there are too few row groups to occupy half the warps.
   const int ngroups = (p.N + R - 1) / R;
   const int batches = (p.K >> 3) / (32 * U);  // full load batches per row
   const int warps = num_sms * 16;             // two resident CTAs of 8 warps per SM
-  if (batches < 2 || ngroups >= 4 * warps) return 1;
   int ks = 1;
-  while (ks < 8 && ks * 2 <= batches + 1 && ngroups * ks < 4 * warps) ks *= 2;
+  while (ks < 8 && ks * 2 <= batches && ngroups * ks * 2 <= warps) ks *= 2;
   return ks;
 }
 

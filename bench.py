@@ -229,13 +229,14 @@ def run_ours(args, world, rank, local):
                              "gbs": round(b / us / 1e3, 1), "frac_of_peak": round(b / us / 1e3 / hbm, 3)}
         dom = max(kernels, key=lambda k: kernels[k]["us"] * kernels[k]["launches_per_step"])
         d = kernels[dom]
+        # DRAM bytes of one launch of the dominant kernel from the committed ncu
+        # summary (profiles/gemv_gate_up_down_8b_bs1.md), if it covers it.
         traffic = None
-        tpath = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(tpath):
-            try:
-                traffic = json.load(open(tpath)).get(f"{dom}_bs1_tp{world}")
-            except Exception:
-                traffic = None
+        tpath = os.path.join(ROOT, "profiles", "gemv_gate_up_down_8b_bs1.md")
+        if os.path.exists(tpath) and world == 1:
+            for line in open(tpath):
+                if line.startswith(f"traffic_bytes_per_launch {dom}:"):
+                    traffic = int(line.split(":")[1])
         roofline = {"kernel": f"gemv {dom}" if dom != "attention" else "attention", "bound": "hbm",
                     "achieved": d["gbs"], "peak": hbm, "unit": "GB/s", "frac": d["frac_of_peak"],
                     "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
