@@ -20,6 +20,10 @@ using cuda::ElementType;
 
 namespace {
 
+// Weight bytes one GEMV launch may pull into L2 while its predecessor drains
+// (about half of B200's 126 MB L2).
+constexpr long long kL2PrefetchBytes = 64ll << 20;
+
 std::string cudaText(const char *what, cudaError_t e) {
   std::ostringstream s;
   s << what << ": " << cudaGetErrorName(e) << " (" << cudaGetErrorString(e) << ")";
@@ -603,6 +607,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.status = status;
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
+      p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("qkv gemv", e);
 
       return {};
@@ -630,6 +635,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       a.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(D)));
       a.max_splits = splits;
       a.min_chunk = 64;
+      a.max_chunk = 128;
       // One row per sequence: only each row's newest K/V comes from the QKV
       // kernel still running, older rows can be gathered before its completion.
       a.early_mode = distinct ? 1 : 0;
@@ -664,6 +670,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.status = status;
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
+      p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("o gemv", e);
       if (tp && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (o): " + collective_->lastError();
@@ -695,6 +702,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.status = status;
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
+      p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("gate/up gemv", e);
 
       return {};
@@ -721,6 +729,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.status = status;
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
+      p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("down gemv", e);
       if (tp && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (down): " + collective_->lastError();
@@ -764,6 +773,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
     }
     p.trace = traceSink(0, kind);
     p.work_counter = workCounter(0, kind);
+      p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("lm head gemv", e);
     if (tp) {
       if ((e = collective_->allReduceMaxU64(p.argmax_keys, R, s)) != cudaSuccess)

@@ -25,6 +25,12 @@ namespace tmc {
 namespace {
 
 constexpr int kThreads = 128;
+// Largest thread-block cluster (16 is the sm_100 opt-in, non-portable size; a
+// device that cannot hold a 16-CTA cluster of this kernel falls back to 8).
+constexpr int kMaxCluster = 16;
+#ifndef TMC_ATTENTION_CLUSTER_LIMIT
+#define TMC_ATTENTION_CLUSTER_LIMIT 16
+#endif
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -116,11 +122,41 @@ struct Cfg {
   }
 };
 
-// Grid (max_splits, Hkv, rows), 4 warps. A CTA owns one KV head of one query
-// row and a chunk of key positions; each warp runs flash-decoding on its own 16
-// positions of every 64-position tile with tensor-core MMAs (the G query heads
-// of the KV head fill rows of the 16-row A tile; unused rows are zero), keeps
-// its own online-softmax state, and the warps merge once at the end.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+// Shared-memory address of the same variable in cluster CTA `rank`.
+__device__ __forceinline__ uint32_t map_cluster(const void *local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+// All threads of all CTAs of the cluster (a hardware barrier, not a spin).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Grid (max_splits, Hkv, rows), 4 warps, launched in clusters of `cluster`
+// CTAs along the splits. A CTA owns one KV head of one query row and a chunk
+// of key positions; each warp runs flash-decoding on its own 16 positions of
+// every 64-position tile with tensor-core MMAs (the G query heads of the KV
+// head fill rows of the 16-row A tile; unused rows are zero) and keeps its own
+// online-softmax state; the warps merge in shared memory, then the CTAs of a
+// cluster merge through distributed shared memory. Only when a (row, KV head)
+// spans several clusters do the cluster results meet in the global workspace
+// (atomic ticket, last CTA combines).
 template <int D, int G>
 __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionParams p) {
   using C = Cfg<D, G>;
@@ -137,10 +173,12 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       (reinterpret_cast<uintptr_t>(sW + 2 * C::kMaxSplits * G) + 15) & ~uintptr_t(15));
   uint64_t *empty = full + S;
   __shared__ int is_last;
+  __shared__ float xml[G * 2];  // this CTA's (m, l) per head, read by the cluster
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gq = lane >> 2, tq = lane & 3;  // mma fragment coordinates
+  const uint32_t csize = cluster_nctarank(), crank = cluster_ctarank();
   const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
   unsigned long long t_ready = 0ull;
 
@@ -148,7 +186,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
   // produces q (and the newest K/V rows) starts: they are read, and the K/V rows
   // of older positions gathered, before the programmatic-dependency wait.
   const int pos = p.positions[row];
-  if (pos < 0 || pos >= p.capacity) {
+  if (pos < 0 || pos >= p.capacity) {  // the same for every CTA of the row
     if (split == 0 && kvh == 0 && tid == 0)
       report_status(p.status, kStatusLengthRange, kWhereAttention, pos, row);
     pdl_wait();
@@ -156,23 +194,33 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
   }
   const int len = pos + 1;
   int nsplit = (len + p.min_chunk - 1) / p.min_chunk;
+  if (p.max_chunk > 0 && nsplit > (int)csize) {
+    // Fill one cluster before adding more: splits in other clusters meet only
+    // through the global workspace and a ticket, a longer tail than the
+    // distributed-shared-memory merge.
+    const int wide = (len + p.max_chunk - 1) / p.max_chunk;
+    nsplit = wide > (int)csize ? wide : (int)csize;
+  }
   if (nsplit > p.max_splits) nsplit = p.max_splits;
   if (nsplit > C::kMaxSplits) nsplit = C::kMaxSplits;
   if (nsplit < 1) nsplit = 1;
   int chunk = (len + nsplit - 1) / nsplit;
-  chunk = (chunk + T - 1) / T * T;
+  chunk = (chunk + 15) / 16 * 16;  // whole warp rows
   const int active = (len + chunk - 1) / chunk;
-  if (split >= active) {
+  const int first_split = split - (int)crank;
+  if (first_split >= active) {  // the whole cluster is idle
     pdl_wait();
     trace_emit(p.trace, t_entry, t_entry);
     return;
   }
-  const int begin = split * chunk;
-  const int end = min(len, begin + chunk);
-  const int ntiles = (end - begin + T - 1) / T;
+  const bool idle = split >= active;  // no positions, but joins the cluster merge
+  const int begin = idle ? len : split * chunk;
+  const int end = idle ? len : min(len, begin + chunk);
+  const int ntiles = idle ? 0 : (end - begin + T - 1) / T;
   const int *table = p.block_table + (size_t)p.table_rows[row] * p.table_stride;
   // Positions below `fresh` are never written by the producer kernel.
   const int fresh = p.early_mode == 2 ? end : (p.early_mode == 1 ? pos : begin);
+  bool failed = false;
 
   if (tid == 0) {
 #pragma unroll
@@ -255,7 +303,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
 #pragma unroll
     for (int kk = 0; kk < C::kKSteps; ++kk) {
       const int c0 = kk * 16 + 2 * tq;
-      if (gq < G) {
+      if (gq < G && !idle) {
         qa[kk][0] = *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0);
         qa[kk][2] = *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0 + 8);
       } else {
@@ -274,86 +322,89 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
 #pragma unroll
   for (int i = 0; i < C::kDTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
 
-  for (int t = 0; t < ntiles; ++t) {
+  for (int t = 0; t < ntiles && !failed; ++t) {
     const int stage = t % S;
     if (!mbar_wait(&full[stage], (t / S) & 1)) {
       if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
-      return;
+      failed = true;
+      break;
     }
     const int r0 = warp * 16;  // this warp's 16 rows of the tile
     const int p0 = begin + t * T + r0;
     const __half *k = sK + ((size_t)stage * T + r0) * ROW;
     const __half *v = sV + ((size_t)stage * T + r0) * ROW;
     const int *valid = sValid + stage * T + r0;
-    // Scores S[16 heads x 16 positions] as two n-tiles of 8 positions.
-    float sc[2][4];
+    if (p0 < end) {
+      // Scores S[16 heads x 16 positions] as two n-tiles of 8 positions.
+      float sc[2][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+      for (int nt = 0; nt < 2; ++nt) {
+        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
 #pragma unroll
-      for (int kk = 0; kk < C::kKSteps; ++kk) {
+        for (int kk = 0; kk < C::kKSteps; ++kk) {
+          uint32_t b0, b1;
+          // matrices: rows = positions nt*8..+7, columns = dims kk*16..+7 and +8..+15
+          const __half *addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
+          ldmatrix_x2(b0, b1, addr);
+          mma_16816(sc[nt], qa[kk], b0, b1);
+        }
+      }
+      // Scale, mask, online softmax (row gq owns c0/c1; c2/c3 are rows gq+8, unused).
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int lp = nt * 8 + 2 * tq + j;
+          const bool ok = p0 + lp < end && valid[lp];
+          sc[nt][j] = ok ? sc[nt][j] * p.scale : -INFINITY;
+          mx = fmaxf(mx, sc[nt][j]);
+        }
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+      float psum = 0.0f;
+      float pr[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          pr[nt][j] = (sc[nt][j] == -INFINITY) ? 0.0f : expf(sc[nt][j] - m_new);
+          psum += pr[nt][j];
+        }
+      }
+      psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+      psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+      l_run = l_run * rescale + psum;
+      m_run = m_new;
+      // P as the A operand (16 heads x 16 positions) in two fp16 parts, hi + lo,
+      // so the probabilities keep ~22 bits (the reference multiplies fp32
+      // probabilities by the values).
+      uint32_t pa[4], pl[4];
+      {
+        const __half2 h0 = __floats2half2_rn(pr[0][0], pr[0][1]);
+        const __half2 h1 = __floats2half2_rn(pr[1][0], pr[1][1]);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        pa[0] = *reinterpret_cast<const uint32_t *>(&h0);
+        pa[2] = *reinterpret_cast<const uint32_t *>(&h1);
+        pl[0] = pack_half2(pr[0][0] - f0.x, pr[0][1] - f0.y);
+        pl[2] = pack_half2(pr[1][0] - f1.x, pr[1][1] - f1.y);
+        pa[1] = pa[3] = pl[1] = pl[3] = 0u;
+      }
+      // O[16 x D] += P . V[16 positions x D].
+#pragma unroll
+      for (int dt = 0; dt < C::kDTiles; ++dt) {
+        acc[dt][0] *= rescale;
+        acc[dt][1] *= rescale;
         uint32_t b0, b1;
-        // matrices: rows = positions nt*8..+7, columns = dims kk*16..+7 and +8..+15
-        const __half *addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
-        ldmatrix_x2(b0, b1, addr);
-        mma_16816(sc[nt], qa[kk], b0, b1);
+        // matrices (transposed on load): rows = positions 0..7 and 8..15, columns = dims dt*8..+7
+        const __half *addr = v + (size_t)(lane & 15) * ROW + dt * 8;
+        ldmatrix_x2_trans(b0, b1, addr);
+        mma_16816(acc[dt], pl, b0, b1);
+        mma_16816(acc[dt], pa, b0, b1);
       }
-    }
-    // Scale, mask, online softmax (row gq owns c0/c1; c2/c3 are rows gq+8, unused).
-    float mx = -INFINITY;
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int lp = nt * 8 + 2 * tq + j;
-        const bool ok = p0 + lp < end && valid[lp];
-        sc[nt][j] = ok ? sc[nt][j] * p.scale : -INFINITY;
-        mx = fmaxf(mx, sc[nt][j]);
-      }
-    }
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float m_new = fmaxf(m_run, mx);
-    const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
-    float psum = 0.0f;
-    float pr[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        pr[nt][j] = (sc[nt][j] == -INFINITY) ? 0.0f : expf(sc[nt][j] - m_new);
-        psum += pr[nt][j];
-      }
-    }
-    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-    l_run = l_run * rescale + psum;
-    m_run = m_new;
-    // P as the A operand (16 heads x 16 positions) in two fp16 parts, hi + lo,
-    // so the probabilities keep ~22 bits (the reference multiplies fp32
-    // probabilities by the values).
-    uint32_t pa[4], pl[4];
-    {
-      const __half2 h0 = __floats2half2_rn(pr[0][0], pr[0][1]);
-      const __half2 h1 = __floats2half2_rn(pr[1][0], pr[1][1]);
-      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-      pa[0] = *reinterpret_cast<const uint32_t *>(&h0);
-      pa[2] = *reinterpret_cast<const uint32_t *>(&h1);
-      pl[0] = pack_half2(pr[0][0] - f0.x, pr[0][1] - f0.y);
-      pl[2] = pack_half2(pr[1][0] - f1.x, pr[1][1] - f1.y);
-      pa[1] = pa[3] = pl[1] = pl[3] = 0u;
-    }
-    // O[16 x D] += P . V[16 positions x D].
-#pragma unroll
-    for (int dt = 0; dt < C::kDTiles; ++dt) {
-      acc[dt][0] *= rescale;
-      acc[dt][1] *= rescale;
-      uint32_t b0, b1;
-      // matrices (transposed on load): rows = positions 0..7 and 8..15, columns = dims dt*8..+7
-      const __half *addr = v + (size_t)(lane & 15) * ROW + dt * 8;
-      ldmatrix_x2_trans(b0, b1, addr);
-      mma_16816(acc[dt], pl, b0, b1);
-      mma_16816(acc[dt], pa, b0, b1);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
@@ -361,7 +412,8 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       // Every warp has finished this stage before it is refilled.
       if (!mbar_wait(&empty[stage], (t / S) & 1)) {
         if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
-        return;
+        failed = true;
+        break;
       }
       arm(t + S);
       copy(t + S, begin, end);
@@ -409,36 +461,75 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       for (int e = 0; e < E; ++e) o_cta[e] = fmaf(mrg[((size_t)w * G + hg) * D + hd + e], f, o_cta[e]);
     }
   }
-
-  const size_t head_base = ((size_t)row * p.hkv + kvh);
-  if (active == 1) {
-    if (own) {
-      const float inv = 1.0f / l_cta;
-      __half *o = p.out + (size_t)row * p.out_stride + (size_t)(kvh * G + hg) * D + hd;
+  __syncthreads();
+  // Publish this CTA's (m, l, o) for the cluster (o reuses the merge area).
+  float *xo = mrg;
+  if (own) {
 #pragma unroll
-      for (int e = 0; e < E; ++e) o[e] = __float2half_rn(o_cta[e] * inv);
+    for (int e = 0; e < E; ++e) xo[(size_t)hg * D + hd + e] = o_cta[e];
+    if (hd == 0) {
+      xml[hg * 2] = m_cta;
+      xml[hg * 2 + 1] = l_cta;
     }
-    trace_emit(p.trace, t_entry, t_ready);
-    return;
   }
-  // Write this split's partial, then the last CTA of the (row, KV head) combines.
-  {
-    float *wa = p.ws_acc + ((head_base * p.max_splits + split) * G) * D;
-    if (own) {
+  cluster_sync();
+
+  // Cluster merge: CTA `crank` combines outputs [lo, hi) of G*D across the
+  // cluster's CTAs through distributed shared memory.
+  const size_t head_base = ((size_t)row * p.hkv + kvh);
+  const int nclusters = (active + (int)csize - 1) / (int)csize;
+  const int cidx = split / (int)csize;       // this cluster along the splits
+  const int stride = gridDim.x / (int)csize;  // cluster slots per (row, KV head)
+  const int per = (G * D + (int)csize - 1) / (int)csize;
+  const int lo = (int)crank * per, hi = min(G * D, lo + per);
+  for (int i = lo + tid; i < hi; i += kThreads) {
+    const int h = i / D;
+    // Issue every remote load before using any (csize <= kMaxCluster).
+    float mv[kMaxCluster], lv[kMaxCluster], ov[kMaxCluster];
 #pragma unroll
-      for (int e = 0; e < E; ++e) wa[(size_t)hg * D + hd + e] = o_cta[e];
-      if (hd == 0) {
-        float *wm = p.ws_ml + ((head_base * p.max_splits + split) * G + hg) * 2;
-        wm[0] = m_cta;
-        wm[1] = l_cta;
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < (int)csize) {
+        mv[c] = ld_cluster_f32(map_cluster(&xml[h * 2], c));
+        lv[c] = ld_cluster_f32(map_cluster(&xml[h * 2 + 1], c));
+        ov[c] = ld_cluster_f32(map_cluster(&xo[i], c));
+      }
+    }
+    float mmax = -INFINITY;
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c)
+      if (c < (int)csize) mmax = fmaxf(mmax, mv[c]);
+    float den = 0.0f, num = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kMaxCluster; ++c) {
+      if (c < (int)csize) {
+        const float f = (mv[c] == -INFINITY) ? 0.0f : expf(mv[c] - mmax);
+        den = fmaf(lv[c], f, den);
+        num = fmaf(ov[c], f, num);
+      }
+    }
+    if (nclusters == 1) {
+      p.out[(size_t)row * p.out_stride + (size_t)kvh * G * D + i] = __float2half_rn(num / den);
+    } else {
+      p.ws_acc[(head_base * stride + cidx) * G * D + i] = num;
+      if (i % D == 0) {
+        float *wm = p.ws_ml + ((head_base * stride + cidx) * G + h) * 2;
+        wm[0] = mmax;
+        wm[1] = den;
       }
     }
   }
+  cluster_sync();  // every CTA's shared memory stays valid until all reads are done
+  if (nclusters == 1) {
+    trace_emit(p.trace, t_entry, t_ready);
+    return;
+  }
+
+  // Several clusters: the last CTA of the (row, KV head) combines them.
   __threadfence();
   __syncthreads();
   if (tid == 0) {
     const unsigned int prev = atomicAdd(p.counters + head_base, 1u);
-    is_last = (prev == static_cast<unsigned int>(active - 1)) ? 1 : 0;
+    is_last = (prev == static_cast<unsigned int>(nclusters * (int)csize - 1)) ? 1 : 0;
   }
   __syncthreads();
   if (!is_last) {
@@ -446,12 +537,9 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
     return;
   }
   __threadfence();
-  // Combine: per (split, head) weights exp(m_s - M) / sum_s l_s exp(m_s - M)
-  // from one pass over the (m, l) pairs, then every thread sums its outputs
-  // over the splits with eight partial loads in flight.
-  const float2 *ml = reinterpret_cast<const float2 *>(p.ws_ml + (head_base * p.max_splits) * G * 2);
+  const float2 *ml = reinterpret_cast<const float2 *>(p.ws_ml + (head_base * stride) * G * 2);
   float *sWl = sW + C::kMaxSplits * G;
-  for (int i = tid; i < active * G; i += kThreads) {
+  for (int i = tid; i < nclusters * G; i += kThreads) {
     const float2 v = __ldcg(ml + i);
     sW[i] = v.x;
     sWl[i] = v.y;
@@ -459,11 +547,11 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
   __syncthreads();
   for (int g = warp; g < G; g += kThreads / 32) {
     float mx = -INFINITY;
-    for (int sp = lane; sp < active; sp += 32) mx = fmaxf(mx, sW[sp * G + g]);
+    for (int c = lane; c < nclusters; c += 32) mx = fmaxf(mx, sW[c * G + g]);
     mx = warp_max(mx);
     float den = 0.0f;
-    for (int sp = lane; sp < active; sp += 32) {
-      const int i = sp * G + g;
+    for (int c = lane; c < nclusters; c += 32) {
+      const int i = c * G + g;
       const float ms = sW[i];
       const float f = (ms == -INFINITY) ? 0.0f : expf(ms - mx);
       den += sWl[i] * f;
@@ -471,36 +559,19 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
     }
     den = warp_sum(den);
     const float inv = 1.0f / den;
-    for (int sp = lane; sp < active; sp += 32) sW[sp * G + g] *= inv;
+    for (int c = lane; c < nclusters; c += 32) sW[c * G + g] *= inv;
   }
   __syncthreads();
-  if (own) {
-    float out[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) out[e] = 0.0f;
-    const float *wa = p.ws_acc + (head_base * p.max_splits) * G * D + (size_t)hg * D + hd;
-    for (int s0 = 0; s0 < active; s0 += 8) {
-      float part[8][E];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int sp = s0 + j;
-        const float *src = wa + (size_t)sp * G * D;
-#pragma unroll
-        for (int e = 0; e < E; ++e) part[j][e] = sp < active ? __ldcg(src + e) : 0.0f;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float f = s0 + j < active ? sW[(s0 + j) * G + hg] : 0.0f;
-#pragma unroll
-        for (int e = 0; e < E; ++e) out[e] = fmaf(part[j][e], f, out[e]);
-      }
-    }
-    __half *o = p.out + (size_t)row * p.out_stride + (size_t)(kvh * G + hg) * D + hd;
-#pragma unroll
-    for (int e = 0; e < E; ++e) o[e] = __float2half_rn(out[e]);
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int h = i / D;
+    float out = 0.0f;
+    for (int c = 0; c < nclusters; ++c)
+      out = fmaf(__ldcg(p.ws_acc + (head_base * stride + c) * G * D + i), sW[c * G + h], out);
+    p.out[(size_t)row * p.out_stride + (size_t)kvh * G * D + i] = __float2half_rn(out);
   }
   if (tid == 0) atomicExch(p.counters + head_base, 0u);
   trace_emit(p.trace, t_entry, t_ready);
+  (void)failed;
 }
 
 template <int D, int G>
@@ -508,29 +579,70 @@ cudaError_t launch_instance(const AttentionParams &p, cudaStream_t stream, bool 
   auto kernel = attention_kernel<D, G>;
   const size_t smem = Cfg<D, G>::smem_bytes();
   static std::mutex mu;
-  static std::unordered_map<int, bool> configured;
+  static std::unordered_map<int, int> cluster_limit;  // per device, 0 = not configured
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  int limit = 0;
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (!configured[dev]) {
+    limit = cluster_limit[dev];
+    if (limit == 0) {
       e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(smem));
       if (e != cudaSuccess) return e;
-      configured[dev] = true;
+      limit = 8;
+      if (TMC_ATTENTION_CLUSTER_LIMIT > 8 &&
+          cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+              cudaSuccess) {
+        cudaLaunchConfig_t probe = {};
+        probe.gridDim = dim3(TMC_ATTENTION_CLUSTER_LIMIT, 1, 1);
+        probe.blockDim = dim3(kThreads);
+        probe.dynamicSmemBytes = smem;
+        cudaLaunchAttribute ca;
+        ca.id = cudaLaunchAttributeClusterDimension;
+        ca.val.clusterDim.x = TMC_ATTENTION_CLUSTER_LIMIT;
+        ca.val.clusterDim.y = 1;
+        ca.val.clusterDim.z = 1;
+        probe.attrs = &ca;
+        probe.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &probe) == cudaSuccess && clusters > 0)
+          limit = TMC_ATTENTION_CLUSTER_LIMIT;
+        (void)cudaGetLastError();
+      }
+      if (limit > TMC_ATTENTION_CLUSTER_LIMIT) limit = TMC_ATTENTION_CLUSTER_LIMIT;
+      cluster_limit[dev] = limit;
     }
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.max_splits, p.hkv, p.rows);
+  // Clusters along the splits; the grid covers whole clusters.
+  const int splits = p.max_splits < Cfg<D, G>::kMaxSplits ? p.max_splits : Cfg<D, G>::kMaxSplits;
+  int cluster = p.cluster;
+  if (cluster <= 0) {
+    cluster = 1;
+    while (cluster < splits && cluster < limit) cluster *= 2;
+  } else if (cluster > limit) {
+    return cudaErrorInvalidValue;
+  }
+  cfg.gridDim = dim3((splits + cluster - 1) / cluster * cluster, p.hkv, p.rows);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  attr[n].id = cudaLaunchAttributeClusterDimension;
+  attr[n].val.clusterDim.x = cluster;
+  attr[n].val.clusterDim.y = 1;
+  attr[n].val.clusterDim.z = 1;
+  ++n;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, p);
 }
 
@@ -556,7 +668,8 @@ size_t attention_workspace_bytes(int rows, int hq, int hkv, int head_dim, int ma
 
 cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool pdl) {
   if (p.rows <= 0 || p.hkv <= 0 || p.hq <= 0 || p.hq % p.hkv != 0 || p.max_splits <= 0 ||
-      p.min_chunk <= 0 || p.page_size <= 0 || p.rows > 65535 || p.hkv > 65535)
+      p.min_chunk <= 0 || p.page_size <= 0 || p.rows > 65535 || p.hkv > 65535 ||
+      p.cluster < 0 || p.cluster > kMaxCluster || (p.cluster & (p.cluster - 1)) != 0)
     return cudaErrorInvalidValue;
   const int g = p.hq / p.hkv;
   switch (p.head_dim) {

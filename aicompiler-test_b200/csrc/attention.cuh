@@ -30,14 +30,18 @@ struct AttentionParams {
   const int *positions;    // [rows] query position; keys [0, position] are attended
   int rows, hq, hkv, head_dim, page_size, pool_pages, capacity;
   float scale;
-  int max_splits;  // grid.x; splits actually used <= min(max_splits, 64)
+  int max_splits;  // splits actually used <= min(max_splits, 64)
+  int cluster;     // CTAs per thread-block cluster along the splits (1..16, a power of two; 0 = auto)
   // Which K/V rows may be gathered before the programmatic-dependency wait:
   // 0 none, 1 positions below the row's own position (decode: only the newest
   // row is produced by the preceding kernel), 2 all (no concurrent producer).
   int early_mode;
   int min_chunk;   // positions per split at least this many
-  float *ws_acc;   // [rows, hkv, max_splits, G, D]
-  float *ws_ml;    // [rows, hkv, max_splits, G, 2]
+  // When > 0 and the splits need more than one cluster: use one full cluster
+  // unless that gives splits longer than max_chunk positions.
+  int max_chunk;
+  float *ws_acc;   // [rows, hkv, <= max_splits cluster slots, G, D] (splits spanning clusters)
+  float *ws_ml;    // [rows, hkv, <= max_splits cluster slots, G, 2]
   unsigned int *counters;  // [rows, hkv], zero between launches
   TmcDeviceStatus *status;
   TraceSink trace;         // optional timeline (records == nullptr: off)

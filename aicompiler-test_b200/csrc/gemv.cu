@@ -24,8 +24,9 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-__device__ __forceinline__ void prefetch_l2(const void *p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, size multiple of 16).
+__device__ __forceinline__ void prefetch_bulk_l2(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 template <typename XS>
@@ -336,7 +337,6 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   __shared__ float red[32];
   __shared__ unsigned long long warp_best[kWarps][M];
   __shared__ float team_part[kWarps][R * M];
-  __shared__ int team_next[kWarps][2];
   __shared__ int is_last;
 
   // A team of KS warps shares each row group; warp `wt` of the team streams
@@ -376,39 +376,44 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
   uint4 w[R][U];
   int g = gt, c0 = c_lo;
-  if (g < ngroups && c_lo < c_hi) {
-    load_batch(g, c_lo, w);
+  if (g < ngroups && c_lo < c_hi) load_batch(g, c_lo, w);
+  // While the producer of x finishes, pull this warp's static share of the
+  // weights (its slice of the groups gt, gt + total_teams, ...) into L2 with
+  // bulk prefetches, up to a budget that keeps a whole launch's prefetch well
+  // inside L2. CTAs of this kernel become resident as the previous kernel's
+  // CTAs drain, so its tail streams this kernel's weights instead of idling.
+  if (p.l2_prefetch_bytes > 0 && lane == 0 && c_lo < c_hi) {
+    const long long per_warp = p.l2_prefetch_bytes / ((long long)total_teams * KS);
+    const uint32_t slice = static_cast<uint32_t>(c_hi - c_lo) * 16u;
+    long long budget = per_warp;
+    for (int gg = gt; gg < ngroups && budget > 0; gg += total_teams) {
 #pragma unroll
-    for (int r = 0; r < R; ++r) {
-      const int row = g * R + r;
-      if (row < p.N) {
-        const uint4 *wr = reinterpret_cast<const uint4 *>(p.W + (size_t)row * p.K);
-        for (int c = c_lo + 32 * U + lane; c < c_hi && c < c_lo + 4 * 32 * U; c += 32) prefetch_l2(wr + c);
+      for (int r = 0; r < R; ++r) {
+        const int row = gg * R + r;
+        if (row >= p.N || budget <= 0) continue;
+        const char *src = reinterpret_cast<const char *>(p.W + (size_t)row * p.K) + (size_t)c_lo * 16;
+        prefetch_bulk_l2(src, slice);
+        budget -= slice;
       }
     }
   }
   pdl_wait();
-  // Dynamic scheduling: SMs do not get equal HBM bandwidth, so equal static
-  // shares finish at different times. Groups are split into kGemvPools
-  // interleaved pools (group = pool + kGemvPools * k) with one ticket counter
-  // each; a team keeps to the pool of its first group. Its first three groups
-  // are static; afterwards the team leader keeps one ticket in flight and
-  // publishes it a group later, so the atomic's round trip never stalls the
-  // weight stream. A group's arithmetic does not depend on the team that runs
-  // it, so results stay deterministic.
-  const bool dynamic = p.work_counter != nullptr && total_teams % kGemvPools == 0 &&
-                       ngroups > 3 * total_teams;
-  const bool leader = lane == 0 && wt == 0;
+  // Dynamic scheduling (one-warp teams): SMs do not get equal HBM bandwidth,
+  // so equal static shares finish at different times. After its first (static)
+  // group a warp takes groups from one of kGemvPools interleaved pools
+  // (group = pool + kGemvPools * k), each with its own ticket counter on its
+  // own cache line. Lane 0 takes the next ticket when a group starts and the
+  // warp uses it when the group ends, so the atomic's round trip hides behind
+  // the group's loads. A group's arithmetic does not depend on the warp that
+  // runs it, so results stay deterministic.
+  const bool dynamic = KS == 1 && p.work_counter != nullptr && total_teams % kGemvPools == 0 &&
+                       ngroups > 2 * total_teams;
   const int pool = gt % kGemvPools;
-  const int pool_base = 3 * (total_teams / kGemvPools);
+  const int pool_base = total_teams / kGemvPools;
   unsigned int *ticket = p.work_counter + pool * kGemvPoolStride;
   int g_next = gt + total_teams;
-  int slot = 0;
-  int pending = 0;
-  if (dynamic && leader) {
-    team_next[team][0] = gt + 2 * total_teams;
-    pending = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
-  }
+  int fetched = 0;
+  if (dynamic && lane == 0) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
   stage_x<XS, M>(p, xs, red);
   __syncthreads();
   pdl_launch_dependents();
@@ -445,19 +450,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     int ng = g, nc = c0 + 32 * U;
     if (nc >= c_hi) {
       nc = c_lo;
-      ng = g_next;
       if (dynamic) {
-        // Written by the team leader one group ago (two team barriers, or a
-        // warp sync when KS == 1, separate that write from this read).
-        g_next = team_next[team][slot];
-        slot ^= 1;
-        if (KS == 1) __syncwarp();
-        if (leader) {
-          team_next[team][slot] = pending;
-          pending = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
-        }
-        if (KS == 1) __syncwarp();
+        ng = __shfl_sync(0xffffffffu, fetched, 0);
+        if (lane == 0 && ng < ngroups) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
       } else {
+        ng = g_next;
         g_next += total_teams;
       }
     }

@@ -86,6 +86,9 @@ struct GemvParams {
   // ticket; all zero before the launch and reset by the last CTA. Null: the
   // static interleaved assignment.
   unsigned int *work_counter;
+  // Bytes of W this launch may bulk-prefetch into L2 before its inputs are
+  // ready (0: none).
+  long long l2_prefetch_bytes;
 };
 
 constexpr int kGemvPools = 8;

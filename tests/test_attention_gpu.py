@@ -1,7 +1,9 @@
 """Paged GQA decode attention on the GPU vs the CPU oracle (fp64 restatement of
 emitServingPagedKVAttention, reference KVCacheMetalEmitter.cpp:312-406, plus the
-GQA head map). Tolerance: max |gpu - ref| <= 2e-3 x RMS(ref) per case, after
-the reference's storage rounding of the context to fp16."""
+GQA head map). Tolerance, per element after the reference's storage rounding
+of the context to fp16: |gpu - ref| <= max(2e-3 x RMS(ref), one fp16 ulp of
+ref) -- the context is stored in fp16, so an fp32 result a hair away from the
+fp64 one can round to the neighbouring fp16 value near a rounding midpoint."""
 
 import numpy as np
 import pytest
@@ -53,8 +55,11 @@ def run_attention(rt, q, k_pool, v_pool, table, table_rows, positions, hkv, page
 def check(got, ref):
     ref16 = oracle.round_f16(ref.astype(np.float32)).reshape(ref.shape)
     rms = float(np.sqrt(np.mean(ref ** 2)))
-    err = float(np.max(np.abs(got.astype(np.float64) - ref16)))
-    assert err <= 2e-3 * rms, (err, rms)
+    ulp = np.spacing(np.abs(ref16).astype(np.float16)).astype(np.float64)
+    err = np.abs(got.astype(np.float64) - ref16)
+    bound = np.maximum(2e-3 * rms, ulp)
+    worst = int(np.argmax(err - bound))
+    assert np.all(err <= bound), (float(err.flat[worst]), float(bound.flat[worst]), rms)
 
 
 CASES = [
