@@ -261,9 +261,12 @@ def run_ours(args, world, rank, local):
                        "vocab": CFG["vocab"], "batch": 1, "prompt": args.prompt,
                        "parallelism": f"tp{world}",
                        "l2": "inputs larger than L2: 15 GB of weights streamed per step"},
-            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (step_ms * 1e-3) / 1e9,
+            # Whole-job bytes: every rank streams its own shard (step_bytes is one rank's).
+            "step_roofline": {"bytes_per_step": step_bytes * world,
+                              "bytes_per_step_per_rank": step_bytes,
+                              "achieved_gbs": step_bytes * world / (step_ms * 1e-3) / 1e9,
                               "aggregate_peak_gbs": hbm * world,
-                              "frac": step_bytes / (step_ms * 1e-3) / 1e9 / (hbm * world)},
+                              "frac": step_bytes / (step_ms * 1e-3) / 1e9 / hbm},
             "e2e": e2e,
             "gpu_launches": dec.kernels_per_step(1) * K,
             "roofline": roofline,

@@ -197,3 +197,98 @@ def random_weights(spec: DecoderSpec, seed: int, std: float = 0.02) -> dict:
         w[p + "up.weight"] = mat(I, H)
         w[p + "down.weight"] = mat(H, I)
     return w
+
+
+def argmax_key(values: torch.Tensor, offset: int) -> torch.Tensor:
+    """Orderable int64 key per row of `values` [S, n] (fp16/fp32): the larger
+    value wins, then the smaller global index (offset + column) -- the tie rule
+    of emitTokenArgmax (TransformerDecodeMetalEmitter.cpp:198-257) and of
+    torch.argmax on the reference's fp16 logits. A max-reduction of keys over
+    vocab shards therefore equals argmax over the whole vocabulary."""
+    bits = values.float().contiguous().view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+    negative = (bits >> 31) == 1
+    ordered = torch.where(negative, (~bits) & 0xFFFFFFFF, bits | 0x80000000)
+    idx = offset + torch.arange(values.shape[-1], dtype=torch.int64)
+    keys = (ordered << 31) | (0x7FFFFFFF - idx)
+    return keys.max(dim=-1).values
+
+
+def argmax_key_index(key: torch.Tensor) -> torch.Tensor:
+    return 0x7FFFFFFF - (key & 0x7FFFFFFF)
+
+
+@dataclass
+class TensorParallelOracle(DecoderOracle):
+    """One rank of the tensor-parallel decomposition the device decoder uses:
+    column-parallel Q/K/V (whole heads per rank; the GQA group of a KV head
+    stays on one rank), gate and up; row-parallel O and down whose fp32 partial
+    sums are summed over ranks (`all_reduce_sum`) before the storage rounding
+    and the residual add; vocab-parallel LM head whose greedy token comes from
+    a max-reduction of packed (value, index) keys (`all_reduce_max`). Rank r
+    owns the r-th contiguous slice of every split dimension. Not in the
+    reference (it has no multi-GPU code); with world = 1 it is DecoderOracle."""
+
+    rank: int = 0
+    world: int = 1
+    all_reduce_sum: object = None  # callable(torch.float32 tensor) -> summed tensor
+    all_reduce_max: object = None  # callable(torch.int64 tensor) -> max tensor
+
+    def _rows(self, w, parts):
+        n = w.shape[0] // parts
+        return w[self.rank * n:(self.rank + 1) * n]
+
+    def _cols(self, w, parts):
+        n = w.shape[1] // parts
+        return w[:, self.rank * n:(self.rank + 1) * n]
+
+    @torch.no_grad()
+    def forward(self, seq, token_ids):
+        """Returns (local logits [S, vocab / world] in storage dtype, next token)."""
+        s = self.spec
+        dt = s.dtype
+        W = self.world
+        hq, hkv, D = s.heads // W, s.kv_heads // W, s.head_dim
+        ids = torch.as_tensor(np.asarray(token_ids, dtype=np.int64)).view(1, -1)
+        S = ids.shape[1]
+        past = self.caches.get(seq)
+        start = self.length(seq)
+        if start + S > s.capacity:
+            raise ValueError("decoder KV cache capacity exceeded")
+        positions = torch.arange(start, start + S).view(1, S)
+        x = F.embedding(ids, self.w["embedding.weight"])
+        group = s.heads // s.kv_heads
+        new_cache = []
+        for layer in range(s.layers):
+            p = f"layer{layer}."
+            h = _rms_norm(x, self.w[p + "input_norm.weight"], s.epsilon)
+            q = F.linear(h, self._rows(self.w[p + "q.weight"], W)).view(1, S, hq, D).transpose(1, 2)
+            k = F.linear(h, self._rows(self.w[p + "k.weight"], W)).view(1, S, hkv, D).transpose(1, 2)
+            v = F.linear(h, self._rows(self.w[p + "v.weight"], W)).view(1, S, hkv, D).transpose(1, 2)
+            q = _rope(q, self.rope_cos, self.rope_sin, positions)
+            k = _rope(k, self.rope_cos, self.rope_sin, positions)
+            if past is not None:
+                k = torch.cat((past[layer][0].unsqueeze(0), k), dim=2)
+                v = torch.cat((past[layer][1].unsqueeze(0), v), dim=2)
+            new_cache.append((k[0], v[0]))
+            kk = k.repeat_interleave(group, dim=1) if group > 1 else k
+            vv = v.repeat_interleave(group, dim=1) if group > 1 else v
+            scores = torch.matmul(q.float(), kk.float().transpose(-2, -1)) / math.sqrt(D)
+            qpos = torch.arange(start, start + S).view(S, 1)
+            kpos = torch.arange(kk.size(2)).view(1, -1)
+            scores = scores.masked_fill(kpos > qpos, float("-inf"))
+            ctx = torch.matmul(torch.softmax(scores, dim=-1), vv.float()).to(dt)
+            ctx = ctx.transpose(1, 2).contiguous().view(1, S, -1)
+            partial = F.linear(ctx.float(), self._cols(self.w[p + "o.weight"], W).float())
+            x = x + self.all_reduce_sum(partial).to(dt)
+            h = _rms_norm(x, self.w[p + "post_norm.weight"], s.epsilon)
+            gate = F.linear(h, self._rows(self.w[p + "gate.weight"], W))
+            up = F.linear(h, self._rows(self.w[p + "up.weight"], W))
+            act = F.silu(gate) * up
+            partial = F.linear(act.float(), self._cols(self.w[p + "down.weight"], W).float())
+            x = x + self.all_reduce_sum(partial).to(dt)
+        logits = F.linear(_rms_norm(x, self.w["final_norm.weight"], s.epsilon),
+                          self._rows(self.w["lm_head.weight"], W))
+        self.caches[seq] = new_cache
+        vl = s.vocab // W
+        key = self.all_reduce_max(argmax_key(logits[0, -1:], self.rank * vl))
+        return logits[0], int(argmax_key_index(key)[0])

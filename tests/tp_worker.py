@@ -1,0 +1,54 @@
+"""One tensor-parallel rank of the decoder, run as a spawned child process by
+tests/test_tp_gpu.py (one process per GPU, NCCL between them).
+
+The rank loads the unsharded golden weights (the decoder keeps its own shard:
+column-parallel Q/K/V/gate/up, row-parallel O/down, vocab-parallel LM head),
+replays the reference exporter's prefill and decode tokens, and returns its
+local logits slice, its local KV heads and the greedy tokens it saw."""
+
+import json
+import os
+import sys
+import traceback
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+
+
+def decode_worker(rank, world, uid, npz, page_size, generate_steps, queue):
+    try:
+        sys.path.insert(0, ROOT)
+        sys.path.insert(0, os.path.join(ROOT, "aicompiler-test_b200"))
+        import tmc_cuda
+        from oracle.decoder_ref import weight_names
+
+        g = np.load(os.path.join(HERE, "golden", npz))
+        meta = json.loads(str(g["meta"]))
+        rt = tmc_cuda.Runtime(rank)
+        dec = tmc_cuda.Decoder(rt, meta["hidden_size"], meta["heads"], meta["intermediate_size"],
+                               meta["vocabulary_size"], meta["layers"], meta["capacity"],
+                               epsilon=meta["epsilon"], page_size=page_size, max_rows=8,
+                               tp_rank=rank, tp_size=world)
+        dec.attach_nccl(uid, world, rank)
+        for n in weight_names(meta["layers"]):
+            dec.load_weight(n, g[n])
+        dec.load_weight("rope.cosine", g["rope.cosine"])
+        dec.load_weight("rope.sine", g["rope.sine"])
+        out = {"rank": rank, "local_vocab": dec.local_vocab, "local_kv_heads": dec.local_kv_heads}
+        logits, nxt = dec.prefill(g["prefill.tokens"][0])
+        out["prefill.logits"] = logits
+        out["prefill.next"] = int(nxt)
+        for step in range(meta["decode_count"]):
+            lg, n = dec.decode(g[f"decode{step}.tokens"][0])
+            out[f"decode{step}.logits"] = lg[0]
+            out[f"decode{step}.next"] = int(n[0])
+        out["kv"] = [dec.read_kv(layer) for layer in range(meta["layers"])]
+        toks, _ = dec.generate([out[f"decode{meta['decode_count'] - 1}.next"]], generate_steps)
+        out["generate"] = toks[:, 0].tolist()
+        dec.close()  # step graphs (which hold NCCL calls) go before the communicator
+        rt.close()
+        queue.put(out)
+    except Exception:
+        queue.put({"rank": rank, "error": traceback.format_exc()})
