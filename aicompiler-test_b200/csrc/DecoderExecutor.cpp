@@ -79,6 +79,22 @@ DecoderExecutor::~DecoderExecutor() {
   }
   slots_.clear();
   if (pinnedIO_) cudaFreeHost(pinnedIO_);
+  if (!peerMappings_.empty()) {
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(rt_.device());
+    cudaStreamSynchronize(rt_.stream());
+    for (void *ptr : peerMappings_) cudaIpcCloseMemHandle(ptr);
+    cudaSetDevice(prev);
+  }
+}
+
+void DecoderExecutor::dropGraphs() {
+  for (auto &kv : graphs_) {
+    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
+  }
+  graphs_.clear();
 }
 
 std::unique_ptr<DecoderExecutor> DecoderExecutor::create(cuda::CudaRuntime &runtime,
@@ -160,6 +176,14 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)R * H, F16, &h_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)R * H, F16, &hB_, &activationBytes_)).empty()) return e;  // second residual buffer (TP)
   if (cfg_.tpSize > 1 && !(e = make((size_t)R * H, F32, &partialF32_, &activationBytes_)).empty()) return e;
+  if (cfg_.tpSize > 1) {
+    // Exchange window (zeroed int32 words), CTA-done counters per partial-sum
+    // phase (one 128-byte line each) and the step epoch.
+    const size_t words = (tmc::peer_window_bytes(R, H) + 3) / 4;
+    if (!(e = make(words, I32, &xchgWindow_, &activationBytes_)).empty()) return e;
+    if (!(e = make((size_t)cfg_.layers * 2 * 32, I32, &xchgDone_, &activationBytes_)).empty()) return e;
+    if (!(e = make(32, I32, &xchgEpoch_, &activationBytes_)).empty()) return e;
+  }
   if (!(e = make((size_t)R * hqL_ * D, F16, &q_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)R * hqL_ * D, F16, &ctx_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)R * iL_, F16, &act_, &activationBytes_)).empty()) return e;
@@ -236,12 +260,87 @@ std::string DecoderExecutor::setRope(const float *cosine, const float *sine, std
 std::string DecoderExecutor::setCollective(std::shared_ptr<Collective> collective) {
   if (cfg_.tpSize > 1 && !collective) return "tensor parallelism needs a collective.";
   collective_ = std::move(collective);
-  for (auto &kv : graphs_) {
-    if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-    if (kv.second.graph) cudaGraphDestroy(kv.second.graph);
-  }
-  graphs_.clear();
+  dropGraphs();
   return {};
+}
+
+std::string DecoderExecutor::exchangeHandle(void *out, std::size_t size) {
+  if (cfg_.tpSize <= 1 || !xchgWindow_) return "peer exchange needs tensor parallelism (tp_size > 1).";
+  if (out == nullptr || size != sizeof(cudaIpcMemHandle_t))
+    return "exchange handle: buffer must hold " + std::to_string(sizeof(cudaIpcMemHandle_t)) + " bytes.";
+  auto e = rt_.synchronize();  // the window's zero fill has landed before any peer can write
+  if (!e.empty()) return e;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(rt_.device());
+  cudaIpcMemHandle_t h;
+  const cudaError_t ce = cudaIpcGetMemHandle(&h, xchgWindow_->data());
+  cudaSetDevice(prev);
+  if (ce != cudaSuccess) return cudaText("cudaIpcGetMemHandle", ce);
+  std::memcpy(out, &h, sizeof(h));
+  return {};
+}
+
+std::string DecoderExecutor::attachPeers(const void *handles, std::size_t size, int world, int rank) {
+  if (cfg_.tpSize <= 1 || !xchgWindow_) return "peer exchange needs tensor parallelism (tp_size > 1).";
+  if (world != cfg_.tpSize || rank != cfg_.tpRank)
+    return "peer exchange: world size and rank must equal the decoder's tp_size and tp_rank.";
+  if (world > tmc::kMaxPeers) return "peer exchange: at most 8 ranks.";
+  if (handles == nullptr || size != sizeof(cudaIpcMemHandle_t))
+    return "peer exchange: handles must be " + std::to_string(sizeof(cudaIpcMemHandle_t)) + " bytes each.";
+  if (peersAttached_) return "peer exchange already attached.";
+  auto e = rt_.synchronize();
+  if (!e.empty()) return e;
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(rt_.device());
+  const auto *bytes = static_cast<const unsigned char *>(handles);
+  std::string err;
+  for (int r = 0; r < world && err.empty(); ++r) {
+    if (r == rank) {
+      peerWindows_[r] = static_cast<char *>(xchgWindow_->data());
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, bytes + (size_t)r * size, sizeof(h));
+    void *ptr = nullptr;
+    const cudaError_t ce = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (ce != cudaSuccess) {
+      cudaGetLastError();
+      err = "cudaIpcOpenMemHandle (rank " + std::to_string(r) + "): " + cudaGetErrorString(ce);
+      break;
+    }
+    peerMappings_.push_back(ptr);
+    peerWindows_[r] = static_cast<char *>(ptr);
+  }
+  if (!err.empty()) {
+    for (void *ptr : peerMappings_) cudaIpcCloseMemHandle(ptr);
+    peerMappings_.clear();
+    for (auto &w : peerWindows_) w = nullptr;
+  }
+  cudaSetDevice(prev);
+  if (!err.empty()) return err;
+  peersAttached_ = true;
+  dropGraphs();
+  return {};
+}
+
+tmc::PeerExchange DecoderExecutor::exchange(int phase) const {
+  tmc::PeerExchange x{};
+  if (!peersAttached_) return x;
+  x.world = cfg_.tpSize;
+  x.rank = cfg_.tpRank;
+  x.wait = profiling_ ? 0 : 1;
+  x.signal = 1;
+  x.slot_rows = cfg_.maxRows;
+  x.width = cfg_.hidden;
+  x.row0 = 0;
+  x.phase = static_cast<unsigned int>(phase);
+  x.phases = static_cast<unsigned int>(2 * cfg_.layers);
+  for (int r = 0; r < cfg_.tpSize; ++r) x.window[r] = peerWindows_[r];
+  x.epoch = static_cast<unsigned int *>(xchgEpoch_->data());
+  x.done = static_cast<unsigned int *>(xchgDone_->data()) + (size_t)phase * 32;
+  return x;
 }
 
 // ---- weights ----------------------------------------------------------------
@@ -531,7 +630,7 @@ std::string DecoderExecutor::restoreKV(int slot, std::size_t length,
 int DecoderExecutor::kernelsPerStep(int rows) const {
   (void)rows;
   const bool tp = cfg_.tpSize > 1;
-  return cfg_.layers * 5 + 1 + (tp ? 1 : 0);
+  return cfg_.layers * 5 + 1 + (tp && !peersAttached_ ? 1 : 0);  // + argmax finalize after the collective
 }
 
 double DecoderExecutor::stepAlgorithmicBytes(int rows, const std::vector<int> &ctx) const {
@@ -558,7 +657,9 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
   __half *hA = hp(h_), *hB = hp(hB_);
   auto *status = rt_.deviceStatus();
   const int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
-  float *partialF32 = fp(partialF32_);  // [R, H] row-parallel sums (TP only)
+  float *partialF32 = fp(partialF32_);  // [R, H] row-parallel sums (TP with a collective)
+  // TP over peer memory: partial-sum phase 2l = O of layer l, 2l + 1 = down.
+  const bool xchg = tp && peersAttached_;
   cudaError_t e;
   Layer &L = layers_[kind == kKernelLMHead ? 0 : l];
   switch (kind) {
@@ -580,6 +681,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
         p.x = hB;
         p.partial = partialF32;
         p.h_out = hA;
+        if (xchg) p.xchg = exchange(2 * (l - 1) + 1);
       } else {
         p.prologue = tmc::kProF16Norm;
         p.x = hA;
@@ -662,6 +764,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       if (tp) {
         p.epilogue = tmc::kEpiF32Partial;
         p.y_f32 = partialF32;
+        if (xchg) p.xchg = exchange(2 * l);
       } else {
         p.epilogue = tmc::kEpiResidual;
         p.y_f16 = hA;
@@ -672,7 +775,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.work_counter = workCounter(l, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("o gemv", e);
-      if (tp && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
+      if (tp && !xchg && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (o): " + collective_->lastError();
 
       return {};
@@ -689,6 +792,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
         p.x = hA;
         p.partial = partialF32;
         p.h_out = hB;
+        if (xchg) p.xchg = exchange(2 * l);
       } else {
         p.prologue = tmc::kProF16Norm;
         p.x = hA;
@@ -721,6 +825,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       if (tp) {
         p.epilogue = tmc::kEpiF32Partial;
         p.y_f32 = partialF32;
+        if (xchg) p.xchg = exchange(2 * l + 1);
       } else {
         p.epilogue = tmc::kEpiResidual;
         p.y_f16 = hA;
@@ -731,7 +836,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.work_counter = workCounter(l, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("down gemv", e);
-      if (tp && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
+      if (tp && !xchg && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (down): " + collective_->lastError();
 
       return {};
@@ -748,6 +853,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.x = hB;
       p.partial = partialF32;
       p.h_out = hA;
+      if (xchg) p.xchg = exchange(2 * (cfg_.layers - 1) + 1);  // also carries the argmax keys
     } else {
       p.prologue = tmc::kProF16Norm;
       p.x = hA;
@@ -762,7 +868,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
     p.argmax_counter = static_cast<unsigned int *>(argmaxCounter_->data());
     p.vocab_offset = cfg_.tpRank * vL_;
     p.status = status;
-    if (!tp) {
+    if (!tp || xchg) {
       p.next_tokens = static_cast<int *>(nextTokens_->data());
       if (feed) {
         p.feed_tokens = tokens;
@@ -775,7 +881,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
     p.work_counter = workCounter(0, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
       if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("lm head gemv", e);
-    if (tp) {
+    if (tp && !xchg) {
       if ((e = collective_->allReduceMaxU64(p.argmax_keys, R, s)) != cudaSuccess)
         return "allreduce (argmax): " + collective_->lastError();
       if ((e = tmc::launch_argmax_finalize(p.argmax_keys, R, static_cast<int *>(nextTokens_->data()),
@@ -795,7 +901,8 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
 
 std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct) {
   const bool tp = cfg_.tpSize > 1;
-  if (tp && !collective_) return "tensor parallelism needs a collective (setCollective).";
+  if (tp && !collective_ && !peersAttached_)
+    return "tensor parallelism needs a collective (setCollective) or attached peers (attachPeers).";
   for (int l = 0; l < cfg_.layers; ++l)
     for (int kind = kKernelQKV; kind <= kKernelDown; ++kind) {
       auto e = enqueueKernel(kind, l, R, feed, distinct);
@@ -891,8 +998,10 @@ std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *
   if (!sync.empty()) return sync;
   TMC_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
   std::string err;
+  profiling_ = true;  // partial-sum consumers read whatever the slots hold
   for (int r = 0; r < rounds && err.empty(); ++r)
     for (int l = 0; l < perRound && err.empty(); ++l) err = enqueueKernel(kind, l, R, false, true);
+  profiling_ = false;
   cudaGraph_t graph = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(s, &graph);
   if (!err.empty() || ce != cudaSuccess) {

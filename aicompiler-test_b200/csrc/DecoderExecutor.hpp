@@ -36,6 +36,7 @@
 #include "CudaRuntime.hpp"
 #include "KVCacheState.hpp"
 #include "common.cuh"
+#include "gemv.cuh"
 
 namespace tensor::runtime {
 
@@ -110,6 +111,15 @@ class DecoderExecutor {
   // RoPE tables [capacity, headDim/2] (the manifest's rope.cosine/rope.sine).
   std::string setRope(const float *cosine, const float *sine, std::size_t rows);
   std::string setCollective(std::shared_ptr<Collective> collective);
+  // ---- tensor parallelism over peer memory (no reference counterpart: the
+  // reference has no multi-GPU code) ----
+  // CUDA IPC handle (cudaIpcMemHandle_t bytes) of this rank's exchange window.
+  std::string exchangeHandle(void *out, std::size_t size);
+  // Map every rank's window (rank r's exchangeHandle at handles + r * size)
+  // and switch the row-parallel reductions and the LM-head argmax from the
+  // collective to the one-shot peer exchange fused into the GEMV kernels.
+  std::string attachPeers(const void *handles, std::size_t size, int world, int rank);
+  bool peersAttached() const { return peersAttached_; }
 
   // ---- execution (CompiledDecoderLLM API) ----
   // Prefill `count` tokens of one sequence in chunks of maxRows rows.
@@ -212,6 +222,15 @@ class DecoderExecutor {
   int historyCapacity_ = 0;
   std::vector<int> lastPositions_;  // positions of the last staged step (profiling)
   cuda::BufferHandle traceRecords_, traceCount_;
+  // Peer exchange (TP): this rank's window, per-phase CTA-done counters, the
+  // step epoch; every rank's window as mapped here.
+  cuda::BufferHandle xchgWindow_, xchgDone_, xchgEpoch_;
+  char *peerWindows_[8] = {};
+  std::vector<void *> peerMappings_;
+  bool peersAttached_ = false;
+  bool profiling_ = false;  // isolated kernel timing: consumers do not wait for peers
+  void dropGraphs();
+  tmc::PeerExchange exchange(int phase) const;
   std::size_t traceCapacity_ = 0;
   tmc::TraceSink traceSink(int layer, int kind) const;
   bool ropeSet_ = false;

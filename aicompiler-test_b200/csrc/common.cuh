@@ -43,6 +43,7 @@ enum : int {
   kWhereAppend = 5,
   kWhereMisc = 6,
   kWhereGemm = 7,
+  kWhereExchange = 8,  // a peer's flag did not arrive in time (info0 = source rank)
 };
 
 __device__ __forceinline__ void report_status(TmcDeviceStatus *s, int code, int where,
@@ -101,6 +102,32 @@ __device__ __forceinline__ void pdl_wait() {
 }
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- system-scope flags (peer memory over NVLink) ----------------------------
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int *p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned int *p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ unsigned int atomic_add_acq_rel_gpu(unsigned int *p, unsigned int v) {
+  unsigned int old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+// Wait until *flag >= value (wrap-safe), at most budget_ns of global time.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned int *flag, unsigned int value,
+                                              unsigned long long budget_ns) {
+  const unsigned long long t0 = global_ns();
+  while (static_cast<int>(ld_acquire_sys(flag) - value) < 0) {
+    if (global_ns() - t0 > budget_ns) return false;
+    __nanosleep(32);
+  }
+  return true;
 }
 
 // ---- global loads ----------------------------------------------------------

@@ -270,4 +270,19 @@ int tmc_decoder_attach_nccl(tmc_decoder *dec, const uint8_t *id, size_t nbytes, 
   return done(dec->ex->setCollective(coll));
 }
 
+static_assert(sizeof(cudaIpcMemHandle_t) == TMC_EXCHANGE_HANDLE_BYTES, "IPC handle size");
+
+int tmc_decoder_exchange_handle(tmc_decoder *dec, uint8_t *handle, size_t nbytes) {
+  if (!bind(dec) || handle == nullptr) return fail(TMC_ERR_INVALID, "bad argument");
+  if (nbytes != TMC_EXCHANGE_HANDLE_BYTES) return fail(TMC_ERR_INVALID, "handle buffer must be TMC_EXCHANGE_HANDLE_BYTES");
+  return done(dec->ex->exchangeHandle(handle, nbytes));
+}
+
+int tmc_decoder_attach_peers(tmc_decoder *dec, const uint8_t *handles, size_t nbytes_each, int world,
+                             int rank) {
+  if (!bind(dec) || handles == nullptr) return fail(TMC_ERR_INVALID, "bad argument");
+  if (nbytes_each != TMC_EXCHANGE_HANDLE_BYTES) return fail(TMC_ERR_INVALID, "handles must be TMC_EXCHANGE_HANDLE_BYTES each");
+  return done(dec->ex->attachPeers(handles, nbytes_each, world, rank));
+}
+
 }  // extern "C"

@@ -87,12 +87,39 @@ __device__ __forceinline__ float dot8(const uint4 w, const float (&x)[8], float 
   return acc;
 }
 
+// ---- peer exchange addressing (layout in gemv.cuh) ----------------------------
+constexpr unsigned long long kPeerWaitNs = 10ull * 1000 * 1000 * 1000;  // 10 s of global time
+
+__device__ __forceinline__ unsigned int *peer_flag(const PeerExchange &x, int owner, int set, int src) {
+  return reinterpret_cast<unsigned int *>(x.window[owner]) + ((size_t)set * kMaxPeers + src) * kPeerFlagStride;
+}
+__device__ __forceinline__ unsigned long long *peer_key(const PeerExchange &x, int owner, int parity,
+                                                        int src, int m) {
+  return reinterpret_cast<unsigned long long *>(x.window[owner] + peer_key_offset()) +
+         ((size_t)parity * kMaxPeers + src) * x.slot_rows + m;
+}
+__device__ __forceinline__ float *peer_slot(const PeerExchange &x, int owner, int parity, int src, int m) {
+  return reinterpret_cast<float *>(x.window[owner] + peer_slot_offset(x.slot_rows)) +
+         (((size_t)parity * kMaxPeers + src) * x.slot_rows + m) * x.width;
+}
+
 // Stage the M activation rows (after the fused prologue) into shared memory.
 // K is a multiple of 8 (checked on the host).
 template <typename XS, int M>
 __device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
   const int K = p.K;
   const int nvec = K >> 3;
+  const bool exchanged = p.prologue == kProResidualNorm && p.xchg.world > 0;
+  if (exchanged) {
+    // The reduced projection is the sum of every rank's slot: wait for each
+    // rank's flag on this phase (one thread per source rank).
+    if (p.xchg.wait && threadIdx.x < p.xchg.world) {
+      const unsigned int value = *p.xchg.epoch * p.xchg.phases + p.xchg.phase + 1u;
+      if (!wait_flag_geq(peer_flag(p.xchg, p.xchg.rank, p.xchg.phase & 1, threadIdx.x), value, kPeerWaitNs))
+        report_status(p.status, kStatusWaitTimeout, kWhereExchange, threadIdx.x, (int)p.xchg.phase);
+    }
+    __syncthreads();
+  }
   for (int m = 0; m < M; ++m) {
     XS *dst = xs + (size_t)m * K;
     if (m >= p.M) {
@@ -139,15 +166,29 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
         // x = half(h + half(partial)): the residual add after a cross-rank
         // reduction, fused into the consumer's prologue. Staged into dst first.
         const __half *hrow = static_cast<const __half *>(p.x) + (size_t)m * p.x_stride;
-        const float *prow = p.partial + (size_t)m * K;
+        const float *prow = exchanged ? nullptr : p.partial + (size_t)m * K;
         const bool write_back = blockIdx.x == 0 && p.h_out != nullptr;
         float ss = 0.0f;
         for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-          float hv[8], f[8];
+          float hv[8], f[8], pv[8];
           XLoad<__half>::get(hrow, v, hv);
-          const float4 a = reinterpret_cast<const float4 *>(prow)[2 * v];
-          const float4 b = reinterpret_cast<const float4 *>(prow)[2 * v + 1];
-          const float pv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+          if (exchanged) {
+            // Rank-ordered sum of the slots (L2 loads: peers wrote them).
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pv[j] = 0.0f;
+            for (int src = 0; src < p.xchg.world; ++src) {
+              const float4 *sp = reinterpret_cast<const float4 *>(
+                  peer_slot(p.xchg, p.xchg.rank, p.xchg.phase & 1, src, p.xchg.row0 + m));
+              const float4 a = __ldcg(sp + 2 * v), b = __ldcg(sp + 2 * v + 1);
+              pv[0] += a.x; pv[1] += a.y; pv[2] += a.z; pv[3] += a.w;
+              pv[4] += b.x; pv[5] += b.y; pv[6] += b.z; pv[7] += b.w;
+            }
+          } else {
+            const float4 a = reinterpret_cast<const float4 *>(prow)[2 * v];
+            const float4 b = reinterpret_cast<const float4 *>(prow)[2 * v + 1];
+            pv[0] = a.x; pv[1] = a.y; pv[2] = a.z; pv[3] = a.w;
+            pv[4] = b.x; pv[5] = b.y; pv[6] = b.z; pv[7] = b.w;
+          }
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             f[j] = round_half(__fadd_rn(hv[j], round_half(pv[j])));
@@ -319,7 +360,11 @@ __device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&
       if (m >= p.M) continue;
       const size_t idx = (size_t)m * p.y_stride + row;
       const float v = acc[r][m];
-      if (epi == kEpiF32 || epi == kEpiF32Partial) {
+      if (epi == kEpiF32Partial && p.xchg.world > 0) {
+        // Straight into this rank's slot of every rank's window (NVLink stores).
+        for (int q = 0; q < p.xchg.world; ++q)
+          peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0 + m)[row] = v;
+      } else if (epi == kEpiF32 || epi == kEpiF32Partial) {
         p.y_f32[idx] = v;
       } else if (epi == kEpiF16) {
         p.y_f16[idx] = __float2half_rn(v);
@@ -509,6 +554,26 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       }
     }
   }
+  if (p.epilogue == kEpiF32Partial && p.xchg.world > 0) {
+    // Causality chain, with one system-scope release per launch instead of a
+    // system fence per CTA (which costs microseconds at every CTA's exit):
+    // each thread's peer stores -> CTA barrier -> thread 0's GPU-scope
+    // acq_rel arrival on the done counter -> the last CTA's acquire of it ->
+    // its system-scope release store of this rank's flag in every window ->
+    // the consumer's system-scope acquire of the flag.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int done = atomic_add_acq_rel_gpu(p.xchg.done, 1u);
+      if (done == gridDim.x - 1) {
+        atomicExch(p.xchg.done, 0u);
+        if (p.xchg.signal) {
+          const unsigned int value = *p.xchg.epoch * p.xchg.phases + p.xchg.phase + 1u;
+          for (int q = 0; q < p.xchg.world; ++q)
+            st_release_sys(peer_flag(p.xchg, q, p.xchg.phase & 1, p.xchg.rank), value);
+        }
+      }
+    }
+  }
   if (p.epilogue != kEpiArgmax) {
     if (p.trace.records) {
       __syncthreads();  // record the CTA's last warp, not warp 0
@@ -538,7 +603,44 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       is_last = (prev == gridDim.x - 1) ? 1 : 0;
     }
     __syncthreads();
-    if (is_last) {
+    if (is_last && p.xchg.world > 0) {
+      // Vocab-parallel head: send this rank's best key per row to every rank,
+      // wait for every rank's keys, and finalise from their maximum.
+      __threadfence();
+      const PeerExchange &x = p.xchg;
+      const unsigned int step = p.history != nullptr ? *p.history_counter : 0u;
+      const unsigned int e = *x.epoch;
+      const int parity = static_cast<int>(e & 1u);
+      if (threadIdx.x < p.M) {
+        const unsigned long long key = atomicExch(p.argmax_keys + threadIdx.x, 0ull);
+        for (int q = 0; q < x.world; ++q) *peer_key(x, q, parity, x.rank, x.row0 + threadIdx.x) = key;
+      }
+      __syncthreads();  // the key stores, then thread 0's system-scope releases
+      if (threadIdx.x == 0)
+        for (int q = 0; q < x.world; ++q) st_release_sys(peer_flag(x, q, 2 + parity, x.rank), e + 1u);
+      if (threadIdx.x < x.world &&
+          !wait_flag_geq(peer_flag(x, x.rank, 2 + parity, threadIdx.x), e + 1u, kPeerWaitNs))
+        report_status(p.status, kStatusWaitTimeout, kWhereExchange, threadIdx.x, -1);
+      __syncthreads();
+      if (threadIdx.x < p.M) {
+        unsigned long long key = 0ull;
+        for (int src = 0; src < x.world; ++src) {
+          const unsigned long long k = __ldcg(peer_key(x, x.rank, parity, src, x.row0 + threadIdx.x));
+          key = k > key ? k : key;
+        }
+        const int tok = argmax_key_index(key);
+        p.next_tokens[threadIdx.x] = tok;
+        if (p.feed_tokens != nullptr) p.feed_tokens[threadIdx.x] = tok;
+        if (p.feed_positions != nullptr) p.feed_positions[threadIdx.x] += 1;
+        if (p.history != nullptr) p.history[(size_t)step * p.M + threadIdx.x] = tok;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        if (p.history != nullptr) *p.history_counter = step + 1;
+        atomicExch(p.argmax_counter, 0u);
+        *x.epoch = e + 1u;
+      }
+    } else if (is_last) {
       __threadfence();
       const unsigned int step = p.history != nullptr ? *p.history_counter : 0u;
       if (threadIdx.x < p.M) {
@@ -688,6 +790,7 @@ cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int 
   // Too many rows to stage at once: one launch per group of `cap` rows with
   // every row-indexed pointer offset (each launch streams the weights again).
   if (p.history != nullptr) return cudaErrorInvalidValue;  // greedy history indexes rows by M
+  if (p.xchg.world > 0 && p.epilogue == kEpiArgmax) return cudaErrorInvalidValue;  // one key exchange per step
   for (int m0 = 0; m0 < p.M; m0 += cap) {
     GemvParams q = p;
     q.M = p.M - m0 < cap ? p.M - m0 : cap;
@@ -706,6 +809,8 @@ cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int 
     if (p.next_tokens) q.next_tokens = p.next_tokens + m0;
     if (p.feed_tokens) q.feed_tokens = p.feed_tokens + m0;
     if (p.feed_positions) q.feed_positions = p.feed_positions + m0;
+    q.xchg.row0 = p.xchg.row0 + m0;
+    q.xchg.signal = p.xchg.signal && m0 + cap >= p.M;  // flags once every row is stored
     cudaError_t e = launch_rows(q, stream, pdl, num_sms);
     if (e != cudaSuccess) return e;
   }

@@ -21,7 +21,8 @@ enum GemvPrologue : int {
   kProF16 = 2,        // xs = x (fp16 input)
   kProF16Norm = 3,    // xs = half(x * inv * gamma)   (decoder RMSNorm, fp16 storage)
   kProEmbedNorm = 4,  // x = embedding[token[m]]; CTA 0 stores x to h_out; then kProF16Norm
-  kProResidualNorm = 5,  // x = half(h[m] + half(partial[m])) (reduced row-parallel output);
+  kProResidualNorm = 5,  // x = half(h[m] + half(partial[m])) (reduced row-parallel output,
+                         // or the rank-ordered sum of the peer-exchange slots);
                          // CTA 0 stores x to h_out; then kProF16Norm
 };
 
@@ -32,7 +33,50 @@ enum GemvEpilogue : int {
   kEpiQKV = 3,       // rows = [q | k | v]; RoPE on q,k; q -> y_f16; k,v -> paged cache
   kEpiSwiGLU = 4,    // rows interleaved (gate_i, up_i) -> y_f16[m, i] = half(half(silu(g)) * u)
   kEpiArgmax = 5,    // LM head: logits (fp16-rounded) -> y_f32 (optional) + argmax token
-  kEpiF32Partial = 6 // y_f32[m, n] = acc (row-parallel partial sum, reduced across ranks)
+  kEpiF32Partial = 6 // y_f32[m, n] = acc (row-parallel partial sum, reduced across ranks),
+                     // or stored into every rank's exchange slot (xchg.world > 0)
+};
+
+// ---- one-shot peer exchange over NVLink (tensor parallelism) ------------------
+// Each rank owns an exchange window in its HBM that every other rank maps
+// (CUDA IPC). A row-parallel GEMV (O, down) stores its fp32 partial outputs
+// straight into slot [parity][own rank] of EVERY rank's window as it produces
+// them, and its last CTA then raises flag [parity][own rank] in every window;
+// the next kernel's prologue waits (bounded) for all ranks' flags in its own
+// window and sums the slots in rank order -- the same values in the same order
+// on every rank, so the replicated residual stream stays bit-identical. The
+// LM head exchanges its packed argmax keys the same way and its last CTA
+// finalises the token. Flag values grow monotonically (epoch * phases + phase
+// + 1 for partial sums, epoch + 1 for argmax keys), so a wait is "flag >=
+// value"; a slot parity is reused only after every rank has consumed it (a
+// rank writes phase q + 2 only after it waited for every rank's phase q + 1,
+// which each rank produces only after consuming phase q).
+constexpr int kMaxPeers = 8;
+constexpr int kPeerFlagStride = 32;  // uints: one 128-byte line per (set, source rank)
+constexpr int kPeerFlagSets = 4;     // partial-sum parity 0/1, argmax parity 0/1
+constexpr size_t kPeerFlagBytes = (size_t)kPeerFlagSets * kMaxPeers * kPeerFlagStride * 4;
+
+__host__ __device__ inline size_t peer_key_offset() { return kPeerFlagBytes; }
+__host__ __device__ inline size_t peer_slot_offset(int slot_rows) {
+  return kPeerFlagBytes + ((size_t)2 * kMaxPeers * slot_rows * 8 + 255) / 256 * 256;
+}
+__host__ __device__ inline size_t peer_window_bytes(int slot_rows, int width) {
+  return peer_slot_offset(slot_rows) + (size_t)2 * kMaxPeers * slot_rows * width * 4;
+}
+
+struct PeerExchange {
+  int world;             // ranks exchanging; 0 = this launch exchanges nothing
+  int rank;
+  int wait;              // consumers wait for the flags (0 only for isolated timing runs)
+  int signal;            // producers raise the flags (0 on all but the last row-split launch)
+  int slot_rows;         // rows per slot (the decoder's max rows)
+  int width;             // features per slot row (hidden size)
+  int row0;              // first slot row of this launch (row-split launches)
+  unsigned int phase;    // partial-sum phase produced or consumed by this launch
+  unsigned int phases;   // partial-sum phases per step
+  char *window[kMaxPeers];  // every rank's window, mapped into this process
+  unsigned int *epoch;   // steps completed on this rank (the LM head's last CTA advances it)
+  unsigned int *done;    // CTA-completion counter of this launch site (zero between launches)
 };
 
 struct GemvParams {
@@ -89,6 +133,9 @@ struct GemvParams {
   // Bytes of W this launch may bulk-prefetch into L2 before its inputs are
   // ready (0: none).
   long long l2_prefetch_bytes;
+  // Tensor parallelism over peer memory (kEpiF32Partial producers,
+  // kProResidualNorm consumers, kEpiArgmax key exchange); world 0: off.
+  PeerExchange xchg;
 };
 
 constexpr int kGemvPools = 8;

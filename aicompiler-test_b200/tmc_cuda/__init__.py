@@ -294,6 +294,9 @@ _sig("tmc_decoder_set_trace", c_int, c_void_p, c_size_t)
 _sig("tmc_decoder_read_trace", c_int, c_void_p, POINTER(ctypes.c_uint64), c_size_t, POINTER(c_size_t))
 _sig("tmc_nccl_unique_id", c_int, ctypes.c_char_p, c_size_t)
 _sig("tmc_decoder_attach_nccl", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_int, c_int)
+_sig("tmc_decoder_exchange_handle", c_int, c_void_p, ctypes.c_char_p, c_size_t)
+_sig("tmc_decoder_attach_peers", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_int, c_int)
+EXCHANGE_HANDLE_BYTES = 64
 
 
 def _i32(a):
@@ -471,6 +474,18 @@ class Decoder:
 
     def attach_nccl(self, unique_id: bytes, world: int, rank: int):
         check(lib.tmc_decoder_attach_nccl(self.handle, unique_id, len(unique_id), world, rank))
+
+    def exchange_handle(self) -> bytes:
+        """CUDA IPC handle of this rank's peer-exchange window."""
+        buf = ctypes.create_string_buffer(EXCHANGE_HANDLE_BYTES)
+        check(lib.tmc_decoder_exchange_handle(self.handle, buf, EXCHANGE_HANDLE_BYTES))
+        return buf.raw
+
+    def attach_peers(self, handles, rank: int):
+        """Map every rank's window (handles in rank order) and switch the
+        tensor-parallel reductions to the fused peer exchange."""
+        blob = b"".join(handles)
+        check(lib.tmc_decoder_attach_peers(self.handle, blob, EXCHANGE_HANDLE_BYTES, len(handles), rank))
 
 
 def nccl_unique_id() -> bytes:

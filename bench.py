@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=CFG["layers"])
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timing")
+    ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
+                    help="TP reductions: peer exchange fused into the kernels, or NCCL allreduce")
     return ap.parse_args()
 
 
@@ -181,7 +183,11 @@ def run_ours(args, world, rank, local):
                            capacity, kv_heads=CFG["kv_heads"], epsilon=CFG["epsilon"],
                            rope_theta=CFG["rope_theta"], max_rows=8, max_slots=1, page_size=16,
                            tp_rank=rank, tp_size=world)
-    if world > 1:
+    if world > 1 and args.collective == "p2p":
+        handles = [None] * world
+        dist.all_gather_object(handles, dec.exchange_handle())
+        dec.attach_peers(handles, rank)
+    elif world > 1:
         uid = [tmc_cuda.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         dec.attach_nccl(uid[0], world, rank)
@@ -260,6 +266,7 @@ def run_ours(args, world, rank, local):
                        "kv_heads": CFG["kv_heads"], "intermediate": CFG["intermediate"],
                        "vocab": CFG["vocab"], "batch": 1, "prompt": args.prompt,
                        "parallelism": f"tp{world}",
+                       "tp_reduction": (args.collective if world > 1 else None),
                        "l2": "inputs larger than L2: 15 GB of weights streamed per step"},
             # Whole-job bytes: every rank streams its own shard (step_bytes is one rank's).
             "step_roofline": {"bytes_per_step": step_bytes * world,

@@ -293,6 +293,21 @@ int tmc_nccl_unique_id(uint8_t *id, size_t nbytes);
 int tmc_decoder_attach_nccl(tmc_decoder *dec, const uint8_t *id, size_t nbytes, int world,
                             int rank);
 
+/* Tensor parallelism over peer memory, fused into the kernels (no reference
+ * counterpart). Each rank exports the CUDA IPC handle of its exchange window
+ * (TMC_EXCHANGE_HANDLE_BYTES bytes), the ranks share them out of band, and
+ * every rank attaches all of them in rank order. From then on the O and down
+ * GEMVs store their fp32 partial sums straight into every rank's window over
+ * NVLink and the next kernel sums them in rank order after bounded flag waits
+ * (a timeout surfaces as TMC_ERR_DEVICE_STATUS); the LM head exchanges its
+ * packed argmax keys the same way. No collective library call remains in the
+ * step. All ranks must run the same sequence of steps; release every rank's
+ * decoder only after all ranks have synchronised. */
+#define TMC_EXCHANGE_HANDLE_BYTES 64
+int tmc_decoder_exchange_handle(tmc_decoder *dec, uint8_t *handle, size_t nbytes);
+int tmc_decoder_attach_peers(tmc_decoder *dec, const uint8_t *handles, size_t nbytes_each, int world,
+                             int rank);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,5 +1,6 @@
-"""Tensor-parallel decode (one process per GPU, NCCL allreduce after O and
-down, packed-key argmax max-allreduce for the vocab-parallel LM head) against
+"""Tensor-parallel decode (one process per GPU; the row-parallel O/down sums
+and the vocab-parallel LM-head argmax reduced either by the peer exchange fused
+into the GEMV kernels ("p2p") or by NCCL allreduce ("nccl")) against
 the reference exporter's golden outputs (export_decoder_llm.py:446-551 with the
 checks of decoder_llm_main.cpp:122-166).
 
@@ -30,13 +31,21 @@ def rms_close(got, ref, what):
     assert err <= 2e-3 * rms, f"{what}: max err {err} > {2e-3 * rms} (rms {rms})"
 
 
-def run_ranks(world, npz, page_size, generate_steps=6, timeout=240):
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_ranks(world, npz, page_size, mode, generate_steps=6, timeout=240):
     import tmc_cuda
-    uid = tmc_cuda.nccl_unique_id()
+    uid = tmc_cuda.nccl_unique_id() if mode == "nccl" else b""
+    port = _free_port()
     ctx = mp.get_context("spawn")  # never fork a process that has touched CUDA
     queue = ctx.Queue()
     procs = [ctx.Process(target=tp_worker.decode_worker,
-                         args=(r, world, uid, npz, page_size, generate_steps, queue))
+                         args=(r, world, uid, npz, page_size, generate_steps, queue, mode, port))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -56,17 +65,18 @@ def run_ranks(world, npz, page_size, generate_steps=6, timeout=240):
     return [results[r] for r in range(world)]
 
 
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
 @pytest.mark.parametrize("world,npz,page_size", [
     (2, "decoder_default_fp16.npz", 0),
     (2, "decoder_wide_fp16.npz", 4),
     (4, "decoder_wide_fp16.npz", 0),
 ])
-def test_tensor_parallel_matches_reference_exporter(world, npz, page_size):
+def test_tensor_parallel_matches_reference_exporter(world, npz, page_size, mode):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     g = np.load(os.path.join(GOLDEN, npz))
     meta = json.loads(str(g["meta"]))
-    ranks = run_ranks(world, npz, page_size)
+    ranks = run_ranks(world, npz, page_size, mode)
     assert sum(r["local_vocab"] for r in ranks) == meta["vocabulary_size"]
     logits = np.concatenate([r["prefill.logits"] for r in ranks], axis=-1)
     rms_close(logits, g["prefill.logits"][0], "prefill logits")

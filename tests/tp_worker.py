@@ -17,7 +17,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 
 
-def decode_worker(rank, world, uid, npz, page_size, generate_steps, queue):
+def decode_worker(rank, world, uid, npz, page_size, generate_steps, queue, mode="nccl", port=0):
+    """mode "nccl": reductions through the NCCL collective (uid = its unique
+    id); mode "p2p": the fused peer exchange, IPC handles shared over a gloo
+    group on 127.0.0.1:port."""
+    dist = None
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "aicompiler-test_b200"))
@@ -31,7 +35,15 @@ def decode_worker(rank, world, uid, npz, page_size, generate_steps, queue):
                                meta["vocabulary_size"], meta["layers"], meta["capacity"],
                                epsilon=meta["epsilon"], page_size=page_size, max_rows=8,
                                tp_rank=rank, tp_size=world)
-        dec.attach_nccl(uid, world, rank)
+        if mode == "p2p":
+            import torch.distributed as dist
+            dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                    world_size=world)
+            handles = [None] * world
+            dist.all_gather_object(handles, dec.exchange_handle())
+            dec.attach_peers(handles, rank)
+        else:
+            dec.attach_nccl(uid, world, rank)
         for n in weight_names(meta["layers"]):
             dec.load_weight(n, g[n])
         dec.load_weight("rope.cosine", g["rope.cosine"])
@@ -47,8 +59,14 @@ def decode_worker(rank, world, uid, npz, page_size, generate_steps, queue):
         out["kv"] = [dec.read_kv(layer) for layer in range(meta["layers"])]
         toks, _ = dec.generate([out[f"decode{meta['decode_count'] - 1}.next"]], generate_steps)
         out["generate"] = toks[:, 0].tolist()
+        rt.synchronize()
+        if dist is not None:
+            dist.barrier()  # no rank unmaps its window while a peer may still write into it
         dec.close()  # step graphs (which hold NCCL calls) go before the communicator
         rt.close()
         queue.put(out)
     except Exception:
         queue.put({"rank": rank, "error": traceback.format_exc()})
+    finally:
+        if dist is not None and dist.is_initialized():
+            dist.destroy_process_group()
