@@ -561,16 +561,21 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
     // acq_rel arrival on the done counter -> the last CTA's acquire of it ->
     // its system-scope release store of this rank's flag in every window ->
     // the consumer's system-scope acquire of the flag.
+    // The releases to the ranks go out in parallel, one lane each (a release
+    // store waits for a system-scope round trip; serial ones add up).
     __syncthreads();
-    if (threadIdx.x == 0) {
-      const unsigned int done = atomic_add_acq_rel_gpu(p.xchg.done, 1u);
-      if (done == gridDim.x - 1) {
-        atomicExch(p.xchg.done, 0u);
-        if (p.xchg.signal) {
-          const unsigned int value = *p.xchg.epoch * p.xchg.phases + p.xchg.phase + 1u;
-          for (int q = 0; q < p.xchg.world; ++q)
-            st_release_sys(peer_flag(p.xchg, q, p.xchg.phase & 1, p.xchg.rank), value);
-        }
+    if (threadIdx.x < 32) {
+      int last = 0;
+      if (threadIdx.x == 0) {
+        const unsigned int done = atomic_add_acq_rel_gpu(p.xchg.done, 1u);
+        last = done == gridDim.x - 1;
+        if (last) atomicExch(p.xchg.done, 0u);
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      __syncwarp();  // orders lane 0's acquire before the other lanes' releases
+      if (last && p.xchg.signal && (int)threadIdx.x < p.xchg.world) {
+        const unsigned int value = *p.xchg.epoch * p.xchg.phases + p.xchg.phase + 1u;
+        st_release_sys(peer_flag(p.xchg, threadIdx.x, p.xchg.phase & 1, p.xchg.rank), value);
       }
     }
   }
@@ -615,9 +620,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
         const unsigned long long key = atomicExch(p.argmax_keys + threadIdx.x, 0ull);
         for (int q = 0; q < x.world; ++q) *peer_key(x, q, parity, x.rank, x.row0 + threadIdx.x) = key;
       }
-      __syncthreads();  // the key stores, then thread 0's system-scope releases
-      if (threadIdx.x == 0)
-        for (int q = 0; q < x.world; ++q) st_release_sys(peer_flag(x, q, 2 + parity, x.rank), e + 1u);
+      __syncthreads();  // the key stores, then one system-scope release per rank (parallel lanes)
+      if ((int)threadIdx.x < x.world) st_release_sys(peer_flag(x, threadIdx.x, 2 + parity, x.rank), e + 1u);
       if (threadIdx.x < x.world &&
           !wait_flag_geq(peer_flag(x, x.rank, 2 + parity, threadIdx.x), e + 1u, kPeerWaitNs))
         report_status(p.status, kStatusWaitTimeout, kWhereExchange, threadIdx.x, -1);
