@@ -8,6 +8,7 @@
 #include "CudaRuntime.hpp"
 #include "api_util.hpp"
 #include "attention.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
 #include "tmc_cuda.h"
@@ -235,6 +236,55 @@ int tmc_k_gemv_f16(const void *x_f16, const void *w_f16, void *y_f16, int rows, 
 int tmc_k_gemv_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k, int n,
                           void *stream) {
   return gemv_f16_common(x_f16, w_f16, nullptr, y, rows, k, n, stream);
+}
+
+namespace {
+int sm_count() {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+}  // namespace
+
+size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows) {
+  if (n <= 0 || k <= 0 || rows <= 0 || rows > 128) return 0;
+  const tmc::GemmPlan plan = tmc::plan_gemm(n, k, rows, sm_count());
+  const size_t partial = (tmc::gemm_workspace_floats(plan) * 4 + 255) / 256 * 256;
+  return partial + (size_t)plan.tiles * 4;
+}
+
+int tmc_k_batched_gemm_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k, int n,
+                                  void *workspace, void *status, void *stream) {
+  if (!x_f16 || !w_f16 || !y || !workspace) return fail(TMC_ERR_INVALID, "null pointer");
+  if (rows <= 0 || rows > 128 || n <= 0 || k <= 0 || k % 64 != 0)
+    return fail(TMC_ERR_UNSUPPORTED, "batched gemm: rows in [1, 128], k % 64 == 0");
+  const tmc::GemmPlan plan = tmc::plan_gemm(n, k, rows, sm_count());
+  const size_t partial = (tmc::gemm_workspace_floats(plan) * 4 + 255) / 256 * 256;
+  auto *ws = static_cast<unsigned char *>(workspace);
+  auto *tickets = reinterpret_cast<unsigned int *>(ws + partial);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(tickets, 0, (size_t)plan.tiles * 4, s);
+  if (e != cudaSuccess) return cuda_fail(e, "clearing gemm tickets");
+  CUtensorMap wm, xm;
+  if ((e = tmc::make_tensor_map_f16(&wm, w_f16, n, k, tmc::kGemmTileRows)) != cudaSuccess)
+    return cuda_fail(e, "weight tensor map");
+  if ((e = tmc::make_tensor_map_f16(&xm, x_f16, rows, k, plan.tn)) != cudaSuccess)
+    return cuda_fail(e, "activation tensor map");
+  tmc::GemvParams p{};
+  p.W = static_cast<const __half *>(w_f16);
+  p.N = n;
+  p.K = k;
+  p.M = rows;
+  p.prologue = tmc::kProF16;
+  p.x = x_f16;
+  p.x_stride = k;
+  p.epilogue = tmc::kEpiF32;
+  p.y_f32 = y;
+  p.y_stride = n;
+  p.status = static_cast<tmc::TmcDeviceStatus *>(status);
+  e = tmc::launch_gemm(p, wm, xm, plan, reinterpret_cast<float *>(ws), tickets, s, false);
+  if (e == cudaErrorInvalidValue) return fail(TMC_ERR_UNSUPPORTED, "batched gemm: unsupported shape");
+  return e == cudaSuccess ? ok() : cuda_fail(e, "batched gemm launch");
 }
 
 size_t tmc_k_attention_workspace_bytes(int rows, int hq, int hkv, int d, int max_splits) {

@@ -1,0 +1,496 @@
+// Batched decode projections on tcgen05 tensor cores (see gemm.cuh).
+//
+// One persistent CTA per SM, 6 warps, warp-specialised:
+//   warp 0    TMA producer: streams 128-row x 64-column weight tiles (A) and
+//             the matching 64-column slice of the token rows (B) into a ring
+//             of shared-memory stages (128-byte swizzle). Weight tiles do not
+//             depend on earlier kernels, so the first ring-full is requested
+//             before the programmatic-dependency wait;
+//   warp 1    owns the tensor memory (two TN-column fp32 accumulators) and
+//             issues the MMAs from one thread: 4 x (M=128, N=TN, K=16) per
+//             stage, tcgen05.commit frees the stage, a final commit hands the
+//             accumulator to the epilogue;
+//   warps 2-5 epilogue: tcgen05.ld of their 32-lane quarter of the
+//             accumulator (one output feature per thread, TN tokens), then the
+//             GEMV's per-element epilogues. With two accumulators the
+//             epilogue of one tile overlaps the MMAs of the next.
+// Work units are (tile, K split) pairs, assigned round-robin to the CTAs.
+// With several K splits each unit writes its fp32 partial to a workspace and
+// the tile's last unit (atomic ticket) sums the partials in split order, so
+// results do not depend on timing.
+// Every mbarrier wait is bounded (mbarrier.cuh); a timeout is reported in the
+// device status block and the CTA still releases its tensor memory and exits.
+#include "gemm.cuh"
+
+#include <mutex>
+#include <unordered_map>
+
+#include "epilogue.cuh"
+#include "mbarrier.cuh"
+
+namespace tmc {
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kTileBytesA = kGemmTileRows * kGemmKBlock * 2;  // 16 KB
+
+template <int TN>
+struct GemmCfg {
+  static constexpr int kBytesB = TN * kGemmKBlock * 2;
+  static constexpr int kStageBytes = kTileBytesA + kBytesB;
+  static constexpr int kStages = (200 * 1024 / kStageBytes) < 8 ? (200 * 1024 / kStageBytes) : 8;
+  static constexpr int kTmemCols = 2 * TN < 32 ? 32 : 2 * TN;  // a power of two for TN in {16..128}
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256;
+};
+
+struct GemmWork {
+  int tiles, splits, kblocks;
+  float *ws;
+  unsigned int *tile_counters;
+};
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major tile with 128-byte rows and
+// 128-byte swizzle (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B):
+// start address, leading offset 1 (unused when K fits one swizzle row),
+// stride 1024 bytes between 8-row groups, descriptor version 1, layout 2.
+__device__ __forceinline__ uint64_t sw128_desc(const void *smem) {
+  uint64_t d = (uint64_t)((smem_u32(smem) >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 16 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Named barrier of the four epilogue warps.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int TN>
+__device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float (&v)[TN], int row, int lane,
+                                               int ew, int t, unsigned long long (*red_keys)[TN]) {
+  const int epi = p.epilogue;
+  if (epi == kEpiArgmax) {
+#pragma unroll
+    for (int m = 0; m < TN; ++m) {
+      if (m >= p.M) break;
+      unsigned long long key = 0ull;
+      if (row < p.N) {
+        const float h = round_half(v[m]);
+        if (p.y_f32 != nullptr) p.y_f32[(size_t)m * p.y_stride + row] = h;
+        key = argmax_key(h, p.vocab_offset + row);
+      }
+      key = warp_max_u64(key);
+      if (lane == 0) red_keys[ew][m] = key;
+    }
+    epi_sync();
+    if (t < p.M) {
+      unsigned long long k = red_keys[0][t];
+#pragma unroll
+      for (int e = 1; e < 4; ++e) k = red_keys[e][t] > k ? red_keys[e][t] : k;
+      if (k != 0ull) atomicMax(p.argmax_keys + t, k);
+    }
+    epi_sync();
+    return;
+  }
+  if (epi == kEpiQKV || epi == kEpiSwiGLU) {
+#pragma unroll
+    for (int m = 0; m < TN; ++m) {
+      if (m >= p.M) break;
+      const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
+      if (!(lane & 1) && row < p.N) epilogue_pair(p, row, m, v[m], partner);
+    }
+    return;
+  }
+#pragma unroll
+  for (int m = 0; m < TN; ++m) {
+    if (m >= p.M) break;
+    if (row < p.N) epilogue_one(p, row, m, v[m]);
+  }
+}
+
+template <int TN>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
+                const GemvParams p, const GemmWork w) {
+  using C = GemmCfg<TN>;
+  constexpr int S = C::kStages;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *base = reinterpret_cast<unsigned char *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *sA = base;
+  unsigned char *sB = base + (size_t)S * kTileBytesA;
+  uint64_t *full = reinterpret_cast<uint64_t *>(sB + (size_t)S * C::kBytesB);
+  uint64_t *empty = full + S;
+  uint64_t *acc_full = empty + S;
+  uint64_t *acc_empty = acc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  __shared__ unsigned long long red_keys[4][TN];
+  __shared__ int s_last, s_fail;
+  __shared__ unsigned long long s_ready;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = w.tiles * w.splits;
+  const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    fence_barrier_init();
+    s_fail = 0;
+    s_ready = t_entry;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      int pending_kb[S];
+      int it = 0;
+      bool waited = false, ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int tile = u / w.splits, ks = u % w.splits;
+        const int kb0 = (int)((long long)w.kblocks * ks / w.splits);
+        const int kb1 = (int)((long long)w.kblocks * (ks + 1) / w.splits);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = it % S, round = it / S;
+          if (it == S && !waited) {
+            // The ring is full of weight tiles: wait for the producer of x,
+            // then request the token slices of those stages.
+            pdl_wait();
+            if (p.trace.records) s_ready = global_ns();
+            for (int j = 0; j < S; ++j)
+              tma_load_2d(sB + (size_t)j * C::kBytesB, &x_map, pending_kb[j] * kGemmKBlock, 0, &full[j]);
+            waited = true;
+          }
+          if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[st], C::kStageBytes);
+          tma_load_2d(sA + (size_t)st * kTileBytesA, &w_map, kb * kGemmKBlock, tile * kGemmTileRows, &full[st]);
+          if (waited) {
+            tma_load_2d(sB + (size_t)st * C::kBytesB, &x_map, kb * kGemmKBlock, 0, &full[st]);
+          } else {
+            pending_kb[st] = kb;
+          }
+        }
+      }
+      if (!waited) {
+        pdl_wait();
+        if (p.trace.records) s_ready = global_ns();
+        const int n = it < S ? it : S;
+        for (int j = 0; j < n; ++j)
+          tma_load_2d(sB + (size_t)j * C::kBytesB, &x_map, pending_kb[j] * kGemmKBlock, 0, &full[j]);
+      }
+      pdl_launch_dependents();
+      if (!ok) report_status(p.status, kStatusWaitTimeout, kWhereGemm, 0, blockIdx.x);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer: D[128 features x TN tokens] += W_tile . x_slice^T ----
+      const uint32_t idesc = (1u << 4)                                  // D: fp32
+                             | ((uint32_t)(TN >> 3) << 17)              // N
+                             | ((uint32_t)(kGemmTileRows >> 4) << 24);  // M; A, B: fp16, K-major
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
+        const int ks = u % w.splits;
+        const int kb0 = (int)((long long)w.kblocks * ks / w.splits);
+        const int kb1 = (int)((long long)w.kblocks * (ks + 1) / w.splits);
+        const int buf = j & 1;
+        if (j >= 2 && !mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * TN);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int st = it % S;
+          if (!mbar_wait(&full[st], (it / S) & 1)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = sw128_desc(sA + (size_t)st * kTileBytesA);
+          const uint64_t db = sw128_desc(sB + (size_t)st * C::kBytesB);
+#pragma unroll
+          for (int k = 0; k < kGemmKBlock / 16; ++k)  // +32 bytes along K per step
+            umma_f16(d, da + 2u * k, db + 2u * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[st]);
+        }
+        if (ok) umma_commit(&acc_full[buf]);
+      }
+      if (!ok) report_status(p.status, kStatusWaitTimeout, kWhereGemm, 1, blockIdx.x);
+    }
+  } else {
+    // ---- epilogue warps ----
+    pdl_wait();
+    const int q = warp & 3;  // the TMEM lane quarter this warp may read
+    const int ew = warp - 2;
+    const int t = threadIdx.x - 64;
+    const int r = q * 32 + lane;
+    int j = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
+      const int tile = u / w.splits, ks = u % w.splits;
+      const int buf = j & 1;
+      if (!mbar_wait(&acc_full[buf], (j >> 1) & 1)) s_fail = 1;
+      epi_sync();
+      if (s_fail) break;
+      tc_fence_after();
+      float v[TN];
+#pragma unroll
+      for (int c = 0; c < TN / 16; ++c)
+        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TN + c * 16), v + c * 16);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      const int row = tile * kGemmTileRows + r;
+      if (w.splits > 1) {
+        float *part = w.ws + (size_t)(tile * w.splits + ks) * TN * kGemmTileRows;
+#pragma unroll
+        for (int m = 0; m < TN; ++m) {
+          if (m >= p.M) break;
+          part[(size_t)m * kGemmTileRows + r] = v[m];
+        }
+        __threadfence();
+        epi_sync();
+        if (t == 0) {
+          const unsigned int prev = atomicAdd(w.tile_counters + tile, 1u);
+          s_last = prev == (unsigned int)(w.splits - 1);
+          if (s_last) atomicExch(w.tile_counters + tile, 0u);
+        }
+        epi_sync();
+        if (!s_last) continue;
+        __threadfence();
+#pragma unroll
+        for (int m = 0; m < TN; ++m) {
+          if (m >= p.M) break;
+          float sum = 0.0f;
+          for (int k2 = 0; k2 < w.splits; ++k2)
+            sum += __ldcg(w.ws + ((size_t)(tile * w.splits + k2) * TN + m) * kGemmTileRows + r);
+          v[m] = sum;
+        }
+      }
+      apply_epilogue<TN>(p, v, row, lane, ew, t, red_keys);
+    }
+    epi_sync();
+    if (p.epilogue == kEpiF32Partial && p.xchg.world > 0 && t < 32) {
+      // Same causality chain as the GEMV: epilogue stores -> group barrier ->
+      // GPU-scope arrival -> the last CTA's per-rank system-scope releases.
+      int last = 0;
+      if (t == 0) {
+        const unsigned int done = atomic_add_acq_rel_gpu(p.xchg.done, 1u);
+        last = done == gridDim.x - 1;
+        if (last) atomicExch(p.xchg.done, 0u);
+      }
+      last = __shfl_sync(0xffffffffu, last, 0);
+      __syncwarp();
+      if (last && p.xchg.signal && t < p.xchg.world) {
+        const unsigned int value = *p.xchg.epoch * p.xchg.phases + p.xchg.phase + 1u;
+        st_release_sys(peer_flag(p.xchg, t, p.xchg.phase & 1, p.xchg.rank), value);
+      }
+    }
+    if (p.epilogue == kEpiArgmax && p.next_tokens != nullptr) {
+      __threadfence();
+      epi_sync();
+      if (t == 0) {
+        const unsigned int prev = atomicAdd(p.argmax_counter, 1u);
+        s_last = prev == gridDim.x - 1;
+      }
+      epi_sync();
+      if (s_last) {
+        __threadfence();
+        argmax_finalize(p, t, [] { epi_sync(); });
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols)
+                 : "memory");
+  }
+  trace_emit(p.trace, t_entry, s_ready);
+}
+
+template <int TN>
+cudaError_t launch_tn(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,
+                      const GemmPlan &plan, float *ws, unsigned int *tile_counters, cudaStream_t stream, bool pdl) {
+  using C = GemmCfg<TN>;
+  auto kernel = gemm_kernel<TN>;
+  static std::mutex mu;
+  static std::unordered_map<int, bool> configured;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
+      if (e != cudaSuccess) return e;
+      configured[dev] = true;
+    }
+  }
+  GemmWork w{plan.tiles, plan.splits, plan.kblocks, ws, tile_counters};
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan.grid);
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, w_map, x_map, p, w);
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+}  // namespace
+
+GemmPlan plan_gemm(int N, int K, int M, int num_sms) {
+  GemmPlan g{};
+  g.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  g.tiles = (N + kGemmTileRows - 1) / kGemmTileRows;
+  g.kblocks = K / kGemmKBlock;
+  // Cost of a plan in full-K tile times: waves of persistent CTAs times the
+  // work of one unit plus a fixed per-unit overhead (pipeline fill, epilogue).
+  const double overhead = 0.05;
+  double best = 1e30;
+  g.splits = 1;
+  for (int s = 1; s <= 16; ++s) {
+    if (s > 1 && g.kblocks / s < 4) break;
+    const long long units = (long long)g.tiles * s;
+    const long long waves = (units + num_sms - 1) / num_sms;
+    const double cost = (double)waves * (1.0 / s + overhead);
+    if (cost < best - 1e-9) {
+      best = cost;
+      g.splits = s;
+    }
+  }
+  const long long units = (long long)g.tiles * g.splits;
+  g.grid = (int)(units < num_sms ? units : num_sms);
+  return g;
+}
+
+size_t gemm_workspace_floats(const GemmPlan &plan) {
+  return plan.splits > 1 ? (size_t)plan.tiles * plan.splits * plan.tn * kGemmTileRows : 0;
+}
+
+cudaError_t make_tensor_map_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                                uint32_t box_rows) {
+  static std::mutex mu;
+  static EncodeTiledFn encode = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (encode == nullptr) {
+      void *fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+        return e != cudaSuccess ? e : cudaErrorNotSupported;
+      encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+  }
+  if (map == nullptr || base == nullptr || (reinterpret_cast<uintptr_t>(base) & 15) != 0 || cols % 8 != 0 ||
+      box_rows == 0 || box_rows > 256)
+    return cudaErrorInvalidValue;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kGemmKBlock, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box,
+                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,
+                        const GemmPlan &plan, float *ws, unsigned int *tile_counters, cudaStream_t stream,
+                        bool pdl) {
+  if (p.N <= 0 || p.K <= 0 || p.K % kGemmKBlock != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 128 ||
+      plan.tiles != (p.N + kGemmTileRows - 1) / kGemmTileRows || plan.kblocks != p.K / kGemmKBlock ||
+      plan.splits < 1 || plan.grid < 1 || tile_counters == nullptr || (plan.splits > 1 && ws == nullptr))
+    return cudaErrorInvalidValue;
+  switch (p.epilogue) {
+    case kEpiQKV:
+    case kEpiSwiGLU:
+      if (p.N & 1) return cudaErrorInvalidValue;
+      break;
+    case kEpiResidual:
+    case kEpiF16:
+    case kEpiF32:
+    case kEpiF32Partial:
+    case kEpiArgmax:
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  switch (plan.tn) {
+    case 16: return launch_tn<16>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 32: return launch_tn<32>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 64: return launch_tn<64>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 128: return launch_tn<128>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tmc

@@ -1,0 +1,53 @@
+// Batched decode projections on the 5th-generation tensor cores (tcgen05).
+//
+// Replaces emitTiledGEMM (DecodeGEMVMetalEmitter.cpp:134-169), the
+// reference's batched/prefill linear layer, for rows > 8: y = epilogue(W x^T)
+// with W [N, K] fp16 row-major (the decoder's weights, unchanged) and x
+// [M <= 128, K] fp16 rows (the GEMV prologue, written by launch_row_prologue,
+// or an fp16 activation). The weight tile is the MMA's A operand (128 output
+// features = the UMMA M dimension) and the token rows are its B operand
+// (UMMA N = 16..128), so one weight byte feeds up to 128 tokens; the fp32
+// accumulator lives in tensor memory. Epilogues are the GEMV's own
+// (epilogue.cuh), so rows computed here round and store exactly as there.
+#pragma once
+
+#include <cuda.h>
+
+#include "gemv.cuh"
+
+namespace tmc {
+
+constexpr int kGemmTileRows = 128;  // weight rows per tile (UMMA M)
+constexpr int kGemmKBlock = 64;     // K elements per pipeline stage: one 128-byte swizzle row
+
+struct GemmPlan {
+  int tn;       // token columns per MMA (16, 32, 64 or 128), >= M
+  int tiles;    // ceil(N / 128)
+  int splits;   // K splits per tile (partials reduced in order by the tile's last CTA)
+  int kblocks;  // K / 64
+  int grid;     // persistent CTAs (one per SM at most)
+};
+
+// Work split for N x K weights and M rows on `num_sms` SMs: the split count
+// that best fills whole waves of persistent CTAs.
+GemmPlan plan_gemm(int N, int K, int M, int num_sms);
+// fp32 elements of split-K partials the plan needs (0 when splits == 1).
+size_t gemm_workspace_floats(const GemmPlan &plan);
+
+// 2-D tensor map of an fp16 row-major matrix [rows, cols] with a
+// [box_rows, 64] box and 128-byte swizzle (the UMMA K-major SW128 layout).
+cudaError_t make_tensor_map_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
+                                uint32_t box_rows);
+
+// y = epilogue(W . x^T) for p.M rows. w_map: W with box_rows 128; x_map: the
+// x rows with box_rows plan.tn. p.W/p.N/p.K/p.M and the epilogue fields are
+// used as by launch_gemv; the prologue must already be applied (x is read as
+// fp16 rows). ws: gemm_workspace_floats(plan) floats; tile_counters:
+// plan.tiles zeroed words (left zeroed). Supported epilogues: kEpiQKV,
+// kEpiSwiGLU, kEpiResidual, kEpiF16, kEpiF32, kEpiF32Partial (with or
+// without peer exchange) and kEpiArgmax.
+cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,
+                        const GemmPlan &plan, float *ws, unsigned int *tile_counters,
+                        cudaStream_t stream, bool pdl);
+
+}  // namespace tmc

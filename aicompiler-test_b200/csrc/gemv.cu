@@ -14,6 +14,7 @@
 //    before griddepcontrol.wait, so weight streaming overlaps the tail of the
 //    previous kernel in the decode graph.
 #include "gemv.cuh"
+#include "epilogue.cuh"
 
 #include <mutex>
 #include <unordered_map>
@@ -87,26 +88,12 @@ __device__ __forceinline__ float dot8(const uint4 w, const float (&x)[8], float 
   return acc;
 }
 
-// ---- peer exchange addressing (layout in gemv.cuh) ----------------------------
-constexpr unsigned long long kPeerWaitNs = 10ull * 1000 * 1000 * 1000;  // 10 s of global time
-
-__device__ __forceinline__ unsigned int *peer_flag(const PeerExchange &x, int owner, int set, int src) {
-  return reinterpret_cast<unsigned int *>(x.window[owner]) + ((size_t)set * kMaxPeers + src) * kPeerFlagStride;
-}
-__device__ __forceinline__ unsigned long long *peer_key(const PeerExchange &x, int owner, int parity,
-                                                        int src, int m) {
-  return reinterpret_cast<unsigned long long *>(x.window[owner] + peer_key_offset()) +
-         ((size_t)parity * kMaxPeers + src) * x.slot_rows + m;
-}
-__device__ __forceinline__ float *peer_slot(const PeerExchange &x, int owner, int parity, int src, int m) {
-  return reinterpret_cast<float *>(x.window[owner] + peer_slot_offset(x.slot_rows)) +
-         (((size_t)parity * kMaxPeers + src) * x.slot_rows + m) * x.width;
-}
-
 // Stage the M activation rows (after the fused prologue) into shared memory.
 // K is a multiple of 8 (checked on the host).
+// `writer`: this CTA writes the residual-stream rows back to h_out (one CTA
+// of a GEMV launch; every CTA of the row-prologue kernel, one row each).
 template <typename XS, int M>
-__device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
+__device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
   const int K = p.K;
   const int nvec = K >> 3;
   const bool exchanged = p.prologue == kProResidualNorm && p.xchg.world > 0;
@@ -167,7 +154,7 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
         // reduction, fused into the consumer's prologue. Staged into dst first.
         const __half *hrow = static_cast<const __half *>(p.x) + (size_t)m * p.x_stride;
         const float *prow = exchanged ? nullptr : p.partial + (size_t)m * K;
-        const bool write_back = blockIdx.x == 0 && p.h_out != nullptr;
+        const bool write_back = writer && p.h_out != nullptr;
         float ss = 0.0f;
         for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
           float hv[8], f[8], pv[8];
@@ -227,7 +214,7 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red) {
         src = static_cast<const __half *>(p.x) + (size_t)m * p.x_stride;
       }
       const bool norm = (pro == kProF16Norm || pro == kProEmbedNorm);
-      const bool write_h = (pro == kProEmbedNorm) && blockIdx.x == 0 && p.h_out != nullptr;
+      const bool write_h = (pro == kProEmbedNorm) && writer && p.h_out != nullptr;
       // Pass 1: global -> shared (raw values; exact in XS), sum of squares.
       float ss = 0.0f;
 #pragma unroll 2
@@ -285,70 +272,11 @@ __device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&
     return;
   }
   if (lane != 0) return;
-  if (epi == kEpiSwiGLU) {
-    // rows (row0, row0+1) = (gate_i, up_i) with i = row0 / 2
+  if (epi == kEpiSwiGLU || epi == kEpiQKV) {
+    // (row0, row0 + 1): a (gate, up) pair or an interleaved RoPE pair.
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      if (m >= p.M) continue;
-      const float g = round_half(acc[0][m]);
-      const float u = round_half(acc[R - 1][m]);
-      const float a = round_half(g / (1.0f + expf(-g)));
-      p.y_f16[(size_t)m * p.y_stride + (row0 >> 1)] = __float2half_rn(__fmul_rn(a, u));
-    }
-    return;
-  }
-  if (epi == kEpiQKV) {
-    // (row0, row0+1) is an interleaved RoPE pair inside one head.
-    const int D = p.head_dim;
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      if (m >= p.M) continue;
-      float e = round_half(acc[0][m]);
-      float o = round_half(acc[R - 1][m]);
-      const int pos = p.positions[m];
-      if (pos < 0 || pos >= p.capacity) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
-        continue;
-      }
-      if (row0 < p.q_rows + p.kv_rows) {
-        const int pair = (row0 % D) >> 1;
-        const float c = p.rope_cos[(size_t)pos * (D >> 1) + pair];
-        const float s = p.rope_sin[(size_t)pos * (D >> 1) + pair];
-        const float re = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
-        const float ro = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
-        e = re;
-        o = ro;
-      }
-      if (row0 < p.q_rows) {
-        __half2 hv = __floats2half2_rn(e, o);
-        *reinterpret_cast<__half2 *>(p.y_f16 + (size_t)m * p.y_stride + row0) = hv;
-        continue;
-      }
-      int local = row0 - p.q_rows;
-      __half *pool = p.k_pool;
-      if (local >= p.kv_rows) {
-        local -= p.kv_rows;
-        pool = p.v_pool;
-      }
-      const int kvh = local / D, d = local % D;
-      const int lp = pos / p.page_size, off = pos % p.page_size;
-      if (lp >= p.table_stride) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
-        continue;
-      }
-      const int page = p.block_table[(size_t)p.table_rows[m] * p.table_stride + lp];
-      if (page < 0) {
-        report_status(p.status, kStatusPageMissing, kWhereAppend, lp, m);
-        continue;
-      }
-      if (page >= p.pool_pages) {
-        report_status(p.status, kStatusPageRange, kWhereAppend, page, m);
-        continue;
-      }
-      const int hkv = p.kv_rows / D;
-      const size_t addr = (((size_t)page * hkv + kvh) * p.page_size + off) * D + d;
-      *reinterpret_cast<__half2 *>(pool + addr) = __floats2half2_rn(e, o);
-    }
+    for (int m = 0; m < M; ++m)
+      if (m < p.M) epilogue_pair(p, row0, m, acc[0][m], acc[R - 1][m]);
     return;
   }
 #pragma unroll
@@ -356,22 +284,8 @@ __device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&
     const int row = row0 + r;
     if (row >= p.N) continue;
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      if (m >= p.M) continue;
-      const size_t idx = (size_t)m * p.y_stride + row;
-      const float v = acc[r][m];
-      if (epi == kEpiF32Partial && p.xchg.world > 0) {
-        // Straight into this rank's slot of every rank's window (NVLink stores).
-        for (int q = 0; q < p.xchg.world; ++q)
-          peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0 + m)[row] = v;
-      } else if (epi == kEpiF32 || epi == kEpiF32Partial) {
-        p.y_f32[idx] = v;
-      } else if (epi == kEpiF16) {
-        p.y_f16[idx] = __float2half_rn(v);
-      } else if (epi == kEpiResidual) {
-        p.y_f16[idx] = __float2half_rn(__fadd_rn(__half2float(p.residual[idx]), round_half(v)));
-      }
-    }
+    for (int m = 0; m < M; ++m)
+      if (m < p.M) epilogue_one(p, row, m, acc[r][m]);
   }
 }
 
@@ -459,7 +373,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   int g_next = gt + total_teams;
   int fetched = 0;
   if (dynamic && lane == 0) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
-  stage_x<XS, M>(p, xs, red);
+  stage_x<XS, M>(p, xs, red, blockIdx.x == 0);
   __syncthreads();
   pdl_launch_dependents();
   const unsigned long long t_ready = p.trace.records ? global_ns() : 0ull;
@@ -608,61 +522,39 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       is_last = (prev == gridDim.x - 1) ? 1 : 0;
     }
     __syncthreads();
-    if (is_last && p.xchg.world > 0) {
-      // Vocab-parallel head: send this rank's best key per row to every rank,
-      // wait for every rank's keys, and finalise from their maximum.
+    if (is_last) {
       __threadfence();
-      const PeerExchange &x = p.xchg;
-      const unsigned int step = p.history != nullptr ? *p.history_counter : 0u;
-      const unsigned int e = *x.epoch;
-      const int parity = static_cast<int>(e & 1u);
-      if (threadIdx.x < p.M) {
-        const unsigned long long key = atomicExch(p.argmax_keys + threadIdx.x, 0ull);
-        for (int q = 0; q < x.world; ++q) *peer_key(x, q, parity, x.rank, x.row0 + threadIdx.x) = key;
-      }
-      __syncthreads();  // the key stores, then one system-scope release per rank (parallel lanes)
-      if ((int)threadIdx.x < x.world) st_release_sys(peer_flag(x, threadIdx.x, 2 + parity, x.rank), e + 1u);
-      if (threadIdx.x < x.world &&
-          !wait_flag_geq(peer_flag(x, x.rank, 2 + parity, threadIdx.x), e + 1u, kPeerWaitNs))
-        report_status(p.status, kStatusWaitTimeout, kWhereExchange, threadIdx.x, -1);
-      __syncthreads();
-      if (threadIdx.x < p.M) {
-        unsigned long long key = 0ull;
-        for (int src = 0; src < x.world; ++src) {
-          const unsigned long long k = __ldcg(peer_key(x, x.rank, parity, src, x.row0 + threadIdx.x));
-          key = k > key ? k : key;
-        }
-        const int tok = argmax_key_index(key);
-        p.next_tokens[threadIdx.x] = tok;
-        if (p.feed_tokens != nullptr) p.feed_tokens[threadIdx.x] = tok;
-        if (p.feed_positions != nullptr) p.feed_positions[threadIdx.x] += 1;
-        if (p.history != nullptr) p.history[(size_t)step * p.M + threadIdx.x] = tok;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        if (p.history != nullptr) *p.history_counter = step + 1;
-        atomicExch(p.argmax_counter, 0u);
-        *x.epoch = e + 1u;
-      }
-    } else if (is_last) {
-      __threadfence();
-      const unsigned int step = p.history != nullptr ? *p.history_counter : 0u;
-      if (threadIdx.x < p.M) {
-        const unsigned long long key = atomicExch(p.argmax_keys + threadIdx.x, 0ull);
-        const int tok = argmax_key_index(key);
-        p.next_tokens[threadIdx.x] = tok;
-        if (p.feed_tokens != nullptr) p.feed_tokens[threadIdx.x] = tok;
-        if (p.feed_positions != nullptr) p.feed_positions[threadIdx.x] += 1;
-        if (p.history != nullptr) p.history[(size_t)step * p.M + threadIdx.x] = tok;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        if (p.history != nullptr) *p.history_counter = step + 1;
-        atomicExch(p.argmax_counter, 0u);
-      }
+      argmax_finalize(p, threadIdx.x, [] { __syncthreads(); });
     }
     trace_emit(p.trace, t_entry, t_ready);
   }
+}
+
+// Row prologue for the batched tensor-core GEMM: one CTA per activation row
+// runs the GEMV prologue (embedding gather, residual + reduced projection,
+// RMSNorm; exchange waits included) and writes the fp16 row the GEMM's TMA
+// reads. The rounding is the GEMV's own (same stage_x).
+__global__ void __launch_bounds__(kThreads) row_prologue_kernel(const GemvParams p, __half *xn) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  __half *xs = reinterpret_cast<__half *>(smem_raw);
+  __shared__ float red[32];
+  const int m = blockIdx.x;
+  GemvParams q = p;
+  q.M = 1;
+  const bool f32_in = (p.prologue == kProF32 || p.prologue == kProF32Norm);
+  if (p.x) q.x = f32_in ? static_cast<const void *>(static_cast<const float *>(p.x) + (size_t)m * p.x_stride)
+                       : static_cast<const void *>(static_cast<const __half *>(p.x) + (size_t)m * p.x_stride);
+  if (p.tokens) q.tokens = p.tokens + m;
+  if (p.h_out) q.h_out = p.h_out + (size_t)m * p.K;
+  if (p.partial) q.partial = p.partial + (size_t)m * p.K;
+  q.xchg.row0 = p.xchg.row0 + m;
+  pdl_wait();
+  pdl_launch_dependents();
+  stage_x<__half, 1>(q, xs, red, true);
+  __syncthreads();
+  const uint4 *src = reinterpret_cast<const uint4 *>(xs);
+  uint4 *dst = reinterpret_cast<uint4 *>(xn + (size_t)m * p.K);
+  for (int v = threadIdx.x; v < (p.K >> 3); v += blockDim.x) dst[v] = src[v];
 }
 
 template <typename XS, int M, int R, int U, int KS>
@@ -784,6 +676,36 @@ int max_rows_per_launch(const GemvParams &p) {
 }
 
 }  // namespace
+
+cudaError_t launch_row_prologue(const GemvParams &p, __half *xn, cudaStream_t stream, bool pdl) {
+  if (p.K <= 0 || (p.K & 7) != 0 || p.M <= 0 || p.prologue == kProF32 || p.prologue == kProF32Norm)
+    return cudaErrorInvalidValue;
+  const size_t smem = (size_t)p.K * sizeof(__half);
+  static std::mutex mu;
+  static std::unordered_map<int, bool> configured;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      e = cudaFuncSetAttribute(row_prologue_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+      if (e != cudaSuccess) return e;
+      configured[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.M);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, row_prologue_kernel, p, xn);
+}
 
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
   if (p.K <= 0 || (p.K & 7) != 0 || p.N <= 0 || p.M <= 0 || p.M > 8) return cudaErrorInvalidValue;

@@ -147,4 +147,9 @@ constexpr int kGemvCounterWords = (kGemvPools + 1) * kGemvPoolStride;
 cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl,
                         int num_sms);
 
+// The prologue alone, for the batched tensor-core GEMM: xn[m, :] = fp16 row m
+// after p.prologue (fp16 prologues only; M any positive count), one CTA per
+// row; h_out and the exchange waits behave as in the GEMV.
+cudaError_t launch_row_prologue(const GemvParams &p, __half *xn, cudaStream_t stream, bool pdl);
+
 }  // namespace tmc

@@ -90,6 +90,9 @@ _sig("tmc_k_rmsnorm_gemv_f32", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_
      c_float, c_void_p)
 _sig("tmc_k_gemv_f16", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p)
 _sig("tmc_k_gemv_f16_f32out", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p)
+_sig("tmc_k_batched_gemm_workspace_bytes", c_size_t, c_int, c_int, c_int)
+_sig("tmc_k_batched_gemm_f16_f32out", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p,
+     c_void_p, c_void_p)
 _sig("tmc_k_attention_workspace_bytes", c_size_t, c_int, c_int, c_int, c_int, c_int)
 _sig("tmc_k_paged_attention_f16", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
      c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
@@ -228,6 +231,17 @@ def gemv_f16(rt: Runtime, x: Buffer, w: Buffer, y: Buffer, rows: int, k: int, n:
         check(lib.tmc_k_gemv_f16(x.ptr, w.ptr, y.ptr, rows, k, n, rt.stream))
     else:
         check(lib.tmc_k_gemv_f16_f32out(x.ptr, w.ptr, y.ptr, rows, k, n, rt.stream))
+
+
+def batched_gemm_workspace_bytes(n: int, k: int, rows: int) -> int:
+    return int(lib.tmc_k_batched_gemm_workspace_bytes(n, k, rows))
+
+
+def batched_gemm_f16(rt: Runtime, x: Buffer, w: Buffer, y: Buffer, rows: int, k: int, n: int,
+                     workspace: Buffer):
+    """y [rows, n] fp32 = x [rows, k] . W [n, k]^T on the tcgen05 tensor cores."""
+    check(lib.tmc_k_batched_gemm_f16_f32out(x.ptr, w.ptr, y.ptr, rows, k, n, workspace.ptr,
+                                            rt.status_ptr, rt.stream))
 
 
 def attention_workspace_bytes(rows, hq, hkv, d, max_splits) -> int:

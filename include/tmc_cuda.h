@@ -122,6 +122,16 @@ int tmc_k_gemv_f16(const void *x_f16, const void *w_f16, void *y_f16, int rows, 
 int tmc_k_gemv_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k,
                           int n, void *stream);
 
+/* Batched projection on tcgen05 tensor cores, y = x W^T with fp16 x [rows, k]
+ * and W [n, k], fp32 accumulation in tensor memory, fp32 y [rows, n]:
+ * replaces emitTiledGEMM (DecodeGEMVMetalEmitter.cpp:134-169), the
+ * reference's batched linear layer. rows <= 128, k % 64 == 0, x and W 16-byte
+ * aligned. `workspace` holds tmc_k_batched_gemm_workspace_bytes(n, k, rows)
+ * bytes (split-K partials and tile tickets; the call clears the tickets). */
+size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows);
+int tmc_k_batched_gemm_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k,
+                                  int n, void *workspace, void *status, void *stream);
+
 /* Block-table GQA decode attention over a paged fp16 KV pool, split-K:
  * replaces emitServingPagedKVAttention (KVCacheMetalEmitter.cpp:312-406).
  *   q        [rows, hq, d] f16         out [rows, hq, d] f16
