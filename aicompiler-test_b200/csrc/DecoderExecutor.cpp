@@ -9,6 +9,7 @@
 #include <stdexcept>
 
 #include "attention.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 #include "half_convert.hpp"
 #include "misc.cuh"
@@ -115,7 +116,8 @@ std::unique_ptr<DecoderExecutor> DecoderExecutor::create(cuda::CudaRuntime &runt
     why = "heads, kvHeads, intermediate and vocab must divide by the tensor-parallel size.";
   else if ((c.intermediate / c.tpSize) % 8 != 0 || ((c.heads / c.tpSize) * c.headDim) % 8 != 0)
     why = "Per-rank intermediate and head widths must be multiples of 8.";
-  else if (c.maxRows < 1 || c.maxRows > 8) why = "maxRows must be in [1, 8] for the GEMV decode path.";
+  else if (c.maxRows < 1 || c.maxRows > 128)
+    why = "maxRows must be in [1, 128] (up to 8: GEMV; more: tensor-core projections).";
   else if (c.maxSlots < 1) why = "maxSlots must be positive.";
   else if (c.pageSize < 0 || c.pageSize > c.capacity) why = "pageSize must be in [0, capacity].";
   else if (!(c.epsilon > 0.0f) || !std::isfinite(c.epsilon)) why = "epsilon must be finite and positive.";
@@ -176,6 +178,20 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)R * H, F16, &h_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)R * H, F16, &hB_, &activationBytes_)).empty()) return e;  // second residual buffer (TP)
   if (cfg_.tpSize > 1 && !(e = make((size_t)R * H, F32, &partialF32_, &activationBytes_)).empty()) return e;
+  if (R > kGemvMaxRows) {
+    // Batched steps: prologue rows for the tensor-core projections, split-K
+    // partials (the largest any projection's plan needs) and tile tickets.
+    if (!(e = make((size_t)R * H, F16, &xn_, &activationBytes_)).empty()) return e;
+    const int dims[5][2] = {{qkvRows_, H}, {H, hqL_ * D}, {2 * iL_, H}, {H, iL_}, {vL_, H}};
+    size_t wsFloats = 1, tiles = 1;
+    for (const auto &d : dims) {
+      const tmc::GemmPlan plan = tmc::plan_gemm(d[0], d[1], R, numSms_);
+      wsFloats = std::max(wsFloats, tmc::gemm_workspace_floats(plan));
+      tiles = std::max(tiles, (size_t)plan.tiles);
+    }
+    if (!(e = make(wsFloats, F32, &gemmWs_, &activationBytes_)).empty()) return e;
+    if (!(e = make(tiles, I32, &gemmTickets_, &activationBytes_)).empty()) return e;
+  }
   if (cfg_.tpSize > 1) {
     // Exchange window (zeroed int32 words), CTA-done counters per partial-sum
     // phase (one 128-byte line each) and the step epoch.
@@ -628,9 +644,11 @@ std::string DecoderExecutor::restoreKV(int slot, std::size_t length,
 // ---- step --------------------------------------------------------------------
 
 int DecoderExecutor::kernelsPerStep(int rows) const {
-  (void)rows;
   const bool tp = cfg_.tpSize > 1;
-  return cfg_.layers * 5 + 1 + (tp && !peersAttached_ ? 1 : 0);  // + argmax finalize after the collective
+  // Batched steps add a prologue kernel before the QKV, gate/up and LM-head projections.
+  const int perLayer = rows > kGemvMaxRows ? 7 : 5;
+  const int head = rows > kGemvMaxRows ? 2 : 1;
+  return cfg_.layers * perLayer + head + (tp && !peersAttached_ ? 1 : 0);  // + argmax finalize after the collective
 }
 
 double DecoderExecutor::stepAlgorithmicBytes(int rows, const std::vector<int> &ctx) const {
@@ -643,6 +661,47 @@ double DecoderExecutor::stepAlgorithmicBytes(int rows, const std::vector<int> &c
   for (int c : ctx) bytes += 2.0 * 2.0 * hkvL_ * D * c * cfg_.layers;  // K and V reads
   bytes += 2.0 * 2.0 * hkvL_ * D * rows * cfg_.layers;                // K and V appends
   return bytes;
+}
+
+const CUtensorMap *DecoderExecutor::tensorMap(const void *base, int rows, int cols, int boxRows, std::string *err) {
+  const auto key = std::make_tuple(base, rows, cols, boxRows);
+  auto it = tensorMaps_.find(key);
+  if (it != tensorMaps_.end()) return &it->second;
+  CUtensorMap map;
+  const cudaError_t e = tmc::make_tensor_map_f16(&map, base, rows, cols, boxRows);
+  if (e != cudaSuccess) {
+    *err = cudaText("tensor map", e);
+    return nullptr;
+  }
+  return &tensorMaps_.emplace(key, map).first->second;
+}
+
+// One projection: the GEMV for up to 8 rows; for more, the prologue kernel
+// (when there is one) and the tensor-core GEMM over the same parameters.
+std::string DecoderExecutor::launchProjection(const tmc::GemvParams &p, const char *what) {
+  cudaStream_t s = rt_.stream();
+  const bool pdl = cfg_.usePDL;
+  cudaError_t e;
+  if (p.M <= kGemvMaxRows) {
+    if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText(what, e);
+    return {};
+  }
+  const void *x = p.x;
+  if (p.prologue != tmc::kProF16) {
+    if ((e = tmc::launch_row_prologue(p, hp(xn_), s, pdl)) != cudaSuccess) return cudaText(what, e);
+    x = xn_->data();
+  } else if (p.x_stride != p.K) {
+    return std::string(what) + ": batched projection needs contiguous activation rows.";
+  }
+  const tmc::GemmPlan plan = tmc::plan_gemm(p.N, p.K, p.M, numSms_);
+  std::string err;
+  const CUtensorMap *wm = tensorMap(p.W, p.N, p.K, tmc::kGemmTileRows, &err);
+  const CUtensorMap *xm = wm ? tensorMap(x, cfg_.maxRows, p.K, plan.tn, &err) : nullptr;
+  if (!xm) return std::string(what) + ": " + err;
+  if ((e = tmc::launch_gemm(p, *wm, *xm, plan, fp(gemmWs_), static_cast<unsigned int *>(gemmTickets_->data()), s,
+                            pdl)) != cudaSuccess)
+    return cudaText(what, e);
+  return {};
 }
 
 std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bool distinct) {
@@ -710,7 +769,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("qkv gemv", e);
+      if (auto pe = launchProjection(p, "qkv projection"); !pe.empty()) return pe;
 
       return {};
     }
@@ -774,7 +833,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("o gemv", e);
+      if (auto pe = launchProjection(p, "o projection"); !pe.empty()) return pe;
       if (tp && !xchg && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (o): " + collective_->lastError();
 
@@ -807,7 +866,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("gate/up gemv", e);
+      if (auto pe = launchProjection(p, "gate/up projection"); !pe.empty()) return pe;
 
       return {};
     }
@@ -835,7 +894,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.trace = traceSink(l, kind);
       p.work_counter = workCounter(l, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("down gemv", e);
+      if (auto pe = launchProjection(p, "down projection"); !pe.empty()) return pe;
       if (tp && !xchg && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
         return "allreduce (down): " + collective_->lastError();
 
@@ -880,7 +939,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
     p.trace = traceSink(0, kind);
     p.work_counter = workCounter(0, kind);
       p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if ((e = tmc::launch_gemv(p, s, pdl, numSms_)) != cudaSuccess) return cudaText("lm head gemv", e);
+      if (auto pe = launchProjection(p, "lm head projection"); !pe.empty()) return pe;
     if (tp && !xchg) {
       if ((e = collective_->allReduceMaxU64(p.argmax_keys, R, s)) != cudaSuccess)
         return "allreduce (argmax): " + collective_->lastError();

@@ -28,6 +28,7 @@
 
 #include <cstdint>
 #include <map>
+#include <tuple>
 #include <memory>
 #include <string>
 #include <utility>
@@ -36,6 +37,7 @@
 #include "CudaRuntime.hpp"
 #include "KVCacheState.hpp"
 #include "common.cuh"
+#include "gemm.cuh"
 #include "gemv.cuh"
 
 namespace tensor::runtime {
@@ -231,6 +233,12 @@ class DecoderExecutor {
   bool profiling_ = false;  // isolated kernel timing: consumers do not wait for peers
   void dropGraphs();
   tmc::PeerExchange exchange(int phase) const;
+  // Batched (> 8 rows) projections on the tensor cores.
+  static constexpr int kGemvMaxRows = 8;
+  cuda::BufferHandle xn_, gemmWs_, gemmTickets_;
+  std::map<std::tuple<const void *, int, int, int>, CUtensorMap> tensorMaps_;
+  const CUtensorMap *tensorMap(const void *base, int rows, int cols, int boxRows, std::string *err);
+  std::string launchProjection(const tmc::GemvParams &p, const char *what);
   std::size_t traceCapacity_ = 0;
   tmc::TraceSink traceSink(int layer, int kind) const;
   bool ropeSet_ = false;

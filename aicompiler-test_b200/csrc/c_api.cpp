@@ -256,8 +256,8 @@ size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows) {
 int tmc_k_batched_gemm_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k, int n,
                                   void *workspace, void *status, void *stream) {
   if (!x_f16 || !w_f16 || !y || !workspace) return fail(TMC_ERR_INVALID, "null pointer");
-  if (rows <= 0 || rows > 128 || n <= 0 || k <= 0 || k % 64 != 0)
-    return fail(TMC_ERR_UNSUPPORTED, "batched gemm: rows in [1, 128], k % 64 == 0");
+  if (rows <= 0 || rows > 128 || n <= 0 || k <= 0 || k % 8 != 0)
+    return fail(TMC_ERR_UNSUPPORTED, "batched gemm: rows in [1, 128], k % 8 == 0");
   const tmc::GemmPlan plan = tmc::plan_gemm(n, k, rows, sm_count());
   const size_t partial = (tmc::gemm_workspace_floats(plan) * 4 + 255) / 256 * 256;
   auto *ws = static_cast<unsigned char *>(workspace);

@@ -29,38 +29,52 @@ __device__ __forceinline__ float *peer_slot(const PeerExchange &x, int owner, in
          (((size_t)parity * kMaxPeers + src) * x.slot_rows + m) * x.width;
 }
 
+// ---- the arithmetic of each epilogue, shared by every kernel ---------------
+// SwiGLU of one (gate, up) pair of fp32 sums: half(half(silu(half(g))) * half(u)).
+__device__ __forceinline__ __half swiglu_value(float acc_gate, float acc_up) {
+  const float g = round_half(acc_gate);
+  const float u = round_half(acc_up);
+  const float a = round_half(g / (1.0f + expf(-g)));
+  return __float2half_rn(__fmul_rn(a, u));
+}
+// Interleaved RoPE of one (even, odd) pair of fp32 sums, rounded to fp16
+// first; (c, s) = cos/sin of the pair's angle at the token's position.
+__device__ __forceinline__ __half2 rope_pair_value(float acc_e, float acc_o, float c, float s) {
+  const float e = round_half(acc_e);
+  const float o = round_half(acc_o);
+  return __floats2half2_rn(__fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s)), __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c)));
+}
+// Residual add of a projection sum: half(residual + half(acc)).
+__device__ __forceinline__ __half residual_value(__half residual, float acc) {
+  return __float2half_rn(__fadd_rn(__half2float(residual), round_half(acc)));
+}
+
 // Rows (row0, row0 + 1) of token m, row0 even, with fp32 sums (acc_e, acc_o):
 // kEpiSwiGLU: a (gate_i, up_i) pair, i = row0 / 2 -> y_f16[m, i];
 // kEpiQKV: an interleaved RoPE pair inside one head of [q | k | v]; q goes to
 // y_f16, k and v to the paged cache at the row's position.
 __device__ __forceinline__ void epilogue_pair(const GemvParams &p, int row0, int m, float acc_e, float acc_o) {
   if (p.epilogue == kEpiSwiGLU) {
-    const float g = round_half(acc_e);
-    const float u = round_half(acc_o);
-    const float a = round_half(g / (1.0f + expf(-g)));
-    p.y_f16[(size_t)m * p.y_stride + (row0 >> 1)] = __float2half_rn(__fmul_rn(a, u));
+    p.y_f16[(size_t)m * p.y_stride + (row0 >> 1)] = swiglu_value(acc_e, acc_o);
     return;
   }
   // kEpiQKV
   const int D = p.head_dim;
-  float e = round_half(acc_e);
-  float o = round_half(acc_o);
   const int pos = p.positions[m];
   if (pos < 0 || pos >= p.capacity) {
     report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
     return;
   }
+  __half2 pair_value;
   if (row0 < p.q_rows + p.kv_rows) {
     const int pair = (row0 % D) >> 1;
-    const float c = p.rope_cos[(size_t)pos * (D >> 1) + pair];
-    const float s = p.rope_sin[(size_t)pos * (D >> 1) + pair];
-    const float re = __fsub_rn(__fmul_rn(e, c), __fmul_rn(o, s));
-    const float ro = __fadd_rn(__fmul_rn(e, s), __fmul_rn(o, c));
-    e = re;
-    o = ro;
+    pair_value = rope_pair_value(acc_e, acc_o, p.rope_cos[(size_t)pos * (D >> 1) + pair],
+                                 p.rope_sin[(size_t)pos * (D >> 1) + pair]);
+  } else {
+    pair_value = __floats2half2_rn(round_half(acc_e), round_half(acc_o));
   }
   if (row0 < p.q_rows) {
-    *reinterpret_cast<__half2 *>(p.y_f16 + (size_t)m * p.y_stride + row0) = __floats2half2_rn(e, o);
+    *reinterpret_cast<__half2 *>(p.y_f16 + (size_t)m * p.y_stride + row0) = pair_value;
     return;
   }
   int local = row0 - p.q_rows;
@@ -86,7 +100,7 @@ __device__ __forceinline__ void epilogue_pair(const GemvParams &p, int row0, int
   }
   const int hkv = p.kv_rows / D;
   const size_t addr = (((size_t)page * hkv + kvh) * p.page_size + off) * D + d;
-  *reinterpret_cast<__half2 *>(pool + addr) = __floats2half2_rn(e, o);
+  *reinterpret_cast<__half2 *>(pool + addr) = pair_value;
 }
 
 // One output (row, token m) with fp32 sum v: kEpiF32, kEpiF16, kEpiResidual,
@@ -103,7 +117,7 @@ __device__ __forceinline__ void epilogue_one(const GemvParams &p, int row, int m
   } else if (epi == kEpiF16) {
     p.y_f16[idx] = __float2half_rn(v);
   } else if (epi == kEpiResidual) {
-    p.y_f16[idx] = __float2half_rn(__fadd_rn(__half2float(p.residual[idx]), round_half(v)));
+    p.y_f16[idx] = residual_value(p.residual[idx], v);
   }
 }
 

@@ -6,14 +6,14 @@
 //             of shared-memory stages (128-byte swizzle). Weight tiles do not
 //             depend on earlier kernels, so the first ring-full is requested
 //             before the programmatic-dependency wait;
-//   warp 1    owns the tensor memory (two TN-column fp32 accumulators) and
+//   warp 1    owns the tensor memory (four TN-column fp32 accumulators) and
 //             issues the MMAs from one thread: 4 x (M=128, N=TN, K=16) per
 //             stage, tcgen05.commit frees the stage, a final commit hands the
 //             accumulator to the epilogue;
 //   warps 2-5 epilogue: tcgen05.ld of their 32-lane quarter of the
 //             accumulator (one output feature per thread, TN tokens), then the
-//             GEMV's per-element epilogues. With two accumulators the
-//             epilogue of one tile overlaps the MMAs of the next.
+//             GEMV's per-element epilogues. With four accumulators the
+//             epilogues of finished units overlap the MMAs of the next ones.
 // Work units are (tile, K split) pairs, assigned round-robin to the CTAs.
 // With several K splits each unit writes its fp32 partial to a workspace and
 // the tile's last unit (atomic ticket) sums the partials in split order, so
@@ -39,7 +39,8 @@ struct GemmCfg {
   static constexpr int kBytesB = TN * kGemmKBlock * 2;
   static constexpr int kStageBytes = kTileBytesA + kBytesB;
   static constexpr int kStages = (200 * 1024 / kStageBytes) < 8 ? (200 * 1024 / kStageBytes) : 8;
-  static constexpr int kTmemCols = 2 * TN < 32 ? 32 : 2 * TN;  // a power of two for TN in {16..128}
+  static constexpr int kAcc = 4;  // accumulators in tensor memory (epilogues overlap later MMAs)
+  static constexpr int kTmemCols = kAcc * TN < 32 ? 32 : kAcc * TN;  // a power of two, <= 512
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256;
 };
 
@@ -101,25 +102,34 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // Named barrier of the four epilogue warps.
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// The epilogue of one finished tile for this thread's output feature `row`
+// and the TN token columns in v: one loop per epilogue kind with every
+// parameter read once (a generic per-element dispatch costs more than the
+// stores), the arithmetic shared with the GEMV (epilogue.cuh).
 template <int TN>
 __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float (&v)[TN], int row, int lane,
                                                int ew, int t, unsigned long long (*red_keys)[TN]) {
   const int epi = p.epilogue;
+  const int M = p.M;
+  const bool in_range = row < p.N;
   if (epi == kEpiArgmax) {
+    float *y = p.y_f32;
+    const long long ys = p.y_stride;
+    const int voff = p.vocab_offset;
 #pragma unroll
     for (int m = 0; m < TN; ++m) {
-      if (m >= p.M) break;
+      if (m >= M) break;
       unsigned long long key = 0ull;
-      if (row < p.N) {
+      if (in_range) {
         const float h = round_half(v[m]);
-        if (p.y_f32 != nullptr) p.y_f32[(size_t)m * p.y_stride + row] = h;
-        key = argmax_key(h, p.vocab_offset + row);
+        if (y != nullptr) y[(size_t)m * ys + row] = h;
+        key = argmax_key(h, voff + row);
       }
       key = warp_max_u64(key);
       if (lane == 0) red_keys[ew][m] = key;
     }
     epi_sync();
-    if (t < p.M) {
+    if (t < M) {
       unsigned long long k = red_keys[0][t];
 #pragma unroll
       for (int e = 1; e < 4; ++e) k = red_keys[e][t] > k ? red_keys[e][t] : k;
@@ -128,19 +138,97 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
     epi_sync();
     return;
   }
-  if (epi == kEpiQKV || epi == kEpiSwiGLU) {
+  if (epi == kEpiSwiGLU) {
+    __half *y = p.y_f16 + (row >> 1);
+    const long long ys = p.y_stride;
+    const bool store = !(lane & 1) && in_range;
 #pragma unroll
     for (int m = 0; m < TN; ++m) {
-      if (m >= p.M) break;
+      if (m >= M) break;
       const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
-      if (!(lane & 1) && row < p.N) epilogue_pair(p, row, m, v[m], partner);
+      if (store) y[(size_t)m * ys] = swiglu_value(v[m], partner);
     }
     return;
   }
+  if (epi == kEpiQKV) {
+    const int D = p.head_dim, q_rows = p.q_rows, kv_rows = p.kv_rows, cap = p.capacity;
+    const int ps = p.page_size, pool_pages = p.pool_pages, tstride = p.table_stride;
+    const int *positions = p.positions, *trows = p.table_rows, *table = p.block_table;
+    const float *rc = p.rope_cos + ((row % D) >> 1), *rs = p.rope_sin + ((row % D) >> 1);
+    __half *y = p.y_f16 + row;
+    const long long ys = p.y_stride;
+    const bool rope = row < q_rows + kv_rows, is_q = row < q_rows;
+    int local = row - q_rows;
+    __half *pool = p.k_pool;
+    if (local >= kv_rows) {
+      local -= kv_rows;
+      pool = p.v_pool;
+    }
+    const int hkv = kv_rows / D;
+    const size_t head_off = (size_t)(local / D) * ps * D + (local % D);
+    const bool store = !(lane & 1) && in_range;
+#pragma unroll
+    for (int m = 0; m < TN; ++m) {
+      if (m >= M) break;
+      const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
+      if (!store) continue;
+      const int pos = positions[m];
+      if (pos < 0 || pos >= cap) {
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        continue;
+      }
+      const __half2 val = rope ? rope_pair_value(v[m], partner, rc[(size_t)pos * (D >> 1)], rs[(size_t)pos * (D >> 1)])
+                               : __floats2half2_rn(round_half(v[m]), round_half(partner));
+      if (is_q) {
+        *reinterpret_cast<__half2 *>(y + (size_t)m * ys) = val;
+        continue;
+      }
+      const int lp = pos / ps, off = pos % ps;
+      if (lp >= tstride) {
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        continue;
+      }
+      const int page = table[(size_t)trows[m] * tstride + lp];
+      if (page < 0 || page >= pool_pages) {
+        report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
+                      page < 0 ? lp : page, m);
+        continue;
+      }
+      *reinterpret_cast<__half2 *>(pool + (size_t)page * hkv * ps * D + head_off + (size_t)off * D) = val;
+    }
+    return;
+  }
+  if (epi == kEpiResidual || epi == kEpiF16) {
+    __half *y = p.y_f16 + row;
+    const __half *res = p.residual + row;
+    const long long ys = p.y_stride;
+    const bool residual = epi == kEpiResidual;
+#pragma unroll
+    for (int m = 0; m < TN; ++m) {
+      if (m >= M) break;
+      if (in_range) y[(size_t)m * ys] = residual ? residual_value(res[(size_t)m * ys], v[m]) : __float2half_rn(v[m]);
+    }
+    return;
+  }
+  // kEpiF32 / kEpiF32Partial
+  if (epi == kEpiF32Partial && p.xchg.world > 0) {
+    const int world = p.xchg.world, width = p.xchg.width;
+    for (int q = 0; q < world; ++q) {
+      float *dst = peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0) + row;
+#pragma unroll
+      for (int m = 0; m < TN; ++m) {
+        if (m >= M) break;
+        if (in_range) dst[(size_t)m * width] = v[m];
+      }
+    }
+    return;
+  }
+  float *y = p.y_f32 + row;
+  const long long ys = p.y_stride;
 #pragma unroll
   for (int m = 0; m < TN; ++m) {
-    if (m >= p.M) break;
-    if (row < p.N) epilogue_one(p, row, m, v[m]);
+    if (m >= M) break;
+    if (in_range) y[(size_t)m * ys] = v[m];
   }
 }
 
@@ -158,8 +246,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *full = reinterpret_cast<uint64_t *>(sB + (size_t)S * C::kBytesB);
   uint64_t *empty = full + S;
   uint64_t *acc_full = empty + S;
-  uint64_t *acc_empty = acc_full + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+  uint64_t *acc_empty = acc_full + C::kAcc;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + C::kAcc);
   __shared__ unsigned long long red_keys[4][TN];
   __shared__ int s_last, s_fail;
   __shared__ unsigned long long s_ready;
@@ -174,7 +262,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < C::kAcc; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
     }
@@ -249,8 +337,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int ks = u % w.splits;
         const int kb0 = (int)((long long)w.kblocks * ks / w.splits);
         const int kb1 = (int)((long long)w.kblocks * (ks + 1) / w.splits);
-        const int buf = j & 1;
-        if (j >= 2 && !mbar_wait(&acc_empty[buf], ((j >> 1) - 1) & 1)) {
+        const int buf = j % C::kAcc;
+        if (j >= C::kAcc && !mbar_wait(&acc_empty[buf], ((j / C::kAcc) - 1) & 1)) {
           ok = false;
           break;
         }
@@ -284,8 +372,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     int j = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
       const int tile = u / w.splits, ks = u % w.splits;
-      const int buf = j & 1;
-      if (!mbar_wait(&acc_full[buf], (j >> 1) & 1)) s_fail = 1;
+      const int buf = j % C::kAcc;
+      if (!mbar_wait(&acc_full[buf], (j / C::kAcc) & 1)) s_fail = 1;
       epi_sync();
       if (s_fail) break;
       tc_fence_after();
@@ -315,13 +403,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epi_sync();
         if (!s_last) continue;
         __threadfence();
+        // Sum the partials in split order; each split's values for all tokens
+        // of a chunk are requested together (one round trip per chunk).
+        constexpr int CH = TN < 64 ? TN : 64;
 #pragma unroll
-        for (int m = 0; m < TN; ++m) {
-          if (m >= p.M) break;
-          float sum = 0.0f;
-          for (int k2 = 0; k2 < w.splits; ++k2)
-            sum += __ldcg(w.ws + ((size_t)(tile * w.splits + k2) * TN + m) * kGemmTileRows + r);
-          v[m] = sum;
+        for (int m = 0; m < TN; ++m) v[m] = 0.0f;
+#pragma unroll
+        for (int c0 = 0; c0 < TN; c0 += CH) {
+          for (int k2 = 0; k2 < w.splits; ++k2) {
+            const float *src = w.ws + (size_t)(tile * w.splits + k2) * TN * kGemmTileRows + r;
+            float tmp[CH];
+#pragma unroll
+            for (int m = 0; m < CH; ++m)
+              tmp[m] = (c0 + m < p.M) ? __ldcg(src + (size_t)(c0 + m) * kGemmTileRows) : 0.0f;
+#pragma unroll
+            for (int m = 0; m < CH; ++m) v[c0 + m] += tmp[m];
+          }
         }
       }
       apply_epilogue<TN>(p, v, row, lane, ew, t, red_keys);
@@ -410,10 +507,10 @@ GemmPlan plan_gemm(int N, int K, int M, int num_sms) {
   GemmPlan g{};
   g.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   g.tiles = (N + kGemmTileRows - 1) / kGemmTileRows;
-  g.kblocks = K / kGemmKBlock;
+  g.kblocks = (K + kGemmKBlock - 1) / kGemmKBlock;  // a ragged last block reads zeros
   // Cost of a plan in full-K tile times: waves of persistent CTAs times the
   // work of one unit plus a fixed per-unit overhead (pipeline fill, epilogue).
-  const double overhead = 0.05;
+  const double overhead = 0.1;
   double best = 1e30;
   g.splits = 1;
   for (int s = 1; s <= 16; ++s) {
@@ -466,8 +563,9 @@ cudaError_t make_tensor_map_f16(CUtensorMap *map, const void *base, uint64_t row
 cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,
                         const GemmPlan &plan, float *ws, unsigned int *tile_counters, cudaStream_t stream,
                         bool pdl) {
-  if (p.N <= 0 || p.K <= 0 || p.K % kGemmKBlock != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 128 ||
-      plan.tiles != (p.N + kGemmTileRows - 1) / kGemmTileRows || plan.kblocks != p.K / kGemmKBlock ||
+  if (p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 128 ||
+      plan.tiles != (p.N + kGemmTileRows - 1) / kGemmTileRows ||
+      plan.kblocks != (p.K + kGemmKBlock - 1) / kGemmKBlock ||
       plan.splits < 1 || plan.grid < 1 || tile_counters == nullptr || (plan.splits > 1 && ws == nullptr))
     return cudaErrorInvalidValue;
   switch (p.epilogue) {

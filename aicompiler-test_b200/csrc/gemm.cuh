@@ -3,7 +3,7 @@
 // Replaces emitTiledGEMM (DecodeGEMVMetalEmitter.cpp:134-169), the
 // reference's batched/prefill linear layer, for rows > 8: y = epilogue(W x^T)
 // with W [N, K] fp16 row-major (the decoder's weights, unchanged) and x
-// [M <= 128, K] fp16 rows (the GEMV prologue, written by launch_row_prologue,
+// [M <= 128, K] fp16 rows, K % 8 == 0 (the GEMV prologue, written by launch_row_prologue,
 // or an fp16 activation). The weight tile is the MMA's A operand (128 output
 // features = the UMMA M dimension) and the token rows are its B operand
 // (UMMA N = 16..128), so one weight byte feeds up to 128 tokens; the fp32
@@ -24,7 +24,7 @@ struct GemmPlan {
   int tn;       // token columns per MMA (16, 32, 64 or 128), >= M
   int tiles;    // ceil(N / 128)
   int splits;   // K splits per tile (partials reduced in order by the tile's last CTA)
-  int kblocks;  // K / 64
+  int kblocks;  // ceil(K / 64)
   int grid;     // persistent CTAs (one per SM at most)
 };
 

@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=CFG["layers"])
     ap.add_argument("--no-kernels", action="store_true", help="skip the per-kernel timing")
+    ap.add_argument("--batch", type=int, default=64, help="rows of the batched decode measurement (bs64)")
+    ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--no-batch", action="store_true", help="skip the batched decode measurement")
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="TP reductions: peer exchange fused into the kernels, or NCCL allreduce")
     return ap.parse_args()
@@ -209,6 +212,7 @@ def run_ours(args, world, rank, local):
     gpu_us = max_over_ranks(gpu_us)
     tok = int(out[-1, 0])
     value = K / (gpu_us * 1e-6)
+    launches = dec.kernels_per_step(1) * K
 
     # e2e through the per-step public API with host buffers
     barrier()
@@ -248,6 +252,11 @@ def run_ours(args, world, rank, local):
                     "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                     "bytes_per_launch": d["bytes"], "launch_us": d["us"]}
 
+    batched = None
+    if not args.no_batch:
+        dec.close()  # release the bs1 model before building the batched one
+        batched = measure_batched(args, world, rank, local, dist, barrier, max_over_ranks, hbm, peak_kind)
+
     cpu = None
     if rank == 0 and world == 1:
         from oracle import cpu_baseline
@@ -275,10 +284,10 @@ def run_ours(args, world, rank, local):
                               "aggregate_peak_gbs": hbm * world,
                               "frac": step_bytes / (step_ms * 1e-3) / 1e9 / hbm},
             "e2e": e2e,
-            "gpu_launches": dec.kernels_per_step(1) * K,
+            "gpu_launches": launches,
             "roofline": roofline,
             "kernels": kernels,
-            "bs64": None,
+            "bs64": batched,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
@@ -287,6 +296,65 @@ def run_ours(args, world, rank, local):
         dec.close()
         dist.destroy_process_group()
     return 0
+
+
+def measure_batched(args, world, rank, local, dist, barrier, max_over_ranks, hbm, peak_kind):
+    """bs64 of the metric: `args.batch` sequences, each prefilled with its own
+    seeded 1024-token prompt (untimed), then the device greedy loop with all
+    rows in every step (tensor-core projections, batched paged attention).
+    value = rows x steps / device time of the steps (max over ranks)."""
+    import numpy as np
+
+    import tmc_cuda
+    B, W, K = args.batch, max(3, args.warmup), args.batch_steps
+    capacity = ((args.prompt + W + K + 16 + 15) // 16) * 16
+    rt = tmc_cuda.Runtime(local)
+    dec = tmc_cuda.Decoder(rt, CFG["hidden"], CFG["heads"], CFG["intermediate"], CFG["vocab"], args.layers,
+                           capacity, kv_heads=CFG["kv_heads"], epsilon=CFG["epsilon"],
+                           rope_theta=CFG["rope_theta"], max_rows=B, max_slots=B, page_size=16,
+                           tp_rank=rank, tp_size=world)
+    if world > 1 and args.collective == "p2p":
+        handles = [None] * world
+        dist.all_gather_object(handles, dec.exchange_handle())
+        dec.attach_peers(handles, rank)
+    elif world > 1:
+        uid = [tmc_cuda.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        dec.attach_nccl(uid[0], world, rank)
+    dec.init_random(seed=0, std=0.02)
+    toks = []
+    for s in range(B):
+        prompt = np.random.default_rng(1000 + s).integers(0, CFG["vocab"], args.prompt).astype(np.int32)
+        toks.append(dec.prefill(prompt, slot=s, logits=False)[1])
+    slots = list(range(B))
+    out, _ = dec.generate(toks, W, slots=slots)
+    toks = [int(t) for t in out[-1]]
+    barrier()
+    out, gpu_us = dec.generate(toks, K, slots=slots)
+    barrier()
+    gpu_us = max_over_ranks(gpu_us)
+    ctx = [args.prompt + W + K // 2] * B
+    step_bytes = dec.step_bytes(ctx)
+    step_ms = gpu_us / K / 1e3
+    kernels = {}
+    if not args.no_kernels:
+        for kind in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head"):
+            if world > 1 and kind in ("o_proj", "down"):
+                continue
+            us, b, n = dec.profile_kernel(kind, rows=B, rounds=2)
+            kernels[kind] = {"us": round(us, 3), "bytes": int(b), "launches_per_step": n,
+                             "gbs": round(b / us / 1e3, 1), "frac_of_peak": round(b / us / 1e3 / hbm, 3)}
+    result = {"value": B * K / (gpu_us * 1e-6), "unit": "tok/s", "rows": B, "steps": K, "warmup": W,
+              "ms_per_step": step_ms, "config": {"prompt": args.prompt, "sequences": B,
+                                                 "parallelism": f"tp{world}"},
+              "step_roofline": {"bytes_per_step": step_bytes * world, "bytes_per_step_per_rank": step_bytes,
+                                "achieved_gbs": step_bytes * world / (step_ms * 1e-3) / 1e9,
+                                "peak_gbs": hbm * world, "frac": step_bytes / (step_ms * 1e-3) / 1e9 / hbm,
+                                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+              "gpu_launches": dec.kernels_per_step(B) * K, "kernels": kernels}
+    barrier()
+    dec.close()
+    return result
 
 
 def main():

@@ -125,7 +125,7 @@ int tmc_k_gemv_f16_f32out(const void *x_f16, const void *w_f16, float *y, int ro
 /* Batched projection on tcgen05 tensor cores, y = x W^T with fp16 x [rows, k]
  * and W [n, k], fp32 accumulation in tensor memory, fp32 y [rows, n]:
  * replaces emitTiledGEMM (DecodeGEMVMetalEmitter.cpp:134-169), the
- * reference's batched linear layer. rows <= 128, k % 64 == 0, x and W 16-byte
+ * reference's batched linear layer. rows <= 128, k % 8 == 0, x and W 16-byte
  * aligned. `workspace` holds tmc_k_batched_gemm_workspace_bytes(n, k, rows)
  * bytes (split-K partials and tile tickets; the call clears the tickets). */
 size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows);
@@ -196,7 +196,7 @@ typedef struct {
   int capacity;      /* KVCachePlan::capacity: positions per sequence */
   float epsilon;     /* DecoderLLMPlan::rmsNormEpsilon */
   double rope_theta;
-  int max_rows;      /* tokens per step, 1..8 */
+  int max_rows;      /* tokens per step, 1..128 (> 8: tensor-core projections) */
   int max_slots;     /* sequences with KV state */
   int page_size;     /* DecoderLLMCompileOptions::kvPageSize; 0 = contiguous */
   int pool_pages;    /* 0 = max_slots * ceil(capacity / page_size) */
