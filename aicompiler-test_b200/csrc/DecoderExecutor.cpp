@@ -715,7 +715,14 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
   // consumer kernel that folds the reduced projection into h also reads h.
   __half *hA = hp(h_), *hB = hp(hB_);
   auto *status = rt_.deviceStatus();
-  const int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
+  // Attention splits per (row, KV head): few pairs -> enough splits to cover
+  // the SMs twice; many pairs (batched decode) -> a power of two that gives
+  // about 16 CTAs per SM, so the last partial wave is short.
+  int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
+  if (R * hkvL_ >= numSms_) {
+    splits = 1;
+    while (splits < 16 && 2 * splits * R * hkvL_ <= 16 * numSms_) splits *= 2;
+  }
   float *partialF32 = fp(partialF32_);  // [R, H] row-parallel sums (TP with a collective)
   // TP over peer memory: partial-sum phase 2l = O of layer l, 2l + 1 = down.
   const bool xchg = tp && peersAttached_;

@@ -26,6 +26,7 @@ namespace tmc {
 namespace {
 
 constexpr int kThreads = 128;
+constexpr int kPageCache = 512;  // page ids a CTA caches (longer chunks read the table per tile)
 // Largest thread-block cluster (16 is the sm_100 opt-in, non-portable size; a
 // device that cannot hold a 16-CTA cluster of this kernel falls back to 8).
 constexpr int kMaxCluster = 16;
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       (reinterpret_cast<uintptr_t>(sW + 2 * C::kMaxSplits * G) + 15) & ~uintptr_t(15));
   uint64_t *empty = full + S;
   __shared__ int is_last;
+  __shared__ int sPages[kPageCache];  // the chunk's physical page ids
   __shared__ float xml[G * 2];  // this CTA's (m, l) per head, read by the cluster
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
@@ -179,6 +181,23 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
   const int fresh = p.early_mode == 2 ? end : (p.early_mode == 1 ? pos : begin);
   bool failed = false;
 
+  // The chunk's physical page ids, looked up once (the block table is final
+  // before the producer kernel starts): the per-tile gathers then read shared
+  // memory instead of waiting on a dependent global load for every tile.
+  const int lp0 = begin / p.page_size;
+  const int npages = end > begin ? (end - 1) / p.page_size - lp0 + 1 : 0;
+  const bool cached = npages <= kPageCache;
+  if (cached) {
+    for (int i = tid; i < npages; i += kThreads) {
+      const int logical = lp0 + i;
+      sPages[i] = logical < p.table_stride ? table[logical] : -1;
+    }
+  }
+  auto page_of = [&](int logical) -> int {
+    if (cached) return sPages[logical - lp0];
+    return logical < p.table_stride ? table[logical] : -1;
+  };
+
   if (tid == 0) {
 #pragma unroll
     for (int st = 0; st < S; ++st) {
@@ -201,7 +220,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       int v = 0;
       if (position < end) {
         const int logical = position / p.page_size;
-        const int page = logical < p.table_stride ? table[logical] : -1;
+        const int page = page_of(logical);
         if (page < 0) {
           report_status(p.status, kStatusPageMissing, kWhereAttention, logical, row);
         } else if (page >= p.pool_pages) {
@@ -234,7 +253,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       const int lp = lane + 32 * j;
       const int position = p0 + lp;
       if (position < lo || position >= hi || position >= end || !sValid[stage * T + lp]) continue;
-      const int page = table[position / p.page_size];
+      const int page = page_of(position / p.page_size);
       const size_t off = (((size_t)page * p.hkv + kvh) * p.page_size + position % p.page_size) * D;
       bulk_g2s(sK + ((size_t)stage * T + lp) * ROW, p.k_pool + off, D * 2, &full[stage]);
       bulk_g2s(sV + ((size_t)stage * T + lp) * ROW, p.v_pool + off, D * 2, &full[stage]);
