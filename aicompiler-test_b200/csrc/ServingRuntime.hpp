@@ -1,0 +1,92 @@
+// Continuous batching over the paged KV cache: the B200 counterpart of the
+// reference's ServingRuntime (src/runtime/ServingRuntime.hpp:15-75,
+// ServingRuntime.cpp:513-930).
+//
+// One scheduler tick, as in the reference:
+//   1. resume preempted requests whose KV snapshot fits the free pages;
+//   2. admit arrived requests (arrival tick <= tick) whose prompt fits the free
+//      pages and a free sequence slot: chunked prefill, first token;
+//   3. while the next decode token of every active request does not fit,
+//      preempt the active request holding the most pages (KV snapshot to the
+//      host, pages and slot released);
+//   4. one batched decode step over all active requests (the executor stages,
+//      decodes and commits each row; more active rows than the executor's
+//      max_rows are decoded in several steps), outputs appended, finished
+//      requests released;
+//   5. audit that no two active requests own the same physical page.
+// Differences by design: one shared KV pool serves every layer (all layers of
+// a sequence use the same page ids), sequence slots are reused across
+// requests, and the decode steps are the executor's CUDA-graph steps with the
+// GEMV (<= 8 rows) or tensor-core (more rows) projections.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <ostream>
+#include <string>
+#include <vector>
+
+#include "DecoderExecutor.hpp"
+
+namespace tensor::runtime {
+
+struct ServingRequestSpec {
+  std::string id;
+  std::vector<std::int32_t> promptTokenIds;
+  std::size_t decodeTokenCount = 0;
+  std::size_t arrivalStep = 0;  // scheduler tick at which the request arrives
+};
+
+struct ServingConfig {
+  bool recordLogits = false;    // keep prefill and decode logits per request
+  std::size_t maxTicks = 1000000;  // progress limit (the reference uses 10000)
+};
+
+struct ServingRequestOutput {
+  std::string id;
+  std::vector<float> prefillLogits;                // [prompt, localVocab] when recorded
+  std::vector<std::vector<float>> decodeLogits;    // per decode step, [localVocab]
+  std::vector<std::int32_t> generatedTokenIds;     // 1 (prefill) + decodeTokenCount
+  double timeToFirstTokenUs = 0.0;                 // arrival -> first token
+  double finishUs = 0.0;                           // arrival -> last token
+};
+
+struct ServingMetrics {
+  double totalTimeUs = 0.0;
+  double tokensPerSecond = 0.0;      // decoded tokens / total time
+  double prefillGpuUs = 0.0;         // sums over all prefill / decode steps
+  double decodeGpuUs = 0.0;
+  double schedulerOverheadUs = 0.0;
+  double kvManagementOverheadUs = 0.0;
+  double preemptionOverheadUs = 0.0;
+  double averageActiveBatchSize = 0.0;
+  std::size_t maximumActiveBatchSize = 0;
+  std::size_t preemptionCount = 0;
+  std::size_t resumeCount = 0;
+  std::size_t peakPages = 0;
+  std::size_t pageAllocationCount = 0;
+  std::size_t pageReleaseCount = 0;
+  std::size_t decodeCommandSubmissions = 0;
+  std::size_t decodedTokens = 0;
+  std::size_t prefillTokens = 0;
+  std::size_t ticks = 0;
+  std::size_t modelStorageBytes = 0;
+  std::size_t kvPoolStorageBytes = 0;
+  std::size_t activationStorageBytes = 0;
+};
+
+struct ServingExecutionResult {
+  bool passed = false;
+  std::vector<ServingRequestOutput> requests;
+  ServingMetrics metrics;
+  std::string errorMessage;
+};
+
+// Serve `requests` on `decoder` (a multi-slot executor; its weights loaded).
+// All tensor-parallel ranks must call this with the same requests: every
+// scheduling decision depends only on ticks and page counts.
+[[nodiscard]] ServingExecutionResult runContinuousBatch(DecoderExecutor &decoder,
+                                                        const std::vector<ServingRequestSpec> &requests,
+                                                        const ServingConfig &config, std::ostream &log);
+
+}  // namespace tensor::runtime

@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cstring>
 #include <memory>
+#include <sstream>
 #include <string>
 #include <vector>
 
@@ -11,6 +12,7 @@
 #include "CudaRuntime.hpp"
 #include "DecoderExecutor.hpp"
 #include "NcclCollective.hpp"
+#include "ServingRuntime.hpp"
 #include "api_util.hpp"
 #include "tmc_cuda.h"
 
@@ -268,6 +270,61 @@ int tmc_decoder_attach_nccl(tmc_decoder *dec, const uint8_t *id, size_t nbytes, 
   auto coll = tensor::runtime::NcclCollective::create(id, world, rank, &err);
   if (!coll) return fail(TMC_ERR_UNAVAILABLE, err);
   return done(dec->ex->setCollective(coll));
+}
+
+int tmc_serving_run(tmc_decoder *dec, int count, const int32_t *prompt_offsets, const int32_t *prompt_tokens,
+                    const int32_t *decode_counts, const int32_t *arrival_ticks, int32_t *generated, double *ttft_us,
+                    double *finish_us, float *prefill_logits, float *decode_logits, tmc_serving_metrics *metrics,
+                    char *log, size_t log_size) {
+  if (!bind(dec) || count <= 0 || !prompt_offsets || !prompt_tokens || !decode_counts || !arrival_ticks ||
+      !generated)
+    return fail(TMC_ERR_INVALID, "bad argument");
+  std::vector<tensor::runtime::ServingRequestSpec> specs(count);
+  for (int i = 0; i < count; ++i) {
+    if (prompt_offsets[i + 1] < prompt_offsets[i] || decode_counts[i] < 0 || arrival_ticks[i] < 0)
+      return fail(TMC_ERR_INVALID, "request " + std::to_string(i) + ": bad offsets, decode count or arrival");
+    specs[i].id = "req" + std::to_string(i);
+    specs[i].promptTokenIds.assign(prompt_tokens + prompt_offsets[i], prompt_tokens + prompt_offsets[i + 1]);
+    specs[i].decodeTokenCount = static_cast<size_t>(decode_counts[i]);
+    specs[i].arrivalStep = static_cast<size_t>(arrival_ticks[i]);
+  }
+  tensor::runtime::ServingConfig config;
+  config.recordLogits = prefill_logits != nullptr || decode_logits != nullptr;
+  std::ostringstream text;
+  auto r = tensor::runtime::runContinuousBatch(*dec->ex, specs, config, text);
+  if (log != nullptr && log_size > 0) {
+    const std::string t = text.str();
+    const size_t n = std::min(log_size - 1, t.size());
+    std::memcpy(log, t.data(), n);
+    log[n] = '\0';
+  }
+  if (!r.passed) return done(r.errorMessage.empty() ? "serving failed" : r.errorMessage);
+  const size_t vL = static_cast<size_t>(dec->ex->localVocab());
+  size_t g = 0, pl = 0, dl = 0;
+  for (int i = 0; i < count; ++i) {
+    const auto &o = r.requests[i];
+    std::copy(o.generatedTokenIds.begin(), o.generatedTokenIds.end(), generated + g);
+    g += o.generatedTokenIds.size();
+    if (ttft_us) ttft_us[i] = o.timeToFirstTokenUs;
+    if (finish_us) finish_us[i] = o.finishUs;
+    if (prefill_logits) std::copy(o.prefillLogits.begin(), o.prefillLogits.end(), prefill_logits + pl * vL);
+    pl += specs[i].promptTokenIds.size();
+    if (decode_logits)
+      for (const auto &step : o.decodeLogits) {
+        std::copy(step.begin(), step.end(), decode_logits + dl * vL);
+        ++dl;
+      }
+  }
+  if (metrics) {
+    const auto &m = r.metrics;
+    *metrics = tmc_serving_metrics{m.totalTimeUs, m.tokensPerSecond, m.prefillGpuUs, m.decodeGpuUs,
+                                   m.schedulerOverheadUs, m.kvManagementOverheadUs, m.preemptionOverheadUs,
+                                   m.averageActiveBatchSize, m.maximumActiveBatchSize, m.preemptionCount,
+                                   m.resumeCount, m.peakPages, m.pageAllocationCount, m.pageReleaseCount,
+                                   m.decodeCommandSubmissions, m.decodedTokens, m.prefillTokens, m.ticks,
+                                   m.modelStorageBytes, m.kvPoolStorageBytes, m.activationStorageBytes};
+  }
+  return ok();
 }
 
 static_assert(sizeof(cudaIpcMemHandle_t) == TMC_EXCHANGE_HANDLE_BYTES, "IPC handle size");

@@ -313,6 +313,24 @@ _sig("tmc_decoder_attach_peers", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_i
 EXCHANGE_HANDLE_BYTES = 64
 
 
+class ServingMetrics(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_double) for n in (
+        "total_time_us", "tokens_per_second", "prefill_gpu_us", "decode_gpu_us", "scheduler_overhead_us",
+        "kv_management_overhead_us", "preemption_overhead_us", "average_active_batch")] + \
+        [(n, ctypes.c_uint64) for n in (
+            "max_active_batch", "preemptions", "resumes", "peak_pages", "page_allocations", "page_releases",
+            "decode_submissions", "decoded_tokens", "prefill_tokens", "ticks", "model_bytes", "kv_pool_bytes",
+            "activation_bytes")]
+
+    def as_dict(self):
+        return {name: getattr(self, name) for name, _ in self._fields_}
+
+
+_sig("tmc_serving_run", c_int, c_void_p, c_int, _I32P, _I32P, _I32P, _I32P, _I32P,
+     POINTER(ctypes.c_double), POINTER(ctypes.c_double), POINTER(c_float), POINTER(c_float),
+     POINTER(ServingMetrics), ctypes.c_char_p, c_size_t)
+
+
 def _i32(a):
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))
 
@@ -500,6 +518,47 @@ class Decoder:
         tensor-parallel reductions to the fused peer exchange."""
         blob = b"".join(handles)
         check(lib.tmc_decoder_attach_peers(self.handle, blob, EXCHANGE_HANDLE_BYTES, len(handles), rank))
+
+
+def serve(decoder: "Decoder", prompts, decode_counts, arrival_ticks=None, logits=False, log=False):
+    """Continuous batching over the decoder's slots (tmc_serving_run).
+
+    Returns a dict: tokens (list of int32 arrays, 1 + decode_count each),
+    ttft_us, finish_us (arrays), metrics (dict), and when asked prefill_logits /
+    decode_logits (lists of [len, local_vocab] arrays) and the scheduler log."""
+    n = len(prompts)
+    lens = [len(p) for p in prompts]
+    offsets = np.zeros(n + 1, dtype=np.int32)
+    offsets[1:] = np.cumsum(lens)
+    flat = _i32(np.concatenate([np.asarray(p, dtype=np.int32) for p in prompts]))
+    counts = _i32(decode_counts)
+    arrivals = _i32(arrival_ticks if arrival_ticks is not None else np.zeros(n))
+    generated = np.zeros(int(counts.sum()) + n, dtype=np.int32)
+    ttft = np.zeros(n, dtype=np.float64)
+    finish = np.zeros(n, dtype=np.float64)
+    vl = decoder.local_vocab
+    pl = np.zeros((int(offsets[-1]), vl), dtype=np.float32) if logits else None
+    dl = np.zeros((int(counts.sum()), vl), dtype=np.float32) if logits else None
+    metrics = ServingMetrics()
+    log_buf = ctypes.create_string_buffer(1 << 20) if log else None
+    dptr = lambda a: a.ctypes.data_as(POINTER(ctypes.c_double))
+    fptr = lambda a: a.ctypes.data_as(POINTER(c_float)) if a is not None else None
+    check(lib.tmc_serving_run(decoder.handle, n, offsets.ctypes.data_as(_I32P), flat.ctypes.data_as(_I32P),
+                              counts.ctypes.data_as(_I32P), arrivals.ctypes.data_as(_I32P),
+                              generated.ctypes.data_as(_I32P), dptr(ttft), dptr(finish), fptr(pl), fptr(dl),
+                              ctypes.byref(metrics), log_buf, (1 << 20) if log else 0))
+    out = {"tokens": [], "ttft_us": ttft, "finish_us": finish, "metrics": metrics.as_dict()}
+    g = 0
+    for c in counts:
+        out["tokens"].append(generated[g:g + 1 + int(c)])
+        g += 1 + int(c)
+    if logits:
+        out["prefill_logits"] = [pl[offsets[i]:offsets[i + 1]] for i in range(n)]
+        d0 = np.concatenate([[0], np.cumsum(counts)])
+        out["decode_logits"] = [dl[d0[i]:d0[i + 1]] for i in range(n)]
+    if log:
+        out["log"] = log_buf.value.decode()
+    return out
 
 
 def nccl_unique_id() -> bytes:

@@ -318,6 +318,38 @@ int tmc_decoder_exchange_handle(tmc_decoder *dec, uint8_t *handle, size_t nbytes
 int tmc_decoder_attach_peers(tmc_decoder *dec, const uint8_t *handles, size_t nbytes_each, int world,
                              int rank);
 
+/* ---- continuous batching (replaces runContinuousBatch,
+ * src/runtime/ServingRuntime.hpp:73-76, ServingRuntime.cpp:513-930) ----
+ * Serves `count` requests on a decoder's sequence slots (its weights loaded,
+ * every slot empty; page_size > 0 for a shared paged pool). Request i has the
+ * prompt prompt_tokens[prompt_offsets[i] .. prompt_offsets[i + 1]), asks for
+ * decode_counts[i] greedy tokens, and arrives at scheduler tick
+ * arrival_ticks[i]. Per tick: resume preempted requests that fit, admit
+ * arrived requests that fit (chunked prefill), preempt the active request with
+ * the most pages while the next token does not fit (KV snapshot to the host),
+ * one batched decode step, release finished requests, audit page isolation.
+ * Outputs in request order: generated tokens at offset i + sum_{j<i}
+ * decode_counts[j] (1 + decode_counts[i] each: the prefill's next token, then
+ * one per decode step), ttft_us[i] (arrival -> first token), finish_us[i]
+ * (arrival -> last token); prefill_logits [sum of prompt lengths, local vocab]
+ * and decode_logits [sum of decode_counts, local vocab] when not NULL. `log`
+ * (optional) receives the scheduler's event log, truncated to log_size. All
+ * tensor-parallel ranks must pass the same requests (decisions depend only on
+ * ticks and page counts). */
+typedef struct tmc_serving_metrics {
+  double total_time_us, tokens_per_second, prefill_gpu_us, decode_gpu_us;
+  double scheduler_overhead_us, kv_management_overhead_us, preemption_overhead_us;
+  double average_active_batch;
+  uint64_t max_active_batch, preemptions, resumes, peak_pages, page_allocations, page_releases;
+  uint64_t decode_submissions, decoded_tokens, prefill_tokens, ticks;
+  uint64_t model_bytes, kv_pool_bytes, activation_bytes;
+} tmc_serving_metrics;
+int tmc_serving_run(tmc_decoder *dec, int count, const int32_t *prompt_offsets,
+                    const int32_t *prompt_tokens, const int32_t *decode_counts,
+                    const int32_t *arrival_ticks, int32_t *generated, double *ttft_us,
+                    double *finish_us, float *prefill_logits, float *decode_logits,
+                    tmc_serving_metrics *metrics, char *log, size_t log_size);
+
 #ifdef __cplusplus
 }
 #endif
