@@ -32,6 +32,7 @@ namespace tmc {
 namespace {
 
 constexpr int kGemmThreads = 192;
+constexpr int kEpiChunk = 64;  // accumulator columns an epilogue thread holds at a time
 constexpr int kTileBytesA = kGemmTileRows * kGemmKBlock * 2;  // 16 KB
 
 template <int TN>
@@ -107,13 +108,13 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" :::
 // parameter read once (a generic per-element dispatch costs more than the
 // stores), the arithmetic shared with the GEMV (epilogue.cuh).
 template <int TN>
-__device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float (&v)[TN], int row, int lane,
-                                               int ew, int t, unsigned long long (*red_keys)[TN]) {
+__device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float (&v)[TN], int m0, int row, int lane,
+                                               int ew, int t, unsigned long long (*red_keys)[kEpiChunk]) {
   const int epi = p.epilogue;
-  const int M = p.M;
+  const int M = p.M - m0;  // tokens m0 .. m0 + TN - 1 of the launch's rows
   const bool in_range = row < p.N;
   if (epi == kEpiArgmax) {
-    float *y = p.y_f32;
+    float *y = p.y_f32 != nullptr ? p.y_f32 + (size_t)m0 * p.y_stride : nullptr;
     const long long ys = p.y_stride;
     const int voff = p.vocab_offset;
 #pragma unroll
@@ -129,17 +130,17 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
       if (lane == 0) red_keys[ew][m] = key;
     }
     epi_sync();
-    if (t < M) {
+    if (t < TN && t < M) {  // one thread per token of this chunk
       unsigned long long k = red_keys[0][t];
 #pragma unroll
       for (int e = 1; e < 4; ++e) k = red_keys[e][t] > k ? red_keys[e][t] : k;
-      if (k != 0ull) atomicMax(p.argmax_keys + t, k);
+      if (k != 0ull) atomicMax(p.argmax_keys + m0 + t, k);
     }
     epi_sync();
     return;
   }
   if (epi == kEpiSwiGLU) {
-    __half *y = p.y_f16 + (row >> 1);
+    __half *y = p.y_f16 + (size_t)m0 * p.y_stride + (row >> 1);
     const long long ys = p.y_stride;
     const bool store = !(lane & 1) && in_range;
 #pragma unroll
@@ -153,9 +154,9 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
   if (epi == kEpiQKV) {
     const int D = p.head_dim, q_rows = p.q_rows, kv_rows = p.kv_rows, cap = p.capacity;
     const int ps = p.page_size, pool_pages = p.pool_pages, tstride = p.table_stride;
-    const int *positions = p.positions, *trows = p.table_rows, *table = p.block_table;
+    const int *positions = p.positions + m0, *trows = p.table_rows + m0, *table = p.block_table;
     const float *rc = p.rope_cos + ((row % D) >> 1), *rs = p.rope_sin + ((row % D) >> 1);
-    __half *y = p.y_f16 + row;
+    __half *y = p.y_f16 + (size_t)m0 * p.y_stride + row;
     const long long ys = p.y_stride;
     const bool rope = row < q_rows + kv_rows, is_q = row < q_rows;
     int local = row - q_rows;
@@ -174,7 +175,7 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
       if (!store) continue;
       const int pos = positions[m];
       if (pos < 0 || pos >= cap) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m0 + m);
         continue;
       }
       const __half2 val = rope ? rope_pair_value(v[m], partner, rc[(size_t)pos * (D >> 1)], rs[(size_t)pos * (D >> 1)])
@@ -185,13 +186,13 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
       }
       const int lp = pos / ps, off = pos % ps;
       if (lp >= tstride) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m0 + m);
         continue;
       }
       const int page = table[(size_t)trows[m] * tstride + lp];
       if (page < 0 || page >= pool_pages) {
         report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
-                      page < 0 ? lp : page, m);
+                      page < 0 ? lp : page, m0 + m);
         continue;
       }
       *reinterpret_cast<__half2 *>(pool + (size_t)page * hkv * ps * D + head_off + (size_t)off * D) = val;
@@ -199,8 +200,8 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
     return;
   }
   if (epi == kEpiResidual || epi == kEpiF16) {
-    __half *y = p.y_f16 + row;
-    const __half *res = p.residual + row;
+    __half *y = p.y_f16 + (size_t)m0 * p.y_stride + row;
+    const __half *res = p.residual + (size_t)m0 * p.y_stride + row;
     const long long ys = p.y_stride;
     const bool residual = epi == kEpiResidual;
 #pragma unroll
@@ -214,7 +215,7 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
   if (epi == kEpiF32Partial && p.xchg.world > 0) {
     const int world = p.xchg.world, width = p.xchg.width;
     for (int q = 0; q < world; ++q) {
-      float *dst = peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0) + row;
+      float *dst = peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0 + m0) + row;
 #pragma unroll
       for (int m = 0; m < TN; ++m) {
         if (m >= M) break;
@@ -223,7 +224,7 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
     }
     return;
   }
-  float *y = p.y_f32 + row;
+  float *y = p.y_f32 + (size_t)m0 * p.y_stride + row;
   const long long ys = p.y_stride;
 #pragma unroll
   for (int m = 0; m < TN; ++m) {
@@ -248,7 +249,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *acc_full = empty + S;
   uint64_t *acc_empty = acc_full + C::kAcc;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + C::kAcc);
-  __shared__ unsigned long long red_keys[4][TN];
+  __shared__ unsigned long long red_keys[4][kEpiChunk];
   __shared__ int s_last, s_fail;
   __shared__ unsigned long long s_ready;
 
@@ -377,51 +378,69 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       epi_sync();
       if (s_fail) break;
       tc_fence_after();
-      float v[TN];
+      // The accumulator in chunks of CH columns (registers, not the stack).
+      constexpr int CH = TN < kEpiChunk ? TN : kEpiChunk;
+      const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TN);
+      const int row = tile * kGemmTileRows + r;
+      const int chunks = (p.M + CH - 1) / CH;
+      if (w.splits == 1) {
+#pragma unroll 1
+        for (int c = 0; c < chunks; ++c) {
+          float v[CH];
 #pragma unroll
-      for (int c = 0; c < TN / 16; ++c)
-        tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TN + c * 16), v + c * 16);
-      tmem_wait_ld();
+          for (int k = 0; k < CH / 16; ++k) tmem_ld16(tbase + (uint32_t)(c * CH + k * 16), v + k * 16);
+          tmem_wait_ld();
+          if (c == chunks - 1) {  // the accumulator is free for the MMA warp
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys);
+        }
+        continue;
+      }
+      float *part = w.ws + (size_t)(tile * w.splits + ks) * TN * kGemmTileRows;
+#pragma unroll 1
+      for (int c = 0; c < chunks; ++c) {
+        float v[CH];
+#pragma unroll
+        for (int k = 0; k < CH / 16; ++k) tmem_ld16(tbase + (uint32_t)(c * CH + k * 16), v + k * 16);
+        tmem_wait_ld();
+#pragma unroll
+        for (int m = 0; m < CH; ++m)
+          if (c * CH + m < p.M) part[(size_t)(c * CH + m) * kGemmTileRows + r] = v[m];
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      const int row = tile * kGemmTileRows + r;
-      if (w.splits > 1) {
-        float *part = w.ws + (size_t)(tile * w.splits + ks) * TN * kGemmTileRows;
-#pragma unroll
-        for (int m = 0; m < TN; ++m) {
-          if (m >= p.M) break;
-          part[(size_t)m * kGemmTileRows + r] = v[m];
-        }
-        __threadfence();
-        epi_sync();
-        if (t == 0) {
-          const unsigned int prev = atomicAdd(w.tile_counters + tile, 1u);
-          s_last = prev == (unsigned int)(w.splits - 1);
-          if (s_last) atomicExch(w.tile_counters + tile, 0u);
-        }
-        epi_sync();
-        if (!s_last) continue;
-        __threadfence();
-        // Sum the partials in split order; each split's values for all tokens
-        // of a chunk are requested together (one round trip per chunk).
-        constexpr int CH = TN < 64 ? TN : 64;
-#pragma unroll
-        for (int m = 0; m < TN; ++m) v[m] = 0.0f;
-#pragma unroll
-        for (int c0 = 0; c0 < TN; c0 += CH) {
-          for (int k2 = 0; k2 < w.splits; ++k2) {
-            const float *src = w.ws + (size_t)(tile * w.splits + k2) * TN * kGemmTileRows + r;
-            float tmp[CH];
-#pragma unroll
-            for (int m = 0; m < CH; ++m)
-              tmp[m] = (c0 + m < p.M) ? __ldcg(src + (size_t)(c0 + m) * kGemmTileRows) : 0.0f;
-#pragma unroll
-            for (int m = 0; m < CH; ++m) v[c0 + m] += tmp[m];
-          }
-        }
+      __threadfence();
+      epi_sync();
+      if (t == 0) {
+        const unsigned int prev = atomicAdd(w.tile_counters + tile, 1u);
+        s_last = prev == (unsigned int)(w.splits - 1);
+        if (s_last) atomicExch(w.tile_counters + tile, 0u);
       }
-      apply_epilogue<TN>(p, v, row, lane, ew, t, red_keys);
+      epi_sync();
+      if (!s_last) continue;
+      __threadfence();
+      // Sum the partials in split order; each split's values for a chunk of
+      // tokens are requested together (one round trip per chunk and split).
+#pragma unroll 1
+      for (int c = 0; c < chunks; ++c) {
+        float v[CH];
+#pragma unroll
+        for (int m = 0; m < CH; ++m) v[m] = 0.0f;
+        for (int k2 = 0; k2 < w.splits; ++k2) {
+          const float *src = w.ws + (size_t)(tile * w.splits + k2) * TN * kGemmTileRows + r;
+          float tmp[CH];
+#pragma unroll
+          for (int m = 0; m < CH; ++m)
+            tmp[m] = (c * CH + m < p.M) ? __ldcg(src + (size_t)(c * CH + m) * kGemmTileRows) : 0.0f;
+#pragma unroll
+          for (int m = 0; m < CH; ++m) v[m] += tmp[m];
+        }
+        apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys);
+      }
     }
     epi_sync();
     if (p.epilogue == kEpiF32Partial && p.xchg.world > 0 && t < 32) {

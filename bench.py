@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--batch", type=int, default=64, help="rows of the batched decode measurement (bs64)")
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--no-batch", action="store_true", help="skip the batched decode measurement")
+    ap.add_argument("--serving", type=int, default=0,
+                    help="also serve this many requests (C5: Poisson 20 req/s, prompts U[128,2048], "
+                         "outputs U[64,512], max batch 128; 1000 in the full config)")
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="TP reductions: peer exchange fused into the kernels, or NCCL allreduce")
     return ap.parse_args()
@@ -257,6 +260,14 @@ def run_ours(args, world, rank, local):
         dec.close()  # release the bs1 model before building the batched one
         batched = measure_batched(args, world, rank, local, dist, barrier, max_over_ranks, hbm, peak_kind)
 
+    serving = None
+    if args.serving > 0:
+        if not args.no_batch:
+            tick_s = batched["ms_per_step"] * 1e-3
+        else:
+            tick_s = 0.01
+        serving = measure_serving(args, world, rank, local, dist, barrier, hbm, tick_s)
+
     cpu = None
     if rank == 0 and world == 1:
         from oracle import cpu_baseline
@@ -288,6 +299,7 @@ def run_ours(args, world, rank, local):
             "roofline": roofline,
             "kernels": kernels,
             "bs64": batched,
+            "serving": serving,
             "cpu_baseline": cpu,
             "clocks": clk,
         })
@@ -296,6 +308,73 @@ def run_ours(args, world, rank, local):
         dec.close()
         dist.destroy_process_group()
     return 0
+
+
+def measure_serving(args, world, rank, local, dist, barrier, hbm, tick_s):
+    """C5: continuous batching (tmc_serving_run) of `args.serving` seeded
+    requests: prompts ~U[128, 2048] random ids, outputs ~U[64, 512] greedy
+    tokens, Poisson arrivals at 20 req/s mapped onto scheduler ticks of about
+    one decode step (`tick_s`, measured), max batch 128, KV page pool = 80% of
+    the HBM left after the weights. Reports output tok/s (decoded tokens / wall
+    time of the whole run), TTFT and TPOT percentiles, and the decode steps'
+    fraction of the HBM roofline (weights + KV bytes of every step / their
+    device time)."""
+    import numpy as np
+    import torch
+
+    import tmc_cuda
+    n = args.serving
+    rng = np.random.default_rng(0)
+    prompts = [rng.integers(0, CFG["vocab"], int(rng.integers(128, 2049))).astype(np.int32) for _ in range(n)]
+    outputs = [int(rng.integers(64, 513)) for _ in range(n)]
+    arrival_s = np.cumsum(rng.exponential(1.0 / 20.0, n))
+    arrivals = np.floor(arrival_s / max(tick_s, 1e-4)).astype(np.int32)
+    capacity = 2048 + 512 + 16
+    rt = tmc_cuda.Runtime(local)
+    free, _ = torch.cuda.mem_get_info(local)
+    weights = 2 * (CFG["vocab"] * CFG["hidden"] * (1 + 1.0 / world)
+                   + args.layers * (CFG["hidden"] * (CFG["heads"] + 2 * CFG["kv_heads"]) * 128
+                                    + CFG["hidden"] * CFG["heads"] * 128 + 3 * CFG["hidden"] * CFG["intermediate"])
+                   / world)
+    page_bytes = 2 * 2 * (CFG["kv_heads"] // world) * 16 * 128 * args.layers
+    pool_pages = int(0.8 * (free - weights - (4 << 30)) / page_bytes)
+    dec = tmc_cuda.Decoder(rt, CFG["hidden"], CFG["heads"], CFG["intermediate"], CFG["vocab"], args.layers,
+                           capacity, kv_heads=CFG["kv_heads"], epsilon=CFG["epsilon"],
+                           rope_theta=CFG["rope_theta"], max_rows=128, max_slots=128, page_size=16,
+                           pool_pages=pool_pages, tp_rank=rank, tp_size=world)
+    if world > 1 and args.collective == "p2p":
+        handles = [None] * world
+        dist.all_gather_object(handles, dec.exchange_handle())
+        dec.attach_peers(handles, rank)
+    elif world > 1:
+        uid = [tmc_cuda.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        dec.attach_nccl(uid[0], world, rank)
+    dec.init_random(seed=0, std=0.02)
+    barrier()
+    served = tmc_cuda.serve(dec, prompts, outputs, arrivals)
+    barrier()
+    m = served["metrics"]
+    ttft = served["ttft_us"] / 1e3
+    tpot = (served["finish_us"] - served["ttft_us"]) / np.maximum(1, np.array(outputs)) / 1e3
+    weight_step = dec.step_bytes([])
+    kv_row = 2 * 2 * (CFG["kv_heads"] // world) * 128 * args.layers
+    kv_bytes = sum(kv_row * (len(p) * o + o * (o + 1) // 2) for p, o in zip(prompts, outputs))
+    step_bytes = m["decode_submissions"] * weight_step + kv_bytes
+    frac = step_bytes / (m["decode_gpu_us"] * 1e-6) / 1e9 / hbm if m["decode_gpu_us"] else None
+    result = {"requests": n, "value": m["decoded_tokens"] / (m["total_time_us"] * 1e-6), "unit": "output tok/s",
+              "ttft_ms": {"p50": float(np.percentile(ttft, 50)), "p90": float(np.percentile(ttft, 90))},
+              "tpot_ms": {"p50": float(np.percentile(tpot, 50)), "p90": float(np.percentile(tpot, 90))},
+              "decode_step_roofline_frac": frac, "average_active_batch": m["average_active_batch"],
+              "max_active_batch": m["max_active_batch"], "preemptions": m["preemptions"],
+              "decode_steps": m["decode_submissions"], "prefill_tokens": m["prefill_tokens"],
+              "decoded_tokens": m["decoded_tokens"], "wall_s": m["total_time_us"] * 1e-6,
+              "pool_pages": pool_pages, "tick_ms": tick_s * 1e3,
+              "config": {"arrivals": "Poisson 20 req/s mapped to ticks", "prompts": "U[128,2048]",
+                         "outputs": "U[64,512]", "max_batch": 128, "page_budget": "80% of free HBM",
+                         "parallelism": f"tp{world}"}}
+    dec.close()
+    return result
 
 
 def measure_batched(args, world, rank, local, dist, barrier, max_over_ranks, hbm, peak_kind):

@@ -46,7 +46,7 @@ def serving_close(got, ref, what):
     assert not bad.any(), f"{what}: {int(bad.sum())} logits outside atol = rtol = 2e-2"
 
 
-@pytest.mark.parametrize("batch", [12, 24])
+@pytest.mark.parametrize("batch", [12, 24, 72])  # 72: two 64-column epilogue chunks
 def test_batched_decode_matches_sequential(rt, batch):
     g, meta = load("decoder_wide_fp16.npz")
     full = g["prefill.tokens"][0]
