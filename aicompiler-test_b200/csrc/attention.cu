@@ -596,8 +596,12 @@ cudaError_t launch_instance(const AttentionParams &p, cudaStream_t stream, bool 
   const int splits = p.max_splits < Cfg<D, G>::kMaxSplits ? p.max_splits : Cfg<D, G>::kMaxSplits;
   int cluster = p.cluster;
   if (cluster <= 0) {
+    // Clusters pay off for short splits (latency-bound decode, where the
+    // merge is a large part of a CTA's life); with long splits (min_chunk >=
+    // 512) rows shorter than the cluster would leave idle CTAs holding slots
+    // at the cluster barrier, so those launches merge through the ticket.
     cluster = 1;
-    while (cluster < splits && cluster < limit) cluster *= 2;
+    while (p.min_chunk < 512 && cluster < splits && cluster < limit) cluster *= 2;
   } else if (cluster > limit) {
     return cudaErrorInvalidValue;
   }

@@ -69,8 +69,10 @@ def case_gemv(rt, a):
 def case_attention(rt, a):
     import tmc_cuda
     rng = np.random.default_rng(0)
-    pages_per_seq = (a.ctx + a.page - 1) // a.page
-    pool_pages = a.rows * pages_per_seq + 8
+    # contexts: all a.ctx, or ~U[a.ctx, a.ctx_max] when --ctx-max is given
+    ctx = np.full(a.rows, a.ctx) if a.ctx_max <= a.ctx else rng.integers(a.ctx, a.ctx_max + 1, a.rows)
+    pages_per_seq = int((ctx.max() + a.page - 1) // a.page)
+    pool_pages = max(a.rows * pages_per_seq + 8, a.pool_pages)
     kp = rt.buffer(pool_pages * a.hkv * a.page * a.d, tmc_cuda.F16)
     vp = rt.buffer(pool_pages * a.hkv * a.page * a.d, tmc_cuda.F16)
     tmc_cuda.fill_normal_f16(rt, kp, 2, 0.0, 1.0)
@@ -78,7 +80,7 @@ def case_attention(rt, a):
     perm = rng.permutation(pool_pages)[: a.rows * pages_per_seq].astype(np.int32)
     table = rt.upload(perm.reshape(a.rows, pages_per_seq))
     trows = rt.upload(np.arange(a.rows, dtype=np.int32))
-    pos = rt.upload(np.full(a.rows, a.ctx - 1, dtype=np.int32))
+    pos = rt.upload((ctx - 1).astype(np.int32))
     q = rt.upload(rng.standard_normal((a.rows, a.hq, a.d)).astype(np.float16))
     out = rt.buffer(a.rows * a.hq * a.d, tmc_cuda.F16)
     # The decoder's split policy (DecoderExecutor.cpp, attention launch).
@@ -88,19 +90,22 @@ def case_attention(rt, a):
         splits = 1
         while splits < 16 and 2 * splits * a.rows * a.hkv <= 16 * sms:
             splits *= 2
+    if a.splits > 0:
+        splits = a.splits
     ws = rt.buffer(max(tmc_cuda.attention_workspace_bytes(a.rows, a.hq, a.hkv, a.d, splits) // 4, 1),
                    tmc_cuda.F32)
     counters = rt.upload(np.zeros(a.rows * a.hkv, dtype=np.int32))
 
     def launch():
         tmc_cuda.paged_attention_f16(rt, q, out, kp, vp, table, pages_per_seq, trows, pos, a.rows, a.hq,
-                                     a.hkv, a.d, a.page, pool_pages, pages_per_seq * a.page, splits, 64, ws,
-                                     counters)
+                                     a.hkv, a.d, a.page, pool_pages, pages_per_seq * a.page, splits,
+                                     a.min_chunk, ws, counters)
 
     us = _time(rt, launch, a.warmup, a.reps)
-    nbytes = 2 * 2 * a.rows * a.ctx * a.hkv * a.d + 2 * 2 * a.rows * a.hq * a.d
-    return {"kernel": "attention_kernel", "rows": a.rows, "ctx": a.ctx, "hq": a.hq, "hkv": a.hkv, "d": a.d,
-            "splits": splits, "us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
+    nbytes = 2 * 2 * int(ctx.sum()) * a.hkv * a.d + 2 * 2 * a.rows * a.hq * a.d
+    return {"kernel": "attention_kernel", "rows": a.rows, "ctx": a.ctx, "ctx_max": a.ctx_max, "hq": a.hq,
+            "hkv": a.hkv, "d": a.d, "splits": splits, "min_chunk": a.min_chunk, "us": us, "bytes": nbytes,
+            "gbs": nbytes / us / 1e3}
 
 
 def main(argv=None):
@@ -114,6 +119,10 @@ def main(argv=None):
     ap.add_argument("--hkv", type=int, default=8)
     ap.add_argument("--d", type=int, default=128)
     ap.add_argument("--page", type=int, default=16)
+    ap.add_argument("--ctx-max", type=int, default=0, help="contexts ~U[ctx, ctx_max] (attention)")
+    ap.add_argument("--splits", type=int, default=0, help="attention max splits (0: the decoder's policy)")
+    ap.add_argument("--min-chunk", type=int, default=64, help="attention positions per split at least")
+    ap.add_argument("--pool-pages", type=int, default=0, help="attention page pool size (at least what fits)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--reps", type=int, default=20)
     a = ap.parse_args(argv)

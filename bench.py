@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=64, help="rows of the batched decode measurement (bs64)")
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--no-batch", action="store_true", help="skip the batched decode measurement")
+    ap.add_argument("--no-c4", action="store_true", help="skip the C4 paged-attention measurement")
     ap.add_argument("--serving", type=int, default=0,
                     help="also serve this many requests (C5: Poisson 20 req/s, prompts U[128,2048], "
                          "outputs U[64,512], max batch 128; 1000 in the full config)")
@@ -260,6 +261,10 @@ def run_ours(args, world, rank, local):
         dec.close()  # release the bs1 model before building the batched one
         batched = measure_batched(args, world, rank, local, dist, barrier, max_over_ranks, hbm, peak_kind)
 
+    c4 = None
+    if not args.no_c4:
+        c4 = measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind)
+
     serving = None
     if args.serving > 0:
         if not args.no_batch:
@@ -299,6 +304,7 @@ def run_ours(args, world, rank, local):
             "roofline": roofline,
             "kernels": kernels,
             "bs64": batched,
+            "c4": c4,
             "serving": serving,
             "cpu_baseline": cpu,
             "clocks": clk,
@@ -308,6 +314,71 @@ def run_ours(args, world, rank, local):
         dec.close()
         dist.destroy_process_group()
     return 0
+
+
+def measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind):
+    """C4: block-table GQA decode attention, 64 sequences with contexts ~U[128, 8192],
+    32 q / 8 kv heads x 128 (sharded by KV head across the ranks), fp16 K/V ~N(0,1)
+    in 16-token pages, each block table a random draw of distinct pages from a
+    2^17-page pool (2 x 4.29 GB at TP1), one fp16 query per sequence.
+    value = algorithmic bytes (4096 x sum(ctx) + q + out) / device time, max over
+    ranks; K/V (> L2) are re-read from HBM by every launch."""
+    import numpy as np
+    import torch
+
+    import tmc_cuda
+    rows, hq, hkv, d, page = 64, 32 // world, 8 // world, 128, 16
+    pool_pages = 1 << 17
+    rng = np.random.default_rng(4)
+    ctx = rng.integers(128, 8193, rows)
+    pages_per = (ctx + page - 1) // page
+    stride = int(pages_per.max())
+    perm = rng.permutation(pool_pages)[: int(pages_per.sum())].astype(np.int32)
+    table = np.full((rows, stride), -1, dtype=np.int32)
+    off = 0
+    for r in range(rows):
+        table[r, : pages_per[r]] = perm[off: off + pages_per[r]]
+        off += pages_per[r]
+    rt = tmc_cuda.Runtime(local)
+    kp = rt.buffer(pool_pages * hkv * page * d, tmc_cuda.F16)
+    vp = rt.buffer(pool_pages * hkv * page * d, tmc_cuda.F16)
+    tmc_cuda.fill_normal_f16(rt, kp, 10 + rank, 0.0, 1.0)
+    tmc_cuda.fill_normal_f16(rt, vp, 20 + rank, 0.0, 1.0)
+    tb, trows = rt.upload(table), rt.upload(np.arange(rows, dtype=np.int32))
+    pos = rt.upload((ctx - 1).astype(np.int32))
+    q = rt.upload(rng.standard_normal((rows, hq, d)).astype(np.float16))
+    out = rt.buffer(rows * hq * d, tmc_cuda.F16)
+    max_splits, min_chunk = 8, 1024  # long splits amortise each CTA's setup and merge
+    ws = rt.buffer(tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, max_splits) // 4 + 1, tmc_cuda.F32)
+    counters = rt.upload(np.zeros(rows * hkv, dtype=np.int32))
+
+    def launch():
+        tmc_cuda.paged_attention_f16(rt, q, out, kp, vp, tb, stride, trows, pos, rows, hq, hkv, d, page,
+                                     pool_pages, stride * page, max_splits, min_chunk, ws, counters)
+
+    for _ in range(3):
+        launch()
+    rt.synchronize()
+    stream = torch.cuda.ExternalStream(rt.stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    barrier()
+    e0.record(stream)
+    for _ in range(reps):
+        launch()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    rt.synchronize()
+    us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / reps)
+    nbytes = (4096 * int(ctx.sum()) + 2 * rows * 32 * d * 2) + 0.0  # whole job (all KV heads)
+    rt.close()
+    return {"metric": "paged GQA attention HBM GB/s", "value": nbytes / us / 1e3, "unit": "GB/s",
+            "us_per_call": us, "bytes_per_call": nbytes, "sum_ctx": int(ctx.sum()),
+            "frac_of_peak": nbytes / us / 1e3 / (hbm * world), "peak_gbs": hbm * world,
+            "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
+            "config": {"sequences": rows, "ctx": "U[128,8192]", "heads": "32q/8kv x 128", "page": page,
+                       "pool_pages": pool_pages, "max_splits": max_splits, "min_chunk": min_chunk,
+                       "parallelism": f"kv-head shards x{world}"}}
 
 
 def measure_serving(args, world, rank, local, dist, barrier, hbm, tick_s):
