@@ -812,6 +812,13 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       a.counters = static_cast<unsigned int *>(attnCounters_->data());
       a.status = status;
       a.trace = traceSink(l, kind);
+      if ((D == 64 || D == 128) && pageSize_ % 16 == 0) {
+        // 16-position page boxes through tensor maps over the pools.
+        std::string err;
+        a.k_map = tensorMap(L.kPool->data(), poolPages_ * hkvL_ * pageSize_, D, 16, &err);
+        a.v_map = a.k_map ? tensorMap(L.vPool->data(), poolPages_ * hkvL_ * pageSize_, D, 16, &err) : nullptr;
+        if (!a.v_map) return "attention: " + err;
+      }
       if ((e = tmc::launch_attention(a, s, pdl)) != cudaSuccess) return cudaText("attention", e);
 
       return {};

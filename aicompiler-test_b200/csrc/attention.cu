@@ -59,13 +59,17 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
-template <int D, int G>
+// BOX: K/V tiles arrive as 16-position page boxes through TMA tensor maps
+// (128-byte swizzle, rows of 64 dims per half, no padding); otherwise one
+// bulk copy per position row into padded rows.
+template <int D, int G, bool BOX>
 struct Cfg {
   static constexpr int kWarpsPerCta = kThreads / 32;     // 4
   static constexpr int kRowsPerWarp = 16;                // positions per warp per tile
   static constexpr int T = kWarpsPerCta * kRowsPerWarp;  // 64 positions per tile
-  static constexpr int kRow = D + 8;                     // padded row (halves): conflict-free ldmatrix
+  static constexpr int kRow = BOX ? D : D + 8;           // padded row (halves): conflict-free ldmatrix
   static constexpr size_t kStageBytes = (size_t)T * kRow * 2;  // one of K or V per stage
+  static constexpr size_t kAlign = BOX ? 1024 : 0;       // swizzled stages start on 1024 bytes
   static constexpr int kStages = 2;
   static constexpr int kMaxSplits = 64;
   static constexpr int kKSteps = D / 16;                 // QK^T k-steps
@@ -73,7 +77,7 @@ struct Cfg {
   __host__ __device__ static constexpr size_t merge_bytes() { return (size_t)kWarpsPerCta * (G * D + 2 * G) * 4; }
   __host__ __device__ static constexpr size_t smem_bytes() {
     const size_t stages = (size_t)kStages * 2 * kStageBytes;
-    return (stages > merge_bytes() ? stages : merge_bytes())  // K/V ring, reused for the warp merge
+    return kAlign + (stages > merge_bytes() ? stages : merge_bytes())  // K/V ring, reused for the warp merge
            + (size_t)kStages * T * 4                            // sValid
            + (size_t)kMaxSplits * G * 4 * 2                     // combine weights (m then l)
            + (size_t)2 * kStages * 8 + 32;                      // full/empty barriers (+align)
@@ -115,12 +119,18 @@ __device__ __forceinline__ void cluster_sync() {
 // cluster merge through distributed shared memory. Only when a (row, KV head)
 // spans several clusters do the cluster results meet in the global workspace
 // (atomic ticket, last CTA combines).
-template <int D, int G>
-__global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionParams p) {
-  using C = Cfg<D, G>;
+template <int D, int G, bool BOX>
+__global__ void __launch_bounds__(kThreads)
+    attention_kernel(const __grid_constant__ AttentionParams p, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap) {
+  using C = Cfg<D, G, BOX>;
   constexpr int T = C::T, S = C::kStages, ROW = C::kRow;
   static_assert(G <= 8 && D % 16 == 0, "attention tile shape");
-  extern __shared__ __align__(128) unsigned char smem[];
+  static_assert(!BOX || D % 64 == 0, "page boxes are 64-dim halves");
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char *smem = BOX ? reinterpret_cast<unsigned char *>(
+                                  (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023))
+                            : smem_raw;
   __half *sK = reinterpret_cast<__half *>(smem);
   __half *sV = sK + S * T * ROW;
   const size_t ring = (size_t)S * 2 * C::kStageBytes;
@@ -230,7 +240,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
         }
       }
       sValid[stage * T + lp] = v;
-      if (!v) {
+      if (!BOX && !v) {
         // No copy lands in this row: zero its V (P = 0 there, and 0 * NaN
         // from stale shared memory would poison the P.V product).
         uint4 *vrow = reinterpret_cast<uint4 *>(sV + ((size_t)stage * T + lp) * ROW);
@@ -240,7 +250,16 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
       nvalid += __popc(__ballot_sync(0xffffffffu, v));
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(nvalid) * D * 2 * 2);
+    if (BOX) {
+      // One 16-position box per row group whose first position is valid (a
+      // group lies in one page: group starts and page sizes are multiples of 16).
+      int boxes = 0;
+#pragma unroll
+      for (int w = 0; w < C::kWarpsPerCta; ++w) boxes += sValid[stage * T + w * 16] ? 1 : 0;
+      if (lane == 0) mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(boxes) * 16 * D * 2 * 2);
+    } else if (lane == 0) {
+      mbar_arrive_expect_tx(&full[stage], static_cast<uint32_t>(nvalid) * D * 2 * 2);
+    }
     __syncwarp();
   };
   // Warp 0: one bulk copy per valid row with position in [lo, hi) into the
@@ -248,28 +267,73 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
   auto copy = [&](int t, int lo, int hi) {
     const int stage = t % S;
     const int p0 = begin + t * T;
+    if constexpr (BOX) {
+      // Lane w issues group w's box (both 64-dim halves of K and of V) if its
+      // valid positions all fall in [lo, hi): groups holding positions the
+      // producer kernel still writes are requested after its completion.
+      if (lane < C::kWarpsPerCta) {
+        const int w = lane, g0 = p0 + w * 16;
+        const int g_end = min(g0 + 16, end);
+        if (g0 < end && sValid[stage * T + w * 16] && g0 >= lo && g_end <= hi) {
+          const int page = page_of(g0 / p.page_size);
+          const int y = (page * p.hkv + kvh) * p.page_size + g0 % p.page_size;
 #pragma unroll
-    for (int j = 0; j < T / 32; ++j) {
-      const int lp = lane + 32 * j;
-      const int position = p0 + lp;
-      if (position < lo || position >= hi || position >= end || !sValid[stage * T + lp]) continue;
-      const int page = page_of(position / p.page_size);
-      const size_t off = (((size_t)page * p.hkv + kvh) * p.page_size + position % p.page_size) * D;
-      bulk_g2s(sK + ((size_t)stage * T + lp) * ROW, p.k_pool + off, D * 2, &full[stage]);
-      bulk_g2s(sV + ((size_t)stage * T + lp) * ROW, p.v_pool + off, D * 2, &full[stage]);
+          for (int h = 0; h < D / 64; ++h) {
+            tma_load_2d(reinterpret_cast<unsigned char *>(sK) + (size_t)stage * C::kStageBytes + h * T * 128 + w * 16 * 128,
+                        &kmap, h * 64, y, &full[stage]);
+            tma_load_2d(reinterpret_cast<unsigned char *>(sV) + (size_t)stage * C::kStageBytes + h * T * 128 + w * 16 * 128,
+                        &vmap, h * 64, y, &full[stage]);
+          }
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < T / 32; ++j) {
+        const int lp = lane + 32 * j;
+        const int position = p0 + lp;
+        if (position < lo || position >= hi || position >= end || !sValid[stage * T + lp]) continue;
+        const int page = page_of(position / p.page_size);
+        const size_t off = (((size_t)page * p.hkv + kvh) * p.page_size + position % p.page_size) * D;
+        bulk_g2s(sK + ((size_t)stage * T + lp) * ROW, p.k_pool + off, D * 2, &full[stage]);
+        bulk_g2s(sV + ((size_t)stage * T + lp) * ROW, p.v_pool + off, D * 2, &full[stage]);
+      }
     }
   };
 
   const int first = ntiles < S ? ntiles : S;
+  // Boxes (BOX) are all-or-nothing: a box holding any position at or past
+  // `fresh` waits for the producer kernel.
+  const int early_hi = fresh;
   if (warp == 0) {
     for (int t = 0; t < first; ++t) {
       arm(t);
-      copy(t, begin, fresh);
+      copy(t, begin, early_hi);
     }
   }
   pdl_wait();
   if (warp == 0) {
-    for (int t = 0; t < first; ++t) copy(t, fresh, end);
+    for (int t = 0; t < first; ++t) {
+      if (BOX) {
+        // the boxes not issued early: those ending past `fresh`
+        const int stage = t % S, p0 = begin + t * T;
+        if (lane < C::kWarpsPerCta) {
+          const int w = lane, g0 = p0 + w * 16, g_end = min(g0 + 16, end);
+          if (g0 < end && sValid[stage * T + w * 16] && g_end > early_hi) {
+            const int page = page_of(g0 / p.page_size);
+            const int y = (page * p.hkv + kvh) * p.page_size + g0 % p.page_size;
+#pragma unroll
+            for (int h = 0; h < D / 64; ++h) {
+              tma_load_2d(reinterpret_cast<unsigned char *>(sK) + (size_t)stage * C::kStageBytes + h * T * 128 + w * 16 * 128,
+                          &kmap, h * 64, y, &full[stage]);
+              tma_load_2d(reinterpret_cast<unsigned char *>(sV) + (size_t)stage * C::kStageBytes + h * T * 128 + w * 16 * 128,
+                          &vmap, h * 64, y, &full[stage]);
+            }
+          }
+        }
+      } else {
+        copy(t, fresh, end);
+      }
+    }
   }
   // Query A fragments: rows = the G query heads of this KV head (rows >= G are
   // zero), columns = head dimensions; fp16 values are exact.
@@ -310,6 +374,27 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
     const __half *k = sK + ((size_t)stage * T + r0) * ROW;
     const __half *v = sV + ((size_t)stage * T + r0) * ROW;
     const int *valid = sValid + stage * T + r0;
+    // BOX: a whole box landed; rows of positions past `end` (or of a missing
+    // page) hold stale values: zero their V rows (P is 0 there, 0 * NaN is not).
+    bool zeroed = false;
+    if (BOX && p0 < end) {
+      const int lp = lane & 15;
+      const bool bad = !(p0 + lp < end && valid[lp]);
+      if (__any_sync(0xffffffffu, bad)) {
+        unsigned char *vs = reinterpret_cast<unsigned char *>(sV) + (size_t)stage * C::kStageBytes;
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) {
+          // lanes 0-15 and 16-31 take the two 64-byte halves of row r0 + lp
+          uint4 *dst = reinterpret_cast<uint4 *>(vs + h * T * 128 + (r0 + lp) * 128 + (lane >> 4) * 64);
+          if (bad) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        __syncwarp();
+        zeroed = true;
+      }
+    }
     if (p0 < end) {
       // Scores S[16 heads x 16 positions] as two n-tiles of 8 positions.
       float sc[2][4];
@@ -320,7 +405,15 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
         for (int kk = 0; kk < C::kKSteps; ++kk) {
           uint32_t b0, b1;
           // matrices: rows = positions nt*8..+7, columns = dims kk*16..+7 and +8..+15
-          const __half *addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
+          const __half *addr;
+          if (BOX) {
+            const int R = r0 + nt * 8 + (lane & 7), d0 = kk * 16 + ((lane >> 3) & 1) * 8;
+            addr = reinterpret_cast<const __half *>(reinterpret_cast<const unsigned char *>(sK) +
+                                                    (size_t)stage * C::kStageBytes + (d0 >> 6) * T * 128 + R * 128 +
+                                                    ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
+          } else {
+            addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
+          }
           ldmatrix_x2(b0, b1, addr);
           mma_16816(sc[nt], qa[kk], b0, b1);
         }
@@ -376,12 +469,21 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
         acc[dt][1] *= rescale;
         uint32_t b0, b1;
         // matrices (transposed on load): rows = positions 0..7 and 8..15, columns = dims dt*8..+7
-        const __half *addr = v + (size_t)(lane & 15) * ROW + dt * 8;
+        const __half *addr;
+        if (BOX) {
+          const int R = r0 + (lane & 15), d0 = dt * 8;
+          addr = reinterpret_cast<const __half *>(reinterpret_cast<const unsigned char *>(sV) +
+                                                  (size_t)stage * C::kStageBytes + (d0 >> 6) * T * 128 + R * 128 +
+                                                  ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
+        } else {
+          addr = v + (size_t)(lane & 15) * ROW + dt * 8;
+        }
         ldmatrix_x2_trans(b0, b1, addr);
         mma_16816(acc[dt], pl, b0, b1);
         mma_16816(acc[dt], pa, b0, b1);
       }
     }
+    if (zeroed) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before TMA refills
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);
     if (warp == 0 && t + S < ntiles) {
@@ -550,10 +652,10 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(const AttentionPara
   (void)failed;
 }
 
-template <int D, int G>
+template <int D, int G, bool BOX>
 cudaError_t launch_instance(const AttentionParams &p, cudaStream_t stream, bool pdl) {
-  auto kernel = attention_kernel<D, G>;
-  const size_t smem = Cfg<D, G>::smem_bytes();
+  auto kernel = attention_kernel<D, G, BOX>;
+  const size_t smem = Cfg<D, G, BOX>::smem_bytes();
   static std::mutex mu;
   static std::unordered_map<int, int> cluster_limit;  // per device, 0 = not configured
   int dev = 0;
@@ -593,7 +695,7 @@ cudaError_t launch_instance(const AttentionParams &p, cudaStream_t stream, bool 
   }
   cudaLaunchConfig_t cfg = {};
   // Clusters along the splits; the grid covers whole clusters.
-  const int splits = p.max_splits < Cfg<D, G>::kMaxSplits ? p.max_splits : Cfg<D, G>::kMaxSplits;
+  const int splits = p.max_splits < Cfg<D, G, BOX>::kMaxSplits ? p.max_splits : Cfg<D, G, BOX>::kMaxSplits;
   int cluster = p.cluster;
   if (cluster <= 0) {
     // Clusters pay off for short splits (latency-bound decode, where the
@@ -623,16 +725,21 @@ cudaError_t launch_instance(const AttentionParams &p, cudaStream_t stream, bool 
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  return cudaLaunchKernelEx(&cfg, kernel, p);
+  CUtensorMap km{}, vm{};
+  if (BOX) {
+    km = *p.k_map;
+    vm = *p.v_map;
+  }
+  return cudaLaunchKernelEx(&cfg, kernel, p, km, vm);
 }
 
-template <int D>
+template <int D, bool BOX>
 cudaError_t dispatch_g(const AttentionParams &p, cudaStream_t stream, bool pdl, int g) {
   switch (g) {
-    case 1: return launch_instance<D, 1>(p, stream, pdl);
-    case 2: return launch_instance<D, 2>(p, stream, pdl);
-    case 4: return launch_instance<D, 4>(p, stream, pdl);
-    case 8: return launch_instance<D, 8>(p, stream, pdl);
+    case 1: return launch_instance<D, 1, BOX>(p, stream, pdl);
+    case 2: return launch_instance<D, 2, BOX>(p, stream, pdl);
+    case 4: return launch_instance<D, 4, BOX>(p, stream, pdl);
+    case 8: return launch_instance<D, 8, BOX>(p, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -652,11 +759,14 @@ cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool
       p.cluster < 0 || p.cluster > kMaxCluster || (p.cluster & (p.cluster - 1)) != 0)
     return cudaErrorInvalidValue;
   const int g = p.hq / p.hkv;
+  // Page boxes through tensor maps when the caller built them and the shape
+  // allows (64-dim halves, pages of whole 16-position groups).
+  const bool box = p.k_map != nullptr && p.v_map != nullptr && p.page_size % 16 == 0;
   switch (p.head_dim) {
-    case 16: return dispatch_g<16>(p, stream, pdl, g);
-    case 32: return dispatch_g<32>(p, stream, pdl, g);
-    case 64: return dispatch_g<64>(p, stream, pdl, g);
-    case 128: return dispatch_g<128>(p, stream, pdl, g);
+    case 16: return dispatch_g<16, false>(p, stream, pdl, g);
+    case 32: return dispatch_g<32, false>(p, stream, pdl, g);
+    case 64: return box ? dispatch_g<64, true>(p, stream, pdl, g) : dispatch_g<64, false>(p, stream, pdl, g);
+    case 128: return box ? dispatch_g<128, true>(p, stream, pdl, g) : dispatch_g<128, false>(p, stream, pdl, g);
     default: return cudaErrorInvalidValue;
   }
 }

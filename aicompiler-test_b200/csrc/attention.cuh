@@ -13,6 +13,8 @@
 // table row b = {b}.
 #pragma once
 
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace tmc {
@@ -45,6 +47,13 @@ struct AttentionParams {
   unsigned int *counters;  // [rows, hkv], zero between launches
   TmcDeviceStatus *status;
   TraceSink trace;         // optional timeline (records == nullptr: off)
+  // Optional (host pointers, copied into the launch): tensor maps of k_pool and
+  // v_pool viewed as [pool_pages * hkv * page_size rows, head_dim] fp16 with a
+  // [16 rows, 64 columns] box and 128-byte swizzle (make_tensor_map_f16 with
+  // box_rows 16). With them, head_dim 64 or 128 and page_size % 16 == 0, K/V
+  // tiles arrive as 16-position page boxes (8x fewer copies than per row).
+  const CUtensorMap *k_map;
+  const CUtensorMap *v_map;
 };
 
 // Workspace bytes needed for a launch with these dimensions.

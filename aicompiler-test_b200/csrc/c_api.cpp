@@ -327,6 +327,16 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
   p.ws_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + acc_bytes);
   p.counters = counters;
   p.status = static_cast<tmc::TmcDeviceStatus *>(status);
+  CUtensorMap km, vm;
+  if ((d == 64 || d == 128) && page_size % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(k_pool) & 15) == 0 && (reinterpret_cast<uintptr_t>(v_pool) & 15) == 0) {
+    const uint64_t rows = (uint64_t)pool_pages * hkv * page_size;
+    if (tmc::make_tensor_map_f16(&km, k_pool, rows, d, 16) == cudaSuccess &&
+        tmc::make_tensor_map_f16(&vm, v_pool, rows, d, 16) == cudaSuccess) {
+      p.k_map = &km;
+      p.v_map = &vm;
+    }
+  }
   cudaError_t e = tmc::launch_attention(p, static_cast<cudaStream_t>(stream), false);
   if (e == cudaErrorInvalidValue) return fail(TMC_ERR_UNSUPPORTED, "attention: unsupported shape");
   return e == cudaSuccess ? ok() : cuda_fail(e, "attention launch");

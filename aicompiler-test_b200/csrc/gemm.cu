@@ -51,13 +51,6 @@ struct GemmWork {
   unsigned int *tile_counters;
 };
 
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-      : "memory");
-}
 
 // Shared-memory matrix descriptor of a K-major tile with 128-byte rows and
 // 128-byte swizzle (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B):

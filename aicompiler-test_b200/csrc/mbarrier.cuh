@@ -4,6 +4,7 @@
 // of a hang.
 #pragma once
 
+#include <cuda.h>
 #include <stdint.h>
 
 namespace tmc {
@@ -50,6 +51,17 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 2-D TMA tile load (no multicast) of the box at element coordinates (x, y)
+// of `map` into shared memory, completing on `bar`. x * element size must be
+// a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ void fence_barrier_init() {
