@@ -102,7 +102,8 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" :::
 // stores), the arithmetic shared with the GEMV (epilogue.cuh).
 template <int TN>
 __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float (&v)[TN], int m0, int row, int lane,
-                                               int ew, int t, unsigned long long (*red_keys)[kEpiChunk]) {
+                                               int ew, int t, unsigned long long (*red_keys)[kEpiChunk],
+                                               int *tok_pos, long long *tok_slot) {
   const int epi = p.epilogue;
   const int M = p.M - m0;  // tokens m0 .. m0 + TN - 1 of the launch's rows
   const bool in_range = row < p.N;
@@ -145,9 +146,8 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
     return;
   }
   if (epi == kEpiQKV) {
-    const int D = p.head_dim, q_rows = p.q_rows, kv_rows = p.kv_rows, cap = p.capacity;
-    const int ps = p.page_size, pool_pages = p.pool_pages, tstride = p.table_stride;
-    const int *positions = p.positions + m0, *trows = p.table_rows + m0, *table = p.block_table;
+    const int D = p.head_dim, q_rows = p.q_rows, kv_rows = p.kv_rows;
+    const int ps = p.page_size;
     const float *rc = p.rope_cos + ((row % D) >> 1), *rs = p.rope_sin + ((row % D) >> 1);
     __half *y = p.y_f16 + (size_t)m0 * p.y_stride + row;
     const long long ys = p.y_stride;
@@ -158,38 +158,49 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
       local -= kv_rows;
       pool = p.v_pool;
     }
-    const int hkv = kv_rows / D;
     const size_t head_off = (size_t)(local / D) * ps * D + (local % D);
+    // One thread per token resolves its position and KV slot (page lookup,
+    // range checks) once for the whole tile; -1 marks a failed check.
+    if (t < TN && t < M) {
+      const int m = m0 + t;
+      const int pos = p.positions[m];
+      long long slot = -1;
+      if (pos < 0 || pos >= p.capacity) {
+        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+      } else {
+        const int lp = pos / ps, off = pos % ps;
+        if (lp >= p.table_stride) {
+          report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
+        } else {
+          const int page = p.block_table[(size_t)p.table_rows[m] * p.table_stride + lp];
+          if (page < 0 || page >= p.pool_pages) {
+            report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
+                          page < 0 ? lp : page, m);
+          } else {
+            slot = ((long long)page * (kv_rows / D) * ps + off) * D;  // page start + row `off`, head 0
+          }
+        }
+      }
+      tok_pos[t] = (pos < 0 || pos >= p.capacity) ? -1 : pos;  // q rows need only the position
+      tok_slot[t] = slot;
+    }
+    epi_sync();
     const bool store = !(lane & 1) && in_range;
 #pragma unroll
     for (int m = 0; m < TN; ++m) {
       if (m >= M) break;
       const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
-      if (!store) continue;
-      const int pos = positions[m];
-      if (pos < 0 || pos >= cap) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m0 + m);
-        continue;
-      }
+      const int pos = tok_pos[m];
+      if (!store || pos < 0) continue;
       const __half2 val = rope ? rope_pair_value(v[m], partner, rc[(size_t)pos * (D >> 1)], rs[(size_t)pos * (D >> 1)])
                                : __floats2half2_rn(round_half(v[m]), round_half(partner));
       if (is_q) {
         *reinterpret_cast<__half2 *>(y + (size_t)m * ys) = val;
-        continue;
+      } else if (tok_slot[m] >= 0) {
+        *reinterpret_cast<__half2 *>(pool + (size_t)tok_slot[m] + head_off) = val;
       }
-      const int lp = pos / ps, off = pos % ps;
-      if (lp >= tstride) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m0 + m);
-        continue;
-      }
-      const int page = table[(size_t)trows[m] * tstride + lp];
-      if (page < 0 || page >= pool_pages) {
-        report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
-                      page < 0 ? lp : page, m0 + m);
-        continue;
-      }
-      *reinterpret_cast<__half2 *>(pool + (size_t)page * hkv * ps * D + head_off + (size_t)off * D) = val;
     }
+    epi_sync();  // the staging arrays are rewritten by the next chunk
     return;
   }
   if (epi == kEpiResidual || epi == kEpiF16) {
@@ -243,6 +254,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *acc_empty = acc_full + C::kAcc;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + C::kAcc);
   __shared__ unsigned long long red_keys[4][kEpiChunk];
+  __shared__ int tok_pos[kEpiChunk];          // QKV epilogue: per-token position (-1: skip)
+  __shared__ long long tok_slot[kEpiChunk];   // ... and KV element offset of its page row
   __shared__ int s_last, s_fail;
   __shared__ unsigned long long s_ready;
 
@@ -388,7 +401,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[buf]);
           }
-          apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys);
+          apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys, tok_pos, tok_slot);
         }
         continue;
       }
@@ -432,7 +445,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int m = 0; m < CH; ++m) v[m] += tmp[m];
         }
-        apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys);
+        apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys, tok_pos, tok_slot);
       }
     }
     epi_sync();
@@ -522,7 +535,10 @@ GemmPlan plan_gemm(int N, int K, int M, int num_sms) {
   g.kblocks = (K + kGemmKBlock - 1) / kGemmKBlock;  // a ragged last block reads zeros
   // Cost of a plan in full-K tile times: waves of persistent CTAs times the
   // work of one unit plus a fixed per-unit overhead (pipeline fill, epilogue).
-  const double overhead = 0.1;
+  // A split unit costs its partial stores, a fence, a ticket and (in the
+  // tile's last unit) an exposed reduction: splits only when the tiles alone
+  // leave SMs idle.
+  const double overhead = 0.5;
   double best = 1e30;
   g.splits = 1;
   for (int s = 1; s <= 16; ++s) {
