@@ -561,6 +561,68 @@ def serve(decoder: "Decoder", prompts, decode_counts, arrival_ticks=None, logits
     return out
 
 
+_sig("tmc_kernel_contract_json", c_int, c_char_p, c_char_p, c_size_t, POINTER(c_size_t))
+_sig("tmc_admit_generated_kernel", c_int, c_char_p, c_char_p, c_int, c_char_p, c_char_p, POINTER(c_int),
+     POINTER(ctypes.c_double), c_char_p, c_size_t)
+_sig("tmc_registry_create", c_int, POINTER(c_void_p))
+_sig("tmc_registry_destroy", None, c_void_p)
+_sig("tmc_registry_load", c_int, c_void_p, c_char_p, POINTER(c_int), c_char_p, c_size_t)
+_sig("tmc_registry_launch", c_int, c_void_p, c_char_p, POINTER(c_void_p), c_int, ctypes.c_uint, c_void_p)
+
+
+def kernel_contract(pattern: str) -> dict:
+    """The generated-kernel contract of `pattern` (makeKernelContract) as a dict."""
+    import json
+    need = c_size_t(0)
+    check(lib.tmc_kernel_contract_json(pattern.encode(), None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(need.value)
+    check(lib.tmc_kernel_contract_json(pattern.encode(), buf, need.value, None))
+    return json.loads(buf.value.decode())
+
+
+def admit_generated_kernel(pattern: str, source: str, block_size: int, feedback_path: str = "",
+                           artifact_path: str = "") -> dict:
+    """Validate-then-benchmark admission (admitGeneratedKernel). Returns
+    {admitted, speedup, log, feedback (dict or None)}."""
+    import json
+    admitted, speedup = c_int(0), ctypes.c_double(0.0)
+    log = ctypes.create_string_buffer(1 << 16)
+    check(lib.tmc_admit_generated_kernel(pattern.encode(), source.encode(), block_size, feedback_path.encode(),
+                                         artifact_path.encode(), ctypes.byref(admitted), ctypes.byref(speedup),
+                                         log, 1 << 16))
+    feedback = None
+    if feedback_path:
+        with open(feedback_path) as f:
+            feedback = json.loads(f.read())
+    return {"admitted": bool(admitted.value), "speedup": speedup.value, "log": log.value.decode(),
+            "feedback": feedback}
+
+
+class KernelRegistry:
+    """Admitted generated kernels loaded from a directory of artifacts."""
+
+    def __init__(self):
+        h = c_void_p()
+        check(lib.tmc_registry_create(ctypes.byref(h)))
+        self.handle = h
+
+    def load(self, directory: str):
+        n = c_int(0)
+        log = ctypes.create_string_buffer(1 << 14)
+        check(lib.tmc_registry_load(self.handle, directory.encode(), ctypes.byref(n), log, 1 << 14))
+        return n.value, log.value.decode()
+
+    def launch(self, rt: "Runtime", pattern: str, buffers, work_items: int):
+        arr = (c_void_p * len(buffers))(*[b.ptr for b in buffers])
+        check(lib.tmc_registry_launch(self.handle, pattern.encode(), arr, len(buffers), work_items, rt.stream))
+
+    def __del__(self):
+        try:
+            lib.tmc_registry_destroy(self.handle)
+        except Exception:
+            pass
+
+
 def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     check(lib.tmc_nccl_unique_id(buf, 128))

@@ -350,6 +350,35 @@ int tmc_serving_run(tmc_decoder *dec, int count, const int32_t *prompt_offsets,
                     double *finish_us, float *prefill_logits, float *decode_logits,
                     tmc_serving_metrics *metrics, char *log, size_t log_size);
 
+/* ---- generated kernels: contract, admission gate, registry (replace
+ * makeKernelContract / serializeKernelContract, src/llm/KernelContract.hpp:54-65,
+ * DecoderKernelContracts.cpp:129-245; admitGeneratedKernel,
+ * src/runtime/GeneratedKernelAdmission.hpp:10-13, .cpp:204-318; KernelRegistry /
+ * writeAdmittedKernel, src/runtime/KernelRegistry.hpp:10-38) ----
+ * Patterns: decoder_gemv_<K>_<N> (K*N <= 8M), decoder_rope,
+ * decoder_residual_rmsnorm, decoder_gated_mlp, each optionally suffixed _fp16.
+ * tmc_kernel_contract_json writes the contract (semantics, buffer interface,
+ * kernel signature, legal block sizes, tolerances, minimum speedup) as JSON
+ * and sets *needed to its size + 1. tmc_admit_generated_kernel compiles CUDA
+ * C++ `source` with NVRTC for sm_100a, checks the parameter layout, validates
+ * every contract case against its fp64 references, runs two paired timing
+ * rounds against the built-in template kernel (each must reach the minimum
+ * speedup), validates again, and writes feedback JSON (and, when admitted,
+ * the artifact JSON) to the given paths (NULL or "" to skip). *admitted is 1
+ * when admitted; *speedup is the worst round's speedup (0 if not timed).
+ * The registry loads every admitted artifact of a directory (recompiling
+ * it) and launches one with device pointers in contract order. */
+int tmc_kernel_contract_json(const char *pattern, char *out, size_t size, size_t *needed);
+int tmc_admit_generated_kernel(const char *pattern, const char *source, int block_size,
+                               const char *feedback_path, const char *artifact_path, int *admitted,
+                               double *speedup, char *log, size_t log_size);
+typedef struct tmc_registry tmc_registry;
+int tmc_registry_create(tmc_registry **out);
+void tmc_registry_destroy(tmc_registry *reg);
+int tmc_registry_load(tmc_registry *reg, const char *directory, int *loaded, char *log, size_t log_size);
+int tmc_registry_launch(tmc_registry *reg, const char *pattern, void *const *buffers, int count,
+                        unsigned work_items, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
