@@ -5,7 +5,11 @@
 #include <string>
 #include <vector>
 
+#include <algorithm>
+
+#include "DecodeGEMVTuner.hpp"
 #include "KernelAdmission.hpp"
+#include "RMSNormTuner.hpp"
 #include "api_util.hpp"
 #include "tmc_cuda.h"
 
@@ -51,6 +55,41 @@ int tmc_admit_generated_kernel(const char *pattern, const char *source, int bloc
   if (speedup) *speedup = f.speedup;
   if (f.status == "fatal") return fail(TMC_ERR_CUDA, f.stage + ": " + f.message);
   return ok();
+}
+
+int tmc_tune_decode_gemv(int rows, int k, int n, const float *input, const float *weight, tmc_gemv_selection *out,
+                         char *log, size_t log_size) {
+  if (input == nullptr || weight == nullptr || out == nullptr || rows <= 0 || k <= 0 || n <= 0)
+    return fail(TMC_ERR_INVALID, "bad argument");
+  std::ostringstream text;
+  const auto sel = tensor::planner::tuneDecodeGEMV(
+      rows, k, n, std::vector<float>(input, input + (size_t)rows * k),
+      std::vector<float>(weight, weight + (size_t)n * k), text);
+  copy_text(text.str(), log, log_size);
+  *out = tmc_gemv_selection{sel.success ? 1 : 0, sel.useBaseline ? 1 : 0, sel.config.ks, sel.config.dynamic ? 1 : 0,
+                            sel.conservativeSpeedup};
+  return sel.success ? ok() : fail(TMC_ERR_INVALID, sel.errorMessage);
+}
+
+int tmc_tune_rmsnorm(int rows, int width, float eps, int fp16, const float *input, const float *weight,
+                     const int *candidate_threads, int candidates, tmc_rmsnorm_selection *out, float *output,
+                     char *log, size_t log_size) {
+  if (input == nullptr || weight == nullptr || out == nullptr || rows <= 0 || width <= 0 || candidates < 0 ||
+      (candidates > 0 && candidate_threads == nullptr))
+    return fail(TMC_ERR_INVALID, "bad argument");
+  std::ostringstream text;
+  const auto t = tensor::planner::tuneRMSNorm(
+      rows, width, eps, fp16 != 0, std::vector<float>(input, input + (size_t)rows * width),
+      std::vector<float>(weight, weight + width), std::vector<int>(candidate_threads, candidate_threads + candidates),
+      text);
+  copy_text(text.str(), log, log_size);
+  double speedup = 1.0;
+  for (const auto &c : t.candidates)
+    if (!t.usedBaseline && c.threads == t.selectedThreads && c.speedup) speedup = *c.speedup;
+  *out = tmc_rmsnorm_selection{t.success ? 1 : 0, t.usedBaseline ? 1 : 0, t.selectedThreads, speedup,
+                               t.maxAbsoluteError};
+  if (t.success && output != nullptr) std::copy(t.output.begin(), t.output.end(), output);
+  return t.success ? ok() : fail(TMC_ERR_INVALID, t.errorMessage);
 }
 
 int tmc_registry_create(tmc_registry **out) {

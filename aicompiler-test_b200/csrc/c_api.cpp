@@ -11,6 +11,7 @@
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
+#include "rmsnorm.cuh"
 #include "tmc_cuda.h"
 
 using tensor::cuda::BufferHandle;
@@ -182,6 +183,19 @@ int tmc_buffer_dtype(const tmc_buffer *buf) {
     case ElementType::Int32: return TMC_I32;
   }
   return -1;
+}
+
+int tmc_k_rmsnorm(const void *x, const void *gamma, void *y, int rows, int width, float eps, int fp16,
+                  int threads, void *stream) {
+  if (!x || !gamma || !y) return fail(TMC_ERR_INVALID, "null pointer");
+  if (rows < 1 || width < 1) return fail(TMC_ERR_INVALID, "rmsnorm: need rows >= 1, width >= 1");
+  if (!(eps > 0.0f)) return fail(TMC_ERR_INVALID, "eps must be positive");
+  if (threads != 0 && (threads < 32 || threads > 1024 || (threads & (threads - 1)) != 0))
+    return fail(TMC_ERR_UNSUPPORTED, "rmsnorm: threads must be 0 or a power of two in [32, 1024]");
+  auto st = static_cast<cudaStream_t>(stream);
+  const cudaError_t e = threads == 0 ? tmc::launch_rmsnorm_baseline(x, gamma, y, rows, width, eps, fp16 != 0, st)
+                                     : tmc::launch_rmsnorm(x, gamma, y, rows, width, eps, fp16 != 0, threads, st);
+  return e == cudaSuccess ? ok() : cuda_fail(e, "rmsnorm launch");
 }
 
 int tmc_k_rmsnorm_gemv_f32(const float *x, const float *gamma, const void *w_f16, float *y,

@@ -624,6 +624,10 @@ int choose_ks(const GemvParams &p, int num_sms) {
   const int warps = num_sms * 16;             // two resident CTAs of 8 warps per SM
   int ks = 1;
   while (ks < 8 && ks * 2 <= batches && ngroups * ks * 2 <= warps) ks *= 2;
+  // A tuned selection (DecodeGEMVTuner) overrides the rule when its team
+  // still gets at least one load batch per warp.
+  if (p.force_ks == 1 || ((p.force_ks == 2 || p.force_ks == 4 || p.force_ks == 8) && p.force_ks <= batches))
+    ks = p.force_ks;
   return ks;
 }
 

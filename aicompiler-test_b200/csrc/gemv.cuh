@@ -133,6 +133,9 @@ struct GemvParams {
   // Bytes of W this launch may bulk-prefetch into L2 before its inputs are
   // ready (0: none).
   long long l2_prefetch_bytes;
+  // K-split team size chosen by the decode GEMV tuner (1, 2, 4 or 8); 0: the
+  // built-in rule.
+  int force_ks;
   // Tensor parallelism over peer memory (kEpiF32Partial producers,
   // kProResidualNorm consumers, kEpiArgmax key exchange); world 0: off.
   PeerExchange xchg;

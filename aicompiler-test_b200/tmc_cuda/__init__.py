@@ -88,6 +88,7 @@ _sig("tmc_buffer_count", c_size_t, c_void_p)
 _sig("tmc_buffer_dtype", c_int, c_void_p)
 _sig("tmc_k_rmsnorm_gemv_f32", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
      c_float, c_void_p)
+_sig("tmc_k_rmsnorm", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_int, c_void_p)
 _sig("tmc_k_gemv_f16", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p)
 _sig("tmc_k_gemv_f16_f32out", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p)
 _sig("tmc_k_batched_gemm_workspace_bytes", c_size_t, c_int, c_int, c_int)
@@ -224,6 +225,12 @@ class Buffer:
 def rmsnorm_gemv_f32(rt: Runtime, x: Buffer, gamma: Buffer, w: Buffer, y: Buffer, rows: int, k: int,
                      n: int, eps: float):
     check(lib.tmc_k_rmsnorm_gemv_f32(x.ptr, gamma.ptr, w.ptr, y.ptr, rows, k, n, eps, rt.stream))
+
+
+def rmsnorm(rt: Runtime, x: Buffer, gamma: Buffer, y: Buffer, rows: int, width: int, eps: float,
+            threads: int = 256):
+    """RMSNormOp over [rows, width]; all three buffers fp32 or all fp16; threads 0 = baseline."""
+    check(lib.tmc_k_rmsnorm(x.ptr, gamma.ptr, y.ptr, rows, width, eps, int(x.dtype == F16), threads, rt.stream))
 
 
 def gemv_f16(rt: Runtime, x: Buffer, w: Buffer, y: Buffer, rows: int, k: int, n: int):
@@ -596,6 +603,55 @@ def admit_generated_kernel(pattern: str, source: str, block_size: int, feedback_
             feedback = json.loads(f.read())
     return {"admitted": bool(admitted.value), "speedup": speedup.value, "log": log.value.decode(),
             "feedback": feedback}
+
+
+class GemvSelection(ctypes.Structure):
+    _fields_ = [("success", c_int), ("use_baseline", c_int), ("ks", c_int), ("dynamic", c_int),
+                ("conservative_speedup", ctypes.c_double)]
+
+
+_sig("tmc_tune_decode_gemv", c_int, c_int, c_int, c_int, POINTER(c_float), POINTER(c_float), POINTER(GemvSelection),
+     c_char_p, c_size_t)
+
+
+def tune_decode_gemv(input, weight) -> dict:
+    """tuneDecodeGEMV: input [rows, k], weight [n, k] (stored as fp16)."""
+    x = np.ascontiguousarray(np.asarray(input, dtype=np.float32))
+    w = np.ascontiguousarray(np.asarray(weight, dtype=np.float32))
+    rows, k = x.shape
+    n = w.shape[0]
+    sel = GemvSelection()
+    log = ctypes.create_string_buffer(1 << 14)
+    check(lib.tmc_tune_decode_gemv(rows, k, n, x.ctypes.data_as(POINTER(c_float)), w.ctypes.data_as(POINTER(c_float)),
+                                   ctypes.byref(sel), log, 1 << 14))
+    return {"success": bool(sel.success), "use_baseline": bool(sel.use_baseline), "ks": sel.ks,
+            "dynamic": bool(sel.dynamic), "speedup": sel.conservative_speedup, "log": log.value.decode()}
+
+
+class RMSNormSelection(ctypes.Structure):
+    _fields_ = [("success", c_int), ("used_baseline", c_int), ("selected_threads", c_int),
+                ("speedup", ctypes.c_double), ("max_abs_error", ctypes.c_double)]
+
+
+_sig("tmc_tune_rmsnorm", c_int, c_int, c_int, c_float, c_int, POINTER(c_float), POINTER(c_float), POINTER(c_int),
+     c_int, POINTER(RMSNormSelection), POINTER(c_float), c_char_p, c_size_t)
+
+
+def tune_rmsnorm(input, weight, eps: float, fp16: bool = False, candidate_threads=(64, 128, 256, 512)) -> dict:
+    """tuneRMSNorm: input [rows, width], weight [width]; returns the selection and its validated output."""
+    x = np.ascontiguousarray(np.asarray(input, dtype=np.float32))
+    w = np.ascontiguousarray(np.asarray(weight, dtype=np.float32))
+    rows, width = x.shape
+    cands = (c_int * len(candidate_threads))(*candidate_threads)
+    sel = RMSNormSelection()
+    out = np.zeros((rows, width), dtype=np.float32)
+    log = ctypes.create_string_buffer(1 << 14)
+    check(lib.tmc_tune_rmsnorm(rows, width, eps, int(fp16), x.ctypes.data_as(POINTER(c_float)),
+                               w.ctypes.data_as(POINTER(c_float)), cands, len(candidate_threads), ctypes.byref(sel),
+                               out.ctypes.data_as(POINTER(c_float)), log, 1 << 14))
+    return {"success": bool(sel.success), "used_baseline": bool(sel.used_baseline),
+            "threads": sel.selected_threads, "speedup": sel.speedup, "max_abs_error": sel.max_abs_error,
+            "output": out, "log": log.value.decode()}
 
 
 class KernelRegistry:

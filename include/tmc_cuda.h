@@ -112,6 +112,14 @@ int tmc_buffer_dtype(const tmc_buffer *buf);
 int tmc_k_rmsnorm_gemv_f32(const float *x, const float *gamma, const void *w_f16, float *y,
                            int rows, int k, int n, float eps, void *stream);
 
+/* Standalone RMSNorm, one CTA of `threads` per row (RMSNormOp, TensorIR.hpp:98-104;
+ * emitRMSNorm, MetalEmitter.cpp:12-76; the frozen 256-thread baseline,
+ * RMSNormBaseline.cpp:13-73, with threads == 0):
+ *   y[r, c] = x[r, c] * rsqrt(mean_c x[r, :]^2 + eps) * gamma[c], fp32 accumulation.
+ * x, gamma, y all fp32 (fp16 == 0) or all fp16 (fp16 != 0); x/y [rows, width]. */
+int tmc_k_rmsnorm(const void *x, const void *gamma, void *y, int rows, int width, float eps, int fp16,
+                  int threads, void *stream);
+
 /* Decode GEMV y = x W^T with fp16 x, W and y, fp32 accumulation: replaces
  * emitDecodeGEMV / emitLinearBaseline (DecodeGEMVMetalEmitter.cpp:18-132).
  * x [rows, k], W [n, k], y [rows, n]; rows <= 8, k % 8 == 0. */
@@ -372,6 +380,33 @@ int tmc_kernel_contract_json(const char *pattern, char *out, size_t size, size_t
 int tmc_admit_generated_kernel(const char *pattern, const char *source, int block_size,
                                const char *feedback_path, const char *artifact_path, int *admitted,
                                double *speedup, char *log, size_t log_size);
+/* Decode GEMV tuning (replaces tuneDecodeGEMV / DecodeGEMVSelection,
+ * src/planner/DecodeGEMVTuner.hpp:13-25, DecodeGEMVTuner.cpp:162-304):
+ * candidates are decode GEMV configurations (K-split team 1/2/4/8, dynamic
+ * row scheduling), each validated against fp64 (<= 64M MACs; else the
+ * baseline's output) and admitted only with >= 1.05x over the generic linear
+ * baseline in two paired rounds; the fastest admitted one is selected.
+ * input [rows, k] and weight [n, k] are logical values stored as fp16. */
+typedef struct tmc_gemv_selection {
+  int success, use_baseline, ks, dynamic;
+  double conservative_speedup;
+} tmc_gemv_selection;
+int tmc_tune_decode_gemv(int rows, int k, int n, const float *input, const float *weight,
+                         tmc_gemv_selection *out, char *log, size_t log_size);
+
+/* RMSNorm tuning (replaces tuneRMSNorm / TuningResult, RMSNormTuner.hpp:14-44,
+ * RMSNormTuner.cpp:159-309): block-size candidates against the frozen
+ * 256-thread baseline, fp64-validated (fp32 atol 1e-5 / rtol 1e-4, fp16 2e-3),
+ * admitted at >= 1.05x in two paired rounds. `output` (rows * width floats,
+ * may be NULL) receives the final validated execution of the selection. */
+typedef struct tmc_rmsnorm_selection {
+  int success, used_baseline, selected_threads;
+  double speedup, max_abs_error;
+} tmc_rmsnorm_selection;
+int tmc_tune_rmsnorm(int rows, int width, float eps, int fp16, const float *input, const float *weight,
+                     const int *candidate_threads, int candidates, tmc_rmsnorm_selection *out, float *output,
+                     char *log, size_t log_size);
+
 typedef struct tmc_registry tmc_registry;
 int tmc_registry_create(tmc_registry **out);
 void tmc_registry_destroy(tmc_registry *reg);

@@ -133,3 +133,21 @@ extern "C" __global__ void generated_decoder_gated_mlp_fp16(const __half *x, con
     r, _ = admit(tmp_path, "decoder_gated_mlp_fp16", src, 32)
     assert "all outputs numerical validation: PASS" in r["log"]
     assert r["feedback"]["status"] == "admitted" or r["feedback"]["stage"] == "performance", r["log"]
+
+
+@pytest.mark.parametrize("rows,k,n", [(1, 4096, 4096), (4, 1024, 2816), (1, 4096, 14336)])
+def test_decode_gemv_tuner_selects_an_admitted_config(rt, rows, k, n):
+    # tuneDecodeGEMV (DecodeGEMVTuner.cpp:162-304): every candidate validated,
+    # selection only with >= 1.05x in two rounds over the generic linear layer.
+    rng = np.random.default_rng(rows + k + n)
+    x = rng.standard_normal((rows, k)).astype(np.float16).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float16).astype(np.float32)
+    sel = tmc_cuda.tune_decode_gemv(x, w)
+    assert sel["success"], sel["log"]
+    assert "numerical: FAIL" not in sel["log"], sel["log"]
+    if not sel["use_baseline"]:
+        assert sel["speedup"] >= 1.05 and sel["ks"] in (1, 2, 4, 8)
+        assert "-> admitted" in sel["log"]
+    # At weight-streaming sizes the decode GEMV beats one CTA per output.
+    if k * n >= 16 << 20:
+        assert not sel["use_baseline"], sel["log"]
