@@ -179,8 +179,9 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)R * H, F16, &hB_, &activationBytes_)).empty()) return e;  // second residual buffer (TP)
   if (cfg_.tpSize > 1 && !(e = make((size_t)R * H, F32, &partialF32_, &activationBytes_)).empty()) return e;
   if (R > kGemvMaxRows) {
-    // Batched steps: prologue rows for the tensor-core projections, split-K
-    // partials (the largest any projection's plan needs) and tile tickets.
+    // Batched steps: prologue rows for the tensor-core projections, the
+    // partial-tile workspace (the largest any projection's plan needs) and
+    // tile tickets.
     if (!(e = make((size_t)R * H, F16, &xn_, &activationBytes_)).empty()) return e;
     const int dims[5][2] = {{qkvRows_, H}, {H, hqL_ * D}, {2 * iL_, H}, {H, iL_}, {vL_, H}};
     size_t wsFloats = 1, tiles = 1;

@@ -14,10 +14,11 @@
 //             accumulator (one output feature per thread, TN tokens), then the
 //             GEMV's per-element epilogues. With four accumulators the
 //             epilogues of finished units overlap the MMAs of the next ones.
-// Work units are (tile, K split) pairs, assigned round-robin to the CTAs.
-// With several K splits each unit writes its fp32 partial to a workspace and
-// the tile's last unit (atomic ticket) sums the partials in split order, so
-// results do not depend on timing.
+// Work division is stream-K (gemm.cuh): CTA c streams the iterations
+// [W c / G, W (c + 1) / G) of the W = tiles x kblocks (tile, K block) space;
+// each tile it touches is one piece. A piece that covers only part of its
+// tile writes an fp32 partial to the CTA's workspace slot, and the tile's
+// last-arriving piece (atomic ticket) sums the tile's partials in K order.
 // Every mbarrier wait is bounded (mbarrier.cuh); a timeout is reported in the
 // device status block and the CTA still releases its tensor memory and exits.
 #include "gemm.cuh"
@@ -46,9 +47,42 @@ struct GemmCfg {
 };
 
 struct GemmWork {
-  int tiles, splits, kblocks;
+  int tiles, kblocks;
   float *ws;
   unsigned int *tile_counters;
+};
+
+// First iteration of CTA c's run (iterations [run_begin(c), run_begin(c + 1))).
+__device__ __forceinline__ long long run_begin(long long iters, int grid, int c) { return iters * c / grid; }
+// The CTA whose run holds iteration i: the largest c with run_begin(c) <= i.
+__device__ __forceinline__ int run_of(long long iters, int grid, long long i) {
+  return (int)(((i + 1) * grid + iters - 1) / iters) - 1;
+}
+
+// The pieces of this CTA's run, in order: tile, K blocks [kb0, kb1), and its
+// index among the run's pieces (partials use slot 0 for the first piece and
+// 1 for the last; middle pieces always cover whole tiles).
+struct Piece {
+  int tile, kb0, kb1, index;
+};
+struct RunCursor {
+  long long next, end;
+  int kblocks, index;
+  __device__ RunCursor(const GemmWork &w)
+      : next(run_begin((long long)w.tiles * w.kblocks, gridDim.x, blockIdx.x)),
+        end(run_begin((long long)w.tiles * w.kblocks, gridDim.x, blockIdx.x + 1)),
+        kblocks(w.kblocks),
+        index(0) {}
+  __device__ bool get(Piece &pc) {
+    if (next >= end) return false;
+    pc.tile = (int)(next / kblocks);
+    const long long t0 = (long long)pc.tile * kblocks;
+    pc.kb0 = (int)(next - t0);
+    pc.kb1 = (int)((end - t0) < kblocks ? (end - t0) : kblocks);
+    pc.index = index++;
+    next = t0 + pc.kb1;
+    return true;
+  }
 };
 
 
@@ -186,18 +220,33 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
     }
     epi_sync();
     const bool store = !(lane & 1) && in_range;
+    // Groups of kG tokens: every table load of a group is issued before any of
+    // its stores (a store may alias a later load as far as the compiler can
+    // tell, which would serialise one global round trip per token).
+    constexpr int kG = 16;
 #pragma unroll
-    for (int m = 0; m < TN; ++m) {
-      if (m >= M) break;
-      const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
-      const int pos = tok_pos[m];
-      if (!store || pos < 0) continue;
-      const __half2 val = rope ? rope_pair_value(v[m], partner, rc[(size_t)pos * (D >> 1)], rs[(size_t)pos * (D >> 1)])
-                               : __floats2half2_rn(round_half(v[m]), round_half(partner));
-      if (is_q) {
-        *reinterpret_cast<__half2 *>(y + (size_t)m * ys) = val;
-      } else if (tok_slot[m] >= 0) {
-        *reinterpret_cast<__half2 *>(pool + (size_t)tok_slot[m] + head_off) = val;
+    for (int g = 0; g < TN; g += kG) {
+      float cs[kG], sn[kG];
+#pragma unroll
+      for (int i = 0; i < kG; ++i) {
+        const int pos = tok_pos[g + i];
+        const bool use = rope && store && g + i < M && pos >= 0;
+        cs[i] = use ? rc[(size_t)pos * (D >> 1)] : 0.0f;
+        sn[i] = use ? rs[(size_t)pos * (D >> 1)] : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < kG; ++i) {
+        const int m = g + i;
+        const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
+        const int pos = tok_pos[m];
+        if (!store || m >= M || pos < 0) continue;
+        const __half2 val = rope ? rope_pair_value(v[m], partner, cs[i], sn[i])
+                                 : __floats2half2_rn(round_half(v[m]), round_half(partner));
+        if (is_q) {
+          *reinterpret_cast<__half2 *>(y + (size_t)m * ys) = val;
+        } else if (tok_slot[m] >= 0) {
+          *reinterpret_cast<__half2 *>(pool + (size_t)tok_slot[m] + head_off) = val;
+        }
       }
     }
     epi_sync();  // the staging arrays are rewritten by the next chunk
@@ -208,11 +257,14 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
     const __half *res = p.residual + (size_t)m0 * p.y_stride + row;
     const long long ys = p.y_stride;
     const bool residual = epi == kEpiResidual;
+    // All residual loads first: y and res are the same buffer (in place), so
+    // interleaved loads and stores would serialise one round trip per token.
+    __half rv[TN];
 #pragma unroll
-    for (int m = 0; m < TN; ++m) {
-      if (m >= M) break;
-      if (in_range) y[(size_t)m * ys] = residual ? residual_value(res[(size_t)m * ys], v[m]) : __float2half_rn(v[m]);
-    }
+    for (int m = 0; m < TN; ++m) rv[m] = residual && in_range && m < M ? res[(size_t)m * ys] : __half(0.0f);
+#pragma unroll
+    for (int m = 0; m < TN; ++m)
+      if (in_range && m < M) y[(size_t)m * ys] = residual ? residual_value(rv[m], v[m]) : __float2half_rn(v[m]);
     return;
   }
   // kEpiF32 / kEpiF32Partial
@@ -260,7 +312,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ unsigned long long s_ready;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int units = w.tiles * w.splits;
   const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
 
   if (threadIdx.x == 0) {
@@ -294,11 +345,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int pending_kb[S];
       int it = 0;
       bool waited = false, ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int tile = u / w.splits, ks = u % w.splits;
-        const int kb0 = (int)((long long)w.kblocks * ks / w.splits);
-        const int kb1 = (int)((long long)w.kblocks * (ks + 1) / w.splits);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+      RunCursor run(w);
+      Piece pc;
+      while (ok && run.get(pc)) {
+        const int tile = pc.tile;
+        for (int kb = pc.kb0; kb < pc.kb1; ++kb, ++it) {
           const int st = it % S, round = it / S;
           if (it == S && !waited) {
             // The ring is full of weight tiles: wait for the producer of x,
@@ -338,12 +389,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t idesc = (1u << 4)                                  // D: fp32
                              | ((uint32_t)(TN >> 3) << 17)              // N
                              | ((uint32_t)(kGemmTileRows >> 4) << 24);  // M; A, B: fp16, K-major
-      int it = 0, j = 0;
+      int it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++j) {
-        const int ks = u % w.splits;
-        const int kb0 = (int)((long long)w.kblocks * ks / w.splits);
-        const int kb1 = (int)((long long)w.kblocks * (ks + 1) / w.splits);
+      RunCursor run(w);
+      Piece pc;
+      while (ok && run.get(pc)) {
+        const int j = pc.index, kb0 = pc.kb0, kb1 = pc.kb1;
         const int buf = j % C::kAcc;
         if (j >= C::kAcc && !mbar_wait(&acc_empty[buf], ((j / C::kAcc) - 1) & 1)) {
           ok = false;
@@ -376,9 +427,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int ew = warp - 2;
     const int t = threadIdx.x - 64;
     const int r = q * 32 + lane;
-    int j = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++j) {
-      const int tile = u / w.splits, ks = u % w.splits;
+    const long long iters = (long long)w.tiles * w.kblocks;
+    RunCursor run(w);
+    Piece pc;
+    while (run.get(pc)) {
+      const int tile = pc.tile, j = pc.index;
       const int buf = j % C::kAcc;
       if (!mbar_wait(&acc_full[buf], (j / C::kAcc) & 1)) s_fail = 1;
       epi_sync();
@@ -389,7 +442,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TN);
       const int row = tile * kGemmTileRows + r;
       const int chunks = (p.M + CH - 1) / CH;
-      if (w.splits == 1) {
+      if (pc.kb0 == 0 && pc.kb1 == w.kblocks) {
 #pragma unroll 1
         for (int c = 0; c < chunks; ++c) {
           float v[CH];
@@ -405,7 +458,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         continue;
       }
-      float *part = w.ws + (size_t)(tile * w.splits + ks) * TN * kGemmTileRows;
+      float *part = w.ws + ((size_t)blockIdx.x * 2 + (j == 0 ? 0 : 1)) * TN * kGemmTileRows;
 #pragma unroll 1
       for (int c = 0; c < chunks; ++c) {
         float v[CH];
@@ -421,23 +474,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
       __threadfence();
       epi_sync();
+      // The tile's pieces belong to the consecutive runs c_first .. c_last.
+      const int c_first = run_of(iters, gridDim.x, (long long)tile * w.kblocks);
+      const int c_last = run_of(iters, gridDim.x, (long long)(tile + 1) * w.kblocks - 1);
       if (t == 0) {
         const unsigned int prev = atomicAdd(w.tile_counters + tile, 1u);
-        s_last = prev == (unsigned int)(w.splits - 1);
+        s_last = prev == (unsigned int)(c_last - c_first);
         if (s_last) atomicExch(w.tile_counters + tile, 0u);
       }
       epi_sync();
       if (!s_last) continue;
       __threadfence();
-      // Sum the partials in split order; each split's values for a chunk of
-      // tokens are requested together (one round trip per chunk and split).
+      // Sum the partials in K order (run order); each piece's values for a
+      // chunk of tokens are requested together (one round trip per piece).
 #pragma unroll 1
       for (int c = 0; c < chunks; ++c) {
         float v[CH];
 #pragma unroll
         for (int m = 0; m < CH; ++m) v[m] = 0.0f;
-        for (int k2 = 0; k2 < w.splits; ++k2) {
-          const float *src = w.ws + (size_t)(tile * w.splits + k2) * TN * kGemmTileRows + r;
+        for (int c2 = c_first; c2 <= c_last; ++c2) {
+          const bool first_piece = run_begin(iters, gridDim.x, c2) / w.kblocks == tile;
+          const float *src = w.ws + ((size_t)c2 * 2 + (first_piece ? 0 : 1)) * TN * kGemmTileRows + r;
           float tmp[CH];
 #pragma unroll
           for (int m = 0; m < CH; ++m)
@@ -508,7 +565,7 @@ cudaError_t launch_tn(const GemvParams &p, const CUtensorMap &w_map, const CUten
       configured[dev] = true;
     }
   }
-  GemmWork w{plan.tiles, plan.splits, plan.kblocks, ws, tile_counters};
+  GemmWork w{plan.tiles, plan.kblocks, ws, tile_counters};
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(plan.grid);
   cfg.blockDim = dim3(kGemmThreads);
@@ -533,31 +590,19 @@ GemmPlan plan_gemm(int N, int K, int M, int num_sms) {
   g.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   g.tiles = (N + kGemmTileRows - 1) / kGemmTileRows;
   g.kblocks = (K + kGemmKBlock - 1) / kGemmKBlock;  // a ragged last block reads zeros
-  // Cost of a plan in full-K tile times: waves of persistent CTAs times the
-  // work of one unit plus a fixed per-unit overhead (pipeline fill, epilogue).
-  // A split unit costs its partial stores, a fence, a ticket and (in the
-  // tile's last unit) an exposed reduction: splits only when the tiles alone
-  // leave SMs idle.
-  const double overhead = 0.5;
-  double best = 1e30;
-  g.splits = 1;
-  for (int s = 1; s <= 16; ++s) {
-    if (s > 1 && g.kblocks / s < 4) break;
-    const long long units = (long long)g.tiles * s;
-    const long long waves = (units + num_sms - 1) / num_sms;
-    const double cost = (double)waves * (1.0 / s + overhead);
-    if (cost < best - 1e-9) {
-      best = cost;
-      g.splits = s;
-    }
-  }
-  const long long units = (long long)g.tiles * g.splits;
-  g.grid = (int)(units < num_sms ? units : num_sms);
+  const long long iters = (long long)g.tiles * g.kblocks;
+  long long grid = iters / kGemmMinRun;
+  if (grid > num_sms) grid = num_sms;
+  if (grid < 1) grid = 1;
+  g.grid = (int)grid;
   return g;
 }
 
 size_t gemm_workspace_floats(const GemmPlan &plan) {
-  return plan.splits > 1 ? (size_t)plan.tiles * plan.splits * plan.tn * kGemmTileRows : 0;
+  const long long iters = (long long)plan.tiles * plan.kblocks;
+  for (int c = 1; c < plan.grid; ++c)
+    if (iters * c / plan.grid % plan.kblocks != 0) return (size_t)plan.grid * 2 * plan.tn * kGemmTileRows;
+  return 0;
 }
 
 cudaError_t make_tensor_map_f16(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols,
@@ -594,7 +639,8 @@ cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUt
   if (p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 128 ||
       plan.tiles != (p.N + kGemmTileRows - 1) / kGemmTileRows ||
       plan.kblocks != (p.K + kGemmKBlock - 1) / kGemmKBlock ||
-      plan.splits < 1 || plan.grid < 1 || tile_counters == nullptr || (plan.splits > 1 && ws == nullptr))
+      plan.grid < 1 || plan.grid > (long long)plan.tiles * plan.kblocks ||  // every run non-empty
+      tile_counters == nullptr || (gemm_workspace_floats(plan) > 0 && ws == nullptr))
     return cudaErrorInvalidValue;
   switch (p.epilogue) {
     case kEpiQKV:

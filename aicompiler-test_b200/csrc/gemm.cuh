@@ -20,18 +20,24 @@ namespace tmc {
 constexpr int kGemmTileRows = 128;  // weight rows per tile (UMMA M)
 constexpr int kGemmKBlock = 64;     // K elements per pipeline stage: one 128-byte swizzle row
 
+// Stream-K work division: the tiles x kblocks (tile, K block) iterations, in
+// tile-major order, are cut into `grid` contiguous equal runs, one per
+// persistent CTA. A run covers whole tiles and at most two partial tiles (its
+// first and its last); a partial tile's pieces are written as fp32 partials
+// and summed in K order by the tile's last-arriving piece, so the result is
+// fixed for a given plan and does not depend on timing.
 struct GemmPlan {
   int tn;       // token columns per MMA (16, 32, 64 or 128), >= M
   int tiles;    // ceil(N / 128)
-  int splits;   // K splits per tile (partials reduced in order by the tile's last CTA)
   int kblocks;  // ceil(K / 64)
-  int grid;     // persistent CTAs (one per SM at most)
+  int grid;     // persistent CTAs (one per SM at most, each with >= kGemmMinRun iterations)
 };
 
-// Work split for N x K weights and M rows on `num_sms` SMs: the split count
-// that best fills whole waves of persistent CTAs.
+constexpr int kGemmMinRun = 4;  // fewest K blocks a CTA streams (shorter runs cost more in partials)
+
 GemmPlan plan_gemm(int N, int K, int M, int num_sms);
-// fp32 elements of split-K partials the plan needs (0 when splits == 1).
+// fp32 elements of partial-tile workspace the plan needs (0 when every run is
+// whole tiles): two [128 x tn] slots per CTA.
 size_t gemm_workspace_floats(const GemmPlan &plan);
 
 // 2-D tensor map of an fp16 row-major matrix [rows, cols] with a
