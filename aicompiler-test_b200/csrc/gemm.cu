@@ -1,6 +1,6 @@
 // Batched decode projections on tcgen05 tensor cores (see gemm.cuh).
 //
-// One persistent CTA per SM, 6 warps, warp-specialised:
+// One persistent CTA per SM, 10 warps, warp-specialised:
 //   warp 0    TMA producer: streams 128-row x 64-column weight tiles (A) and
 //             the matching 64-column slice of the token rows (B) into a ring
 //             of shared-memory stages (128-byte swizzle). Weight tiles do not
@@ -10,7 +10,9 @@
 //             issues the MMAs from one thread: 4 x (M=128, N=TN, K=16) per
 //             stage, tcgen05.commit frees the stage, a final commit hands the
 //             accumulator to the epilogue;
-//   warps 2-5 epilogue: tcgen05.ld of their 32-lane quarter of the
+//   warps 2-9 epilogue, two per 32-lane quarter of the accumulator (warp w
+//             reads lanes 32 (w % 4) ..), taking alternate 16-token groups:
+//             tcgen05.ld of their quarter of the
 //             accumulator (one output feature per thread, TN tokens), then the
 //             GEMV's per-element epilogues. With four accumulators the
 //             epilogues of finished units overlap the MMAs of the next ones.
@@ -32,8 +34,17 @@
 namespace tmc {
 namespace {
 
-constexpr int kGemmThreads = 192;
-constexpr int kEpiChunk = 64;  // accumulator columns an epilogue thread holds at a time
+constexpr int kGemmThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kGroup = 16;      // token columns an epilogue step handles (one tcgen05.ld)
+constexpr int kMaxTokens = 128;  // the largest TN
+
+// Epilogue kinds the kernel is specialised on: each instantiation carries one
+// epilogue body, run by a non-unrolled loop over 16-token groups, so the
+// kernel's code stays small enough for the instruction caches (a 64-token
+// unrolled body of every kind made the code ~700 KB, and the tile's last,
+// once-per-launch reduction ran out of cold instruction memory).
+enum EpiKind : int { kEkQKV, kEkSwiGLU, kEkHalf, kEkF32, kEkArgmax };
 constexpr int kTileBytesA = kGemmTileRows * kGemmKBlock * 2;  // 16 KB
 
 template <int TN>
@@ -127,64 +138,74 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Named barrier of the four epilogue warps.
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Named barrier of the eight epilogue warps.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
 
-// The epilogue of one finished tile for this thread's output feature `row`
-// and the TN token columns in v: one loop per epilogue kind with every
-// parameter read once (a generic per-element dispatch costs more than the
-// stores), the arithmetic shared with the GEMV (epilogue.cuh).
-template <int TN>
-__device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float (&v)[TN], int m0, int row, int lane,
-                                               int ew, int t, unsigned long long (*red_keys)[kEpiChunk],
-                                               int *tok_pos, long long *tok_slot) {
-  const int epi = p.epilogue;
-  const int M = p.M - m0;  // tokens m0 .. m0 + TN - 1 of the launch's rows
+// The epilogue of 16 tokens (m0 .. m0 + 15 of the launch's rows) for this
+// thread's output feature `row`, values in v: the arithmetic shared with the
+// GEMV (epilogue.cuh). Values are computed unconditionally; loads and stores
+// are predicated (M <= 0 for a warp half without a group this round). QKV
+// reads the per-token position / KV slot staged in shared memory for the
+// piece (tok_pos, tok_slot, indexed by token). The two warp halves (ew / 4)
+// work on groups m0 and m0 +- 16 at the same time.
+template <int EK>
+__device__ __forceinline__ void apply_group(const GemvParams &p, const float (&v)[kGroup], int m0, bool active,
+                                            int row, int lane, int ew, int t,
+                                            unsigned long long (*red_keys)[kGroup], const int *tok_pos,
+                                            const long long *tok_slot) {
+  const int M = active ? p.M - m0 : 0;
   const bool in_range = row < p.N;
-  if (epi == kEpiArgmax) {
-    float *y = p.y_f32 != nullptr ? p.y_f32 + (size_t)m0 * p.y_stride : nullptr;
-    const long long ys = p.y_stride;
+  const long long ys = p.y_stride;
+  if constexpr (EK == kEkArgmax) {
+    float *y = p.y_f32 != nullptr ? p.y_f32 + (size_t)m0 * ys : nullptr;
     const int voff = p.vocab_offset;
+    unsigned long long key[kGroup];
 #pragma unroll
-    for (int m = 0; m < TN; ++m) {
-      if (m >= M) break;
-      unsigned long long key = 0ull;
-      if (in_range) {
-        const float h = round_half(v[m]);
-        if (y != nullptr) y[(size_t)m * ys + row] = h;
-        key = argmax_key(h, voff + row);
+    for (int m = 0; m < kGroup; ++m) {
+      const float h = round_half(v[m]);
+      key[m] = in_range && m < M ? argmax_key(h, voff + row) : 0ull;
+      if (y != nullptr && in_range && m < M) y[(size_t)m * ys + row] = h;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+      for (int m = 0; m < kGroup; ++m) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key[m], o);
+        key[m] = other > key[m] ? other : key[m];
       }
-      key = warp_max_u64(key);
-      if (lane == 0) red_keys[ew][m] = key;
     }
-    epi_sync();
-    if (t < TN && t < M) {  // one thread per token of this chunk
-      unsigned long long k = red_keys[0][t];
+    if (lane == 0) {
 #pragma unroll
-      for (int e = 1; e < 4; ++e) k = red_keys[e][t] > k ? red_keys[e][t] : k;
-      if (k != 0ull) atomicMax(p.argmax_keys + m0 + t, k);
+      for (int m = 0; m < kGroup; ++m) red_keys[ew][m] = key[m];
     }
     epi_sync();
-    return;
-  }
-  if (epi == kEpiSwiGLU) {
-    __half *y = p.y_f16 + (size_t)m0 * p.y_stride + (row >> 1);
-    const long long ys = p.y_stride;
+    if (t < 2 * kGroup) {  // one thread per token of the two halves' groups
+      const int hf = t / kGroup, tok = t % kGroup;
+      const int mm = m0 - (ew >> 2) * kGroup + hf * kGroup + tok;
+      if (mm < p.M) {
+        unsigned long long k = red_keys[hf * 4][tok];
+#pragma unroll
+        for (int e = 1; e < 4; ++e) k = red_keys[hf * 4 + e][tok] > k ? red_keys[hf * 4 + e][tok] : k;
+        if (k != 0ull) atomicMax(p.argmax_keys + mm, k);
+      }
+    }
+    epi_sync();
+  } else if constexpr (EK == kEkSwiGLU) {
+    __half *y = p.y_f16 + (size_t)m0 * ys + (row >> 1);
     const bool store = !(lane & 1) && in_range;
+    __half out[kGroup];
 #pragma unroll
-    for (int m = 0; m < TN; ++m) {
-      if (m >= M) break;
+    for (int m = 0; m < kGroup; ++m) {
       const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
-      if (store) y[(size_t)m * ys] = swiglu_value(v[m], partner);
+      out[m] = swiglu_value(v[m], partner);
     }
-    return;
-  }
-  if (epi == kEpiQKV) {
+#pragma unroll
+    for (int m = 0; m < kGroup; ++m)
+      if (store && m < M) y[(size_t)m * ys] = out[m];
+  } else if constexpr (EK == kEkQKV) {
     const int D = p.head_dim, q_rows = p.q_rows, kv_rows = p.kv_rows;
-    const int ps = p.page_size;
     const float *rc = p.rope_cos + ((row % D) >> 1), *rs = p.rope_sin + ((row % D) >> 1);
-    __half *y = p.y_f16 + (size_t)m0 * p.y_stride + row;
-    const long long ys = p.y_stride;
+    __half *y = p.y_f16 + (size_t)m0 * ys + row;
     const bool rope = row < q_rows + kv_rows, is_q = row < q_rows;
     int local = row - q_rows;
     __half *pool = p.k_pool;
@@ -192,104 +213,64 @@ __device__ __forceinline__ void apply_epilogue(const GemvParams &p, const float 
       local -= kv_rows;
       pool = p.v_pool;
     }
-    const size_t head_off = (size_t)(local / D) * ps * D + (local % D);
-    // One thread per token resolves its position and KV slot (page lookup,
-    // range checks) once for the whole tile; -1 marks a failed check.
-    if (t < TN && t < M) {
-      const int m = m0 + t;
-      const int pos = p.positions[m];
-      long long slot = -1;
-      if (pos < 0 || pos >= p.capacity) {
-        report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
-      } else {
-        const int lp = pos / ps, off = pos % ps;
-        if (lp >= p.table_stride) {
-          report_status(p.status, kStatusLengthRange, kWhereAppend, pos, m);
-        } else {
-          const int page = p.block_table[(size_t)p.table_rows[m] * p.table_stride + lp];
-          if (page < 0 || page >= p.pool_pages) {
-            report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
-                          page < 0 ? lp : page, m);
-          } else {
-            slot = ((long long)page * (kv_rows / D) * ps + off) * D;  // page start + row `off`, head 0
-          }
-        }
-      }
-      tok_pos[t] = (pos < 0 || pos >= p.capacity) ? -1 : pos;  // q rows need only the position
-      tok_slot[t] = slot;
-    }
-    epi_sync();
+    const size_t head_off = (size_t)(local / D) * p.page_size * D + (local % D);
     const bool store = !(lane & 1) && in_range;
-    // Groups of kG tokens: every table load of a group is issued before any of
-    // its stores (a store may alias a later load as far as the compiler can
-    // tell, which would serialise one global round trip per token).
-    constexpr int kG = 16;
+    float cs[kGroup], sn[kGroup];
 #pragma unroll
-    for (int g = 0; g < TN; g += kG) {
-      float cs[kG], sn[kG];
+    for (int m = 0; m < kGroup; ++m) {
+      const int pos = m < M ? tok_pos[m0 + m] : -1;
+      const bool use = rope && store && pos >= 0;
+      cs[m] = use ? rc[(size_t)pos * (D >> 1)] : 0.0f;
+      sn[m] = use ? rs[(size_t)pos * (D >> 1)] : 0.0f;
+    }
+    __half2 val[kGroup];
 #pragma unroll
-      for (int i = 0; i < kG; ++i) {
-        const int pos = tok_pos[g + i];
-        const bool use = rope && store && g + i < M && pos >= 0;
-        cs[i] = use ? rc[(size_t)pos * (D >> 1)] : 0.0f;
-        sn[i] = use ? rs[(size_t)pos * (D >> 1)] : 0.0f;
-      }
+    for (int m = 0; m < kGroup; ++m) {
+      const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
+      val[m] = rope ? rope_pair_value(v[m], partner, cs[m], sn[m])
+                    : __floats2half2_rn(round_half(v[m]), round_half(partner));
+    }
 #pragma unroll
-      for (int i = 0; i < kG; ++i) {
-        const int m = g + i;
-        const float partner = __shfl_xor_sync(0xffffffffu, v[m], 1);
-        const int pos = tok_pos[m];
-        if (!store || m >= M || pos < 0) continue;
-        const __half2 val = rope ? rope_pair_value(v[m], partner, cs[i], sn[i])
-                                 : __floats2half2_rn(round_half(v[m]), round_half(partner));
-        if (is_q) {
-          *reinterpret_cast<__half2 *>(y + (size_t)m * ys) = val;
-        } else if (tok_slot[m] >= 0) {
-          *reinterpret_cast<__half2 *>(pool + (size_t)tok_slot[m] + head_off) = val;
-        }
+    for (int m = 0; m < kGroup; ++m) {
+      if (!store || m >= M || tok_pos[m0 + m] < 0) continue;
+      if (is_q) {
+        *reinterpret_cast<__half2 *>(y + (size_t)m * ys) = val[m];
+      } else if (tok_slot[m0 + m] >= 0) {
+        *reinterpret_cast<__half2 *>(pool + (size_t)tok_slot[m0 + m] + head_off) = val[m];
       }
     }
-    epi_sync();  // the staging arrays are rewritten by the next chunk
-    return;
-  }
-  if (epi == kEpiResidual || epi == kEpiF16) {
-    __half *y = p.y_f16 + (size_t)m0 * p.y_stride + row;
-    const __half *res = p.residual + (size_t)m0 * p.y_stride + row;
-    const long long ys = p.y_stride;
-    const bool residual = epi == kEpiResidual;
-    // All residual loads first: y and res are the same buffer (in place), so
-    // interleaved loads and stores would serialise one round trip per token.
-    __half rv[TN];
+  } else if constexpr (EK == kEkHalf) {
+    __half *y = p.y_f16 + (size_t)m0 * ys + row;
+    const __half *res = p.residual + (size_t)m0 * ys + row;
+    const bool residual = p.epilogue == kEpiResidual;
+    // All residual loads first: y and res are the same buffer (in place).
+    __half out[kGroup];
 #pragma unroll
-    for (int m = 0; m < TN; ++m) rv[m] = residual && in_range && m < M ? res[(size_t)m * ys] : __half(0.0f);
+    for (int m = 0; m < kGroup; ++m) out[m] = residual && in_range && m < M ? res[(size_t)m * ys] : __half(0.0f);
 #pragma unroll
-    for (int m = 0; m < TN; ++m)
-      if (in_range && m < M) y[(size_t)m * ys] = residual ? residual_value(rv[m], v[m]) : __float2half_rn(v[m]);
-    return;
-  }
-  // kEpiF32 / kEpiF32Partial
-  if (epi == kEpiF32Partial && p.xchg.world > 0) {
-    const int world = p.xchg.world, width = p.xchg.width;
-    for (int q = 0; q < world; ++q) {
-      float *dst = peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0 + m0) + row;
+    for (int m = 0; m < kGroup; ++m) out[m] = residual ? residual_value(out[m], v[m]) : __float2half_rn(v[m]);
 #pragma unroll
-      for (int m = 0; m < TN; ++m) {
-        if (m >= M) break;
-        if (in_range) dst[(size_t)m * width] = v[m];
+    for (int m = 0; m < kGroup; ++m)
+      if (in_range && m < M) y[(size_t)m * ys] = out[m];
+  } else {  // kEkF32: kEpiF32, kEpiF32Partial (optionally into every rank's exchange slot)
+    if (p.epilogue == kEpiF32Partial && p.xchg.world > 0) {
+      const int world = p.xchg.world, width = p.xchg.width;
+      for (int q = 0; q < world; ++q) {
+        float *dst = peer_slot(p.xchg, q, p.xchg.phase & 1, p.xchg.rank, p.xchg.row0 + m0) + row;
+#pragma unroll
+        for (int m = 0; m < kGroup; ++m)
+          if (in_range && m < M) dst[(size_t)m * width] = v[m];
       }
-    }
-    return;
-  }
-  float *y = p.y_f32 + (size_t)m0 * p.y_stride + row;
-  const long long ys = p.y_stride;
+    } else {
+      float *y = p.y_f32 + (size_t)m0 * ys + row;
 #pragma unroll
-  for (int m = 0; m < TN; ++m) {
-    if (m >= M) break;
-    if (in_range) y[(size_t)m * ys] = v[m];
+      for (int m = 0; m < kGroup; ++m)
+        if (in_range && m < M) y[(size_t)m * ys] = v[m];
+    }
   }
 }
 
-template <int TN>
+template <int TN, int EK>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map,
                 const GemvParams p, const GemmWork w) {
@@ -305,9 +286,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *acc_full = empty + S;
   uint64_t *acc_empty = acc_full + C::kAcc;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + C::kAcc);
-  __shared__ unsigned long long red_keys[4][kEpiChunk];
-  __shared__ int tok_pos[kEpiChunk];          // QKV epilogue: per-token position (-1: skip)
-  __shared__ long long tok_slot[kEpiChunk];   // ... and KV element offset of its page row
+  __shared__ unsigned long long red_keys[kEpiWarps][kGroup];
+  __shared__ int tok_pos[kMaxTokens];          // QKV epilogue: per-token position (-1: skip)
+  __shared__ long long tok_slot[kMaxTokens];   // ... and KV element offset of its page row
   __shared__ int s_last, s_fail;
   __shared__ unsigned long long s_ready;
 
@@ -322,7 +303,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < C::kAcc; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+      mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
     }
     fence_barrier_init();
     s_fail = 0;
@@ -425,6 +406,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     pdl_wait();
     const int q = warp & 3;  // the TMEM lane quarter this warp may read
     const int ew = warp - 2;
+    const int half = ew >> 2;  // this warp's 16-token groups: half, half + 2, ...
     const int t = threadIdx.x - 64;
     const int r = q * 32 + lane;
     const long long iters = (long long)w.tiles * w.kblocks;
@@ -437,76 +419,117 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       epi_sync();
       if (s_fail) break;
       tc_fence_after();
-      // The accumulator in chunks of CH columns (registers, not the stack).
-      constexpr int CH = TN < kEpiChunk ? TN : kEpiChunk;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TN);
       const int row = tile * kGemmTileRows + r;
-      const int chunks = (p.M + CH - 1) / CH;
-      if (pc.kb0 == 0 && pc.kb1 == w.kblocks) {
+      const int groups = (p.M + kGroup - 1) / kGroup;
+      const bool whole = pc.kb0 == 0 && pc.kb1 == w.kblocks;
+      int c_first = 0, c_last = 0;
+      if (!whole) {
+        // Part of the tile: store this piece's partial, then the tile's
+        // last-arriving piece sums all of them. The group barrier plus one
+        // acquire-release ticket orders every thread's partial stores before
+        // the reducer's loads (no separate fences).
+        float *part = w.ws + ((size_t)blockIdx.x * 2 + (j == 0 ? 0 : 1)) * TN * kGemmTileRows + r;
 #pragma unroll 1
-        for (int c = 0; c < chunks; ++c) {
-          float v[CH];
-#pragma unroll
-          for (int k = 0; k < CH / 16; ++k) tmem_ld16(tbase + (uint32_t)(c * CH + k * 16), v + k * 16);
+        for (int g = half; g < groups; g += 2) {
+          float v[kGroup];
+          tmem_ld16(tbase + (uint32_t)(g * kGroup), v);
           tmem_wait_ld();
-          if (c == chunks - 1) {  // the accumulator is free for the MMA warp
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+#pragma unroll
+          for (int m = 0; m < kGroup; ++m)
+            if (g * kGroup + m < p.M) __stcg(part + (size_t)(g * kGroup + m) * kGemmTileRows, v[m]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        epi_sync();
+        // The tile's pieces belong to the consecutive runs c_first .. c_last.
+        c_first = run_of(iters, gridDim.x, (long long)tile * w.kblocks);
+        c_last = run_of(iters, gridDim.x, (long long)(tile + 1) * w.kblocks - 1);
+        if (t == 0) {
+          const unsigned int prev = atomic_add_acq_rel_gpu(w.tile_counters + tile, 1u);
+          s_last = prev == (unsigned int)(c_last - c_first);
+          if (s_last) atomicExch(w.tile_counters + tile, 0u);
+        }
+        epi_sync();
+        if (!s_last) continue;
+      }
+      if constexpr (EK == kEkQKV) {
+        // One thread per token resolves its position and KV slot (page
+        // lookup, range checks) once for the tile; -1 marks a failed check.
+        if (t < p.M) {
+          const int pos = p.positions[t];
+          long long slot = -1;
+          const int ps = p.page_size;
+          if (pos < 0 || pos >= p.capacity) {
+            report_status(p.status, kStatusLengthRange, kWhereAppend, pos, t);
+          } else {
+            const int lp = pos / ps, off = pos % ps;
+            if (lp >= p.table_stride) {
+              report_status(p.status, kStatusLengthRange, kWhereAppend, pos, t);
+            } else {
+              const int page = p.block_table[(size_t)p.table_rows[t] * p.table_stride + lp];
+              if (page < 0 || page >= p.pool_pages) {
+                report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
+                              page < 0 ? lp : page, t);
+              } else {
+                slot = ((long long)page * (p.kv_rows / p.head_dim) * ps + off) * p.head_dim;
+              }
+            }
           }
-          apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys, tok_pos, tok_slot);
+          tok_pos[t] = (pos < 0 || pos >= p.capacity) ? -1 : pos;  // q rows need only the position
+          tok_slot[t] = slot;
         }
-        continue;
+        epi_sync();
       }
-      float *part = w.ws + ((size_t)blockIdx.x * 2 + (j == 0 ? 0 : 1)) * TN * kGemmTileRows;
 #pragma unroll 1
-      for (int c = 0; c < chunks; ++c) {
-        float v[CH];
+      for (int g0 = 0; g0 < groups; g0 += 2) {
+        const int g = g0 + half;
+        const bool active = g < groups;
+        float v[kGroup];
 #pragma unroll
-        for (int k = 0; k < CH / 16; ++k) tmem_ld16(tbase + (uint32_t)(c * CH + k * 16), v + k * 16);
-        tmem_wait_ld();
-#pragma unroll
-        for (int m = 0; m < CH; ++m)
-          if (c * CH + m < p.M) part[(size_t)(c * CH + m) * kGemmTileRows + r] = v[m];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
-      __threadfence();
-      epi_sync();
-      // The tile's pieces belong to the consecutive runs c_first .. c_last.
-      const int c_first = run_of(iters, gridDim.x, (long long)tile * w.kblocks);
-      const int c_last = run_of(iters, gridDim.x, (long long)(tile + 1) * w.kblocks - 1);
-      if (t == 0) {
-        const unsigned int prev = atomicAdd(w.tile_counters + tile, 1u);
-        s_last = prev == (unsigned int)(c_last - c_first);
-        if (s_last) atomicExch(w.tile_counters + tile, 0u);
-      }
-      epi_sync();
-      if (!s_last) continue;
-      __threadfence();
-      // Sum the partials in K order (run order); each piece's values for a
-      // chunk of tokens are requested together (one round trip per piece).
+        for (int m = 0; m < kGroup; ++m) v[m] = 0.0f;
+        if (!active) {
+        } else if (whole) {
+          tmem_ld16(tbase + (uint32_t)(g * kGroup), v);
+          tmem_wait_ld();
+        } else {
+          // The partials in K order (run order), kBatch pieces' loads in flight.
+          constexpr int kBatch = 4;
 #pragma unroll 1
-      for (int c = 0; c < chunks; ++c) {
-        float v[CH];
+          for (int c2 = c_first; c2 <= c_last; c2 += kBatch) {
+            float tmp[kBatch][kGroup];
 #pragma unroll
-        for (int m = 0; m < CH; ++m) v[m] = 0.0f;
-        for (int c2 = c_first; c2 <= c_last; ++c2) {
-          const bool first_piece = run_begin(iters, gridDim.x, c2) / w.kblocks == tile;
-          const float *src = w.ws + ((size_t)c2 * 2 + (first_piece ? 0 : 1)) * TN * kGemmTileRows + r;
-          float tmp[CH];
+            for (int e = 0; e < kBatch; ++e) {
+              const int cc = c2 + e;
+              if (cc <= c_last) {
+                const bool first_piece = run_begin(iters, gridDim.x, cc) / w.kblocks == tile;
+                const float *src = w.ws + ((size_t)cc * 2 + (first_piece ? 0 : 1)) * TN * kGemmTileRows + r +
+                                   (size_t)g * kGroup * kGemmTileRows;
 #pragma unroll
-          for (int m = 0; m < CH; ++m)
-            tmp[m] = (c * CH + m < p.M) ? __ldcg(src + (size_t)(c * CH + m) * kGemmTileRows) : 0.0f;
+                for (int m = 0; m < kGroup; ++m)
+                  tmp[e][m] = g * kGroup + m < p.M ? __ldcg(src + (size_t)m * kGemmTileRows) : 0.0f;
+              }
+            }
 #pragma unroll
-          for (int m = 0; m < CH; ++m) v[m] += tmp[m];
+            for (int e = 0; e < kBatch; ++e)
+              if (c2 + e <= c_last) {
+#pragma unroll
+                for (int m = 0; m < kGroup; ++m) v[m] += tmp[e][m];
+              }
+          }
         }
-        apply_epilogue<CH>(p, v, c * CH, row, lane, ew, t, red_keys, tok_pos, tok_slot);
+        apply_group<EK>(p, v, g * kGroup, active, row, lane, ew, t, red_keys, tok_pos, tok_slot);
       }
+      if (whole) {  // the accumulator is free for the MMA warp
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      }
+      if constexpr (EK == kEkQKV) epi_sync();  // the staging arrays are rewritten by the next piece
     }
     epi_sync();
-    if (p.epilogue == kEpiF32Partial && p.xchg.world > 0 && t < 32) {
+    if (EK == kEkF32 && p.epilogue == kEpiF32Partial && p.xchg.world > 0 && t < 32) {
       // Same causality chain as the GEMV: epilogue stores -> group barrier ->
       // GPU-scope arrival -> the last CTA's per-rank system-scope releases.
       int last = 0;
@@ -522,7 +545,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         st_release_sys(peer_flag(p.xchg, t, p.xchg.phase & 1, p.xchg.rank), value);
       }
     }
-    if (p.epilogue == kEpiArgmax && p.next_tokens != nullptr) {
+    if (EK == kEkArgmax && p.next_tokens != nullptr) {
       __threadfence();
       epi_sync();
       if (t == 0) {
@@ -547,11 +570,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   trace_emit(p.trace, t_entry, s_ready);
 }
 
-template <int TN>
+template <int TN, int EK>
 cudaError_t launch_tn(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,
                       const GemmPlan &plan, float *ws, unsigned int *tile_counters, cudaStream_t stream, bool pdl) {
   using C = GemmCfg<TN>;
-  auto kernel = gemm_kernel<TN>;
+  auto kernel = gemm_kernel<TN, EK>;
   static std::mutex mu;
   static std::unordered_map<int, bool> configured;
   int dev = 0;
@@ -577,6 +600,18 @@ cudaError_t launch_tn(const GemvParams &p, const CUtensorMap &w_map, const CUten
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, w_map, x_map, p, w);
+}
+
+template <int EK>
+cudaError_t launch_ek(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map, const GemmPlan &plan,
+                      float *ws, unsigned int *tile_counters, cudaStream_t stream, bool pdl) {
+  switch (plan.tn) {
+    case 16: return launch_tn<16, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 32: return launch_tn<32, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 64: return launch_tn<64, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 128: return launch_tn<128, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -656,12 +691,13 @@ cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUt
     default:
       return cudaErrorInvalidValue;
   }
-  switch (plan.tn) {
-    case 16: return launch_tn<16>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
-    case 32: return launch_tn<32>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
-    case 64: return launch_tn<64>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
-    case 128: return launch_tn<128>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
-    default: return cudaErrorInvalidValue;
+  switch (p.epilogue) {
+    case kEpiQKV: return launch_ek<kEkQKV>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case kEpiSwiGLU: return launch_ek<kEkSwiGLU>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case kEpiResidual:
+    case kEpiF16: return launch_ek<kEkHalf>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case kEpiArgmax: return launch_ek<kEkArgmax>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    default: return launch_ek<kEkF32>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
   }
 }
 
