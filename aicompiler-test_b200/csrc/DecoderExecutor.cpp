@@ -191,7 +191,7 @@ std::string DecoderExecutor::allocate() {
       tiles = std::max(tiles, (size_t)plan.tiles);
     }
     if (!(e = make(wsFloats, F32, &gemmWs_, &activationBytes_)).empty()) return e;
-    if (!(e = make(tiles, I32, &gemmTickets_, &activationBytes_)).empty()) return e;
+    if (!(e = make(2 * tiles, I32, &gemmTickets_, &activationBytes_)).empty()) return e;
   }
   if (cfg_.tpSize > 1) {
     // Exchange window (zeroed int32 words), CTA-done counters per partial-sum

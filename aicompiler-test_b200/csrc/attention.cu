@@ -110,6 +110,133 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// One warp's 16 positions [p0, p0 + 16) of a K/V tile held in stage memory
+// (sKs, sVs: the stage's K and V bytes; rows r0 .. r0 + 15 of the tile):
+// scores against the query fragments qa, masking (positions >= end, rows
+// whose page failed its checks), the online-softmax update of (m_run, l_run)
+// and P.V into acc. BOX stages hold 128-byte-swizzled 64-dim halves, others
+// padded rows. Returns true when V rows were zeroed (generic-proxy writes: a
+// proxy fence is due before TMA refills the stage).
+template <int D, int G, bool BOX>
+__device__ __forceinline__ bool tile_step(unsigned char *sKs, unsigned char *sVs, int r0, int p0, int end,
+                                          const int *valid, float scale, const uint32_t (&qa)[D / 16][4],
+                                          float &m_run, float &l_run, float (&acc)[D / 8][4], int lane) {
+  using C = Cfg<D, G, BOX>;
+  constexpr int T = C::T, ROW = C::kRow;
+  const int tq = lane & 3;
+  const __half *k = reinterpret_cast<const __half *>(sKs) + (size_t)r0 * ROW;
+  const __half *v = reinterpret_cast<const __half *>(sVs) + (size_t)r0 * ROW;
+  (void)T;
+  // BOX: a whole box landed; rows of positions past `end` (or of a missing
+  // page) hold stale values: zero their V rows (P is 0 there, 0 * NaN is not).
+  bool zeroed = false;
+  if (BOX && p0 < end) {
+    const int lp = lane & 15;
+    const bool bad = !(p0 + lp < end && valid[lp]);
+    if (__any_sync(0xffffffffu, bad)) {
+      unsigned char *vs = sVs;
+#pragma unroll
+      for (int h = 0; h < D / 64; ++h) {
+        // lanes 0-15 and 16-31 take the two 64-byte halves of row r0 + lp
+        uint4 *dst = reinterpret_cast<uint4 *>(vs + h * T * 128 + (r0 + lp) * 128 + (lane >> 4) * 64);
+        if (bad) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      __syncwarp();
+      zeroed = true;
+    }
+  }
+  if (p0 < end) {
+    // Scores S[16 heads x 16 positions] as two n-tiles of 8 positions.
+    float sc[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+      for (int kk = 0; kk < C::kKSteps; ++kk) {
+        uint32_t b0, b1;
+        // matrices: rows = positions nt*8..+7, columns = dims kk*16..+7 and +8..+15
+        const __half *addr;
+        if (BOX) {
+          const int R = r0 + nt * 8 + (lane & 7), d0 = kk * 16 + ((lane >> 3) & 1) * 8;
+          addr = reinterpret_cast<const __half *>(sKs + (d0 >> 6) * T * 128 + R * 128 +
+                                                  ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
+        } else {
+          addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
+        }
+        ldmatrix_x2(b0, b1, addr);
+        mma_16816(sc[nt], qa[kk], b0, b1);
+      }
+    }
+    // Scale, mask, online softmax (row gq owns c0/c1; c2/c3 are rows gq+8, unused).
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int lp = nt * 8 + 2 * tq + j;
+        const bool ok = p0 + lp < end && valid[lp];
+        sc[nt][j] = ok ? sc[nt][j] * scale : -INFINITY;
+        mx = fmaxf(mx, sc[nt][j]);
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float m_new = fmaxf(m_run, mx);
+    const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
+    float psum = 0.0f;
+    float pr[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        pr[nt][j] = (sc[nt][j] == -INFINITY) ? 0.0f : expf(sc[nt][j] - m_new);
+        psum += pr[nt][j];
+      }
+    }
+    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+    l_run = l_run * rescale + psum;
+    m_run = m_new;
+    // P as the A operand (16 heads x 16 positions) in two fp16 parts, hi + lo,
+    // so the probabilities keep ~22 bits (the reference multiplies fp32
+    // probabilities by the values).
+    uint32_t pa[4], pl[4];
+    {
+      const __half2 h0 = __floats2half2_rn(pr[0][0], pr[0][1]);
+      const __half2 h1 = __floats2half2_rn(pr[1][0], pr[1][1]);
+      const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+      pa[0] = *reinterpret_cast<const uint32_t *>(&h0);
+      pa[2] = *reinterpret_cast<const uint32_t *>(&h1);
+      pl[0] = pack_half2(pr[0][0] - f0.x, pr[0][1] - f0.y);
+      pl[2] = pack_half2(pr[1][0] - f1.x, pr[1][1] - f1.y);
+      pa[1] = pa[3] = pl[1] = pl[3] = 0u;
+    }
+    // O[16 x D] += P . V[16 positions x D].
+#pragma unroll
+    for (int dt = 0; dt < C::kDTiles; ++dt) {
+      acc[dt][0] *= rescale;
+      acc[dt][1] *= rescale;
+      uint32_t b0, b1;
+      // matrices (transposed on load): rows = positions 0..7 and 8..15, columns = dims dt*8..+7
+      const __half *addr;
+      if (BOX) {
+        const int R = r0 + (lane & 15), d0 = dt * 8;
+        addr = reinterpret_cast<const __half *>(sVs + (d0 >> 6) * T * 128 + R * 128 +
+                                                ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
+      } else {
+        addr = v + (size_t)(lane & 15) * ROW + dt * 8;
+      }
+      ldmatrix_x2_trans(b0, b1, addr);
+      mma_16816(acc[dt], pl, b0, b1);
+      mma_16816(acc[dt], pa, b0, b1);
+    }
+  }
+  return zeroed;
+}
+
 // Grid (max_splits, Hkv, rows), 4 warps, launched in clusters of `cluster`
 // CTAs along the splits. A CTA owns one KV head of one query row and a chunk
 // of key positions; each warp runs flash-decoding on its own 16 positions of
@@ -370,119 +497,10 @@ __global__ void __launch_bounds__(kThreads)
       break;
     }
     const int r0 = warp * 16;  // this warp's 16 rows of the tile
-    const int p0 = begin + t * T + r0;
-    const __half *k = sK + ((size_t)stage * T + r0) * ROW;
-    const __half *v = sV + ((size_t)stage * T + r0) * ROW;
-    const int *valid = sValid + stage * T + r0;
-    // BOX: a whole box landed; rows of positions past `end` (or of a missing
-    // page) hold stale values: zero their V rows (P is 0 there, 0 * NaN is not).
-    bool zeroed = false;
-    if (BOX && p0 < end) {
-      const int lp = lane & 15;
-      const bool bad = !(p0 + lp < end && valid[lp]);
-      if (__any_sync(0xffffffffu, bad)) {
-        unsigned char *vs = reinterpret_cast<unsigned char *>(sV) + (size_t)stage * C::kStageBytes;
-#pragma unroll
-        for (int h = 0; h < D / 64; ++h) {
-          // lanes 0-15 and 16-31 take the two 64-byte halves of row r0 + lp
-          uint4 *dst = reinterpret_cast<uint4 *>(vs + h * T * 128 + (r0 + lp) * 128 + (lane >> 4) * 64);
-          if (bad) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
-          }
-        }
-        __syncwarp();
-        zeroed = true;
-      }
-    }
-    if (p0 < end) {
-      // Scores S[16 heads x 16 positions] as two n-tiles of 8 positions.
-      float sc[2][4];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
-#pragma unroll
-        for (int kk = 0; kk < C::kKSteps; ++kk) {
-          uint32_t b0, b1;
-          // matrices: rows = positions nt*8..+7, columns = dims kk*16..+7 and +8..+15
-          const __half *addr;
-          if (BOX) {
-            const int R = r0 + nt * 8 + (lane & 7), d0 = kk * 16 + ((lane >> 3) & 1) * 8;
-            addr = reinterpret_cast<const __half *>(reinterpret_cast<const unsigned char *>(sK) +
-                                                    (size_t)stage * C::kStageBytes + (d0 >> 6) * T * 128 + R * 128 +
-                                                    ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
-          } else {
-            addr = k + (size_t)(nt * 8 + (lane & 7)) * ROW + kk * 16 + ((lane >> 3) & 1) * 8;
-          }
-          ldmatrix_x2(b0, b1, addr);
-          mma_16816(sc[nt], qa[kk], b0, b1);
-        }
-      }
-      // Scale, mask, online softmax (row gq owns c0/c1; c2/c3 are rows gq+8, unused).
-      float mx = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int lp = nt * 8 + 2 * tq + j;
-          const bool ok = p0 + lp < end && valid[lp];
-          sc[nt][j] = ok ? sc[nt][j] * p.scale : -INFINITY;
-          mx = fmaxf(mx, sc[nt][j]);
-        }
-      }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m_run, mx);
-      const float rescale = (m_run == -INFINITY) ? 0.0f : expf(m_run - m_new);
-      float psum = 0.0f;
-      float pr[2][2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          pr[nt][j] = (sc[nt][j] == -INFINITY) ? 0.0f : expf(sc[nt][j] - m_new);
-          psum += pr[nt][j];
-        }
-      }
-      psum += __shfl_xor_sync(0xffffffffu, psum, 1);
-      psum += __shfl_xor_sync(0xffffffffu, psum, 2);
-      l_run = l_run * rescale + psum;
-      m_run = m_new;
-      // P as the A operand (16 heads x 16 positions) in two fp16 parts, hi + lo,
-      // so the probabilities keep ~22 bits (the reference multiplies fp32
-      // probabilities by the values).
-      uint32_t pa[4], pl[4];
-      {
-        const __half2 h0 = __floats2half2_rn(pr[0][0], pr[0][1]);
-        const __half2 h1 = __floats2half2_rn(pr[1][0], pr[1][1]);
-        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
-        pa[0] = *reinterpret_cast<const uint32_t *>(&h0);
-        pa[2] = *reinterpret_cast<const uint32_t *>(&h1);
-        pl[0] = pack_half2(pr[0][0] - f0.x, pr[0][1] - f0.y);
-        pl[2] = pack_half2(pr[1][0] - f1.x, pr[1][1] - f1.y);
-        pa[1] = pa[3] = pl[1] = pl[3] = 0u;
-      }
-      // O[16 x D] += P . V[16 positions x D].
-#pragma unroll
-      for (int dt = 0; dt < C::kDTiles; ++dt) {
-        acc[dt][0] *= rescale;
-        acc[dt][1] *= rescale;
-        uint32_t b0, b1;
-        // matrices (transposed on load): rows = positions 0..7 and 8..15, columns = dims dt*8..+7
-        const __half *addr;
-        if (BOX) {
-          const int R = r0 + (lane & 15), d0 = dt * 8;
-          addr = reinterpret_cast<const __half *>(reinterpret_cast<const unsigned char *>(sV) +
-                                                  (size_t)stage * C::kStageBytes + (d0 >> 6) * T * 128 + R * 128 +
-                                                  ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
-        } else {
-          addr = v + (size_t)(lane & 15) * ROW + dt * 8;
-        }
-        ldmatrix_x2_trans(b0, b1, addr);
-        mma_16816(acc[dt], pl, b0, b1);
-        mma_16816(acc[dt], pa, b0, b1);
-      }
-    }
+    const bool zeroed = tile_step<D, G, BOX>(reinterpret_cast<unsigned char *>(sK) + (size_t)stage * C::kStageBytes,
+                                             reinterpret_cast<unsigned char *>(sV) + (size_t)stage * C::kStageBytes,
+                                             r0, begin + t * T + r0, end, sValid + stage * T + r0, p.scale, qa,
+                                             m_run, l_run, acc, lane);
     if (zeroed) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before TMA refills
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[stage]);

@@ -264,7 +264,7 @@ size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows) {
   if (n <= 0 || k <= 0 || rows <= 0 || rows > 128) return 0;
   const tmc::GemmPlan plan = tmc::plan_gemm(n, k, rows, sm_count());
   const size_t partial = (tmc::gemm_workspace_floats(plan) * 4 + 255) / 256 * 256;
-  return partial + (size_t)plan.tiles * 4;
+  return partial + (size_t)plan.tiles * 8;
 }
 
 int tmc_k_batched_gemm_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k, int n,
@@ -277,7 +277,7 @@ int tmc_k_batched_gemm_f16_f32out(const void *x_f16, const void *w_f16, float *y
   auto *ws = static_cast<unsigned char *>(workspace);
   auto *tickets = reinterpret_cast<unsigned int *>(ws + partial);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(tickets, 0, (size_t)plan.tiles * 4, s);
+  cudaError_t e = cudaMemsetAsync(tickets, 0, (size_t)plan.tiles * 8, s);
   if (e != cudaSuccess) return cuda_fail(e, "clearing gemm tickets");
   CUtensorMap wm, xm;
   if ((e = tmc::make_tensor_map_f16(&wm, w_f16, n, k, tmc::kGemmTileRows)) != cudaSuccess)

@@ -130,6 +130,22 @@ __device__ __forceinline__ bool wait_flag_geq(const unsigned int *flag, unsigned
   return true;
 }
 
+// GPU-scope acquire load and bounded wait (counters shared by the CTAs of one
+// kernel on one GPU).
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int *p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool wait_count_geq_gpu(const unsigned int *counter, unsigned int value,
+                                                   unsigned long long budget_ns) {
+  const unsigned long long t0 = global_ns();
+  while (ld_acquire_gpu(counter) < value) {
+    if (global_ns() - t0 > budget_ns) return false;
+  }
+  return true;
+}
+
 // ---- global loads ----------------------------------------------------------
 // Streaming 16-byte load of immutable data: read-only path, no L1 allocation.
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {

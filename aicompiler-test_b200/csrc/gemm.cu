@@ -19,8 +19,14 @@
 // Work division is stream-K (gemm.cuh): CTA c streams the iterations
 // [W c / G, W (c + 1) / G) of the W = tiles x kblocks (tile, K block) space;
 // each tile it touches is one piece. A piece that covers only part of its
-// tile writes an fp32 partial to the CTA's workspace slot, and the tile's
-// last-arriving piece (atomic ticket) sums the tile's partials in K order.
+// tile writes an fp32 partial to the CTA's workspace slot and counts itself
+// in on the tile's arrival counter. The tile's "closers" -- the pieces whose
+// runs end inside the tile, so their CTAs have nothing left to stream -- wait
+// (bounded) for all pieces, then share the reduction: closer i sums groups
+// i, i + closers, ... of 16 tokens over all partials in K order and applies
+// the epilogue. Every CTA of the grid is resident before any closer waits
+// (grid <= SMs, one CTA per SM, and the next kernel launches only after all of
+// them passed their dependency trigger), so the waits end.
 // Every mbarrier wait is bounded (mbarrier.cuh); a timeout is reported in the
 // device status block and the CTA still releases its tensor memory and exits.
 #include "gemm.cuh"
@@ -38,6 +44,7 @@ constexpr int kGemmThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kGroup = 16;      // token columns an epilogue step handles (one tcgen05.ld)
 constexpr int kMaxTokens = 128;  // the largest TN
+constexpr unsigned long long kTileWaitNs = 1000000000ull;  // a closer waits at most 1 s for the tile's pieces
 
 // Epilogue kinds the kernel is specialised on: each instantiation carries one
 // epilogue body, run by a non-unrolled loop over 16-token groups, so the
@@ -151,8 +158,8 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 256;" :::
 template <int EK>
 __device__ __forceinline__ void apply_group(const GemvParams &p, const float (&v)[kGroup], int m0, bool active,
                                             int row, int lane, int ew, int t,
-                                            unsigned long long (*red_keys)[kGroup], const int *tok_pos,
-                                            const long long *tok_slot) {
+                                            unsigned long long (*red_keys)[kGroup], int *half_m0,
+                                            const int *tok_pos, const long long *tok_slot) {
   const int M = active ? p.M - m0 : 0;
   const bool in_range = row < p.N;
   const long long ys = p.y_stride;
@@ -177,12 +184,13 @@ __device__ __forceinline__ void apply_group(const GemvParams &p, const float (&v
     if (lane == 0) {
 #pragma unroll
       for (int m = 0; m < kGroup; ++m) red_keys[ew][m] = key[m];
+      if ((ew & 3) == 0) half_m0[ew >> 2] = active ? m0 : -1;
     }
     epi_sync();
     if (t < 2 * kGroup) {  // one thread per token of the two halves' groups
       const int hf = t / kGroup, tok = t % kGroup;
-      const int mm = m0 - (ew >> 2) * kGroup + hf * kGroup + tok;
-      if (mm < p.M) {
+      const int mm = half_m0[hf] + tok;
+      if (half_m0[hf] >= 0 && mm < p.M) {
         unsigned long long k = red_keys[hf * 4][tok];
 #pragma unroll
         for (int e = 1; e < 4; ++e) k = red_keys[hf * 4 + e][tok] > k ? red_keys[hf * 4 + e][tok] : k;
@@ -287,6 +295,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint64_t *acc_empty = acc_full + C::kAcc;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + C::kAcc);
   __shared__ unsigned long long red_keys[kEpiWarps][kGroup];
+  __shared__ int half_m0[2];
   __shared__ int tok_pos[kMaxTokens];          // QKV epilogue: per-token position (-1: skip)
   __shared__ long long tok_slot[kMaxTokens];   // ... and KV element offset of its page row
   __shared__ int s_last, s_fail;
@@ -423,12 +432,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int row = tile * kGemmTileRows + r;
       const int groups = (p.M + kGroup - 1) / kGroup;
       const bool whole = pc.kb0 == 0 && pc.kb1 == w.kblocks;
-      int c_first = 0, c_last = 0;
+      int c_first = 0, closers = 1, ci = 0;
       if (!whole) {
-        // Part of the tile: store this piece's partial, then the tile's
-        // last-arriving piece sums all of them. The group barrier plus one
-        // acquire-release ticket orders every thread's partial stores before
-        // the reducer's loads (no separate fences).
+        // Part of the tile: store this piece's partial; the group barrier
+        // plus one acquire-release arrival orders every thread's stores
+        // before the closers' loads.
         float *part = w.ws + ((size_t)blockIdx.x * 2 + (j == 0 ? 0 : 1)) * TN * kGemmTileRows + r;
 #pragma unroll 1
         for (int g = half; g < groups; g += 2) {
@@ -443,16 +451,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
         epi_sync();
-        // The tile's pieces belong to the consecutive runs c_first .. c_last.
+        // The tile's pieces belong to the consecutive runs c_first .. c_last;
+        // the closers are those whose runs end inside the tile.
         c_first = run_of(iters, gridDim.x, (long long)tile * w.kblocks);
-        c_last = run_of(iters, gridDim.x, (long long)(tile + 1) * w.kblocks - 1);
+        const int c_last = run_of(iters, gridDim.x, (long long)(tile + 1) * w.kblocks - 1);
+        const long long tile_end = (long long)(tile + 1) * w.kblocks;
+        const int c_close = run_begin(iters, gridDim.x, c_last + 1) <= tile_end ? c_last : c_last - 1;
+        closers = c_close - c_first + 1;
+        ci = (int)blockIdx.x - c_first;
+        unsigned int *arrived = w.tile_counters + tile;
         if (t == 0) {
-          const unsigned int prev = atomic_add_acq_rel_gpu(w.tile_counters + tile, 1u);
-          s_last = prev == (unsigned int)(c_last - c_first);
-          if (s_last) atomicExch(w.tile_counters + tile, 0u);
+          atomic_add_acq_rel_gpu(arrived, 1u);
+          if (ci < closers && !wait_count_geq_gpu(arrived, (unsigned int)(c_last - c_first + 1), kTileWaitNs)) {
+            report_status(p.status, kStatusWaitTimeout, kWhereGemm, 2, tile);
+            s_fail = 1;
+          }
         }
         epi_sync();
-        if (!s_last) continue;
+        if (ci >= closers) continue;  // not a closer: its run goes on
+        if (s_fail) break;
       }
       if constexpr (EK == kEkQKV) {
         // One thread per token resolves its position and KV slot (page
@@ -482,10 +499,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         epi_sync();
       }
+      // Groups this CTA applies: all of a whole tile, or a closer's share.
+      const int assigned = whole ? groups : (ci < groups ? (groups - ci + closers - 1) / closers : 0);
 #pragma unroll 1
-      for (int g0 = 0; g0 < groups; g0 += 2) {
-        const int g = g0 + half;
-        const bool active = g < groups;
+      for (int j0 = 0; j0 < assigned; j0 += 2) {
+        const int jj = j0 + half;
+        const bool active = jj < assigned;
+        const int g = whole ? jj : ci + jj * closers;
         float v[kGroup];
 #pragma unroll
         for (int m = 0; m < kGroup; ++m) v[m] = 0.0f;
@@ -496,6 +516,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         } else {
           // The partials in K order (run order), kBatch pieces' loads in flight.
           constexpr int kBatch = 4;
+          const int c_last = run_of(iters, gridDim.x, (long long)(tile + 1) * w.kblocks - 1);
 #pragma unroll 1
           for (int c2 = c_first; c2 <= c_last; c2 += kBatch) {
             float tmp[kBatch][kGroup];
@@ -519,7 +540,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               }
           }
         }
-        apply_group<EK>(p, v, g * kGroup, active, row, lane, ew, t, red_keys, tok_pos, tok_slot);
+        apply_group<EK>(p, v, g * kGroup, active, row, lane, ew, t, red_keys, half_m0, tok_pos, tok_slot);
+      }
+      if (!whole) {
+        // The last closer to finish resets the tile's counters.
+        epi_sync();
+        if (t == 0 && atomicAdd(w.tile_counters + w.tiles + tile, 1u) == (unsigned int)(closers - 1)) {
+          w.tile_counters[tile] = 0u;
+          w.tile_counters[w.tiles + tile] = 0u;
+        }
       }
       if (whole) {  // the accumulator is free for the MMA warp
         tc_fence_before();

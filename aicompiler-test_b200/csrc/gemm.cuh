@@ -49,7 +49,7 @@ cudaError_t make_tensor_map_f16(CUtensorMap *map, const void *base, uint64_t row
 // x rows with box_rows plan.tn. p.W/p.N/p.K/p.M and the epilogue fields are
 // used as by launch_gemv; the prologue must already be applied (x is read as
 // fp16 rows). ws: gemm_workspace_floats(plan) floats; tile_counters:
-// plan.tiles zeroed words (left zeroed). Supported epilogues: kEpiQKV,
+// 2 * plan.tiles zeroed words (left zeroed). Supported epilogues: kEpiQKV,
 // kEpiSwiGLU, kEpiResidual, kEpiF16, kEpiF32, kEpiF32Partial (with or
 // without peer exchange) and kEpiArgmax.
 cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,

@@ -101,6 +101,40 @@ def test_paged_attention_c4_subset(rt):
     check(got, ref)
 
 
+# Batched launches: more (split, KV head, row) CTAs than fit on the GPU at
+# once (several waves of clustered CTAs), ragged contexts.
+ROWS_CASES = [
+    # (rows, hq, hkv, d, lengths seed, max length, splits)
+    (64, 32, 8, 128, 11, 1500, (8, 64)),
+    (64, 32, 8, 128, 12, 1200, (4, 64)),
+    (96, 16, 2, 128, 13, 700, (16, 32)),   # G = 8
+    (200, 4, 2, 64, 14, 300, (8, 16)),     # G = 2, head_dim 64
+]
+
+
+@pytest.mark.parametrize("rows,hq,hkv,d,seed,max_len,splits", ROWS_CASES)
+def test_paged_attention_many_waves_matches_oracle(rt, rows, hq, hkv, d, seed, max_len, splits):
+    rng = np.random.default_rng(seed)
+    lengths = [int(x) for x in rng.integers(1, max_len, rows)]
+    lengths[0], lengths[1], lengths[2] = 1, 64, 1024 if max_len > 1024 else 48
+    q, kp, vp, table, trows, pos = make_case(seed, rows, hq, hkv, d, 16, lengths)
+    capacity = table.shape[1] * 16
+    ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
+                                 table, trows, pos, hkv, 16)
+    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, 16, capacity, *splits)
+    check(got, ref)
+
+
+def test_many_waves_missing_page_reports_device_status(rt):
+    import tmc_cuda
+    lengths = [700] * 64
+    q, kp, vp, table, trows, pos = make_case(21, 64, 32, 8, 128, 16, lengths)
+    table[40, 7] = -1
+    with pytest.raises(tmc_cuda.TmcError) as err:
+        run_attention(rt, q, kp, vp, table, trows, pos, 8, 16, table.shape[1] * 16, 8, 64)
+    assert err.value.code == tmc_cuda.ERR_DEVICE_STATUS
+
+
 def test_missing_page_reports_device_status(rt):
     import tmc_cuda
     q, kp, vp, table, trows, pos = make_case(3, 1, 4, 4, 16, 4, [20])
