@@ -591,8 +591,12 @@ cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, 
   const int ngroups = (p.N + R - 1) / R;
   int grid = (ngroups + kWarps / KS - 1) / (kWarps / KS);
   const int wave = occ * num_sms;
+  // Whole multiples of the SM count: teams take groups CTA-minor (group g goes
+  // to CTA g % grid), so equal CTA counts per SM give every SM an equal share
+  // of the rows (256 CTAs on 148 SMs would leave 108 SMs with twice the rows
+  // of the other 40, and the launch would wait for them).
+  if (grid > num_sms) grid = (grid + num_sms - 1) / num_sms * num_sms;
   if (grid > wave) grid = wave;
-  if (p.work_counter != nullptr && grid > kGemvPools) grid -= grid % kGemvPools;
   if (grid < 1) grid = 1;
 
   cudaLaunchConfig_t cfg = {};
