@@ -720,6 +720,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
   // the SMs twice; many pairs (batched decode) -> a power of two that gives
   // about 16 CTAs per SM, so the last partial wave is short.
   int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
+  if (R * hkvL_ < numSms_) splits = std::min(splits, attnSplitCap_);
   if (R * hkvL_ >= numSms_) {
     splits = 1;
     while (splits < 16 && 2 * splits * R * hkvL_ <= 16 * numSms_) splits *= 2;
@@ -1140,8 +1141,15 @@ std::string DecoderExecutor::launchStep(int R, bool feed, bool distinct) {
 }
 
 std::string DecoderExecutor::uploadStepInputs(int R, const std::int32_t *tokens, const std::int32_t *positions,
-                                              const std::int32_t *tableRows) {
+                                              const std::int32_t *tableRows, int steps) {
   const int M = cfg_.maxRows;
+  // The attention chunk policy below (min_chunk 64, max_chunk 128, one
+  // 16-CTA cluster filled before a second): splits for the longest context.
+  int maxLen = 1;
+  for (int r = 0; r < R; ++r) maxLen = std::max(maxLen, positions[r] + steps);
+  int need = (maxLen + 63) / 64;
+  if (need > 16) need = std::max((maxLen + 127) / 128, 16);
+  attnSplitCap_ = (need + 15) / 16 * 16;
   for (int i = 0; i < 3 * M; ++i) pinnedIO_[i] = 0;
   for (int r = 0; r < M; ++r) lastPositions_[r] = r < R ? positions[r] : 0;
   for (int r = 0; r < R; ++r) {
@@ -1310,7 +1318,7 @@ std::string DecoderExecutor::generate(const std::int32_t *slots, const std::int3
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
   const auto c0 = std::chrono::steady_clock::now();
-  err = uploadStepInputs(rows, tokens, positions.data(), tableRows.data());
+  err = uploadStepInputs(rows, tokens, positions.data(), tableRows.data(), steps);
   if (err.empty()) {
     cudaError_t ce = cudaMemsetAsync(historyCounter_->data(), 0, 4, rt_.stream());
     if (ce != cudaSuccess) err = cudaText("history reset", ce);

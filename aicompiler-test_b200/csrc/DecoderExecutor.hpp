@@ -188,9 +188,15 @@ class DecoderExecutor {
   std::string enqueueStep(int rows, bool feed, bool distinct);
   std::string enqueueKernel(int kind, int layer, int rows, bool feed, bool distinct);
   std::string launchStep(int rows, bool feed, bool distinct);
-  static int graphKey(int rows, bool feed, bool distinct) { return rows * 4 + (feed ? 2 : 0) + (distinct ? 1 : 0); }
+  // Step graphs differ by rows, feed-back, distinct rows and the attention
+  // split cap the step's contexts need.
+  int graphKey(int rows, bool feed, bool distinct) const {
+    return attnSplitCap_ * 1024 + rows * 4 + (feed ? 2 : 0) + (distinct ? 1 : 0);
+  }
+  // Uploads a step's tokens, positions and table rows and sets the attention
+  // split cap for contexts up to max(position) + steps.
   std::string uploadStepInputs(int rows, const std::int32_t *tokens, const std::int32_t *positions,
-                               const std::int32_t *tableRows);
+                               const std::int32_t *tableRows, int steps = 1);
   std::string writeBlockRow(int slot, const std::vector<std::int32_t> &row);
   void computeRope();
 
@@ -252,6 +258,10 @@ class DecoderExecutor {
     cudaGraphExec_t exec = nullptr;
   };
   std::map<int, Graph> graphs_;
+  // Attention split slots of the next step's launch: the splits its longest
+  // context can use under this decoder's chunk policy, in whole 16-CTA
+  // clusters (idle clusters would still be launched and scheduled).
+  int attnSplitCap_ = 64;
 
   std::size_t modelBytes_ = 0, kvBytes_ = 0, activationBytes_ = 0;
 };
