@@ -70,3 +70,52 @@ def decode_worker(rank, world, uid, npz, page_size, generate_steps, queue, mode=
     finally:
         if dist is not None and dist.is_initialized():
             dist.destroy_process_group()
+
+
+def batched_worker(rank, world, uid, queue, mode="nccl", port=0, rows=12, steps=3):
+    """Batched tensor-parallel decode of a seeded random model: `rows`
+    sequences prefilled (chunks of up to 16 rows) and `steps` batched decode
+    steps through the tensor-core projections; returns the rank's logits slices
+    and the greedy tokens. world == 1 is the single-GPU reference."""
+    dist = None
+    try:
+        sys.path.insert(0, ROOT)
+        sys.path.insert(0, os.path.join(ROOT, "aicompiler-test_b200"))
+        import tmc_cuda
+
+        rt = tmc_cuda.Runtime(rank)
+        dec = tmc_cuda.Decoder(rt, 1024, 16, 2816, 8000, 2, 256, kv_heads=4, page_size=16, max_rows=16,
+                               max_slots=16, tp_rank=rank, tp_size=world)
+        if world > 1 and mode == "p2p":
+            import torch.distributed as dist
+            dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                    world_size=world)
+            handles = [None] * world
+            dist.all_gather_object(handles, dec.exchange_handle())
+            dec.attach_peers(handles, rank)
+        elif world > 1:
+            dec.attach_nccl(uid, world, rank)
+        dec.init_random(seed=3, std=0.05)
+        rng = np.random.default_rng(7)
+        toks = []
+        for s in range(rows):
+            prompt = rng.integers(0, 8000, 20 + 3 * s).astype(np.int32)
+            toks.append(dec.prefill(prompt, slot=s, logits=False)[1])
+        out = {"rank": rank, "local_vocab": dec.local_vocab, "logits": [], "tokens": []}
+        slots = list(range(rows))
+        for _ in range(steps):
+            lg, nxt = dec.decode(toks, slots=slots)
+            out["logits"].append(np.asarray(lg))
+            toks = [int(t) for t in nxt]
+            out["tokens"].append(toks)
+        rt.synchronize()
+        if dist is not None:
+            dist.barrier()
+        dec.close()
+        rt.close()
+        queue.put(out)
+    except Exception:
+        queue.put({"rank": rank, "error": traceback.format_exc()})
+    finally:
+        if dist is not None and dist.is_initialized():
+            dist.destroy_process_group()
