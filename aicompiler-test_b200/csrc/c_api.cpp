@@ -11,6 +11,7 @@
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "misc.cuh"
+#include "fusion.cuh"
 #include "rmsnorm.cuh"
 #include "tmc_cuda.h"
 
@@ -196,6 +197,37 @@ int tmc_k_rmsnorm(const void *x, const void *gamma, void *y, int rows, int width
   const cudaError_t e = threads == 0 ? tmc::launch_rmsnorm_baseline(x, gamma, y, rows, width, eps, fp16 != 0, st)
                                      : tmc::launch_rmsnorm(x, gamma, y, rows, width, eps, fp16 != 0, threads, st);
   return e == cudaSuccess ? ok() : cuda_fail(e, "rmsnorm launch");
+}
+
+int tmc_k_fused_add_norm(const void *x, const void *b, const void *w, const void *c, void *y, int rows, int width,
+                         int b_rows, float eps, int layer_norm, int fp16, void *stream) {
+  if (!x || !b || !w || !y || (layer_norm && !c)) return fail(TMC_ERR_INVALID, "null pointer");
+  if (rows < 1 || width < 1 || (b_rows != 1 && b_rows != rows))
+    return fail(TMC_ERR_INVALID, "fused add-norm: rows, width >= 1 and b_rows 1 or rows");
+  if (!(eps > 0.0f)) return fail(TMC_ERR_INVALID, "eps must be positive");
+  const cudaError_t e = tmc::launch_fused_add_norm(x, b, w, c, y, rows, width, b_rows, eps, layer_norm != 0, fp16 != 0,
+                                                   static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "fused add-norm launch");
+}
+
+int tmc_k_fused_silu_mul(const void *x, const void *b, void *y, int rows, int width, int b_rows, int fp16,
+                         void *stream) {
+  if (!x || !b || !y) return fail(TMC_ERR_INVALID, "null pointer");
+  if (rows < 1 || width < 1 || (b_rows != 1 && b_rows != rows))
+    return fail(TMC_ERR_INVALID, "fused silu-mul: rows, width >= 1 and b_rows 1 or rows");
+  const cudaError_t e =
+      tmc::launch_fused_silu_mul(x, b, y, rows, width, b_rows, fp16 != 0, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? ok() : cuda_fail(e, "fused silu-mul launch");
+}
+
+int tmc_k_fused_linear_relu(const void *a, const void *w, const void *bias, void *y, int m, int k, int n, int fp16,
+                            void *stream) {
+  if (!a || !w || !bias || !y) return fail(TMC_ERR_INVALID, "null pointer");
+  if (m < 1 || k < 1 || n < 1) return fail(TMC_ERR_INVALID, "fused linear-relu: m, k, n >= 1");
+  const cudaError_t e =
+      tmc::launch_fused_linear_relu(a, w, bias, y, m, k, n, fp16 != 0, static_cast<cudaStream_t>(stream));
+  if (e == cudaErrorInvalidValue) return fail(TMC_ERR_UNSUPPORTED, "fused linear-relu: unsupported shape");
+  return e == cudaSuccess ? ok() : cuda_fail(e, "fused linear-relu launch");
 }
 
 int tmc_k_rmsnorm_gemv_f32(const float *x, const float *gamma, const void *w_f16, float *y,

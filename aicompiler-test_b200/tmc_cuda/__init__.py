@@ -88,6 +88,10 @@ _sig("tmc_buffer_count", c_size_t, c_void_p)
 _sig("tmc_buffer_dtype", c_int, c_void_p)
 _sig("tmc_k_rmsnorm_gemv_f32", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int,
      c_float, c_void_p)
+_sig("tmc_k_fused_add_norm", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_float,
+     c_int, c_int, c_void_p)
+_sig("tmc_k_fused_silu_mul", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p)
+_sig("tmc_k_fused_linear_relu", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p)
 _sig("tmc_k_rmsnorm", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_int, c_void_p)
 _sig("tmc_k_gemv_f16", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p)
 _sig("tmc_k_gemv_f16_f32out", c_int, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p)
@@ -231,6 +235,21 @@ def rmsnorm(rt: Runtime, x: Buffer, gamma: Buffer, y: Buffer, rows: int, width: 
             threads: int = 256):
     """RMSNormOp over [rows, width]; all three buffers fp32 or all fp16; threads 0 = baseline."""
     check(lib.tmc_k_rmsnorm(x.ptr, gamma.ptr, y.ptr, rows, width, eps, int(x.dtype == F16), threads, rt.stream))
+
+
+def fused_add_norm(rt: Runtime, x: Buffer, b: Buffer, w: Buffer, y: Buffer, rows: int, width: int, b_rows: int,
+                   eps: float = 1e-5, c: Buffer = None):
+    """Add -> RMSNorm, or Add -> LayerNorm when the bias `c` is given (emitFusion)."""
+    check(lib.tmc_k_fused_add_norm(x.ptr, b.ptr, w.ptr, c.ptr if c is not None else None, y.ptr, rows, width,
+                                   b_rows, eps, int(c is not None), int(x.dtype == F16), rt.stream))
+
+
+def fused_silu_mul(rt: Runtime, x: Buffer, b: Buffer, y: Buffer, rows: int, width: int, b_rows: int):
+    check(lib.tmc_k_fused_silu_mul(x.ptr, b.ptr, y.ptr, rows, width, b_rows, int(x.dtype == F16), rt.stream))
+
+
+def fused_linear_relu(rt: Runtime, a: Buffer, w: Buffer, bias: Buffer, y: Buffer, m: int, k: int, n: int):
+    check(lib.tmc_k_fused_linear_relu(a.ptr, w.ptr, bias.ptr, y.ptr, m, k, n, int(a.dtype == F16), rt.stream))
 
 
 def gemv_f16(rt: Runtime, x: Buffer, w: Buffer, y: Buffer, rows: int, k: int, n: int):

@@ -120,6 +120,24 @@ int tmc_k_rmsnorm_gemv_f32(const float *x, const float *gamma, const void *w_f16
 int tmc_k_rmsnorm(const void *x, const void *gamma, void *y, int rows, int width, float eps, int fp16,
                   int threads, void *stream);
 
+/* Fused graph regions of the TensorGraph path (formRegions,
+ * PatternAnalyzer.cpp:32-132; emitFusion, FusionMetalEmitter.cpp:81-214), same
+ * arithmetic: fp32, each intermediate node rounded to the storage type (all
+ * buffers fp32 when fp16 == 0, fp16 otherwise).
+ *   add_norm:    y = norm(T(x + b)) * w (+ c): RMSNorm (layer_norm == 0) or
+ *                LayerNorm with variance max(E[v^2] - mean^2, 0) (c required);
+ *                x, y [rows, width]; b [b_rows, width], b_rows 1 or rows;
+ *                w, c [width].
+ *   silu_mul:    y = T(T(silu(x)) * b), x, y [rows, width], b as above.
+ *   linear_relu: y = T(max(T(T(a . w) + bias), 0)), a [m, k], w [k, n]
+ *                (row-major K x N), bias [n], y [m, n]. */
+int tmc_k_fused_add_norm(const void *x, const void *b, const void *w, const void *c, void *y, int rows, int width,
+                         int b_rows, float eps, int layer_norm, int fp16, void *stream);
+int tmc_k_fused_silu_mul(const void *x, const void *b, void *y, int rows, int width, int b_rows, int fp16,
+                         void *stream);
+int tmc_k_fused_linear_relu(const void *a, const void *w, const void *bias, void *y, int m, int k, int n, int fp16,
+                            void *stream);
+
 /* Decode GEMV y = x W^T with fp16 x, W and y, fp32 accumulation: replaces
  * emitDecodeGEMV / emitLinearBaseline (DecodeGEMVMetalEmitter.cpp:18-132).
  * x [rows, k], W [n, k], y [rows, n]; rows <= 8, k % 8 == 0. */

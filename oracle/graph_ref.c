@@ -5,9 +5,13 @@
  *
  * A plain-C restatement of the reference's CPU oracle for the ops on the decode
  * hot path, in fp64 with the reference's storage rounding:
- *   - storeValue(): fp64 -> float -> storage dtype, GraphReference.cpp:82-87,
- *     with IEEE round-to-nearest-even fp16 (the reference's floatToHalf,
- *     GraphReference.cpp:36-58, is RNE; this is an independent implementation);
+ *   - storeValue(): fp64 -> float -> storage dtype, GraphReference.cpp:82-87.
+ *     The reference's CPU floatToHalf (GraphReference.cpp:38-59) rounds a
+ *     float's dropped mantissa bits to nearest with ties AWAY from zero (it
+ *     adds half an fp16 ulp and truncates, normals and subnormals alike), so
+ *     oracle_store does the same; a tie is common when two fp16 values are
+ *     added. oracle_round_f16 / oracle_f32_to_f16_bits convert inputs with IEEE
+ *     round-to-nearest-even, the conversion of the GPU (and of Metal).
  *   - rmsNormReference(): Validator.cpp:40-66;
  *   - MatMul: GraphReference.cpp:150-167 (fp64 sums of stored operands);
  *   - Transpose (materialised view): GraphReference.cpp:269-287;
@@ -63,10 +67,32 @@ static float f16_bits_to_f32(uint16_t h) {
   return out;
 }
 
+/* fp32 -> fp16 bits rounding the magnitude to nearest, ties away from zero
+ * (the storage rounding of the reference's CPU graph evaluator). */
+static uint16_t f32_to_f16_bits_ties_away(float value) {
+  uint32_t f;
+  memcpy(&f, &value, 4);
+  const uint32_t sign = (f >> 16) & 0x8000u;
+  const int e = (int)((f >> 23) & 0xffu);
+  const uint32_t m = f & 0x7fffffu;
+  if (e == 0xff) return (uint16_t)(sign | (m != 0u ? 0x7e00u : 0x7c00u));
+  const int he = e - 112; /* fp16 biased exponent */
+  if (he >= 31) return (uint16_t)(sign | 0x7c00u);
+  if (he <= 0) { /* fp16 subnormal (or zero) */
+    if (he < -10) return (uint16_t)sign;
+    const int drop = 14 - he; /* bits of the 24-bit significand below fp16's last */
+    const uint32_t significand = m | 0x800000u;
+    return (uint16_t)(sign | ((significand + (1u << (drop - 1))) >> drop));
+  }
+  const uint32_t up = m + (1u << 12); /* half of fp16's last mantissa bit */
+  if (up & 0x800000u) return (uint16_t)(he + 1 >= 31 ? (sign | 0x7c00u) : (sign | ((uint32_t)(he + 1) << 10)));
+  return (uint16_t)(sign | ((uint32_t)he << 10) | (up >> 13));
+}
+
 /* dtype: 0 = fp16, 1 = fp32 (the TMC_F16 / TMC_F32 codes) */
 float oracle_store(double value, int dtype) {
   const float as_float = (float)value;
-  if (dtype == 0) return f16_bits_to_f32(f32_to_f16_bits(as_float));
+  if (dtype == 0) return f16_bits_to_f32(f32_to_f16_bits_ties_away(as_float));
   return as_float;
 }
 
@@ -198,5 +224,64 @@ int oracle_paged_attention(const float *q, const float *k_pool, const float *v_p
       for (long i = 0; i < d; ++i) o[i] /= den;
     }
   }
+  return 0;
+}
+
+/* ---- fused graph regions (GraphReference.cpp:129-199, node by node) --------
+ * The graph suite's fused regions (tensor_graph_examples.cpp:115-143,210-225):
+ * kind 0 Add -> RMSNorm, 1 Add -> LayerNorm, 2 SiLU -> Mul,
+ * 3 MatMul -> Add(bias) -> ReLU. Inputs hold storage values. x [rows, width];
+ * b: the Add / Mul operand [b_rows, width] (b_rows 1 broadcasts over rows) or
+ * the MatMul weight [width, n]; w, c: the norm weight / LayerNorm bias [width],
+ * or (kind 3) c the ReLU bias [n]. Every intermediate node is stored in the
+ * graph's dtype (oracle_store) before the next node reads it; y receives the
+ * last node's fp64 value, the reference's "precise" output. Returns 0, or 1
+ * for an unknown kind. */
+int oracle_fusion(int kind, const float *x, const float *b, const float *w, const float *c, long rows,
+                  long width, long b_rows, long n, double eps, int dtype, double *y) {
+  const double e = (double)(float)eps; /* the attributes hold a float */
+  if (kind == 3) {
+    for (long r = 0; r < rows; ++r)
+      for (long j = 0; j < n; ++j) {
+        double s = 0.0;
+        for (long k = 0; k < width; ++k) s += (double)x[r * width + k] * (double)b[k * n + j];
+        const float linear = oracle_store(s, dtype);
+        const float biased = oracle_store((double)linear + (double)c[j], dtype);
+        y[r * n + j] = biased > 0.0f ? (double)biased : 0.0;
+      }
+    return 0;
+  }
+  if (kind == 2) {
+    for (long r = 0; r < rows; ++r)
+      for (long i = 0; i < width; ++i) {
+        const double v = x[r * width + i];
+        const double ex = exp(v >= 0.0 ? -v : v);
+        const float act = oracle_store(v >= 0.0 ? v / (1.0 + ex) : v * ex / (1.0 + ex), dtype);
+        y[r * width + i] = (double)act * (double)b[(b_rows == 1 ? 0 : r) * width + i];
+      }
+    return 0;
+  }
+  if (kind != 0 && kind != 1) return 1;
+  float *added = (float *)malloc((size_t)width * sizeof(float));
+  if (added == NULL) return 1;
+  for (long r = 0; r < rows; ++r) {
+    double sum = 0.0, squares = 0.0;
+    for (long i = 0; i < width; ++i) {
+      added[i] = oracle_store((double)x[r * width + i] + (double)b[(b_rows == 1 ? 0 : r) * width + i], dtype);
+      sum += added[i];
+      squares += (double)added[i] * (double)added[i];
+    }
+    if (kind == 0) {
+      const double inv = 1.0 / sqrt(squares / (double)width + e);
+      for (long i = 0; i < width; ++i) y[r * width + i] = (double)added[i] * inv * (double)w[i];
+    } else {
+      const double mean = sum / (double)width;
+      double variance = squares / (double)width - mean * mean;
+      if (variance < 0.0) variance = 0.0;
+      const double inv = 1.0 / sqrt(variance + e);
+      for (long i = 0; i < width; ++i) y[r * width + i] = ((double)added[i] - mean) * inv * (double)w[i] + (double)c[i];
+    }
+  }
+  free(added);
   return 0;
 }

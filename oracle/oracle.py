@@ -52,10 +52,15 @@ if _lib is not None:
     _lib.oracle_paged_attention.argtypes = [_F, _F, _F, _I, c_long, _I, _I, c_long, c_long, c_long,
                                             c_long, c_long, _D]
 
+    _lib.oracle_fusion.restype = c_int
+    _lib.oracle_fusion.argtypes = [c_int, _F, _F, _F, _F, c_long, c_long, c_long, c_long, c_double, c_int, _D]
+
 if _ref is not None:
     _ref.ref_last_error.restype = c_char_p
     _ref.ref_rmsnorm_matmul.restype = c_int
     _ref.ref_rmsnorm_matmul.argtypes = [_F, _F, _F, c_long, c_long, c_long, c_float, _D]
+    _ref.ref_fusion.restype = c_int
+    _ref.ref_fusion.argtypes = [c_int, _F, _F, _F, _F, c_long, c_long, c_long, c_long, c_float, c_int, _D]
     _ref.ref_rmsnorm.restype = c_int
     _ref.ref_rmsnorm.argtypes = [_F, _F, c_long, c_long, c_float, c_int, _D]
 
@@ -189,3 +194,42 @@ def ref_rmsnorm(x, gamma, eps=1e-5, dtype=1) -> np.ndarray:
     if _ref.ref_rmsnorm(_p(x, _F), _p(gamma, _F), rows, width, eps, dtype, _p(y, _D)) != 0:
         raise RuntimeError(_ref.ref_last_error().decode())
     return y
+
+
+FUSION_KINDS = {"add_rmsnorm": 0, "add_layernorm": 1, "silu_mul": 2, "linear_relu": 3}
+
+
+def _fusion_args(kind, x, b, w, c, n):
+    x = _f32(x)
+    rows, width = x.shape
+    b = _f32(b)
+    b_rows = 1 if (kind != "linear_relu" and b.ndim == 1) else (b.shape[0] if kind != "linear_relu" else width)
+    w = _f32(w if w is not None else np.zeros(1, np.float32))
+    c = _f32(c if c is not None else np.zeros(1, np.float32))
+    out_cols = n if kind == "linear_relu" else width
+    return x, b, w, c, rows, width, b_rows, out_cols
+
+
+def fusion(kind, x, b, w=None, c=None, eps=1e-5, fp16=False, n=0) -> np.ndarray:
+    """The graph suite's fused regions in fp64 (graph_ref.c oracle_fusion);
+    inputs must already hold storage values (round_f16 for fp16 graphs)."""
+    _need()
+    x, b, w, c, rows, width, b_rows, out_cols = _fusion_args(kind, x, b, w, c, n)
+    out = np.empty((rows, out_cols), dtype=np.float64)
+    code = _lib.oracle_fusion(FUSION_KINDS[kind], _p(x, _F), _p(b, _F), _p(w, _F), _p(c, _F), rows, width,
+                              b_rows, n, eps, 0 if fp16 else 1, _p(out, _D))
+    if code != 0:
+        raise ValueError(kind)
+    return out
+
+
+def ref_fusion(kind, x, b, w=None, c=None, eps=1e-5, fp16=False, n=0) -> np.ndarray:
+    """The same graph through the reference's own evaluateGraph (oracle/_ref)."""
+    if _ref is None:
+        raise RuntimeError("oracle/_ref not built")
+    x, b, w, c, rows, width, b_rows, out_cols = _fusion_args(kind, x, b, w, c, n)
+    out = np.empty((rows, out_cols), dtype=np.float64)
+    if _ref.ref_fusion(FUSION_KINDS[kind], _p(x, _F), _p(b, _F), _p(w, _F), _p(c, _F), rows, width, b_rows, n,
+                       eps, 0 if fp16 else 1, _p(out, _D)) != 0:
+        raise RuntimeError(_ref.ref_last_error().decode())
+    return out

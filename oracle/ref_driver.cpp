@@ -80,4 +80,61 @@ int ref_rmsnorm(const float *x, const float *gamma, long rows, long width, float
   }
 }
 
+// The graph suite's fused regions (tensor_graph_examples.cpp:115-143,210-225),
+// formed by formRegions (PatternAnalyzer.cpp:32-132) and emitted by emitFusion
+// (FusionMetalEmitter.cpp:81-214): kind 0 Add -> RMSNorm, 1 Add -> LayerNorm,
+// 2 SiLU -> Mul, 3 MatMul -> Add(bias) -> ReLU. x [rows, width]; b is the
+// second operand of the Add / Mul ([b_rows, width], b_rows 1 or rows) or the
+// MatMul weight [width, n]; w / c the norm weight / bias (or the ReLU bias
+// [n]). dtype 0 = fp16 storage, 1 = fp32. y: fp64 precise outputs.
+int ref_fusion(int kind, const float *x, const float *b, const float *w, const float *c, long rows, long width,
+               long b_rows, long n, float eps, int dtype, double *y) {
+  try {
+    const DType dt = dtype == 0 ? DType::Float16 : DType::Float32;
+    const auto R = std::size_t(rows), W = std::size_t(width), BR = std::size_t(b_rows), N = std::size_t(n);
+    TensorGraph graph;
+    GraphInputs inputs;
+    const auto xi = graph.addInput("x", TensorType{{R, W}, dt});
+    inputs[xi] = std::vector<float>(x, x + R * W);
+    if (kind == 3) {
+      const auto wi = graph.addInput("weight", TensorType{{W, N}, dt});
+      const auto bi = graph.addInput("bias", TensorType{{N}, dt});
+      inputs[wi] = std::vector<float>(b, b + W * N);
+      inputs[bi] = std::vector<float>(c, c + N);
+      const auto linear = graph.addNode(OpType::MatMul, {xi, wi});
+      const auto biased = graph.addNode(OpType::Add, {linear, bi});
+      graph.outputs = {graph.addNode(OpType::ReLU, {biased})};
+    } else {
+      const TensorType bt = BR == 1 ? TensorType{{W}, dt} : TensorType{{R, W}, dt};
+      const auto bi = graph.addInput("b", bt);
+      inputs[bi] = std::vector<float>(b, b + BR * W);
+      if (kind == 2) {
+        const auto act = graph.addNode(OpType::SiLU, {xi});
+        graph.outputs = {graph.addNode(OpType::Mul, {act, bi})};
+      } else {
+        const auto wi = graph.addInput("weight", TensorType{{W}, dt});
+        inputs[wi] = std::vector<float>(w, w + W);
+        const auto added = graph.addNode(OpType::Add, {xi, bi});
+        if (kind == 0) {
+          graph.outputs = {graph.addNode(OpType::RMSNorm, {added, wi}, RMSNormAttributes{eps, -1})};
+        } else {
+          const auto ci = graph.addInput("bias", TensorType{{W}, dt});
+          inputs[ci] = std::vector<float>(c, c + W);
+          LayerNormAttributes attributes;
+          attributes.epsilon = eps;
+          graph.outputs = {graph.addNode(OpType::LayerNorm, {added, wi, ci}, attributes)};
+        }
+      }
+    }
+    const auto analyzed = analyzer::analyze(graph);
+    const auto result = validation::evaluateGraph(analyzed, inputs);
+    const auto &o = result.outputs.at(0);
+    std::memcpy(y, o.data(), o.size() * sizeof(double));
+    return 0;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    return 1;
+  }
+}
+
 }  // extern "C"

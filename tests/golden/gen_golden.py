@@ -14,6 +14,9 @@ Outputs (small .npz files beside this script):
                  (inputs are regenerated from the seed by oracle.workloads.c1_inputs).
   rmsnorm.npz    the graph suite's RMSNorm cases ([1,4096]; [3,4097] with a zero row
                  and a x1e-4 row; fp16 [1,257]), apps/tensor_graph_examples.cpp:79-123.
+  fusion.npz     the graph suite's fused regions (Add -> RMSNorm [3,4097], Residual
+                 Add -> LayerNorm [3,17], SiLU -> Mul [3,17], Linear -> ReLU [3,7]x[7,5]),
+                 plus fp32 / fp16 seeded variants of each; y from evaluateGraph.
 """
 
 import os
@@ -68,6 +71,43 @@ def main():
     cases["h1x257_x"] = x
     cases["h1x257_y"] = oracle.ref_rmsnorm(x, rms_weight(257), 1e-5, dtype=0)
     np.savez_compressed(os.path.join(HERE, "rmsnorm.npz"), **cases)
+
+    # Fused regions of the graph suite (tensor_graph_examples.cpp:79-143,210-225),
+    # fp32 as there, then fp16 and larger seeded variants of each.
+    fz = {}
+
+    def put(name, kind, x, b, w=None, c=None, fp16=False, n=0):
+        if fp16:
+            x, b = oracle.round_f16(x).reshape(x.shape), oracle.round_f16(b).reshape(b.shape)
+            w = None if w is None else oracle.round_f16(w).reshape(w.shape)
+            c = None if c is None else oracle.round_f16(c).reshape(c.shape)
+        fz[f"{name}_x"], fz[f"{name}_b"] = x, b
+        if w is not None:
+            fz[f"{name}_w"] = w
+        if c is not None:
+            fz[f"{name}_c"] = c
+        fz[f"{name}_y"] = oracle.ref_fusion(kind, x, b, w, c, 1e-5, fp16, n)
+
+    pat = workloads.graph_pattern
+    x = pat(3 * 4097).reshape(3, 4097)
+    x[0, :] = 0.0
+    x[1, :] *= np.float32(1e-4)
+    put("addrms", "add_rmsnorm", x, pat(4097, seed=3, scale=0.1), rms_weight(4097))
+    ln_w = pat(17, seed=3, scale=0.2) + np.float32(1.0)
+    put("addln", "add_layernorm", pat(3 * 17).reshape(3, 17), pat(17, seed=1, scale=0.1), ln_w,
+        pat(17, seed=2, scale=0.05))
+    put("silumul", "silu_mul", pat(3 * 17).reshape(3, 17), pat(17, seed=2))
+    put("linrelu", "linear_relu", pat(3 * 7).reshape(3, 7), pat(7 * 5, seed=1, scale=0.25).reshape(7, 5), None,
+        pat(5, seed=2, scale=0.1), n=5)
+    rng = np.random.default_rng(11)
+    r = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    for fp16 in (False, True):
+        t = "h" if fp16 else "f"
+        put(f"addrms_{t}8", "add_rmsnorm", r(8, 4096), r(8, 4096), 1 + 0.1 * r(4096), fp16=fp16)
+        put(f"addln_{t}9", "add_layernorm", r(9, 1000), r(1000), 1 + 0.1 * r(1000), 0.1 * r(1000), fp16=fp16)
+        put(f"silumul_{t}8", "silu_mul", 3 * r(8, 1024), r(8, 1024), fp16=fp16)
+        put(f"linrelu_{t}40", "linear_relu", r(40, 96), 0.2 * r(96, 72), None, 0.1 * r(72), fp16=fp16, n=72)
+    np.savez_compressed(os.path.join(HERE, "fusion.npz"), **fz)
     print("golden vectors written to", HERE)
 
 
