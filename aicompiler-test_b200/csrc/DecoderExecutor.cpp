@@ -21,9 +21,10 @@ using cuda::ElementType;
 
 namespace {
 
-// Weight bytes one GEMV launch may pull into L2 while its predecessor drains
-// (about half of B200's 126 MB L2).
-constexpr long long kL2PrefetchBytes = 64ll << 20;
+// Weight bytes one GEMV launch may pull into L2 while its predecessor drains.
+// Measured over a whole bs1 step: 16 MB 3.61 ms, 32 MB 3.67, 64 MB 3.65,
+// none 3.70 -- larger budgets evict more of the next kernels' lines.
+constexpr long long kL2PrefetchBytes = 16ll << 20;
 
 std::string cudaText(const char *what, cudaError_t e) {
   std::ostringstream s;
@@ -718,12 +719,13 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
   auto *status = rt_.deviceStatus();
   // Attention splits per (row, KV head): few pairs -> enough splits to cover
   // the SMs twice; many pairs (batched decode) -> a power of two that gives
-  // about 16 CTAs per SM, so the last partial wave is short.
+  // about 8 CTAs per SM (bs64: 2 splits of ~576 positions; 4 splits, ~16 per
+  // SM, cost 86.6 us against 80.7 per layer), so the last partial wave is short.
   int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
   if (R * hkvL_ < numSms_) splits = std::min(splits, attnSplitCap_);
   if (R * hkvL_ >= numSms_) {
     splits = 1;
-    while (splits < 16 && 2 * splits * R * hkvL_ <= 16 * numSms_) splits *= 2;
+    while (splits < 16 && 2 * splits * R * hkvL_ <= 8 * numSms_) splits *= 2;
   }
   float *partialF32 = fp(partialF32_);  // [R, H] row-parallel sums (TP with a collective)
   // TP over peer memory: partial-sum phase 2l = O of layer l, 2l + 1 = down.

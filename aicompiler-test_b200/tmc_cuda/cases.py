@@ -88,7 +88,7 @@ def case_attention(rt, a):
     splits = max(1, min(64, (2 * sms + a.rows * a.hkv - 1) // (a.rows * a.hkv)))
     if a.rows * a.hkv >= sms:
         splits = 1
-        while splits < 16 and 2 * splits * a.rows * a.hkv <= 16 * sms:
+        while splits < 16 and 2 * splits * a.rows * a.hkv <= 8 * sms:
             splits *= 2
     if a.splits > 0:
         splits = a.splits
