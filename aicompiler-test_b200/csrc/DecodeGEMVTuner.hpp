@@ -3,13 +3,17 @@
 // (src/planner/DecodeGEMVTuner.hpp:13-25, DecodeGEMVTuner.cpp:162-304).
 //
 // The baseline is a generic linear kernel (one CTA per output feature and
-// row). Candidates are configurations of the decode GEMV (K-split team size
-// 1/2/4/8, with and without dynamic row scheduling). Each candidate is
-// validated against an fp64 CPU reference when the shape has at most 64M
-// multiply-adds (otherwise against the baseline's output), then timed in two
-// paired rounds of 31 alternating samples; it is admitted when both rounds
-// reach 1.05x, and the fastest admitted one is selected. With none admitted
-// the selection keeps the baseline.
+// row) in the storage dtype. Decode candidates (batch <= 8) are
+// configurations of the decode GEMV (K-split team size 1/2/4/8, with and
+// without dynamic row scheduling); the prefill candidate (batch <= 128) is
+// the tcgen05 tensor-core GEMM (the reference's tiled-GEMM candidate set,
+// DecodeGEMVTuner.cpp:209-213). Both read fp16 weights, so with fp32 storage
+// every candidate fails the hardware filter and the baseline is kept. Each
+// candidate is validated against an fp64 CPU reference when the shape has at
+// most 64M multiply-adds (otherwise against the baseline's output, with 9
+// samples instead of 31), then timed in two paired rounds of alternating
+// samples; it is admitted when both rounds reach 1.05x, and the fastest
+// admitted one is selected.
 #pragma once
 
 #include <cstddef>
@@ -20,8 +24,9 @@
 namespace tensor::planner {
 
 struct DecodeGEMVConfig {
-  int ks = 0;             // K-split team size (0: the built-in rule)
-  bool dynamic = false;   // pooled dynamic row scheduling
+  int ks = 0;               // K-split team size (0: the built-in rule)
+  bool dynamic = false;     // pooled dynamic row scheduling
+  bool tensorCore = false;  // the tcgen05 GEMM (prefill candidate)
 };
 
 struct DecodeGEMVSelection {
@@ -33,9 +38,10 @@ struct DecodeGEMVSelection {
 };
 
 // input [batch, inputSize] and weight [outputSize, inputSize] are logical
-// values stored as fp16 (rounded); batch <= 8.
+// values stored as fp16 (fp16Storage) or fp32; batch <= 8 for decode, <= 128
+// for prefill; inputSize % 8 == 0.
 DecodeGEMVSelection tuneDecodeGEMV(std::size_t batch, std::size_t inputSize, std::size_t outputSize,
                                    const std::vector<float> &input, const std::vector<float> &weight,
-                                   std::ostream &log);
+                                   std::ostream &log, bool fp16Storage = true, bool prefill = false);
 
 }  // namespace tensor::planner

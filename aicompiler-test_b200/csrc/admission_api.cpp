@@ -57,17 +57,17 @@ int tmc_admit_generated_kernel(const char *pattern, const char *source, int bloc
   return ok();
 }
 
-int tmc_tune_decode_gemv(int rows, int k, int n, const float *input, const float *weight, tmc_gemv_selection *out,
-                         char *log, size_t log_size) {
+int tmc_tune_decode_gemv(int rows, int k, int n, const float *input, const float *weight, int fp16_storage,
+                         int prefill, tmc_gemv_selection *out, char *log, size_t log_size) {
   if (input == nullptr || weight == nullptr || out == nullptr || rows <= 0 || k <= 0 || n <= 0)
     return fail(TMC_ERR_INVALID, "bad argument");
   std::ostringstream text;
   const auto sel = tensor::planner::tuneDecodeGEMV(
       rows, k, n, std::vector<float>(input, input + (size_t)rows * k),
-      std::vector<float>(weight, weight + (size_t)n * k), text);
+      std::vector<float>(weight, weight + (size_t)n * k), text, fp16_storage != 0, prefill != 0);
   copy_text(text.str(), log, log_size);
   *out = tmc_gemv_selection{sel.success ? 1 : 0, sel.useBaseline ? 1 : 0, sel.config.ks, sel.config.dynamic ? 1 : 0,
-                            sel.conservativeSpeedup};
+                            sel.config.tensorCore ? 1 : 0, sel.conservativeSpeedup};
   return sel.success ? ok() : fail(TMC_ERR_INVALID, sel.errorMessage);
 }
 

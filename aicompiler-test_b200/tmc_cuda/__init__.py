@@ -626,15 +626,15 @@ def admit_generated_kernel(pattern: str, source: str, block_size: int, feedback_
 
 class GemvSelection(ctypes.Structure):
     _fields_ = [("success", c_int), ("use_baseline", c_int), ("ks", c_int), ("dynamic", c_int),
-                ("conservative_speedup", ctypes.c_double)]
+                ("tensor_core", c_int), ("conservative_speedup", ctypes.c_double)]
 
 
-_sig("tmc_tune_decode_gemv", c_int, c_int, c_int, c_int, POINTER(c_float), POINTER(c_float), POINTER(GemvSelection),
-     c_char_p, c_size_t)
+_sig("tmc_tune_decode_gemv", c_int, c_int, c_int, c_int, POINTER(c_float), POINTER(c_float), c_int, c_int,
+     POINTER(GemvSelection), c_char_p, c_size_t)
 
 
-def tune_decode_gemv(input, weight) -> dict:
-    """tuneDecodeGEMV: input [rows, k], weight [n, k] (stored as fp16)."""
+def tune_decode_gemv(input, weight, fp16_storage: bool = True, prefill: bool = False) -> dict:
+    """tuneDecodeGEMV: input [rows, k], weight [n, k], stored as fp16 or fp32."""
     x = np.ascontiguousarray(np.asarray(input, dtype=np.float32))
     w = np.ascontiguousarray(np.asarray(weight, dtype=np.float32))
     rows, k = x.shape
@@ -642,9 +642,10 @@ def tune_decode_gemv(input, weight) -> dict:
     sel = GemvSelection()
     log = ctypes.create_string_buffer(1 << 14)
     check(lib.tmc_tune_decode_gemv(rows, k, n, x.ctypes.data_as(POINTER(c_float)), w.ctypes.data_as(POINTER(c_float)),
-                                   ctypes.byref(sel), log, 1 << 14))
+                                   int(fp16_storage), int(prefill), ctypes.byref(sel), log, 1 << 14))
     return {"success": bool(sel.success), "use_baseline": bool(sel.use_baseline), "ks": sel.ks,
-            "dynamic": bool(sel.dynamic), "speedup": sel.conservative_speedup, "log": log.value.decode()}
+            "dynamic": bool(sel.dynamic), "tensor_core": bool(sel.tensor_core),
+            "speedup": sel.conservative_speedup, "log": log.value.decode()}
 
 
 class RMSNormSelection(ctypes.Structure):

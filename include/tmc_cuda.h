@@ -400,17 +400,20 @@ int tmc_admit_generated_kernel(const char *pattern, const char *source, int bloc
                                double *speedup, char *log, size_t log_size);
 /* Decode GEMV tuning (replaces tuneDecodeGEMV / DecodeGEMVSelection,
  * src/planner/DecodeGEMVTuner.hpp:13-25, DecodeGEMVTuner.cpp:162-304):
- * candidates are decode GEMV configurations (K-split team 1/2/4/8, dynamic
- * row scheduling), each validated against fp64 (<= 64M MACs; else the
- * baseline's output) and admitted only with >= 1.05x over the generic linear
- * baseline in two paired rounds; the fastest admitted one is selected.
- * input [rows, k] and weight [n, k] are logical values stored as fp16. */
+ * decode candidates (prefill == 0, rows <= 8) are decode GEMV configurations
+ * (K-split team 1/2/4/8, dynamic row scheduling); the prefill candidate
+ * (rows <= 128) is the tcgen05 GEMM. Each is validated against fp64 (<= 64M
+ * MACs; else the baseline's output, 9 samples) and admitted only with
+ * >= 1.05x over the generic linear baseline in two paired rounds; the fastest
+ * admitted one is selected. input [rows, k] and weight [n, k] are logical
+ * values stored as fp16 (fp16_storage != 0) or fp32 (the candidates read fp16
+ * weights, so fp32 storage keeps the baseline). */
 typedef struct tmc_gemv_selection {
-  int success, use_baseline, ks, dynamic;
+  int success, use_baseline, ks, dynamic, tensor_core;
   double conservative_speedup;
 } tmc_gemv_selection;
-int tmc_tune_decode_gemv(int rows, int k, int n, const float *input, const float *weight,
-                         tmc_gemv_selection *out, char *log, size_t log_size);
+int tmc_tune_decode_gemv(int rows, int k, int n, const float *input, const float *weight, int fp16_storage,
+                         int prefill, tmc_gemv_selection *out, char *log, size_t log_size);
 
 /* RMSNorm tuning (replaces tuneRMSNorm / TuningResult, RMSNormTuner.hpp:14-44,
  * RMSNormTuner.cpp:159-309): block-size candidates against the frozen

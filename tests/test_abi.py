@@ -40,7 +40,8 @@ def test_rmsnorm_and_tuners_validate_arguments_on_the_host():
     import tmc_cuda
     assert tmc_cuda.lib.tmc_k_rmsnorm(None, None, None, 1, 8, 1e-5, 0, 256, None) == tmc_cuda.ERR_INVALID
     sel = tmc_cuda.GemvSelection()
-    assert tmc_cuda.lib.tmc_tune_decode_gemv(1, 8, 8, None, None, ctypes.byref(sel), None, 0) == tmc_cuda.ERR_INVALID
+    assert tmc_cuda.lib.tmc_tune_decode_gemv(1, 8, 8, None, None, 1, 0, ctypes.byref(sel), None, 0) == \
+        tmc_cuda.ERR_INVALID
     rsel = tmc_cuda.RMSNormSelection()
     assert tmc_cuda.lib.tmc_tune_rmsnorm(1, 8, 1e-5, 0, None, None, None, 0, ctypes.byref(rsel), None, None,
                                          0) == tmc_cuda.ERR_INVALID

@@ -151,3 +151,27 @@ def test_decode_gemv_tuner_selects_an_admitted_config(rt, rows, k, n):
     # At weight-streaming sizes the decode GEMV beats one CTA per output.
     if k * n >= 16 << 20:
         assert not sel["use_baseline"], sel["log"]
+
+
+def test_decode_gemv_tuner_prefill_admits_the_tensor_core_gemm(rt):
+    # The prefill candidate set (DecodeGEMVTuner.cpp:209-213): 64 rows, the
+    # tcgen05 GEMM against the generic linear baseline, validated against the
+    # baseline's output (64 x 4096 x 4096 > 64M MACs, 9 samples).
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((64, 4096)).astype(np.float16).astype(np.float32)
+    w = (rng.standard_normal((4096, 4096)) * 0.02).astype(np.float16).astype(np.float32)
+    sel = tmc_cuda.tune_decode_gemv(x, w, prefill=True)
+    assert sel["success"], sel["log"]
+    assert "samples=9" in sel["log"] and "numerical: FAIL" not in sel["log"], sel["log"]
+    assert not sel["use_baseline"] and sel["tensor_core"] and sel["speedup"] >= 1.05, sel["log"]
+
+
+def test_decode_gemv_tuner_fp32_storage_keeps_the_baseline(rt):
+    # Every candidate reads fp16 weights: with fp32 storage the hardware filter
+    # rejects them and the validated baseline is the selection.
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((2, 1024)).astype(np.float32)
+    w = (rng.standard_normal((512, 1024)) * 0.02).astype(np.float32)
+    sel = tmc_cuda.tune_decode_gemv(x, w, fp16_storage=False)
+    assert sel["success"] and sel["use_baseline"], sel["log"]
+    assert sel["log"].count("Hardware Filter: FAIL") == 5 and "dtype=fp32" in sel["log"], sel["log"]
