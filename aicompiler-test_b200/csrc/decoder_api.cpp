@@ -1,6 +1,7 @@
 // extern "C" boundary of the decoder executor (declarations and reference
 // citations in include/tmc_cuda.h).
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <memory>
 #include <sstream>
@@ -11,6 +12,7 @@
 
 #include "CudaRuntime.hpp"
 #include "DecoderExecutor.hpp"
+#include "DecoderManifest.hpp"
 #include "NcclCollective.hpp"
 #include "ServingRuntime.hpp"
 #include "api_util.hpp"
@@ -23,6 +25,10 @@ using namespace tmc_api;
 struct tmc_decoder {
   std::unique_ptr<DecoderExecutor> ex;
   int device = 0;
+};
+
+struct tmc_manifest {
+  tensor::importer::DecoderManifest m;
 };
 
 namespace {
@@ -92,6 +98,59 @@ int tmc_decoder_load_weight(tmc_decoder *dec, const char *name, const float *val
 int tmc_decoder_load_weight_f16(tmc_decoder *dec, const char *name, const uint16_t *bits, size_t count) {
   if (!bind(dec) || name == nullptr || bits == nullptr) return fail(TMC_ERR_INVALID, "null argument");
   return done(dec->ex->loadWeightF16(name, bits, count));
+}
+
+int tmc_manifest_open(const char *path, tmc_manifest **out) {
+  if (path == nullptr || out == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  auto h = std::make_unique<tmc_manifest>();
+  const auto e = tensor::importer::importDecoderManifest(path, &h->m);
+  if (!e.empty()) return fail(TMC_ERR_INVALID, e);
+  *out = h.release();
+  return ok();
+}
+
+void tmc_manifest_close(tmc_manifest *m) { delete m; }
+
+int tmc_manifest_get_info(const tmc_manifest *m, tmc_manifest_info *info) {
+  if (m == nullptr || info == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  const auto &d = m->m;
+  tmc_manifest_info r{};
+  r.version = d.version;
+  r.batch = (int)d.batch;
+  r.hidden_size = (int)d.hidden;
+  r.heads = (int)d.heads;
+  r.head_dim = (int)(d.hidden / d.heads);
+  r.intermediate_size = (int)d.intermediate;
+  r.vocab_size = (int)d.vocab;
+  r.layers = (int)d.layers;
+  r.capacity = (int)d.capacity;
+  r.prefill_length = (int)d.prefillLength;
+  r.decode_count = (int)d.decodeCount;
+  r.epsilon = d.epsilon;
+  std::snprintf(r.requested_dtype, sizeof r.requested_dtype, "%s", d.requestedDtype.c_str());
+  std::snprintf(r.effective_dtype, sizeof r.effective_dtype, "%s", d.effectiveDtype.c_str());
+  *info = r;
+  return ok();
+}
+
+int tmc_manifest_tensor(const tmc_manifest *m, const char *name, const float **values, size_t *count) {
+  if (m == nullptr || name == nullptr || values == nullptr || count == nullptr)
+    return fail(TMC_ERR_INVALID, "null argument");
+  *values = m->m.tensor(name, count);
+  if (*values == nullptr) return fail(TMC_ERR_INVALID, std::string("manifest has no tensor '") + name + "'");
+  return ok();
+}
+
+int tmc_decoder_load_manifest(tmc_decoder *dec, const tmc_manifest *m) {
+  if (!bind(dec) || m == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  for (const auto &name : tensor::importer::decoderWeightNames(m->m.layers)) {
+    size_t count = 0;
+    const float *v = m->m.tensor(name, &count);
+    if (v == nullptr) return fail(TMC_ERR_INVALID, "manifest has no tensor '" + name + "'");
+    const std::string e = dec->ex->loadWeight(name, v, count);
+    if (!e.empty()) return done("manifest tensor '" + name + "': " + e);
+  }
+  return ok();
 }
 
 int tmc_decoder_read_weight(tmc_decoder *dec, const char *name, float *out, size_t count) {

@@ -361,6 +361,57 @@ def _i32(a):
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))
 
 
+class ManifestInfo(ctypes.Structure):
+    _fields_ = [("version", c_int), ("batch", c_int), ("hidden_size", c_int), ("heads", c_int), ("head_dim", c_int),
+                ("intermediate_size", c_int), ("vocab_size", c_int), ("layers", c_int), ("capacity", c_int),
+                ("prefill_length", c_int), ("decode_count", c_int), ("epsilon", c_float),
+                ("requested_dtype", ctypes.c_char * 8), ("effective_dtype", ctypes.c_char * 8)]
+
+
+_sig("tmc_manifest_open", c_int, c_char_p, POINTER(c_void_p))
+_sig("tmc_manifest_close", None, c_void_p)
+_sig("tmc_manifest_get_info", c_int, c_void_p, POINTER(ManifestInfo))
+_sig("tmc_manifest_tensor", c_int, c_void_p, c_char_p, POINTER(POINTER(c_float)), POINTER(c_size_t))
+_sig("tmc_decoder_load_manifest", c_int, c_void_p, c_void_p)
+
+
+class Manifest:
+    """A decoder-only manifest in the reference's export format
+    (importDecoderLLMWorkload, DecoderLLMImporter.cpp:154-281)."""
+
+    def __init__(self, path: str):
+        self.handle = None
+        h = c_void_p()
+        check(lib.tmc_manifest_open(str(path).encode(), ctypes.byref(h)))
+        self.handle = h
+        info = ManifestInfo()
+        check(lib.tmc_manifest_get_info(self.handle, ctypes.byref(info)))
+        self.info = {f: getattr(info, f) for f, _ in ManifestInfo._fields_}
+        for f in ("requested_dtype", "effective_dtype"):
+            self.info[f] = self.info[f].decode()
+
+    def tensor(self, name: str) -> np.ndarray:
+        ptr, n = POINTER(c_float)(), c_size_t()
+        check(lib.tmc_manifest_tensor(self.handle, name.encode(), ctypes.byref(ptr), ctypes.byref(n)))
+        return np.ctypeslib.as_array(ptr, shape=(n.value,)).copy()
+
+    def decoder(self, runtime, **kw) -> "Decoder":
+        """A decoder with the manifest's dimensions and its weights loaded."""
+        i = self.info
+        dec = Decoder(runtime, i["hidden_size"], i["heads"], i["intermediate_size"], i["vocab_size"], i["layers"],
+                      i["capacity"], epsilon=i["epsilon"], **kw)
+        check(lib.tmc_decoder_load_manifest(dec.handle, self.handle))
+        return dec
+
+    def close(self):
+        if self.handle:
+            lib.tmc_manifest_close(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
 class Decoder:
     """Decoder executor (reference CompiledDecoderLLM, DecoderLLMExecutor.hpp:46-102)."""
 

@@ -232,6 +232,27 @@ typedef struct {
 
 typedef struct tmc_decoder tmc_decoder;
 
+/* Decoder-only model manifests in the reference's export format
+ * ("TMC_DECODER_LLM 1|2" text header + float32 payload beside it), read as
+ * importDecoderLLMWorkload does (DecoderLLMImporter.cpp:154-281, written by
+ * export_decoder_llm.py:554-595), with the same checks. tmc_manifest_tensor
+ * gives a view of any named tensor (weights, RoPE tables, the exporter's
+ * reference tokens / logits / KV caches) valid until tmc_manifest_close;
+ * tmc_decoder_load_manifest loads every weight and the RoPE tables into a
+ * decoder created with the manifest's dimensions (kv_heads = heads, head_dim =
+ * hidden / heads). Dtype tokens: "F32", "F16" or "BF16". */
+typedef struct tmc_manifest tmc_manifest;
+typedef struct {
+  int version, batch, hidden_size, heads, head_dim, intermediate_size, vocab_size, layers, capacity;
+  int prefill_length, decode_count;
+  float epsilon;
+  char requested_dtype[8], effective_dtype[8];
+} tmc_manifest_info;
+int tmc_manifest_open(const char *path, tmc_manifest **out);
+void tmc_manifest_close(tmc_manifest *m);
+int tmc_manifest_get_info(const tmc_manifest *m, tmc_manifest_info *info);
+int tmc_manifest_tensor(const tmc_manifest *m, const char *name, const float **values, size_t *count);
+
 /* compileDecoderLLM (DecoderLLMExecutor.hpp:99-101): allocate weights, KV pools
  * and activations on the runtime's device. Weights start at zero (norms at 1). */
 int tmc_decoder_create(tmc_runtime *rt, const tmc_decoder_config *cfg, tmc_decoder **out);
@@ -244,6 +265,7 @@ void tmc_decoder_destroy(tmc_decoder *dec);
 int tmc_decoder_load_weight(tmc_decoder *dec, const char *name, const float *values, size_t count);
 int tmc_decoder_load_weight_f16(tmc_decoder *dec, const char *name, const uint16_t *bits,
                                 size_t count);
+int tmc_decoder_load_manifest(tmc_decoder *dec, const tmc_manifest *m);
 /* Rank-local window of a logical weight as floats (count must match it). */
 int tmc_decoder_read_weight(tmc_decoder *dec, const char *name, float *out, size_t count);
 /* Synthetic random init: every matrix ~N(0, stddev^2) from a counter-based

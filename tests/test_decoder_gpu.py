@@ -276,3 +276,24 @@ def test_gqa_model_matches_oracle(rt, kv_heads, theta, hidden, heads):
         if margin[1] - margin[0] > 1e-2:
             assert int(tg2[0]) == to2
         t = to2
+
+
+def test_decoder_from_reference_manifest_matches_exporter(rt, tmp_path):
+    # The exporter's manifest format (written from the golden fixture), loaded
+    # through the importer into a decoder: greedy tokens bit-exact, logits
+    # within the north-star tolerance.
+    import tmc_cuda
+    from tests.manifest_writer import golden_manifest
+    path, meta, g = golden_manifest(tmp_path, os.path.join(GOLDEN, "decoder_default_fp16.npz"))
+    m = tmc_cuda.Manifest(path)
+    dec = m.decoder(rt)
+    prompt = m.tensor("prefill.tokens").astype(np.int32)
+    logits, nxt = dec.prefill(prompt)
+    assert int(nxt) == int(m.tensor("prefill.next_tokens")[0])
+    rms_close(logits, m.tensor("prefill.logits").reshape(logits.shape), "manifest prefill logits")
+    for step in range(meta["decode_count"]):
+        lg, n = dec.decode(m.tensor(f"decode{step}.tokens").astype(np.int32))
+        assert int(n[0]) == int(m.tensor(f"decode{step}.next_tokens")[0]), step
+        rms_close(lg[0], m.tensor(f"decode{step}.logits"), f"manifest decode{step} logits")
+    dec.close()
+    m.close()
