@@ -81,6 +81,8 @@ DecoderExecutor::~DecoderExecutor() {
   }
   slots_.clear();
   if (pinnedIO_) cudaFreeHost(pinnedIO_);
+  if (spillHost_) cudaFreeHost(spillHost_);
+  if (spillDevice_) cudaFree(spillDevice_);
   if (!peerMappings_.empty()) {
     int prev = 0;
     cudaGetDevice(&prev);
@@ -592,6 +594,95 @@ std::string DecoderExecutor::readKV(int layer, int slot, std::vector<float> *key
           (*key)[dst] = cuda::halfBitsToFloat(kb[src]);
           (*value)[dst] = cuda::halfBitsToFloat(vb[src]);
         }
+  }
+  return {};
+}
+
+std::string DecoderExecutor::snapshotPages(int slot, KVPageSnapshot *out) {
+  if (slot < 0 || slot >= cfg_.maxSlots || out == nullptr) return "slot out of range";
+  const auto &st = *slots_[slot];
+  const size_t len = st.currentLength(), P = pageSize_;
+  out->length = len;
+  out->pages.clear();
+  if (len == 0) return {};
+  const int npages = (int)((len + P - 1) / P);
+  const auto &row = st.blockTableRow();
+  std::vector<std::int32_t> ids(row.begin(), row.begin() + npages);
+  for (int id : ids)
+    if (id < 0) return "KV page missing for a committed position";
+  const size_t pageElems = (size_t)hkvL_ * P * cfg_.headDim;
+  const size_t bytes = (size_t)cfg_.layers * 2 * npages * pageElems * 2;
+  auto e = ensureSpill(bytes, npages);
+  if (!e.empty()) return e;
+  cudaStream_t s = rt_.stream();
+  TMC_TRY(cudaMemcpyAsync(spillPages_->data(), ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, s));
+  TMC_TRY(tmc::launch_page_copy(static_cast<__half *const *>(poolPtrs_->data()),
+                                static_cast<const int *>(spillPages_->data()), npages, cfg_.layers, pageElems,
+                                static_cast<__half *>(spillDevice_), true, s));
+  TMC_TRY(cudaMemcpyAsync(spillHost_, spillDevice_, bytes, cudaMemcpyDeviceToHost, s));
+  TMC_TRY(cudaStreamSynchronize(s));
+  out->pages.resize(bytes / 2);
+  std::memcpy(out->pages.data(), spillHost_, bytes);
+  return {};
+}
+
+std::string DecoderExecutor::restorePages(int slot, const KVPageSnapshot &snap) {
+  if (slot < 0 || slot >= cfg_.maxSlots) return "slot out of range";
+  auto &st = *slots_[slot];
+  if (st.currentLength() != 0) return "KV cache restore requires an empty request state.";
+  const size_t len = snap.length, P = pageSize_;
+  if (len == 0 || len > (size_t)cfg_.capacity) return "KV cache restore snapshot shape is invalid.";
+  const int npages = (int)((len + P - 1) / P);
+  const size_t pageElems = (size_t)hkvL_ * P * cfg_.headDim;
+  const size_t bytes = (size_t)cfg_.layers * 2 * npages * pageElems * 2;
+  if (snap.pages.size() * 2 != bytes) return "KV cache restore snapshot shape is invalid.";
+  auto e = ensureSpill(bytes, npages);
+  if (!e.empty()) return e;
+  e = st.stageLength(len);
+  if (!e.empty()) return e;
+  const auto &row = st.blockTableRow();
+  std::vector<std::int32_t> ids(row.begin(), row.begin() + npages);
+  cudaStream_t s = rt_.stream();
+  std::memcpy(spillHost_, snap.pages.data(), bytes);
+  cudaError_t ce = cudaMemcpyAsync(spillPages_->data(), ids.data(), ids.size() * 4, cudaMemcpyHostToDevice, s);
+  if (ce == cudaSuccess) ce = cudaMemcpyAsync(spillDevice_, spillHost_, bytes, cudaMemcpyHostToDevice, s);
+  if (ce == cudaSuccess)
+    ce = tmc::launch_page_copy(static_cast<__half *const *>(poolPtrs_->data()),
+                               static_cast<const int *>(spillPages_->data()), npages, cfg_.layers, pageElems,
+                               static_cast<__half *>(spillDevice_), false, s);
+  if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
+  if (ce != cudaSuccess) {
+    (void)st.rollbackLength(0);
+    return cudaText("page restore", ce);
+  }
+  st.commitLength(len);
+  return {};
+}
+
+std::string DecoderExecutor::ensureSpill(std::size_t bytes, int npages) {
+  if (!poolPtrs_) {
+    std::vector<void *> ptrs;
+    for (const auto &L : layers_) {
+      ptrs.push_back(L.kPool->data());
+      ptrs.push_back(L.vPool->data());
+    }
+    auto r = rt_.createBuffer(ptrs.size() * 2, nullptr, ElementType::Int32);  // 8-byte pointers as int32 pairs
+    if (!r.buffer) return r.errorMessage;
+    poolPtrs_ = r.buffer;
+    TMC_TRY(cudaMemcpy(poolPtrs_->data(), ptrs.data(), ptrs.size() * sizeof(void *), cudaMemcpyHostToDevice));
+    auto q = rt_.createBuffer((size_t)maxPagesPerSeq_, nullptr, ElementType::Int32);
+    if (!q.buffer) return q.errorMessage;
+    spillPages_ = q.buffer;
+  }
+  if (npages > maxPagesPerSeq_) return "KV snapshot has more pages than a sequence can hold";
+  if (bytes > spillBytes_) {
+    if (spillDevice_) cudaFree(spillDevice_);
+    if (spillHost_) cudaFreeHost(spillHost_);
+    spillDevice_ = spillHost_ = nullptr;
+    spillBytes_ = 0;
+    TMC_TRY(cudaMalloc(&spillDevice_, bytes));
+    TMC_TRY(cudaMallocHost(&spillHost_, bytes));
+    spillBytes_ = bytes;
   }
   return {};
 }

@@ -167,6 +167,22 @@ class DecoderExecutor {
   std::string restoreKV(int slot, std::size_t length, const std::vector<std::vector<float>> &keys,
                         const std::vector<std::vector<float>> &values);
   KVPagePool &pagePool() { return *pool_; }
+  // Spill / restore of a whole sequence as raw fp16 page images (every layer,
+  // K and V): one gather kernel and one device-to-host copy out, one copy and
+  // one scatter kernel back into freshly staged pages -- the preemption path
+  // of the serving scheduler (reference preempt / resume, ServingRuntime.cpp:
+  // 469-490, which rewrites per-head rows instead).
+  struct KVPageSnapshot {
+    std::size_t length = 0;
+    std::vector<std::uint16_t> pages;  // [layers][K, V][pages][page elements]
+  };
+  std::string snapshotPages(int slot, KVPageSnapshot *out);
+  std::string restorePages(int slot, const KVPageSnapshot &snap);
+
+ private:
+  std::string ensureSpill(std::size_t bytes, int npages);
+
+ public:
 
   // ---- accounting (DecoderLLMExecutor.cpp:205-229) ----
   std::size_t modelStorageBytes() const { return modelBytes_; }
@@ -227,6 +243,11 @@ class DecoderExecutor {
   cuda::BufferHandle workCounters_;  // per launch site: tmc::kGemvCounterWords uints
   unsigned int *workCounter(int layer, int kind) const;
   std::int32_t *pinnedIO_ = nullptr;   // host staging [3 * maxRows + maxRows]
+  // Page spill / restore: device array of the 2 * layers pool pointers, page-id
+  // list, packed device staging and pinned host staging (grown on demand).
+  cuda::BufferHandle poolPtrs_, spillPages_;
+  void *spillDevice_ = nullptr, *spillHost_ = nullptr;
+  std::size_t spillBytes_ = 0;
   int historyCapacity_ = 0;
   std::vector<int> lastPositions_;  // positions of the last staged step (profiling)
   cuda::BufferHandle traceRecords_, traceCount_;

@@ -20,10 +20,8 @@ std::size_t pagesFor(std::size_t length, std::size_t pageSize) { return (length 
 
 enum class RequestState { Waiting, Decode, Preempted, Finished };
 
-struct KVSnapshot {
-  std::size_t length = 0;
-  std::vector<std::vector<float>> keys, values;  // per layer [localKVHeads, length, headDim]
-};
+// A preempted request's KV state: raw fp16 page images of every layer.
+using KVSnapshot = DecoderExecutor::KVPageSnapshot;
 
 struct Request {
   ServingRequestSpec spec;
@@ -96,7 +94,7 @@ ServingExecutionResult runContinuousBatch(DecoderExecutor &dec, const std::vecto
         const auto p0 = Clock::now();
         r.slot = freeSlots.back();
         freeSlots.pop_back();
-        const auto e = dec.restoreKV(r.slot, r.snapshot->length, r.snapshot->keys, r.snapshot->values);
+        const auto e = dec.restorePages(r.slot, *r.snapshot);
         m.preemptionOverheadUs += elapsedUs(p0, Clock::now());
         if (!e.empty()) throw std::runtime_error("Request " + r.spec.id + " resume failed: " + e);
         r.snapshot.reset();
@@ -172,13 +170,8 @@ ServingExecutionResult runContinuousBatch(DecoderExecutor &dec, const std::vecto
         auto &r = reqs[victim];
         const auto p0 = Clock::now();
         KVSnapshot snap;
-        snap.length = dec.currentLength(r.slot);
-        snap.keys.resize(cfg.layers);
-        snap.values.resize(cfg.layers);
-        for (int l = 0; l < cfg.layers; ++l) {
-          const auto e = dec.readKV(l, r.slot, &snap.keys[l], &snap.values[l]);
-          if (!e.empty()) throw std::runtime_error("Request " + r.spec.id + " snapshot failed: " + e);
-        }
+        const auto e = dec.snapshotPages(r.slot, &snap);
+        if (!e.empty()) throw std::runtime_error("Request " + r.spec.id + " snapshot failed: " + e);
         r.snapshot = std::move(snap);
         m.preemptionOverheadUs += elapsedUs(p0, Clock::now());
         releaseRequest(r);

@@ -172,4 +172,27 @@ cudaError_t launch_add_residual_f32(__half *h, const float *partial, int n, cuda
   return cudaLaunchKernelEx(&cfg, add_residual_f32_kernel, h, partial, n);
 }
 
+namespace {
+__global__ void page_copy_kernel(__half *const *pools, const int *pages, int npages, size_t page_elems,
+                                 __half *packed, bool to_packed) {
+  const int i = blockIdx.x, lk = blockIdx.y;  // page index, layer * 2 + kv
+  uint4 *pool = reinterpret_cast<uint4 *>(pools[lk] + (size_t)pages[i] * page_elems);
+  uint4 *pack = reinterpret_cast<uint4 *>(packed + ((size_t)lk * npages + i) * page_elems);
+  const size_t n = page_elems / 8;
+  for (size_t j = threadIdx.x; j < n; j += blockDim.x) {
+    if (to_packed)
+      pack[j] = pool[j];
+    else
+      pool[j] = pack[j];
+  }
+}
+}  // namespace
+
+cudaError_t launch_page_copy(__half *const *pools, const int *pages, int npages, int layers, size_t page_elems,
+                             __half *packed, bool to_packed, cudaStream_t stream) {
+  if (npages <= 0 || layers <= 0 || page_elems % 8 != 0 || layers * 2 > 65535) return cudaErrorInvalidValue;
+  page_copy_kernel<<<dim3(npages, layers * 2), 256, 0, stream>>>(pools, pages, npages, page_elems, packed, to_packed);
+  return cudaGetLastError();
+}
+
 }  // namespace tmc

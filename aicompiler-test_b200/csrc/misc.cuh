@@ -22,4 +22,11 @@ cudaError_t launch_argmax_finalize(unsigned long long *keys, int rows, int *next
 cudaError_t launch_add_residual_f32(__half *h, const float *partial, int n, cudaStream_t stream,
                                     bool pdl);
 
+// Page images between the per-layer K/V pools and a packed buffer:
+// packed[((l * 2 + kv) * npages + i) * page_elems ..] <-> pools[l * 2 + kv][pages[i] * page_elems ..]
+// (pools: a device array of 2 * layers pool pointers, K then V per layer).
+// to_packed gathers (spill), otherwise scatters (restore). page_elems % 8 == 0.
+cudaError_t launch_page_copy(__half *const *pools, const int *pages, int npages, int layers, size_t page_elems,
+                             __half *packed, bool to_packed, cudaStream_t stream);
+
 }  // namespace tmc
