@@ -256,22 +256,29 @@ def run_ours(args, world, rank, local):
                     "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                     "bytes_per_launch": d["bytes"], "launch_us": d["us"]}
 
+    def guarded(name, fn):
+        # The secondary measurements must not take the headline line with them:
+        # a failure is reported in the line as that measurement's "error".
+        try:
+            return fn()
+        except Exception as exc:  # noqa: BLE001
+            print(f"[bench] {name} failed on rank {rank}: {exc}", file=sys.stderr, flush=True)
+            return {"error": f"{type(exc).__name__}: {exc}"[:400]}
+
     batched = None
     if not args.no_batch:
         dec.close()  # release the bs1 model before building the batched one
-        batched = measure_batched(args, world, rank, local, dist, barrier, max_over_ranks, hbm, peak_kind)
+        batched = guarded("bs64", lambda: measure_batched(args, world, rank, local, dist, barrier, max_over_ranks,
+                                                           hbm, peak_kind))
 
     c4 = None
     if not args.no_c4:
-        c4 = measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind)
+        c4 = guarded("c4", lambda: measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind))
 
     serving = None
     if args.serving > 0:
-        if not args.no_batch:
-            tick_s = batched["ms_per_step"] * 1e-3
-        else:
-            tick_s = 0.01
-        serving = measure_serving(args, world, rank, local, dist, barrier, hbm, tick_s)
+        tick_s = batched.get("ms_per_step", 10.0) * 1e-3 if batched else 0.01
+        serving = guarded("serving", lambda: measure_serving(args, world, rank, local, dist, barrier, hbm, tick_s))
 
     cpu = None
     if rank == 0 and world == 1:
