@@ -79,8 +79,18 @@ std::string importDecoderManifest(const std::string &path, DecoderManifest *out)
       throw std::runtime_error("Decoder-only manifest dimensions must be positive.");
     if (m.prefillLength > m.capacity || m.decodeCount > m.capacity - m.prefillLength)
       throw std::runtime_error("Decoder decode steps exceed cache capacity.");
+    m.kvHeads = m.heads;
     std::string marker;
     if (!(in >> marker)) throw std::runtime_error("Missing decoder-only tensor section.");
+    if (marker == "ATTENTION") {
+      m.kvHeads = readCount(in, "KV head count");
+      if (m.kvHeads == 0 || m.heads % m.kvHeads != 0)
+        throw std::runtime_error("Decoder KV head count must divide the head count.");
+      if (!(in >> m.ropeTheta) || !(m.ropeTheta > 0.0))
+        throw std::runtime_error("Invalid RoPE theta in decoder-only manifest.");
+      m.attentionLine = true;
+      if (!(in >> marker)) throw std::runtime_error("Missing decoder-only tensor section.");
+    }
     if (marker == "DTYPE") {
       if (!(in >> m.requestedDtype) || !knownDtype(m.requestedDtype))
         throw std::runtime_error("Unsupported decoder-only dtype.");

@@ -4,6 +4,7 @@
 //   TMC_DECODER_LLM <version>
 //   MODEL "<name>"  PAYLOAD "<file>"
 //   CONFIG batch hidden heads intermediate vocab layers capacity prefill decodes epsilon
+//   [ATTENTION kv_heads rope_theta]
 //   [DTYPE <requested> [<effective> (version 2)]]
 //   TENSORS <n>  (TENSOR "<name>" <offset> <count>) x n  END
 // and a float32 payload file beside it holding every named tensor (weights by
@@ -11,6 +12,12 @@
 // tokens / logits / KV caches). The same checks as the reference importer:
 // heads divide hidden, decode steps fit the cache, no duplicate names, nothing
 // after END, a float-aligned payload and every range inside it.
+//
+// The ATTENTION line is this backend's extension for grouped-query models (the
+// reference's descriptors have no KV-head count or RoPE base): kv_heads must
+// divide heads, rope_theta must be positive. Without it the model is MHA
+// (kv_heads = heads) with the reference exporter's base 10000, so manifests the
+// reference writes import unchanged.
 #pragma once
 
 #include <cstddef>
@@ -27,6 +34,9 @@ struct DecoderManifest {
   std::size_t batch = 0, hidden = 0, heads = 0, intermediate = 0, vocab = 0, layers = 0, capacity = 0;
   std::size_t prefillLength = 0, decodeCount = 0;
   float epsilon = 0.0f;
+  std::size_t kvHeads = 0;     // = heads unless an ATTENTION line names it
+  double ropeTheta = 10000.0;  // RoPE base of the rope.cosine / rope.sine tables
+  bool attentionLine = false;
   std::string requestedDtype = "F32", effectiveDtype = "F32";  // F32, F16 or BF16
   std::map<std::string, std::pair<std::size_t, std::size_t>> ranges;  // name -> (offset, count) in floats
   std::vector<float> payload;

@@ -129,6 +129,8 @@ int tmc_manifest_get_info(const tmc_manifest *m, tmc_manifest_info *info) {
   r.epsilon = d.epsilon;
   std::snprintf(r.requested_dtype, sizeof r.requested_dtype, "%s", d.requestedDtype.c_str());
   std::snprintf(r.effective_dtype, sizeof r.effective_dtype, "%s", d.effectiveDtype.c_str());
+  r.kv_heads = (int)d.kvHeads;
+  r.rope_theta = d.ropeTheta;
   *info = r;
   return ok();
 }
@@ -143,6 +145,20 @@ int tmc_manifest_tensor(const tmc_manifest *m, const char *name, const float **v
 
 int tmc_decoder_load_manifest(tmc_decoder *dec, const tmc_manifest *m) {
   if (!bind(dec) || m == nullptr) return fail(TMC_ERR_INVALID, "null argument");
+  const auto &c = dec->ex->config();
+  const auto &d = m->m;
+  const std::pair<const char *, std::pair<std::size_t, std::size_t>> dims[] = {
+      {"hidden size", {(std::size_t)c.hidden, d.hidden}},
+      {"head count", {(std::size_t)c.heads, d.heads}},
+      {"KV head count", {(std::size_t)c.kvHeads, d.kvHeads}},
+      {"head dimension", {(std::size_t)c.headDim, d.hidden / d.heads}},
+      {"intermediate size", {(std::size_t)c.intermediate, d.intermediate}},
+      {"vocabulary size", {(std::size_t)c.vocab, d.vocab}},
+      {"layer count", {(std::size_t)c.layers, d.layers}}};
+  for (const auto &x : dims)
+    if (x.second.first != x.second.second)
+      return fail(TMC_ERR_INVALID, std::string("decoder ") + x.first + " " + std::to_string(x.second.first) +
+                                       " does not match the manifest's " + std::to_string(x.second.second));
   for (const auto &name : tensor::importer::decoderWeightNames(m->m.layers)) {
     size_t count = 0;
     const float *v = m->m.tensor(name, &count);

@@ -365,7 +365,8 @@ class ManifestInfo(ctypes.Structure):
     _fields_ = [("version", c_int), ("batch", c_int), ("hidden_size", c_int), ("heads", c_int), ("head_dim", c_int),
                 ("intermediate_size", c_int), ("vocab_size", c_int), ("layers", c_int), ("capacity", c_int),
                 ("prefill_length", c_int), ("decode_count", c_int), ("epsilon", c_float),
-                ("requested_dtype", ctypes.c_char * 8), ("effective_dtype", ctypes.c_char * 8)]
+                ("requested_dtype", ctypes.c_char * 8), ("effective_dtype", ctypes.c_char * 8),
+                ("kv_heads", c_int), ("rope_theta", ctypes.c_double)]
 
 
 _sig("tmc_manifest_open", c_int, c_char_p, POINTER(c_void_p))
@@ -399,7 +400,7 @@ class Manifest:
         """A decoder with the manifest's dimensions and its weights loaded."""
         i = self.info
         dec = Decoder(runtime, i["hidden_size"], i["heads"], i["intermediate_size"], i["vocab_size"], i["layers"],
-                      i["capacity"], epsilon=i["epsilon"], **kw)
+                      i["capacity"], kv_heads=i["kv_heads"], epsilon=i["epsilon"], rope_theta=i["rope_theta"], **kw)
         check(lib.tmc_decoder_load_manifest(dec.handle, self.handle))
         return dec
 

@@ -239,14 +239,20 @@ typedef struct tmc_decoder tmc_decoder;
  * gives a view of any named tensor (weights, RoPE tables, the exporter's
  * reference tokens / logits / KV caches) valid until tmc_manifest_close;
  * tmc_decoder_load_manifest loads every weight and the RoPE tables into a
- * decoder created with the manifest's dimensions (kv_heads = heads, head_dim =
- * hidden / heads). Dtype tokens: "F32", "F16" or "BF16". */
+ * decoder created with the manifest's dimensions (head_dim = hidden / heads) and
+ * rejects a decoder whose dimensions differ. An optional header line
+ * "ATTENTION <kv_heads> <rope_theta>" after CONFIG (this backend's extension for
+ * grouped-query models) sets kv_heads and rope_theta; without it kv_heads =
+ * heads and rope_theta = 10000, so the reference's manifests import unchanged.
+ * Dtype tokens: "F32", "F16" or "BF16". */
 typedef struct tmc_manifest tmc_manifest;
 typedef struct {
   int version, batch, hidden_size, heads, head_dim, intermediate_size, vocab_size, layers, capacity;
   int prefill_length, decode_count;
   float epsilon;
   char requested_dtype[8], effective_dtype[8];
+  int kv_heads;
+  double rope_theta;
 } tmc_manifest_info;
 int tmc_manifest_open(const char *path, tmc_manifest **out);
 void tmc_manifest_close(tmc_manifest *m);

@@ -11,7 +11,10 @@ CONFIG_KEYS = ("batch", "hidden_size", "heads", "intermediate_size", "vocabulary
                "prefill_length", "decode_count")
 
 
-def write_manifest(path, meta, tensors, model="golden", version=2, dtypes=("F16", "F16"), extra_lines=()):
+def write_manifest(path, meta, tensors, model="golden", version=2, dtypes=("F16", "F16"), extra_lines=(),
+                   attention=None):
+    """`attention` = (kv_heads, rope_theta) writes the optional ATTENTION line
+    of this backend's grouped-query extension after CONFIG."""
     payload_name = os.path.basename(path) + ".bin"
     chunks, ranges, offset = [], [], 0
     for name, value in tensors.items():
@@ -24,8 +27,10 @@ def write_manifest(path, meta, tensors, model="golden", version=2, dtypes=("F16"
             f.write(c.tobytes())
     lines = [f"TMC_DECODER_LLM {version}", f"MODEL {json.dumps(model)}", f"PAYLOAD {json.dumps(payload_name)}",
              "CONFIG " + " ".join(str(meta[k]) for k in CONFIG_KEYS) + f" {meta['epsilon']:.9g}"]
+    if attention is not None:
+        lines.append(f"ATTENTION {attention[0]} {attention[1]!r}")
     if dtypes:
-        lines.append("DTYPE " + " ".join(dtypes[:2] if version == 2 else dtypes[:1]))
+        lines.append("DTYPE "+ " ".join(dtypes[:2] if version == 2 else dtypes[:1]))
     lines.append(f"TENSORS {len(ranges)}")
     lines += [f"TENSOR {json.dumps(n)} {o} {c}" for n, o, c in ranges]
     lines.append("END")

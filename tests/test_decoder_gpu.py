@@ -297,3 +297,45 @@ def test_decoder_from_reference_manifest_matches_exporter(rt, tmp_path):
         rms_close(lg[0], m.tensor(f"decode{step}.logits"), f"manifest decode{step} logits")
     dec.close()
     m.close()
+
+
+def test_decoder_from_gqa_manifest_matches_its_source(rt, tmp_path):
+    # A grouped-query decoder (theta 5e5) written out with the manifest's
+    # ATTENTION line and read back: same greedy tokens, bit-exact logits; a
+    # decoder of other dimensions refuses the manifest.
+    import tmc_cuda
+    from tests.manifest_writer import write_manifest
+    hidden, heads, kv, inter, vocab, layers, cap = 256, 4, 2, 512, 300, 2, 64
+    hd = hidden // heads
+    src = tmc_cuda.Decoder(rt, hidden, heads, inter, vocab, layers, cap, kv_heads=kv, rope_theta=5e5)
+    src.init_random(seed=7, std=0.05)
+    sizes = {"embedding.weight": vocab * hidden, "final_norm.weight": hidden, "lm_head.weight": vocab * hidden,
+             "rope.cosine": cap * hd // 2, "rope.sine": cap * hd // 2}
+    per = {"input_norm": hidden, "q": heads * hd * hidden, "k": kv * hd * hidden, "v": kv * hd * hidden,
+           "o": hidden * heads * hd, "post_norm": hidden, "gate": inter * hidden, "up": inter * hidden,
+           "down": hidden * inter}
+    for l in range(layers):
+        sizes.update({f"layer{l}.{k}.weight": n for k, n in per.items()})
+    tensors = {name: src.read_weight(name, n) for name, n in sizes.items()}
+    meta = dict(batch=1, hidden_size=hidden, heads=heads, intermediate_size=inter, vocabulary_size=vocab,
+                layers=layers, capacity=cap, prefill_length=8, decode_count=4, epsilon=1e-5)
+    path = write_manifest(str(tmp_path / "gqa.tmc"), meta, tensors, attention=(kv, 500000.0))
+    m = tmc_cuda.Manifest(path)
+    assert (m.info["kv_heads"], m.info["rope_theta"]) == (kv, 500000.0)
+    dec = m.decoder(rt)
+    prompt = np.random.default_rng(3).integers(0, vocab, 8).astype(np.int32)
+    la, ta = src.prefill(prompt)
+    lb, tb = dec.prefill(prompt)
+    assert ta == tb and np.array_equal(la, lb)
+    for _ in range(4):
+        la, na = src.decode([ta])
+        lb, nb = dec.decode([tb])
+        assert np.array_equal(la, lb) and int(na[0]) == int(nb[0])
+        ta, tb = int(na[0]), int(nb[0])
+    mha = tmc_cuda.Decoder(rt, hidden, heads, inter, vocab, layers, cap)
+    with pytest.raises(tmc_cuda.TmcError, match="KV head count"):
+        lib = tmc_cuda.lib
+        tmc_cuda.check(lib.tmc_decoder_load_manifest(mha.handle, m.handle))
+    for d in (src, dec, mha):
+        d.close()
+    m.close()

@@ -67,3 +67,32 @@ def test_manifest_rejections(tmp_path, case):
         os.remove(path + ".bin")
     with pytest.raises(tmc_cuda.TmcError):
         tmc_cuda.Manifest(path)
+
+
+def _small_meta():
+    return dict(batch=1, hidden_size=8, heads=4, intermediate_size=16, vocabulary_size=10, layers=1, capacity=6,
+                prefill_length=2, decode_count=3, epsilon=1e-5)
+
+
+def test_manifest_attention_line_sets_kv_heads_and_theta(tmp_path):
+    import tmc_cuda
+    path = write_manifest(str(tmp_path / "m.tmc"), _small_meta(), {"a": np.arange(4.0)}, attention=(2, 500000.0))
+    m = tmc_cuda.Manifest(path)
+    assert (m.info["kv_heads"], m.info["rope_theta"], m.info["heads"]) == (2, 500000.0, 4)
+    assert m.info["requested_dtype"] == "F16"
+    assert np.array_equal(m.tensor("a"), np.arange(4.0, dtype=np.float32))
+
+
+def test_manifest_without_attention_line_is_mha(tmp_path):
+    import tmc_cuda
+    path = write_manifest(str(tmp_path / "m.tmc"), _small_meta(), {"a": np.arange(4.0)})
+    m = tmc_cuda.Manifest(path)
+    assert (m.info["kv_heads"], m.info["rope_theta"]) == (4, 10000.0)
+
+
+@pytest.mark.parametrize("attention", [(3, 10000.0), (0, 10000.0), (2, 0.0), (2, -1.0)])
+def test_manifest_attention_line_rejections(tmp_path, attention):
+    import tmc_cuda
+    path = write_manifest(str(tmp_path / "m.tmc"), _small_meta(), {"a": np.arange(4.0)}, attention=attention)
+    with pytest.raises(tmc_cuda.TmcError):
+        tmc_cuda.Manifest(path)
