@@ -37,7 +37,7 @@ CFG = dict(hidden=4096, heads=32, kv_heads=8, intermediate=14336, vocab=128256, 
            rope_theta=500000.0, epsilon=1e-5)
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=128)
@@ -55,7 +55,7 @@ def parse():
                          "outputs U[64,512], max batch 128; 1000 in the full config)")
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="TP reductions: peer exchange fused into the kernels, or NCCL allreduce")
-    return ap.parse_args()
+    return ap.parse_args(argv)
 
 
 def measured_peaks():
@@ -132,6 +132,17 @@ def emit(obj):
     print(json.dumps(obj), flush=True)
 
 
+def headline_config(args, world):
+    """The headline workload; both arms print this same `config`."""
+    return {"workload": "C3 Llama-3-8B-shaped greedy decode, batch 1, prompt 1024",
+            "layers": args.layers, "hidden": CFG["hidden"], "heads": CFG["heads"],
+            "kv_heads": CFG["kv_heads"], "intermediate": CFG["intermediate"],
+            "vocab": CFG["vocab"], "batch": 1, "prompt": args.prompt,
+            "parallelism": f"tp{world}",
+            "tp_reduction": (args.collective if world > 1 else None),
+            "l2": "inputs larger than L2: 15 GB of weights streamed per step"}
+
+
 def run_reference(args, world, rank):
     """CPU reference arm: the reference's PyTorch decoder algorithm on the host."""
     if rank != 0:
@@ -147,8 +158,7 @@ def run_reference(args, world, rank):
     emit({"metric": METRIC, "impl": "reference", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
           "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / value, "higher_is_better": True,
           "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-          "config": {"workload": "C3 Llama-3-8B-shaped decode, batch 1, prompt 1024 (CPU sample)",
-                     "batch": 1, "prompt": args.prompt},
+          "config": headline_config(args, world),
           "cpu_baseline": {"value": value, "unit": "tok/s", "cores": r["threads"], "kind": "port",
                            "sample": r["sample"]},
           "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
@@ -293,13 +303,7 @@ def run_ours(args, world, rank, local):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": step_ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic (random-init N(0,0.02) fp16 weights, random prompt ids)",
-            "config": {"workload": "C3 Llama-3-8B-shaped greedy decode, batch 1, prompt 1024",
-                       "layers": args.layers, "hidden": CFG["hidden"], "heads": CFG["heads"],
-                       "kv_heads": CFG["kv_heads"], "intermediate": CFG["intermediate"],
-                       "vocab": CFG["vocab"], "batch": 1, "prompt": args.prompt,
-                       "parallelism": f"tp{world}",
-                       "tp_reduction": (args.collective if world > 1 else None),
-                       "l2": "inputs larger than L2: 15 GB of weights streamed per step"},
+            "config": headline_config(args, world),
             # Whole-job bytes: every rank streams its own shard (step_bytes is one rank's).
             "step_roofline": {"bytes_per_step": step_bytes * world,
                               "bytes_per_step_per_rank": step_bytes,
