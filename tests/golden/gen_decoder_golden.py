@@ -1,7 +1,7 @@
 """Generate decoder golden vectors with the reference's OWN exporter.
 
-Runs tools/export_decoder_llm.py of the reference project (default
-/root/reference, override with TMC_REFERENCE) in-process: it builds the
+Runs tools/export_decoder_llm.py of the reference project (the checkout named
+by TMC_REFERENCE, else the default below) in-process: it builds the
 reference's PyTorch DecoderOnlyLLM (workloads/pytorch/decoder_llm.py), seeds it,
 runs the fp16 precision admission, and records prefill and per-step decode
 logits, greedy next tokens and full KV caches (export_decoder_llm.py:453-551).

@@ -1,8 +1,9 @@
 """Generate the committed golden vectors for the oracle pin tests.
 
-Run in a container where the reference project is mounted (default
-/root/reference) after `make -C oracle` built oracle/_ref/libtmcref.so, the
-reference's own evaluateGraph compiled from its sources:
+Run where the reference project's sources are present (the oracle Makefile's
+REFERENCE variable names the checkout) after `make -C oracle` built
+oracle/_ref/libtmcref.so, the reference's own evaluateGraph compiled from its
+sources:
 
     python tests/golden/gen_golden.py
 
