@@ -383,7 +383,16 @@ def measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind
     us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / reps)
     nbytes = (4096 * int(ctx.sum()) + 2 * rows * 32 * d * 2) + 0.0  # whole job (all KV heads)
     rt.close()
+    cpu = None
+    if rank == 0 and world == 1:
+        # The C restatement of the reference's serving kernel on the host cores
+        # (a bounded sample of the same distribution; one thread and all threads).
+        from oracle import cpu_baseline
+        r = cpu_baseline.paged_attention_gbs(sequences=8)
+        cpu = {"value": r["gbs_all_threads"], "unit": "GB/s", "cores": r["threads"], "kind": "port",
+               "value_1_thread": r["gbs_1_thread"], "sample": r["sample"]}
     return {"metric": "paged GQA attention HBM GB/s", "value": nbytes / us / 1e3, "unit": "GB/s",
+            "cpu_baseline": cpu,
             "us_per_call": us, "bytes_per_call": nbytes, "sum_ctx": int(ctx.sum()),
             "frac_of_peak": nbytes / us / 1e3 / (hbm * world), "peak_gbs": hbm * world,
             "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",

@@ -83,3 +83,59 @@ def decode_tokens_per_second(steps: int = 6, context: int = 1024, head_calls: in
         "sample": (f"{steps} decode steps of one Llama-3-8B-shaped layer (fp16, GQA 32/8, ctx {context}) "
                    f"+ {head_calls} LM-head GEMVs (128256x4096); per token = 32 layers + head"),
     }
+
+
+def paged_attention_gbs(sequences: int = 12, threads: int | None = None, seed: int = 4):
+    """C4 paged GQA decode attention on the host: the C restatement of the
+    serving kernel (oracle_paged_attention, KVCacheMetalEmitter.cpp:312-406)
+    over `sequences` seeded sequences with contexts ~U[128, 8192], 32 q / 8 kv
+    heads x 128, 16-token pages drawn from a shuffled pool. Timed on one thread
+    and on `threads` threads (sequences split across them; the C call releases
+    the GIL). GB/s counts the same algorithmic bytes as the GPU measurement:
+    fp16 K and V of every context position (4096 B per position) + q + out."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
+
+    from . import oracle
+
+    threads = threads or os.cpu_count() or 1
+    rng = np.random.default_rng(seed)
+    hq, hkv, d, page = 32, 8, 128, 16
+    ctx = rng.integers(128, 8193, sequences)
+    pages_per = (ctx + page - 1) // page
+    stride = int(pages_per.max())
+    npages = int(pages_per.sum())
+    perm = rng.permutation(npages).astype(np.int32)
+    table = np.full((sequences, stride), -1, dtype=np.int32)
+    off = 0
+    for r in range(sequences):
+        table[r, : pages_per[r]] = perm[off: off + pages_per[r]]
+        off += pages_per[r]
+    kp = rng.standard_normal((npages, hkv, page, d), dtype=np.float32).astype(np.float16).astype(np.float32)
+    vp = rng.standard_normal((npages, hkv, page, d), dtype=np.float32).astype(np.float16).astype(np.float32)
+    q = rng.standard_normal((sequences, hq, d), dtype=np.float32).astype(np.float16).astype(np.float32)
+    pos = (ctx - 1).astype(np.int32)
+    nbytes = 4096.0 * float(ctx.sum()) + 2.0 * sequences * hq * d * 2
+
+    def run(rows):
+        rows = np.asarray(rows)
+        return oracle.paged_attention(q[rows], kp, vp, table, rows.astype(np.int32), pos[rows], hkv, page)
+
+    t0 = time.perf_counter()
+    run(np.arange(sequences))
+    one_s = time.perf_counter() - t0
+    workers = min(threads, sequences)
+    # One task per sequence, longest first, so the threads finish together.
+    order = [[int(r)] for r in np.argsort(-ctx)]
+    with ThreadPoolExecutor(max_workers=workers) as ex:
+        t0 = time.perf_counter()
+        list(ex.map(run, order))
+        many_s = time.perf_counter() - t0
+    return {
+        "gbs_1_thread": nbytes / one_s / 1e9,
+        "gbs_all_threads": nbytes / many_s / 1e9,
+        "threads": workers,
+        "sample": (f"{sequences} sequences, contexts U[128,8192] (sum {int(ctx.sum())}), 32q/8kv x 128, "
+                   f"16-token pages; C restatement of the serving kernel (fp64 softmax), once on 1 thread "
+                   f"and once with one task per sequence on {workers} threads"),
+    }
