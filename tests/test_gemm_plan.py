@@ -37,6 +37,11 @@ def run_of(iters, grid, i):
 
 SHAPES = [(6144, 4096, 64), (4096, 4096, 64), (28672, 4096, 64), (4096, 14336, 64), (128256, 4096, 64),
           (2816, 1024, 12), (4096, 1408, 33), (1000, 136, 17), (128, 8, 9), (40, 64, 128), (14336, 2048, 100)]
+# Per-rank shards of the 8B projections at bs64 under tensor parallelism 2 / 4 / 8:
+# QKV and gate/up split their outputs, O and down their inputs, the LM head its vocabulary.
+SHAPES += [shape for tp in (2, 4, 8) for shape in
+           ((6144 // tp, 4096, 64), (4096, 4096 // tp, 64), (28672 // tp, 4096, 64), (4096, 14336 // tp, 64),
+            (128256 // tp, 4096, 64))]
 
 
 @pytest.mark.parametrize("n,k,m", SHAPES)
