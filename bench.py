@@ -387,10 +387,13 @@ def measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind
     if rank == 0 and world == 1:
         # The C restatement of the reference's serving kernel on the host cores
         # (a bounded sample of the same distribution; one thread and all threads).
-        from oracle import cpu_baseline
-        r = cpu_baseline.paged_attention_gbs(sequences=8)
-        cpu = {"value": r["gbs_all_threads"], "unit": "GB/s", "cores": r["threads"], "kind": "port",
-               "value_1_thread": r["gbs_1_thread"], "sample": r["sample"]}
+        try:
+            from oracle import cpu_baseline
+            r = cpu_baseline.paged_attention_gbs(sequences=8)
+            cpu = {"value": r["gbs_all_threads"], "unit": "GB/s", "cores": r["threads"], "kind": "port",
+                   "value_1_thread": r["gbs_1_thread"], "sample": r["sample"]}
+        except Exception as e:  # the GPU measurement above stands without it
+            cpu = {"error": f"{type(e).__name__}: {e}"}
     return {"metric": "paged GQA attention HBM GB/s", "value": nbytes / us / 1e3, "unit": "GB/s",
             "cpu_baseline": cpu,
             "us_per_call": us, "bytes_per_call": nbytes, "sum_ctx": int(ctx.sum()),
