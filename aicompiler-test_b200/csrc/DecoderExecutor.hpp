@@ -172,6 +172,7 @@ class DecoderExecutor {
   // one scatter kernel back into freshly staged pages -- the preemption path
   // of the serving scheduler (reference preempt / resume, ServingRuntime.cpp:
   // 469-490, which rewrites per-head rows instead).
+  using Timing = StepTiming;  // the per-step timing the prefill / decode calls report
   struct KVPageSnapshot {
     std::size_t length = 0;
     std::vector<std::uint16_t> pages;  // [layers][K, V][pages][page elements]

@@ -27,60 +27,9 @@
 #include <vector>
 
 #include "DecoderExecutor.hpp"
+#include "ServingScheduler.hpp"
 
 namespace tensor::runtime {
-
-struct ServingRequestSpec {
-  std::string id;
-  std::vector<std::int32_t> promptTokenIds;
-  std::size_t decodeTokenCount = 0;
-  std::size_t arrivalStep = 0;  // scheduler tick at which the request arrives
-};
-
-struct ServingConfig {
-  bool recordLogits = false;    // keep prefill and decode logits per request
-  std::size_t maxTicks = 1000000;  // progress limit (the reference uses 10000)
-};
-
-struct ServingRequestOutput {
-  std::string id;
-  std::vector<float> prefillLogits;                // [prompt, localVocab] when recorded
-  std::vector<std::vector<float>> decodeLogits;    // per decode step, [localVocab]
-  std::vector<std::int32_t> generatedTokenIds;     // 1 (prefill) + decodeTokenCount
-  double timeToFirstTokenUs = 0.0;                 // arrival -> first token
-  double finishUs = 0.0;                           // arrival -> last token
-};
-
-struct ServingMetrics {
-  double totalTimeUs = 0.0;
-  double tokensPerSecond = 0.0;      // decoded tokens / total time
-  double prefillGpuUs = 0.0;         // sums over all prefill / decode steps
-  double decodeGpuUs = 0.0;
-  double schedulerOverheadUs = 0.0;
-  double kvManagementOverheadUs = 0.0;
-  double preemptionOverheadUs = 0.0;
-  double averageActiveBatchSize = 0.0;
-  std::size_t maximumActiveBatchSize = 0;
-  std::size_t preemptionCount = 0;
-  std::size_t resumeCount = 0;
-  std::size_t peakPages = 0;
-  std::size_t pageAllocationCount = 0;
-  std::size_t pageReleaseCount = 0;
-  std::size_t decodeCommandSubmissions = 0;
-  std::size_t decodedTokens = 0;
-  std::size_t prefillTokens = 0;
-  std::size_t ticks = 0;
-  std::size_t modelStorageBytes = 0;
-  std::size_t kvPoolStorageBytes = 0;
-  std::size_t activationStorageBytes = 0;
-};
-
-struct ServingExecutionResult {
-  bool passed = false;
-  std::vector<ServingRequestOutput> requests;
-  ServingMetrics metrics;
-  std::string errorMessage;
-};
 
 // Serve `requests` on `decoder` (a multi-slot executor; its weights loaded).
 // All tensor-parallel ranks must call this with the same requests: every
