@@ -124,7 +124,6 @@ class DecoderOracle:
         positions = torch.arange(start, start + S).view(1, S)
         x = F.embedding(ids, self.w["embedding.weight"])
         new_cache = []
-        group = s.heads // s.kv_heads
         D = s.head_dim
         for layer in range(s.layers):
             p = f"layer{layer}."
@@ -138,14 +137,7 @@ class DecoderOracle:
                 k = torch.cat((past[layer][0].unsqueeze(0), k), dim=2)
                 v = torch.cat((past[layer][1].unsqueeze(0), v), dim=2)
             new_cache.append((k[0], v[0]))
-            kk = k.repeat_interleave(group, dim=1) if group > 1 else k
-            vv = v.repeat_interleave(group, dim=1) if group > 1 else v
-            scores = torch.matmul(q.float(), kk.float().transpose(-2, -1)) / math.sqrt(D)
-            qpos = torch.arange(start, start + S).view(S, 1)
-            kpos = torch.arange(kk.size(2)).view(1, -1)
-            scores = scores.masked_fill(kpos > qpos, float("-inf"))
-            probs = torch.softmax(scores, dim=-1)
-            ctx = torch.matmul(probs, vv.float()).to(dt)
+            ctx = causal_gqa_attention(q, k, v, start).to(dt)
             ctx = ctx.transpose(1, 2).contiguous().view(1, S, -1)
             x = x + self._linear(ctx, self.w[p + "o.weight"])
             h = _rms_norm(x, self.w[p + "post_norm.weight"], s.epsilon)
@@ -156,6 +148,23 @@ class DecoderOracle:
         self.caches[seq] = new_cache
         nxt = int(logits[0, -1].argmax().item())
         return logits[0], nxt
+
+
+def causal_gqa_attention(q, k, v, start: int):
+    """The decoder's attention (decoder_llm.py's scaled-dot-product step with the
+    GQA head map): q [1, Hq, S, D] for positions start..start+S-1, k / v
+    [1, Hkv, L, D] for positions 0..L-1; fp32 scores / sqrt(D), causal mask, fp32
+    softmax, fp32 context [1, Hq, S, D] (the caller rounds it to storage)."""
+    S, D = q.shape[2], q.shape[3]
+    group = q.shape[1] // k.shape[1]
+    kk = k.repeat_interleave(group, dim=1) if group > 1 else k
+    vv = v.repeat_interleave(group, dim=1) if group > 1 else v
+    scores = torch.matmul(q.float(), kk.float().transpose(-2, -1)) / math.sqrt(D)
+    qpos = torch.arange(start, start + S).view(S, 1)
+    kpos = torch.arange(kk.size(2)).view(1, -1)
+    scores = scores.masked_fill(kpos > qpos, float("-inf"))
+    probs = torch.softmax(scores, dim=-1)
+    return torch.matmul(probs, vv.float())
 
 
 def spec_from_golden(meta: dict, kv_heads=None, rope_theta=10000.0) -> DecoderSpec:

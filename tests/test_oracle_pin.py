@@ -100,3 +100,35 @@ def test_paged_attention_oracle_reduces_to_dense_softmax():
         p = np.exp(s - s.max())
         p /= p.sum()
         np.testing.assert_allclose(out[0, h], p @ v[0, h // 2].astype(np.float64), rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("hq,hkv,page", [(32, 8, 16), (4, 4, 4), (8, 2, 5)])
+def test_paged_attention_oracle_matches_the_decoder_oracle(hq, hkv, page):
+    # The C restatement of the serving kernel (scattered pages, GQA head map,
+    # several rows of different lengths) against the decoder oracle's attention
+    # (causal_gqa_attention, pinned bit for bit to the reference exporter) on the
+    # same fp16-valued data: the C path sums in fp64, the decoder oracle in fp32.
+    import torch
+    from oracle.decoder_ref import causal_gqa_attention
+    rng = np.random.default_rng(hq * 100 + page)
+    d, lengths = 32, [1, page, 3 * page + 2, 70]
+    pages_per = [(n + page - 1) // page for n in lengths]
+    npages = sum(pages_per) + 3
+    perm = rng.permutation(npages).astype(np.int32)
+    stride = max(pages_per)
+    table = np.full((len(lengths), stride), -1, np.int32)
+    off = 0
+    for r, n in enumerate(pages_per):
+        table[r, :n] = perm[off:off + n]
+        off += n
+    f16 = lambda *shape: rng.standard_normal(shape).astype(np.float16).astype(np.float32)
+    kp, vp, q = f16(npages, hkv, page, d), f16(npages, hkv, page, d), f16(len(lengths), hq, d)
+    pos = np.array(lengths, np.int32) - 1
+    out = oracle.paged_attention(q, kp, vp, table, np.arange(len(lengths), dtype=np.int32), pos, hkv, page)
+    for r, n in enumerate(lengths):
+        ids = table[r, :pages_per[r]]
+        # Gather the sequence's pages back into a contiguous [1, hkv, n, d] cache.
+        k = torch.from_numpy(kp[ids].transpose(1, 0, 2, 3).reshape(hkv, -1, d)[:, :n][None].copy())
+        v = torch.from_numpy(vp[ids].transpose(1, 0, 2, 3).reshape(hkv, -1, d)[:, :n][None].copy())
+        ref = causal_gqa_attention(torch.from_numpy(q[r][None, :, None, :].copy()), k, v, n - 1)[0, :, 0].numpy()
+        np.testing.assert_allclose(out[r], ref, rtol=2e-5, atol=2e-6)
