@@ -101,24 +101,37 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        rows = []
         try:
             with open(self.path) as f:
-                for line in f:
-                    parts = [p.strip() for p in line.split(",")]
-                    if len(parts) >= 9:
-                        rows.append(parts)
+                lines = f.readlines()
             os.unlink(self.path)
         except Exception:
             return None
-        if not rows:
+        return summarize_clocks(lines)
+
+
+def summarize_clocks(lines):
+    """Median SM clock, the largest max clock and the throttle reasons seen
+    Active in `nvidia-smi --format=csv,noheader,nounits` lines of
+    ClockSampler.QUERY; None without a complete line. Unreadable values
+    ("[N/A]") are skipped."""
+    rows = [[p.strip() for p in line.split(",")] for line in lines]
+    rows = [r for r in rows if len(r) >= 9]
+    if not rows:
+        return None
+
+    def num(text):
+        try:
+            return float(text)
+        except ValueError:
             return None
-        sm = sorted(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
-        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
-                "samples": len(rows)}
+
+    sm = sorted(v for v in (num(r[1]) for r in rows) if v is not None)
+    mx = [v for v in (num(r[2]) for r in rows) if v is not None]
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+    return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mx) if mx else None,
+            "reasons": reasons, "samples": len(rows)}
 
 
 def dist_info():

@@ -1,6 +1,8 @@
-"""bench.py's reference arm (`--impl reference`) on the CPU: one JSON line with
-the headline arm's metric and config, the reference-arm keys (impl,
-cpu_baseline, a zero-copy e2e), and silence on every rank but 0."""
+"""bench.py's host-side contract on the CPU: the reference arm (`--impl
+reference`) prints one JSON line with the headline arm's metric and config, the
+reference-arm keys (impl, cpu_baseline, a zero-copy e2e), and nothing on ranks
+other than 0; the clock record summarises nvidia-smi samples (median SM clock,
+throttle reasons seen Active) and tolerates unreadable values."""
 
 import json
 import os
@@ -35,3 +37,19 @@ def test_reference_arm_line():
 
 def test_reference_arm_other_ranks_are_silent():
     assert _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
+
+
+def test_clock_summary_reads_nvidia_smi_lines():
+    sys.path.insert(0, ROOT)
+    import bench
+    idle = "0, 1965, 1965, 300.5, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active\n"
+    capped = "0, 1800, 1965, 999.1, 0x0000000000000004, Not Active, Not Active, Not Active, Active\n"
+    hot = "0, 1200, 1965, 700.0, 0x0000000000000008, Active, Not Active, Not Active, Not Active\n"
+    s = bench.summarize_clocks([idle, capped, idle])
+    assert s == {"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3}
+    assert bench.summarize_clocks([idle, hot, hot])["reasons"] == ["hw_slowdown"]
+    assert bench.summarize_clocks([idle, hot, hot])["sm_mhz"] == 1200.0
+    # Unreadable values are skipped; incomplete lines and no lines give None.
+    na = "0, [N/A], [N/A], [N/A], [N/A], Not Active, Not Active, Not Active, Not Active\n"
+    assert bench.summarize_clocks([na]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 1}
+    assert bench.summarize_clocks(["0, 1965\n"]) is None and bench.summarize_clocks([]) is None
