@@ -1,8 +1,11 @@
-"""The C-ABI library loads and exports every function include/*.h declares (CPU only)."""
+"""The C-ABI library loads and exports every function include/*.h declares, and
+refuses bad arguments on the host before any launch (CPU only)."""
 
 import glob
 import os
 import re
+
+import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -45,3 +48,27 @@ def test_rmsnorm_and_tuners_validate_arguments_on_the_host():
     rsel = tmc_cuda.RMSNormSelection()
     assert tmc_cuda.lib.tmc_tune_rmsnorm(1, 8, 1e-5, 0, None, None, None, 0, ctypes.byref(rsel), None, None,
                                          0) == tmc_cuda.ERR_INVALID
+
+
+# Host-side rejections of the graph-path operators: non-null placeholder
+# pointers (never dereferenced), so the size and value checks are what refuse.
+P = 0x1000
+REJECTIONS = [
+    ("rmsnorm rows", lambda l: l.tmc_k_rmsnorm(P, P, P, 0, 8, 1e-5, 0, 256, None), "INVALID", "rows >= 1"),
+    ("rmsnorm eps", lambda l: l.tmc_k_rmsnorm(P, P, P, 1, 8, 0.0, 0, 256, None), "INVALID", "eps"),
+    ("rmsnorm threads", lambda l: l.tmc_k_rmsnorm(P, P, P, 1, 8, 1e-5, 0, 48, None), "UNSUPPORTED", "power of two"),
+    ("add-norm b_rows", lambda l: l.tmc_k_fused_add_norm(P, P, P, P, P, 3, 8, 2, 1e-5, 0, 0, None), "INVALID",
+     "b_rows"),
+    ("layer-norm bias", lambda l: l.tmc_k_fused_add_norm(P, P, P, None, P, 1, 8, 1, 1e-5, 1, 0, None), "INVALID",
+     "null"),
+    ("add-norm eps", lambda l: l.tmc_k_fused_add_norm(P, P, P, P, P, 1, 8, 1, -1.0, 0, 1, None), "INVALID", "eps"),
+    ("silu-mul width", lambda l: l.tmc_k_fused_silu_mul(P, P, P, 1, 0, 1, 0, None), "INVALID", "width"),
+    ("linear-relu n", lambda l: l.tmc_k_fused_linear_relu(P, P, P, P, 2, 3, 0, 0, None), "INVALID", "m, k, n"),
+]
+
+
+@pytest.mark.parametrize("name,call,code,fragment", REJECTIONS, ids=[r[0] for r in REJECTIONS])
+def test_graph_operators_reject_bad_arguments_on_the_host(name, call, code, fragment):
+    import tmc_cuda
+    assert call(tmc_cuda.lib) == getattr(tmc_cuda, "ERR_" + code)
+    assert fragment in tmc_cuda.last_error()
