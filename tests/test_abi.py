@@ -72,3 +72,22 @@ def test_graph_operators_reject_bad_arguments_on_the_host(name, call, code, frag
     import tmc_cuda
     assert call(tmc_cuda.lib) == getattr(tmc_cuda, "ERR_" + code)
     assert fragment in tmc_cuda.last_error()
+
+
+def test_noalloc_attention_refuses_requests_beyond_its_fixed_scratch():
+    # The limit is checked on the host before the scratch array is looked up or
+    # anything is launched: partials rows*hq*splits*(d+2)*4 (rounded up to 256)
+    # plus rows*hkv*4 bytes of tickets must fit in 8 MiB.
+    from ctypes import c_int, c_void_p
+    import tmc_cuda
+    fn = tmc_cuda.lib.tmc_k_paged_attention_f16_noalloc
+    fn.restype = c_int
+    fn.argtypes = [c_void_p] * 5 + [c_int] + [c_void_p] * 2 + [c_int] * 9 + [c_void_p] * 2
+    limit = 8 << 20
+    rows, hq, hkv, d, splits = 64, 32, 8, 128, 8
+    need = (tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, splits) + 255) // 256 * 256 + rows * hkv * 4
+    assert need == (rows * hq * splits * (d + 2) * 4 + 255) // 256 * 256 + rows * hkv * 4 > limit
+    code = fn(P, P, P, P, P, 1, P, P, rows, hq, hkv, d, 16, 64, 1024, splits, 64, None, None)
+    assert code == tmc_cuda.ERR_UNSUPPORTED
+    assert f"needs {need} bytes" in tmc_cuda.last_error() and str(limit) in tmc_cuda.last_error()
+    assert fn(P, P, P, P, P, 1, P, P, 0, hq, hkv, d, 16, 64, 1024, 1, 64, None, None) == tmc_cuda.ERR_INVALID
