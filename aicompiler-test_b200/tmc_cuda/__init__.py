@@ -361,6 +361,51 @@ def _i32(a):
     return np.ascontiguousarray(np.asarray(a, dtype=np.int32).reshape(-1))
 
 
+_sig("tmc_plan_regions", c_int, c_int, _I32P, c_size_t, c_int, _I32P, c_int, _I32P, _I32P, _I32P, c_size_t,
+     POINTER(c_size_t))
+
+REGION_KINDS = ("Unfused", "Add + RMSNorm", "Residual Add + LayerNorm", "SiLU + Mul", "Linear + ReLU")
+
+
+def plan_regions(input_count: int, nodes, outputs, contiguous):
+    """Fused-kernel regions of a typed tensor graph (tmc_plan_regions; the
+    reference's formRegions). nodes: [(op number, operand value ids...)], node i
+    defining value input_count + i; contiguous: per value. Returns (topological
+    order, [(kind, nodes, inputs, outputs)])."""
+    flat = []
+    for op, *operands in nodes:
+        flat += [int(op), len(operands)] + [int(v) for v in operands]
+    flat = np.asarray(flat, np.int32)
+    outs = np.asarray(outputs, np.int32)
+    cont = np.asarray(contiguous, np.int32)
+    if cont.size != input_count + len(nodes):
+        raise ValueError("contiguous needs one flag per value")
+    order = np.zeros(max(len(nodes), 1), np.int32)
+    written = c_size_t(0)
+    cap = 64 * (len(nodes) + 1) + 16
+    while True:
+        regions = np.zeros(cap, np.int32)
+        code = lib.tmc_plan_regions(input_count, flat.ctypes.data_as(_I32P), flat.size, len(nodes),
+                                    outs.ctypes.data_as(_I32P), outs.size, cont.ctypes.data_as(_I32P),
+                                    order.ctypes.data_as(_I32P), regions.ctypes.data_as(_I32P), cap,
+                                    ctypes.byref(written))
+        if code == OK or written.value <= cap:
+            break
+        cap = written.value
+    check(code)
+    out, i = [], 0
+    while i < written.value:
+        kind = int(regions[i])
+        i += 1
+        parts = []
+        for _ in range(3):
+            k = int(regions[i])
+            parts.append([int(x) for x in regions[i + 1:i + 1 + k]])
+            i += 1 + k
+        out.append((kind, *parts))
+    return order[:len(nodes)].tolist(), out
+
+
 class ManifestInfo(ctypes.Structure):
     _fields_ = [("version", c_int), ("batch", c_int), ("hidden_size", c_int), ("heads", c_int), ("head_dim", c_int),
                 ("intermediate_size", c_int), ("vocab_size", c_int), ("layers", c_int), ("capacity", c_int),

@@ -259,6 +259,24 @@ void tmc_manifest_close(tmc_manifest *m);
 int tmc_manifest_get_info(const tmc_manifest *m, tmc_manifest_info *info);
 int tmc_manifest_tensor(const tmc_manifest *m, const char *name, const float **values, size_t *count);
 
+/* formRegions (PatternAnalyzer.cpp:32-132) with analyze()'s topological order
+ * (GraphAnalyzer.cpp:278-364), for a graph whose value types are already known:
+ * which nodes run as one fused kernel (Add+RMSNorm, residual Add+LayerNorm,
+ * SiLU*Mul, MatMul+Add+ReLU -> tmc_k_fused_add_norm / tmc_k_fused_silu_mul /
+ * tmc_k_fused_linear_relu). Values 0..input_count-1 are the graph inputs; the
+ * nodes are encoded as {op, operand count, operands...} (op numbered as the
+ * reference's tensor::OpType), node i defining value input_count + i, in an
+ * array of nodes_len ints; contiguous[v] != 0 when value v's storage is
+ * contiguous (a Transpose view is not). Writes order[node_count] and the regions
+ * as {kind (0 unfused, 1 Add+RMSNorm, 2 Add+LayerNorm, 3 SiLU*Mul,
+ * 4 Linear+ReLU), #nodes, nodes..., #inputs, inputs..., #outputs, outputs...};
+ * *written receives the ints needed (TMC_ERR_INVALID when above capacity). The
+ * reference's rejections (a cycle, a fused region with several results) come
+ * back as TMC_ERR_INVALID with its message. Host only: no device work. */
+int tmc_plan_regions(int input_count, const int32_t *nodes, size_t nodes_len, int node_count,
+                     const int32_t *outputs, int output_count, const int32_t *contiguous, int32_t *order,
+                     int32_t *regions, size_t capacity, size_t *written);
+
 /* compileDecoderLLM (DecoderLLMExecutor.hpp:99-101): allocate weights, KV pools
  * and activations on the runtime's device. Weights start at zero (norms at 1). */
 int tmc_decoder_create(tmc_runtime *rt, const tmc_decoder_config *cfg, tmc_decoder **out);

@@ -63,6 +63,11 @@ if _ref is not None:
     _ref.ref_fusion.argtypes = [c_int, _F, _F, _F, _F, c_long, c_long, c_long, c_long, c_float, c_int, _D]
     _ref.ref_rmsnorm.restype = c_int
     _ref.ref_rmsnorm.argtypes = [_F, _F, c_long, c_long, c_float, c_int, _D]
+    if hasattr(_ref, "ref_form_regions"):
+        _I32P = POINTER(c_int)
+        _ref.ref_form_regions.restype = c_long
+        _ref.ref_form_regions.argtypes = [c_long, c_long, c_long, _I32P, c_long, _I32P, c_long, _I32P, _I32P,
+                                          _I32P, c_long]
 
 
 def available() -> bool:
@@ -233,3 +238,52 @@ def ref_fusion(kind, x, b, w=None, c=None, eps=1e-5, fp16=False, n=0) -> np.ndar
                        eps, 0 if fp16 else 1, _p(out, _D)) != 0:
         raise RuntimeError(_ref.ref_last_error().decode())
     return out
+
+
+def encode_graph(nodes):
+    """Flat node encoding shared with oracle/_ref and the planner tests:
+    per node (op number, operands...) -> {op, operand count, operands...}."""
+    flat = []
+    for op, *operands in nodes:
+        flat += [int(op), len(operands)] + [int(v) for v in operands]
+    return np.asarray(flat, dtype=np.int32)
+
+
+def decode_regions(flat):
+    """{fusion, #nodes, nodes..., #inputs, inputs..., #outputs, outputs...} ->
+    [(fusion, nodes, inputs, outputs)]."""
+    out, i = [], 0
+    while i < len(flat):
+        kind = int(flat[i])
+        i += 1
+        parts = []
+        for _ in range(3):
+            k = int(flat[i])
+            parts.append([int(x) for x in flat[i + 1:i + 1 + k]])
+            i += 1 + k
+        out.append((kind, *parts))
+    return out
+
+
+def ref_form_regions(n, squares, vectors, nodes, outputs):
+    """The reference's own analyze + formRegions (oracle/_ref) on a graph of fp32
+    [n, n] inputs (`squares`), [n] inputs (`vectors`) and `nodes` as
+    (op number, operands...), node i defining value squares + vectors + i.
+    Returns (order, contiguity per value, regions), or raises ValueError with
+    the reference's message when it rejects the graph."""
+    if _ref is None or not hasattr(_ref, "ref_form_regions"):
+        raise RuntimeError("oracle/_ref not built with region formation")
+    flat = encode_graph(nodes)
+    outs = np.asarray(outputs, dtype=np.int32)
+    order = np.zeros(len(nodes), np.int32)
+    values = squares + vectors + len(nodes)
+    contiguous = np.zeros(values, np.int32)
+    cap = 64 * (len(nodes) + 1) + 16
+    regions = np.zeros(cap, np.int32)
+    P = POINTER(c_int)
+    w = _ref.ref_form_regions(n, squares, vectors, flat.ctypes.data_as(P), len(nodes), outs.ctypes.data_as(P),
+                              len(outs), order.ctypes.data_as(P), contiguous.ctypes.data_as(P),
+                              regions.ctypes.data_as(P), cap)
+    if w < 0:
+        raise ValueError(_ref.ref_last_error().decode())
+    return order.tolist(), contiguous.tolist(), decode_regions(regions[:w])

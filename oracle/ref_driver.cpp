@@ -9,10 +9,12 @@
 #include <cstdint>
 #include <cstring>
 #include <exception>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
 #include "analyzer/GraphAnalyzer.hpp"
+#include "analyzer/PatternAnalyzer.hpp"
 #include "validation/GraphReference.hpp"
 
 using namespace tensor;
@@ -134,6 +136,62 @@ int ref_fusion(int kind, const float *x, const float *b, const float *w, const f
   } catch (const std::exception &e) {
     g_error = e.what();
     return 1;
+  }
+}
+
+// The reference's own region formation (analyze + formRegions,
+// src/analyzer/PatternAnalyzer.cpp:32-132) on a graph given as:
+//   n: every tensor is fp32 [n, n] except `vectors` inputs of shape [n];
+//   `squares` [n, n] inputs (value ids 0..squares-1), then the vectors;
+//   nodes: per node {op (OpType number), operand count, operands...}; node i
+//   defines value squares + vectors + i (Transpose swaps axes 0 and 1, Reshape /
+//   View keep [n, n]);
+//   outputs: declared graph outputs.
+// Writes order[node_count], contiguous[value_count] (0/1) and the regions as
+// {fusion, #nodes, nodes..., #inputs, inputs..., #outputs, outputs...} into
+// regions (capacity `cap` ints); returns the number of ints written, or -1
+// with ref_last_error() set when the reference rejects the graph.
+long ref_form_regions(long n, long squares, long vectors, const int *nodes, long node_count, const int *outputs,
+                      long output_count, int *order, int *contiguous, int *regions, long cap) {
+  try {
+    const auto N = std::size_t(n);
+    TensorGraph graph;
+    for (long i = 0; i < squares; ++i) graph.addInput("m" + std::to_string(i), TensorType{{N, N}, DType::Float32});
+    for (long i = 0; i < vectors; ++i) graph.addInput("v" + std::to_string(i), TensorType{{N}, DType::Float32});
+    const int *p = nodes;
+    for (long i = 0; i < node_count; ++i) {
+      const auto op = static_cast<OpType>(*p++);
+      const int arity = *p++;
+      std::vector<ValueId> operands(p, p + arity);
+      p += arity;
+      OpAttributes attributes;
+      if (op == OpType::Transpose) attributes = TransposeAttributes{0, 1};
+      if (op == OpType::Reshape || op == OpType::View) attributes = ReshapeAttributes{{N, N}};
+      graph.addNode(op, operands, attributes);
+    }
+    graph.outputs.assign(outputs, outputs + output_count);
+    const auto planned = analyzer::formRegions(analyzer::analyze(graph));
+    for (std::size_t i = 0; i < planned.analyzed.order.size(); ++i) order[i] = int(planned.analyzed.order[i]);
+    for (std::size_t v = 0; v < planned.analyzed.types.size(); ++v)
+      contiguous[v] = planned.analyzed.types[v].isContiguous() ? 1 : 0;
+    long w = 0;
+    auto put = [&](long value) {
+      if (w >= cap) throw std::runtime_error("region output buffer too small");
+      regions[w++] = int(value);
+    };
+    for (const auto &r : planned.regions) {
+      put(long(r.fusion));
+      put(long(r.nodes.size()));
+      for (auto x : r.nodes) put(long(x));
+      put(long(r.inputs.size()));
+      for (auto x : r.inputs) put(long(x));
+      put(long(r.outputs.size()));
+      for (auto x : r.outputs) put(long(x));
+    }
+    return w;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    return -1;
   }
 }
 
