@@ -233,6 +233,53 @@ inline RegionPlan planRegions(const PlanGraph &g) {
   return plan;
 }
 
+// Buffers and launches of a graph, as the reference's planGraph decides them
+// (src/planner/KernelPlan.cpp:11-59): every value is a graph input, a declared
+// output or an intermediate (an input that is also an output stays an input); a
+// view's result aliases the view's data operand; every node that is not a view
+// launches a kernel, in topological order. (The reference's per-launch
+// threadgroup sizes are Metal dispatch geometry; this library's launchers choose
+// their own grids.)
+enum class BufferRole : int { Input = 0, Intermediate, Output };
+
+struct BufferPlan {
+  std::vector<BufferRole> roles;        // per value
+  std::vector<std::size_t> aliasOf;     // per value; region_detail::kNone when it owns storage
+  std::vector<std::size_t> launches;    // node indices, topological order
+  std::string error;
+};
+
+inline BufferPlan planBuffers(const PlanGraph &g) {
+  using namespace region_detail;
+  BufferPlan plan;
+  for (const auto &node : g.nodes) {
+    if (node.outputs.empty()) plan.error = "Graph node has no results.";
+    for (auto v : node.inputs)
+      if (v >= g.valueCount) plan.error = "Invalid graph ValueId.";
+    for (auto v : node.outputs)
+      if (v >= g.valueCount) plan.error = "Invalid graph ValueId.";
+  }
+  if (!plan.error.empty()) return plan;
+  const Tables t = buildTables(g);
+  const auto order = topologicalOrder(g, t, &plan.error);
+  if (!plan.error.empty()) return plan;
+  plan.roles.assign(g.valueCount, BufferRole::Intermediate);
+  plan.aliasOf.assign(g.valueCount, kNone);
+  for (std::size_t v = 0; v < g.valueCount; ++v) {
+    if (has(g.inputs, v)) plan.roles[v] = BufferRole::Input;
+    else if (has(g.outputs, v)) plan.roles[v] = BufferRole::Output;
+  }
+  for (auto n : order) {
+    const auto &node = g.nodes[n];
+    if (isViewOp(node.op)) {
+      if (!node.inputs.empty()) plan.aliasOf[node.outputs.front()] = node.inputs.front();
+    } else {
+      plan.launches.push_back(n);
+    }
+  }
+  return plan;
+}
+
 inline const char *regionKindName(RegionKind kind) {
   switch (kind) {
     case RegionKind::Single: return "Unfused";

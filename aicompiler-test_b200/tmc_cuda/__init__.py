@@ -364,6 +364,8 @@ def _i32(a):
 _sig("tmc_plan_regions", c_int, c_int, _I32P, c_size_t, c_int, _I32P, c_int, _I32P, _I32P, _I32P, c_size_t,
      POINTER(c_size_t))
 
+_sig("tmc_plan_buffers", c_int, c_int, _I32P, c_size_t, c_int, _I32P, c_int, _I32P, _I32P, _I32P, POINTER(c_int))
+
 REGION_KINDS = ("Unfused", "Add + RMSNorm", "Residual Add + LayerNorm", "SiLU + Mul", "Linear + ReLU")
 
 
@@ -404,6 +406,26 @@ def plan_regions(input_count: int, nodes, outputs, contiguous):
             i += 1 + k
         out.append((kind, *parts))
     return order[:len(nodes)].tolist(), out
+
+
+def plan_buffers(input_count: int, nodes, outputs):
+    """Buffer roles (0 input, 1 intermediate, 2 output), view aliases (-1 for
+    none) and launched nodes of a tensor graph (tmc_plan_buffers; the
+    reference's planGraph); same graph encoding as plan_regions."""
+    flat = []
+    for op, *operands in nodes:
+        flat += [int(op), len(operands)] + [int(v) for v in operands]
+    flat = np.asarray(flat, np.int32)
+    outs = np.asarray(outputs, np.int32)
+    values = input_count + len(nodes)
+    roles = np.zeros(max(values, 1), np.int32)
+    alias = np.zeros(max(values, 1), np.int32)
+    launches = np.zeros(max(len(nodes), 1), np.int32)
+    count = c_int(0)
+    check(lib.tmc_plan_buffers(input_count, flat.ctypes.data_as(_I32P), flat.size, len(nodes),
+                               outs.ctypes.data_as(_I32P), outs.size, roles.ctypes.data_as(_I32P),
+                               alias.ctypes.data_as(_I32P), launches.ctypes.data_as(_I32P), ctypes.byref(count)))
+    return roles[:values].tolist(), alias[:values].tolist(), launches[:count.value].tolist()
 
 
 class ManifestInfo(ctypes.Structure):

@@ -276,6 +276,16 @@ int tmc_manifest_tensor(const tmc_manifest *m, const char *name, const float **v
 int tmc_plan_regions(int input_count, const int32_t *nodes, size_t nodes_len, int node_count,
                      const int32_t *outputs, int output_count, const int32_t *contiguous, int32_t *order,
                      int32_t *regions, size_t capacity, size_t *written);
+/* planGraph's buffer and launch decisions (KernelPlan.cpp:11-59) for the same
+ * graph encoding: roles[v] = 0 graph input, 1 intermediate, 2 declared output
+ * (an input that is also an output stays 0); alias_of[v] = the data operand a
+ * view's result aliases, else -1; launches[] = the non-view nodes in
+ * topological order (*launch_count of them). The reference's per-launch
+ * threadgroup sizes are Metal dispatch geometry and have no counterpart: this
+ * library's launchers choose their own grids. Host only. */
+int tmc_plan_buffers(int input_count, const int32_t *nodes, size_t nodes_len, int node_count,
+                     const int32_t *outputs, int output_count, int32_t *roles, int32_t *alias_of,
+                     int32_t *launches, int *launch_count);
 
 /* compileDecoderLLM (DecoderLLMExecutor.hpp:99-101): allocate weights, KV pools
  * and activations on the runtime's device. Weights start at zero (norms at 1). */

@@ -68,6 +68,11 @@ if _ref is not None:
         _ref.ref_form_regions.restype = c_long
         _ref.ref_form_regions.argtypes = [c_long, c_long, c_long, _I32P, c_long, _I32P, c_long, _I32P, _I32P,
                                           _I32P, c_long]
+    if hasattr(_ref, "ref_plan_buffers"):
+        _I32P = POINTER(c_int)
+        _ref.ref_plan_buffers.restype = c_long
+        _ref.ref_plan_buffers.argtypes = [c_long, c_long, c_long, _I32P, c_long, _I32P, c_long, _I32P, _I32P,
+                                          _I32P]
 
 
 def available() -> bool:
@@ -287,3 +292,23 @@ def ref_form_regions(n, squares, vectors, nodes, outputs):
     if w < 0:
         raise ValueError(_ref.ref_last_error().decode())
     return order.tolist(), contiguous.tolist(), decode_regions(regions[:w])
+
+
+def ref_plan_buffers(n, squares, vectors, nodes, outputs):
+    """The reference's own planGraph (oracle/_ref) on the ref_form_regions graph
+    encoding: (roles per value: 0 input, 1 intermediate, 2 output; alias per
+    value, -1 for none; launched node indices in plan order)."""
+    if _ref is None or not hasattr(_ref, "ref_plan_buffers"):
+        raise RuntimeError("oracle/_ref not built with graph planning")
+    flat = encode_graph(nodes)
+    outs = np.asarray(outputs, dtype=np.int32)
+    values = squares + vectors + len(nodes)
+    roles = np.zeros(values, np.int32)
+    alias = np.zeros(values, np.int32)
+    launches = np.zeros(max(len(nodes), 1), np.int32)
+    P = POINTER(c_int)
+    k = _ref.ref_plan_buffers(n, squares, vectors, flat.ctypes.data_as(P), len(nodes), outs.ctypes.data_as(P),
+                              len(outs), roles.ctypes.data_as(P), alias.ctypes.data_as(P), launches.ctypes.data_as(P))
+    if k < 0:
+        raise ValueError(_ref.ref_last_error().decode())
+    return roles.tolist(), alias.tolist(), launches[:k].tolist()

@@ -15,6 +15,7 @@
 
 #include "analyzer/GraphAnalyzer.hpp"
 #include "analyzer/PatternAnalyzer.hpp"
+#include "planner/KernelPlan.hpp"
 #include "validation/GraphReference.hpp"
 
 using namespace tensor;
@@ -139,6 +140,28 @@ int ref_fusion(int kind, const float *x, const float *b, const float *w, const f
   }
 }
 
+// The graph encoding of ref_form_regions / ref_plan_buffers (see below).
+static TensorGraph build_square_graph(long n, long squares, long vectors, const int *nodes, long node_count,
+                               const int *outputs, long output_count) {
+  const auto N = std::size_t(n);
+  TensorGraph graph;
+  for (long i = 0; i < squares; ++i) graph.addInput("m" + std::to_string(i), TensorType{{N, N}, DType::Float32});
+  for (long i = 0; i < vectors; ++i) graph.addInput("v" + std::to_string(i), TensorType{{N}, DType::Float32});
+  const int *p = nodes;
+  for (long i = 0; i < node_count; ++i) {
+    const auto op = static_cast<OpType>(*p++);
+    const int arity = *p++;
+    std::vector<ValueId> operands(p, p + arity);
+    p += arity;
+    OpAttributes attributes;
+    if (op == OpType::Transpose) attributes = TransposeAttributes{0, 1};
+    if (op == OpType::Reshape || op == OpType::View) attributes = ReshapeAttributes{{N, N}};
+    graph.addNode(op, operands, attributes);
+  }
+  graph.outputs.assign(outputs, outputs + output_count);
+  return graph;
+}
+
 // The reference's own region formation (analyze + formRegions,
 // src/analyzer/PatternAnalyzer.cpp:32-132) on a graph given as:
 //   n: every tensor is fp32 [n, n] except `vectors` inputs of shape [n];
@@ -154,22 +177,7 @@ int ref_fusion(int kind, const float *x, const float *b, const float *w, const f
 long ref_form_regions(long n, long squares, long vectors, const int *nodes, long node_count, const int *outputs,
                       long output_count, int *order, int *contiguous, int *regions, long cap) {
   try {
-    const auto N = std::size_t(n);
-    TensorGraph graph;
-    for (long i = 0; i < squares; ++i) graph.addInput("m" + std::to_string(i), TensorType{{N, N}, DType::Float32});
-    for (long i = 0; i < vectors; ++i) graph.addInput("v" + std::to_string(i), TensorType{{N}, DType::Float32});
-    const int *p = nodes;
-    for (long i = 0; i < node_count; ++i) {
-      const auto op = static_cast<OpType>(*p++);
-      const int arity = *p++;
-      std::vector<ValueId> operands(p, p + arity);
-      p += arity;
-      OpAttributes attributes;
-      if (op == OpType::Transpose) attributes = TransposeAttributes{0, 1};
-      if (op == OpType::Reshape || op == OpType::View) attributes = ReshapeAttributes{{N, N}};
-      graph.addNode(op, operands, attributes);
-    }
-    graph.outputs.assign(outputs, outputs + output_count);
+    const auto graph = build_square_graph(n, squares, vectors, nodes, node_count, outputs, output_count);
     const auto planned = analyzer::formRegions(analyzer::analyze(graph));
     for (std::size_t i = 0; i < planned.analyzed.order.size(); ++i) order[i] = int(planned.analyzed.order[i]);
     for (std::size_t v = 0; v < planned.analyzed.types.size(); ++v)
@@ -189,6 +197,28 @@ long ref_form_regions(long n, long squares, long vectors, const int *nodes, long
       for (auto x : r.outputs) put(long(x));
     }
     return w;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    return -1;
+  }
+}
+
+// The reference's planGraph (src/planner/KernelPlan.cpp:11-59) on the same
+// encoding: roles[value] (0 input, 1 intermediate, 2 output), alias_of[value]
+// (-1 when the value owns storage) and the launched nodes in plan order;
+// returns their count, or -1 with ref_last_error() set.
+long ref_plan_buffers(long n, long squares, long vectors, const int *nodes, long node_count, const int *outputs,
+                      long output_count, int *roles, int *alias_of, int *launches) {
+  try {
+    const auto graph = build_square_graph(n, squares, vectors, nodes, node_count, outputs, output_count);
+    const auto plan = planner::planGraph(analyzer::analyze(graph));
+    for (const auto &b : plan.buffers) {
+      roles[b.value] = b.role == planner::BufferRole::Input ? 0 : b.role == planner::BufferRole::Intermediate ? 1 : 2;
+      alias_of[b.value] = b.aliasOf ? int(*b.aliasOf) : -1;
+    }
+    long k = 0;
+    for (const auto &kernel : plan.kernels) launches[k++] = int(kernel.nodeIndex);
+    return k;
   } catch (const std::exception &e) {
     g_error = e.what();
     return -1;

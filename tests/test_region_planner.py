@@ -104,6 +104,21 @@ def random_graph(rng, size):
     return squares, vectors, nodes, outputs
 
 
+def test_random_graphs_get_the_reference_buffer_plan():
+    # planGraph (KernelPlan.cpp:11-59): buffer roles, view aliases, launched nodes.
+    import tmc_cuda
+    rng = np.random.default_rng(77)
+    aliased = 0
+    for _ in range(300):
+        squares, vectors, nodes, outputs = random_graph(rng, int(rng.integers(2, 24)))
+        if rng.random() < 0.2:
+            outputs = outputs + [0]                  # an input that is also an output stays an input
+        ref = oracle.ref_plan_buffers(4, squares, vectors, nodes, outputs)
+        assert tmc_cuda.plan_buffers(squares + vectors, nodes, outputs) == ref
+        aliased += sum(1 for a in ref[1] if a >= 0)
+    assert aliased > 0
+
+
 def test_random_graphs_split_into_the_reference_regions(planner):
     rng = np.random.default_rng(2024)
     kinds, checked = set(), 0
