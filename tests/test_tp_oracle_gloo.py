@@ -1,5 +1,5 @@
-"""The tensor-parallel decomposition on CPU: two `gloo` ranks each run one
-shard of the golden decoder (oracle.decoder_ref.TensorParallelOracle -- the
+"""The tensor-parallel decomposition on CPU: two or four `gloo` ranks each run
+one shard of the golden decoder (oracle.decoder_ref.TensorParallelOracle -- the
 same column/row/vocab split, fp32 partial-sum allreduce points and packed-key
 argmax max-reduction as the device decoder), and the result must equal the
 reference exporter's recorded outputs (export_decoder_llm.py:446-551):
@@ -69,9 +69,9 @@ def rms_close(got, ref, what):
     assert err <= 2e-3 * rms, f"{what}: max err {err} > {2e-3 * rms}"
 
 
-@pytest.mark.parametrize("npz", ["decoder_default_fp16.npz", "decoder_wide_fp16.npz"])
-def test_two_gloo_ranks_match_reference_exporter(tmp_path, npz):
-    world = 2
+@pytest.mark.parametrize("npz,world", [("decoder_default_fp16.npz", 2), ("decoder_wide_fp16.npz", 2),
+                                       ("decoder_default_fp16.npz", 4)])
+def test_gloo_ranks_match_reference_exporter(tmp_path, npz, world):
     mp.spawn(_rank, args=(world, _free_port(), npz, str(tmp_path)), nprocs=world, join=True)
     g = np.load(os.path.join(GOLDEN, npz))
     meta = json.loads(str(g["meta"]))
