@@ -1,6 +1,7 @@
 // Paired A/B timing for the tuners: alternating baseline / candidate launches,
-// each bracketed by CUDA events on the launching stream, compared by medians
-// (benchmark::measurePair, Benchmark.cpp:68-96).
+// each bracketed by CUDA events on the launching stream, summarised per arm
+// (timing_stats.hpp) and compared by medians (benchmark::measurePair,
+// Benchmark.cpp:68-96).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -10,18 +11,17 @@
 #include <string>
 #include <vector>
 
+#include "timing_stats.hpp"
+
 namespace tensor::planner {
 
 struct PairedTiming {
   bool passed = false;
-  double baselineUs = 0.0, candidateUs = 0.0, speedup = 0.0;
+  TimingStatistics baseline, candidate;           // per arm
+  double baselineUs = 0.0, candidateUs = 0.0;     // the medians
+  double speedup = 0.0;                           // baseline / candidate median
   std::string errorMessage;
 };
-
-inline double medianOf(std::vector<double> v) {
-  std::sort(v.begin(), v.end());
-  return v[v.size() / 2];
-}
 
 // Each launcher enqueues one dispatch on `stream` and returns "" on success.
 inline PairedTiming measurePair(const std::function<std::string()> &baseline,
@@ -50,8 +50,15 @@ inline PairedTiming measurePair(const std::function<std::string()> &baseline,
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   if (!r.errorMessage.empty()) return r;
-  r.baselineUs = medianOf(tb);
-  r.candidateUs = medianOf(tc);
+  const auto sb = summarizeTimings(tb), sc = summarizeTimings(tc);
+  if (!sb || !sc) {
+    r.errorMessage = "Benchmark requires at least one sample.";
+    return r;
+  }
+  r.baseline = *sb;
+  r.candidate = *sc;
+  r.baselineUs = sb->medianUs;
+  r.candidateUs = sc->medianUs;
   r.speedup = r.baselineUs / r.candidateUs;
   r.passed = true;
   return r;
