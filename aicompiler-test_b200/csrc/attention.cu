@@ -12,6 +12,7 @@
 // (m, l, acc) partials; the last CTA of a (row, KV head) combines them
 // (atomic ticket), so no second launch is needed.
 #include "attention.cuh"
+#include "gemm.cuh"
 
 #include <cmath>
 #include <mutex>
@@ -71,7 +72,7 @@ struct Cfg {
   static constexpr size_t kStageBytes = (size_t)T * kRow * 2;  // one of K or V per stage
   static constexpr size_t kAlign = BOX ? 1024 : 0;       // swizzled stages start on 1024 bytes
   static constexpr int kStages = 2;
-  static constexpr int kMaxSplits = 64;
+  static constexpr int kMaxSplits = kAttentionMaxSplits;
   static constexpr int kKSteps = D / 16;                 // QK^T k-steps
   static constexpr int kDTiles = D / 8;                  // PV n-tiles
   __host__ __device__ static constexpr size_t merge_bytes() { return (size_t)kWarpsPerCta * (G * D + 2 * G) * 4; }
@@ -809,7 +810,9 @@ static __device__ __align__(256) unsigned char g_attention_scratch[kNoAllocScrat
 
 // Device address of the scratch array on the current device, resolved once per
 // device (host code cannot use the symbol itself: on the host it names a
-// stand-in, not device memory).
+// stand-in, not device memory). The address stays cached for the life of the
+// process, so the entry point must not be used after cudaDeviceReset (or any
+// other teardown of the device's primary context) in the same process.
 cudaError_t attention_scratch_address(void **out) {
   static std::mutex mu;
   static std::unordered_map<int, void *> addresses;
@@ -841,8 +844,12 @@ extern "C" int tmc_k_paged_attention_f16_noalloc(
     return fail(TMC_ERR_INVALID, "null pointer");
   if (rows <= 0 || hq <= 0 || hkv <= 0 || d <= 0 || max_splits <= 0)
     return fail(TMC_ERR_INVALID, "rows, heads, head_dim and max_splits must be positive");
+  // The kernel never uses more than 64 splits, so the scratch is sized (and
+  // the m/l partials placed) for the capped count: a request with a larger
+  // max_splits runs exactly as the allocating entry point runs it.
+  const int splits = max_splits < tmc::kAttentionMaxSplits ? max_splits : tmc::kAttentionMaxSplits;
   // Scratch layout: split partials (acc, then m/l), then the tickets.
-  const size_t partials = tmc::attention_workspace_bytes(rows, hq, hkv, d, max_splits);
+  const size_t partials = tmc::attention_workspace_bytes(rows, hq, hkv, d, splits);
   const size_t tickets_offset = (partials + 255) / 256 * 256;
   const size_t needed = tickets_offset + (size_t)rows * hkv * sizeof(uint32_t);
   if (needed > tmc::kNoAllocScratchBytes) {
@@ -879,13 +886,26 @@ extern "C" int tmc_k_paged_attention_f16_noalloc(
   p.pool_pages = pool_pages;
   p.capacity = capacity;
   p.scale = static_cast<float>(1.0 / std::sqrt(static_cast<double>(d)));
-  p.max_splits = max_splits;
+  p.max_splits = splits;
   p.min_chunk = min_chunk;
   p.early_mode = 2;  // standalone call: no kernel produces K/V concurrently
   p.ws_acc = reinterpret_cast<float *>(base);
-  p.ws_ml = reinterpret_cast<float *>(base + (size_t)rows * hq * max_splits * d * sizeof(float));
+  p.ws_ml = reinterpret_cast<float *>(base + (size_t)rows * hq * splits * d * sizeof(float));
   p.counters = tickets;
   p.status = static_cast<tmc::TmcDeviceStatus *>(status);
+  // Same kernel variant as the allocating entry point: K/V as 16-position page
+  // boxes through tensor maps when the shape allows. Encoding a tensor map
+  // fills a host-side descriptor and allocates nothing.
+  CUtensorMap km, vm;
+  if ((d == 64 || d == 128) && page_size % 16 == 0 && (reinterpret_cast<uintptr_t>(k_pool) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(v_pool) & 15) == 0) {
+    const uint64_t pool_rows = (uint64_t)pool_pages * hkv * page_size;
+    if (tmc::make_tensor_map_f16(&km, k_pool, pool_rows, d, 16) == cudaSuccess &&
+        tmc::make_tensor_map_f16(&vm, v_pool, pool_rows, d, 16) == cudaSuccess) {
+      p.k_map = &km;
+      p.v_map = &vm;
+    }
+  }
   e = tmc::launch_attention(p, s, false);
   if (e == cudaErrorInvalidValue) return fail(TMC_ERR_UNSUPPORTED, "attention: unsupported shape");
   return e == cudaSuccess ? ok() : cuda_fail(e, "attention (no-alloc) launch");

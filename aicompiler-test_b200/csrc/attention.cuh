@@ -56,6 +56,10 @@ struct AttentionParams {
   const CUtensorMap *v_map;
 };
 
+// Most splits one (row, KV head) is ever cut into; larger max_splits values
+// are capped to this.
+constexpr int kAttentionMaxSplits = 64;
+
 // Workspace bytes needed for a launch with these dimensions.
 size_t attention_workspace_bytes(int rows, int hq, int hkv, int head_dim, int max_splits);
 

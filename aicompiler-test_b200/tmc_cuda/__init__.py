@@ -214,6 +214,12 @@ class Buffer:
         check(lib.tmc_buffer_read_bytes(self.handle, out.ctypes.data_as(c_void_p), out.nbytes, 0))
         return out
 
+    def read_raw_range(self, byte_offset: int, count: int) -> np.ndarray:
+        """`count` elements of the raw storage starting at `byte_offset`."""
+        out = np.empty(count, dtype=_NP_BY_DTYPE[self.dtype])
+        check(lib.tmc_buffer_read_bytes(self.handle, out.ctypes.data_as(c_void_p), out.nbytes, byte_offset))
+        return out
+
     def write(self, values, offset: int = 0):
         values = np.ascontiguousarray(values, dtype=np.float32).reshape(-1)
         check(lib.tmc_buffer_write(self.handle, _fptr(values), values.size, offset))

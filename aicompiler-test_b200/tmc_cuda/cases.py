@@ -8,8 +8,11 @@ Each case builds seeded inputs on the device (larger than L2 where the shape
 allows), launches the kernel `--warmup` times, then `--reps` times between
 CUDA events on the runtime's stream, and prints one JSON line with the mean
 launch time and the algorithmic bytes. Run from `aicompiler-test_b200/` (or
-with it on PYTHONPATH); `ncu -k regex:<kernel> -s <warmup> -c <n>` captures
-the first timed launches.
+with it on PYTHONPATH); `ncu --clock-control none --metrics gpu__time_duration.sum
+-k regex:<kernel> -s <warmup> -c <n>` captures the first timed launches
+(without --clock-control none ncu locks the GPU clocks, which the next user of
+a shared GPU inherits); keep a full-set capture on one kernel and a few
+launches of a small case.
 """
 
 from __future__ import annotations

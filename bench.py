@@ -340,17 +340,16 @@ def run_ours(args, world, rank, local):
     return 0
 
 
-def measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind):
-    """C4: block-table GQA decode attention, 64 sequences with contexts ~U[128, 8192],
-    32 q / 8 kv heads x 128 (sharded by KV head across the ranks), fp16 K/V ~N(0,1)
-    in 16-token pages, each block table a random draw of distinct pages from a
-    2^17-page pool (2 x 4.29 GB at TP1), one fp16 query per sequence.
-    value = algorithmic bytes (4096 x sum(ctx) + q + out) / device time, max over
-    ranks; K/V (> L2) are re-read from HBM by every launch."""
+def c4_case(world=1, rank=0):
+    """The C4 inputs every rank measures (and tests/test_attention_gpu.py
+    checks against the oracle): 64 sequences with contexts ~U[128, 8192] drawn
+    from a seeded generator, this rank's 32/world query and 8/world KV heads of
+    dimension 128, 16-token pages, each block table a run of a random draw of
+    distinct pages from a 2^17-page pool, fp16 queries ~N(0, 1); the K/V pools
+    are filled on the device with the counter-based N(0, 1) generator and the
+    seeds given. The launch policy (8 splits of at least 1024 positions) is the
+    one timed: long splits amortise each CTA's setup and merge."""
     import numpy as np
-    import torch
-
-    import tmc_cuda
     rows, hq, hkv, d, page = 64, 32 // world, 8 // world, 128, 16
     pool_pages = 1 << 17
     rng = np.random.default_rng(4)
@@ -363,16 +362,36 @@ def measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind
     for r in range(rows):
         table[r, : pages_per[r]] = perm[off: off + pages_per[r]]
         off += pages_per[r]
+    q = rng.standard_normal((rows, hq, d)).astype(np.float16)
+    return {"rows": rows, "hq": hq, "hkv": hkv, "d": d, "page": page, "pool_pages": pool_pages, "ctx": ctx,
+            "table": table, "stride": stride, "q": q, "k_seed": 10 + rank, "v_seed": 20 + rank,
+            "max_splits": 8, "min_chunk": 1024}
+
+
+def measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind):
+    """C4: block-table GQA decode attention, 64 sequences with contexts ~U[128, 8192],
+    32 q / 8 kv heads x 128 (sharded by KV head across the ranks), fp16 K/V ~N(0,1)
+    in 16-token pages, each block table a random draw of distinct pages from a
+    2^17-page pool (2 x 4.29 GB at TP1), one fp16 query per sequence.
+    value = algorithmic bytes (4096 x sum(ctx) + q + out) / device time, max over
+    ranks; K/V (> L2) are re-read from HBM by every launch."""
+    import numpy as np
+    import torch
+
+    import tmc_cuda
+    c = c4_case(world, rank)
+    rows, hq, hkv, d, page, pool_pages = c["rows"], c["hq"], c["hkv"], c["d"], c["page"], c["pool_pages"]
+    ctx, table, stride = c["ctx"], c["table"], c["stride"]
     rt = tmc_cuda.Runtime(local)
     kp = rt.buffer(pool_pages * hkv * page * d, tmc_cuda.F16)
     vp = rt.buffer(pool_pages * hkv * page * d, tmc_cuda.F16)
-    tmc_cuda.fill_normal_f16(rt, kp, 10 + rank, 0.0, 1.0)
-    tmc_cuda.fill_normal_f16(rt, vp, 20 + rank, 0.0, 1.0)
+    tmc_cuda.fill_normal_f16(rt, kp, c["k_seed"], 0.0, 1.0)
+    tmc_cuda.fill_normal_f16(rt, vp, c["v_seed"], 0.0, 1.0)
     tb, trows = rt.upload(table), rt.upload(np.arange(rows, dtype=np.int32))
     pos = rt.upload((ctx - 1).astype(np.int32))
-    q = rt.upload(rng.standard_normal((rows, hq, d)).astype(np.float16))
+    q = rt.upload(c["q"])
     out = rt.buffer(rows * hq * d, tmc_cuda.F16)
-    max_splits, min_chunk = 8, 1024  # long splits amortise each CTA's setup and merge
+    max_splits, min_chunk = c["max_splits"], c["min_chunk"]
     ws = rt.buffer(tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, max_splits) // 4 + 1, tmc_cuda.F32)
     counters = rt.upload(np.zeros(rows * hkv, dtype=np.int32))
 

@@ -187,15 +187,17 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
  * workspace and counters: the split partials and tickets live in one fixed
  * 8 MiB device array that the library reserves on every GPU that loads it,
  * until process exit. It calls no allocator.
- * Limit: rows*hq*max_splits*(d+2)*4 bytes, rounded up to 256, plus rows*hkv*4
+ * Limit: with s = min(max_splits, 64) (the kernel never cuts a row into more
+ * than 64 splits), rows*hq*s*(d+2)*4 bytes, rounded up to 256, plus rows*hkv*4
  * bytes must fit in 8 MiB (8388608); larger requests fail with
  * TMC_ERR_UNSUPPORTED before anything is launched (max_splits = 1 needs only
  * the tickets). The first call on a device looks up the array's device address
  * (cudaGetSymbolAddress) with that device current; make that first call before
- * any stream capture. All calls share the array and it keeps the previous
- * call's contents; the tickets are cleared on `stream` before each launch, so
- * calls that overlap on the GPU (e.g. on different streams) race and must be
- * serialised by the caller. */
+ * any stream capture. The address is kept for the life of the process: do not
+ * call this entry point after cudaDeviceReset in the same process. All calls
+ * share the array and it keeps the previous call's contents; the tickets are
+ * cleared on `stream` before each launch, so calls that overlap on the GPU
+ * (e.g. on different streams) race and must be serialised by the caller. */
 int tmc_k_paged_attention_f16_noalloc(const void *q, void *out, const void *k_pool,
                                       const void *v_pool, const int32_t *block_table,
                                       int table_stride, const int32_t *table_rows,

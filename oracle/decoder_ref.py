@@ -25,6 +25,7 @@ Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline import it.
 
 from __future__ import annotations
 
+import copy
 import math
 from dataclasses import dataclass, field
 
@@ -104,6 +105,15 @@ class DecoderOracle:
         k = weight.shape[1]
         perm = torch.from_numpy(np.random.default_rng(self.summation_order_seed + k).permutation(k))
         return F.linear(x[..., perm], weight[:, perm])
+
+    def fork(self, summation_order_seed=None, caches=None):
+        """A new oracle over the same weight tensors (shared, not copied) with
+        its own caches (a shallow copy of `caches`, else empty) and summation
+        order -- full-width models hold gigabytes of weights."""
+        other = copy.copy(self)
+        other.caches = dict(caches) if caches is not None else {}
+        other.summation_order_seed = summation_order_seed
+        return other
 
     def length(self, seq) -> int:
         c = self.caches.get(seq)

@@ -30,7 +30,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("TMC_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ.get("TMC_REFERENCE", Path(__file__).resolve().parents[2].parent / "reference"))
 
 
 def load_exporter():

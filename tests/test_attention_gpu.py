@@ -144,3 +144,56 @@ def test_missing_page_reports_device_status(rt):
     assert err.value.code == tmc_cuda.ERR_DEVICE_STATUS
     assert "no physical page" in err.value.message
     rt.synchronize()  # the status block was consumed; the context is still usable
+
+
+def test_paged_attention_c4_full_size(rt):
+    # The benchmarked C4 case itself (bench.c4_case: 64 sequences, contexts
+    # U[128, 8192], 32q/8kv x 128, pages drawn at random from a 2^17-page pool
+    # of 2 x 4.29 GB filled on the device, 8 splits of >= 1024 positions)
+    # against the fp64 oracle. The oracle reads only the pages the block
+    # tables name (copied back and renumbered densely).
+    from concurrent.futures import ThreadPoolExecutor
+
+    import bench
+    import tmc_cuda
+    from tests.parity_util import fp16_close
+    c = bench.c4_case()
+    rows, hq, hkv, d, page, pool_pages = c["rows"], c["hq"], c["hkv"], c["d"], c["page"], c["pool_pages"]
+    table, ctx = c["table"], c["ctx"]
+    kp = rt.buffer(pool_pages * hkv * page * d, tmc_cuda.F16)
+    vp = rt.buffer(pool_pages * hkv * page * d, tmc_cuda.F16)
+    tmc_cuda.fill_normal_f16(rt, kp, c["k_seed"], 0.0, 1.0)
+    tmc_cuda.fill_normal_f16(rt, vp, c["v_seed"], 0.0, 1.0)
+    qb, out = rt.upload(c["q"]), rt.buffer(c["q"].size, tmc_cuda.F16)
+    tb, trb = rt.upload(table), rt.upload(np.arange(rows, dtype=np.int32))
+    pb = rt.upload((ctx - 1).astype(np.int32))
+    ws = rt.buffer(tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, c["max_splits"]) // 4 + 1, tmc_cuda.F32)
+    counters = rt.upload(np.zeros(rows * hkv, dtype=np.int32))
+    tmc_cuda.paged_attention_f16(rt, qb, out, kp, vp, tb, c["stride"], trb, pb, rows, hq, hkv, d, page,
+                                 pool_pages, c["stride"] * page, c["max_splits"], c["min_chunk"], ws, counters)
+    rt.synchronize()
+    got = out.read().reshape(rows, hq, d).astype(np.float64)
+    used = np.unique(table[table >= 0])
+    dense = np.full(pool_pages, -1, np.int32)
+    dense[used] = np.arange(used.size, dtype=np.int32)
+    dtable = np.where(table >= 0, dense[np.maximum(table, 0)], -1).astype(np.int32)
+    per_page = hkv * page * d
+    kd = np.empty((used.size, per_page), np.float32)
+    vd = np.empty((used.size, per_page), np.float32)
+    for i, pg in enumerate(used):
+        kd[i] = kp.read_raw_range(int(pg) * per_page * 2, per_page).astype(np.float32)
+        vd[i] = vp.read_raw_range(int(pg) * per_page * 2, per_page).astype(np.float32)
+    kd = kd.reshape(used.size, hkv, page, d)
+    vd = vd.reshape(used.size, hkv, page, d)
+    q32 = c["q"].astype(np.float32)
+    pos = (ctx - 1).astype(np.int32)
+
+    def one(r):
+        return oracle.paged_attention(q32[r:r + 1], kd, vd, dtable, np.array([r], np.int32), pos[r:r + 1], hkv, page)
+
+    import os
+    with ThreadPoolExecutor(max_workers=max(1, min(16, os.cpu_count() or 1))) as ex:
+        ref = np.concatenate(list(ex.map(one, range(rows))))
+    print(f"[parity] C4 full size: {rows} sequences, sum ctx {int(ctx.sum())}, {used.size} pages read back")
+    check(got, ref)
+    fp16_close(got, oracle.round_f16(ref.astype(np.float32)).reshape(ref.shape), "C4 full-size attention output")

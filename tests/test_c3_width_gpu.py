@@ -1,0 +1,138 @@
+"""C3 at full width against the CPU oracle.
+
+The benchmarked Llama-3-8B shape (hidden 4096, 32 query / 8 KV heads x 128,
+SwiGLU 14336, vocab 128256, RoPE base 5e5, fp16 weights ~N(0, 0.02) from the
+decoder's seeded generator) with 2 of its 32 layers, so the CPU oracle
+(oracle/decoder_ref.py, the reference's decoder_llm.py restated with GQA and
+rope theta) runs in seconds. Checked against the oracle with the tolerances of
+tests/parity_util.py (2e-3 x RMS, one-ulp storage-rounding cases counted,
+greedy tokens bit-exact except counted fp16 ties):
+- bs1 GEMV path: a 1024-token prompt (all 1024 rows of prefill logits), then
+  16 decode steps teacher-forced with the oracle's tokens, and the two layers'
+  KV caches after the last step;
+- tensor-core path: the same prompt prefilled in 64-row chunks through the
+  tcgen05 GEMMs (all 1024 rows of logits), and a 64-sequence batched decode
+  (64 rows, one per sequence, prompts of 8..71 tokens) for 2 steps.
+The oracle's twin with a permuted fp32 summation order gives the noise floor
+printed beside the bs1 numbers.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.decoder_ref import DecoderOracle, DecoderSpec, weight_names
+from tests.parity_util import TokenCheck, fp16_close
+
+pytestmark = pytest.mark.gpu
+
+H, HEADS, KV, INTER, VOCAB, LAYERS = 4096, 32, 8, 14336, 128256, 2
+PROMPT, STEPS = 1024, 16
+CAP = PROMPT + STEPS + 16
+SPEC = DecoderSpec(hidden=H, heads=HEADS, kv_heads=KV, intermediate=INTER, vocab=VOCAB, layers=LAYERS,
+                   capacity=CAP, rope_theta=5e5)
+SIZES = {"embedding.weight": (VOCAB, H), "final_norm.weight": (H,), "lm_head.weight": (VOCAB, H),
+         "input_norm": (H,), "post_norm": (H,), "q": (HEADS * 128, H), "k": (KV * 128, H), "v": (KV * 128, H),
+         "o": (H, HEADS * 128), "gate": (INTER, H), "up": (INTER, H), "down": (H, INTER)}
+
+
+def decoder(rt, **kw):
+    import tmc_cuda
+    d = tmc_cuda.Decoder(rt, H, HEADS, INTER, VOCAB, LAYERS, CAP, kv_heads=KV, rope_theta=5e5, page_size=16,
+                         **kw)
+    d.init_random(seed=5, std=0.02)
+    return d
+
+
+def read_weights(dec):
+    w = {}
+    for name in weight_names(LAYERS):
+        shape = SIZES.get(name) or SIZES[name.split(".")[1]]
+        w[name] = dec.read_weight(name, int(np.prod(shape))).reshape(shape).astype(np.float16)
+    return w
+
+
+def tables(dec):
+    half = 64
+    cos = dec.read_weight("rope.cosine", CAP * half).reshape(CAP, half)
+    sin = dec.read_weight("rope.sine", CAP * half).reshape(CAP, half)
+    return torch.from_numpy(cos), torch.from_numpy(sin)
+
+
+@pytest.fixture(scope="module")
+def model(rt):
+    dec = decoder(rt, max_rows=8)
+    weights = read_weights(dec)
+    cos, sin = tables(dec)
+    dec.close()
+    prompt = np.random.default_rng(31).integers(0, VOCAB, PROMPT).astype(np.int32)
+    oracle = DecoderOracle(SPEC, weights, cos, sin)
+    del weights  # the oracle holds its own fp16 tensors
+    ref_logits, ref_tok = oracle.forward(0, prompt)
+    return {"prompt": prompt, "oracle": oracle,
+            "prefill_logits": ref_logits.float().numpy(), "prefill_token": ref_tok}
+
+
+def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
+    twin = model["oracle"].fork(summation_order_seed=7)
+    twin_logits, _ = twin.forward(0, model["prompt"])
+    ref = model["prefill_logits"]
+    floor = float(np.max(np.abs(twin_logits.float().numpy() - ref)))
+    dec = decoder(rt, max_rows=8)
+    logits, tok = dec.prefill(model["prompt"])
+    fp16_close(logits, ref, "C3 width bs1 prefill logits (1024 rows)", floor)
+    tokens = TokenCheck("C3 width bs1")
+    tokens.check(tok, model["prefill_token"], ref[-1], logits[-1])
+    oracle = model["oracle"].fork(caches=model["oracle"].caches)
+    t = model["prefill_token"]
+    for step in range(STEPS):
+        lo, to = oracle.forward(0, [t])
+        lt, _ = twin.forward(0, [t])
+        lg, nxt = dec.decode([t])
+        ref_step = lo[0].float().numpy()
+        floor = float(np.max(np.abs(lt[0].float().numpy() - ref_step)))
+        fp16_close(lg[0], ref_step, f"C3 width bs1 decode {step} logits", floor)
+        tokens.check(int(nxt[0]), to, ref_step, lg[0])
+        t = to  # teacher-forced: both continue from the oracle's token
+    tokens.report()
+    for layer in range(LAYERS):
+        k, v = dec.read_kv(layer)
+        rk, rv = oracle.caches[0][layer]
+        fp16_close(k, rk.float().numpy(), f"C3 width layer {layer} key cache ({PROMPT + STEPS} positions)")
+        fp16_close(v, rv.float().numpy(), f"C3 width layer {layer} value cache")
+    dec.close()
+
+
+def test_c3_width_tensor_core_path_matches_oracle(rt, model):
+    dec = decoder(rt, max_rows=64, max_slots=64)
+    logits, tok = dec.prefill(model["prompt"])  # 16 chunks of 64 rows: tcgen05 GEMMs
+    fp16_close(logits, model["prefill_logits"], "C3 width prefill logits, 64-row tensor-core chunks")
+    tokens = TokenCheck("C3 width 64-row steps")
+    tokens.check(tok, model["prefill_token"], model["prefill_logits"][-1], logits[-1])
+    dec.release(0)
+
+    rng = np.random.default_rng(32)
+    rows = 64
+    oracle = model["oracle"].fork()
+    toks = []
+    for s in range(rows):
+        prompt = rng.integers(0, VOCAB, 8 + s).astype(np.int32)
+        lo, to = oracle.forward(s, prompt)
+        _, tg = dec.prefill(prompt, slot=s, logits=False)  # > 8 rows: tensor-core chunk
+        tokens.check(tg, to, lo[-1].float().numpy())
+        toks.append(to)
+    slots = list(range(rows))
+    for step in range(2):
+        ref = np.empty((rows, VOCAB), np.float32)
+        ref_tok = []
+        for s in range(rows):
+            lo, to = oracle.forward(s, [toks[s]])
+            ref[s] = lo[0].float().numpy()
+            ref_tok.append(to)
+        lg, nxt = dec.decode(toks, slots=slots)  # one 64-row step: tensor-core projections
+        fp16_close(lg, ref, f"C3 width 64-sequence decode step {step} logits")
+        for s in range(rows):
+            tokens.check(int(nxt[s]), ref_tok[s], ref[s], lg[s])
+        toks = ref_tok
+    tokens.report()
+    dec.close()

@@ -99,3 +99,44 @@ def test_serving_reuses_slots_for_more_requests_than_slots(rt):
     served = tmc_cuda.serve(dec, prompts, decode, arrivals, logits=True)
     assert served["metrics"]["max_active_batch"] <= 3
     check(served, sequential(rt, g, meta, prompts, decode), exact=True)
+
+
+@pytest.mark.parametrize("max_rows,pool_pages", [(16, 0), (8, 20)])
+def test_served_requests_match_oracle(rt, max_rows, pool_pages):
+    # Every served request against the CPU oracle (oracle/decoder_ref.py, pinned
+    # to the reference exporter): the oracle runs the request's prompt and then
+    # the tokens the server generated, one step each; the served prefill and
+    # decode logits must meet the north-star tolerance (tests/parity_util.py)
+    # and each served token must be the oracle's argmax (fp16 ties counted).
+    # (16, 0): tensor-core batched steps; (8, 20): preemption and resume.
+    import torch
+
+    from oracle.decoder_ref import DecoderOracle, spec_from_golden, weight_names
+    from tests.parity_util import TokenCheck, fp16_close
+    g, meta = load("decoder_wide_fp16.npz")
+    if pool_pages:
+        rng = np.random.default_rng(5)
+        prompts = [rng.integers(0, meta["vocabulary_size"], 14) for _ in range(6)]
+        decode, arrivals = [12] * 6, None
+    else:
+        prompts, decode, arrivals = workload(meta, 14, seed=21)
+    dec = make_decoder(rt, meta, page_size=4, max_rows=max_rows, max_slots=len(prompts), pool_pages=pool_pages)
+    load_golden_weights(dec, g, meta)
+    served = tmc_cuda.serve(dec, prompts, decode, arrivals, logits=True)
+    if pool_pages:
+        assert served["metrics"]["preemptions"] >= 1
+    oracle = DecoderOracle(spec_from_golden(meta), {n: g[n] for n in weight_names(meta["layers"])},
+                           torch.from_numpy(g["rope.cosine"]), torch.from_numpy(g["rope.sine"]))
+    tokens = TokenCheck(f"served requests (max_rows {max_rows})")
+    for i, p in enumerate(prompts):
+        toks = served["tokens"][i]
+        lo, to = oracle.forward(i, p)
+        fp16_close(served["prefill_logits"][i], lo.float().numpy(), f"request {i} prefill logits")
+        tokens.check(toks[0], to, lo[-1].float().numpy(), served["prefill_logits"][i][-1])
+        for s in range(decode[i]):
+            lo, to = oracle.forward(i, [int(toks[s])])
+            ref = lo[0].float().numpy()
+            fp16_close(served["decode_logits"][i][s], ref, f"request {i} decode {s} logits")
+            tokens.check(toks[s + 1], to, ref, served["decode_logits"][i][s])
+    tokens.report()
+    dec.close()

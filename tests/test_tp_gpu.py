@@ -142,3 +142,104 @@ def test_tensor_parallel_batched_matches_single_gpu(mode):
         np.testing.assert_allclose(got, ref["logits"][step], atol=2e-2, rtol=2e-2)
     agree = np.mean(np.asarray(ranks[0]["tokens"]) == np.asarray(ref["tokens"]))
     assert agree >= 0.9, agree
+
+
+def run_gqa(world, mode, prompt, feed, timeout=300):
+    import tmc_cuda
+    uid = tmc_cuda.nccl_unique_id() if (mode == "nccl" and world > 1) else b""
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=tp_worker.gqa_worker, args=(r, world, uid, queue, mode, port, prompt, feed))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(world):
+            r = queue.get(timeout=timeout)
+            results[r["rank"]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()  # this test's own child, by handle
+                p.join()
+    errors = [r["error"] for r in results.values() if "error" in r]
+    assert not errors, "\n".join(errors)
+    return [results[r] for r in range(world)]
+
+
+_GQA_REFERENCE = {}
+
+
+def gqa_reference():
+    """The oracle's prefill + teacher-forced decode of the GQA model (weights
+    read back from a single-GPU decoder with the same seed) and that decoder's
+    own logits (world 1); computed once per session."""
+    if _GQA_REFERENCE:
+        return _GQA_REFERENCE
+    import tmc_cuda
+    from oracle.decoder_ref import DecoderOracle, DecoderSpec, weight_names
+    g = tp_worker.GQA
+    spec = DecoderSpec(hidden=g["hidden"], heads=g["heads"], kv_heads=g["kv_heads"], intermediate=g["intermediate"],
+                       vocab=g["vocab"], layers=g["layers"], capacity=g["capacity"], rope_theta=g["rope_theta"])
+    rt = tmc_cuda.Runtime(0)
+    dec = tp_worker.gqa_decoder(tmc_cuda, rt)
+    dec.init_random(seed=g["seed"], std=g["std"])
+    H, D, I, V = spec.hidden, spec.head_dim, spec.intermediate, spec.vocab
+    shapes = {"embedding": (V, H), "final_norm": (H,), "lm_head": (V, H), "input_norm": (H,), "post_norm": (H,),
+              "q": (spec.heads * D, H), "k": (spec.kv_heads * D, H), "v": (spec.kv_heads * D, H),
+              "o": (H, spec.heads * D), "gate": (I, H), "up": (I, H), "down": (H, I)}
+    w = {}
+    for n in weight_names(spec.layers):
+        shape = shapes[n.split(".")[-2]]
+        w[n] = dec.read_weight(n, int(np.prod(shape))).reshape(shape).astype(np.float16)
+    cap, half = spec.capacity, D // 2
+    cos = torch.from_numpy(dec.read_weight("rope.cosine", cap * half).reshape(cap, half))
+    sin = torch.from_numpy(dec.read_weight("rope.sine", cap * half).reshape(cap, half))
+    oracle = DecoderOracle(spec, w, cos, sin)
+    prompt = np.random.default_rng(51).integers(0, V, 40).astype(np.int32)
+    logits, tokens = [], []
+    lo, to = oracle.forward(0, prompt)
+    logits.append(lo.float().numpy())
+    tokens.append(to)
+    for _ in range(8):
+        lo, to = oracle.forward(0, [tokens[-1]])
+        logits.append(lo.float().numpy())
+        tokens.append(to)
+    single = [dec.prefill(prompt)[0]] + [dec.decode([t])[0] for t in tokens[:-1]]
+    kv = [tuple(x.float().numpy() for x in oracle.caches[0][layer]) for layer in range(spec.layers)]
+    dec.close()
+    rt.close()
+    _GQA_REFERENCE.update({"prompt": prompt, "feed": tokens[:-1], "logits": logits, "tokens": tokens,
+                           "single": single, "kv": kv})
+    return _GQA_REFERENCE
+
+
+@pytest.mark.parametrize("world,mode", [(2, "p2p"), (4, "p2p"), (8, "p2p"), (8, "nccl")])
+def test_tensor_parallel_gqa_matches_oracle(world, mode):
+    # 32 query / 8 KV heads x 128 split across the ranks (8 / world KV heads per
+    # rank, each with its 4 query heads); row-parallel sums and the
+    # vocab-parallel argmax through the fused peer exchange or NCCL.
+    from tests.parity_util import TokenCheck, fp16_close
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ref = gqa_reference()
+    ranks = run_gqa(world, mode, ref["prompt"], ref["feed"])
+    assert [r["local_kv_heads"] for r in ranks] == [8 // world] * world
+    tokens = TokenCheck(f"TP{world} {mode} GQA")
+    for step in range(len(ref["logits"])):
+        got = np.concatenate([r["logits"][step] for r in ranks], axis=-1)
+        what = f"TP{world} {mode} GQA {'prefill' if step == 0 else f'decode {step - 1}'} logits"
+        fp16_close(got, ref["logits"][step], what)
+        fp16_close(got, ref["single"][step], what + " vs the single-GPU decoder")
+        for r in ranks:
+            assert r["tokens"][step] == ranks[0]["tokens"][step]  # every rank finalises the same token
+        tokens.check(ranks[0]["tokens"][step], ref["tokens"][step], ref["logits"][step][-1], got[-1])
+    tokens.report()
+    for layer in range(2):
+        k = np.concatenate([r["kv"][layer][0] for r in ranks], axis=0)
+        v = np.concatenate([r["kv"][layer][1] for r in ranks], axis=0)
+        fp16_close(k, ref["kv"][layer][0], f"TP{world} {mode} GQA layer {layer} keys")
+        fp16_close(v, ref["kv"][layer][1], f"TP{world} {mode} GQA layer {layer} values")

@@ -119,3 +119,62 @@ def batched_worker(rank, world, uid, queue, mode="nccl", port=0, rows=12, steps=
     finally:
         if dist is not None and dist.is_initialized():
             dist.destroy_process_group()
+
+
+GQA = dict(hidden=4096, heads=32, kv_heads=8, intermediate=1024, vocab=4096, layers=2, capacity=128,
+           rope_theta=5e5, seed=9, std=0.02)
+
+
+def gqa_decoder(tmc_cuda, rt, rank=0, world=1, page_size=16):
+    g = GQA
+    dec = tmc_cuda.Decoder(rt, g["hidden"], g["heads"], g["intermediate"], g["vocab"], g["layers"],
+                           g["capacity"], kv_heads=g["kv_heads"], rope_theta=g["rope_theta"],
+                           page_size=page_size, max_rows=8, tp_rank=rank, tp_size=world)
+    return dec
+
+
+def gqa_worker(rank, world, uid, queue, mode, port, prompt, feed):
+    """One rank of a grouped-query model at the C3 head shape (32 query / 8 KV
+    heads x 128, so one KV head per rank at world 8), seeded random weights:
+    prefill `prompt`, then one decode step per token of `feed` (the oracle's
+    greedy tokens: teacher-forced); returns the rank's logits slices, its greedy
+    tokens and its KV heads."""
+    dist = None
+    try:
+        sys.path.insert(0, ROOT)
+        sys.path.insert(0, os.path.join(ROOT, "aicompiler-test_b200"))
+        import tmc_cuda
+
+        rt = tmc_cuda.Runtime(rank)
+        dec = gqa_decoder(tmc_cuda, rt, rank, world)
+        if world > 1 and mode == "p2p":
+            import torch.distributed as dist
+            dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                                    world_size=world)
+            handles = [None] * world
+            dist.all_gather_object(handles, dec.exchange_handle())
+            dec.attach_peers(handles, rank)
+        elif world > 1:
+            dec.attach_nccl(uid, world, rank)
+        dec.init_random(seed=GQA["seed"], std=GQA["std"])
+        out = {"rank": rank, "local_vocab": dec.local_vocab, "local_kv_heads": dec.local_kv_heads,
+               "logits": [], "tokens": []}
+        lg, t = dec.prefill(np.asarray(prompt, np.int32))
+        out["logits"].append(lg)
+        out["tokens"].append(int(t))
+        for tok in feed:
+            lg, n = dec.decode([int(tok)])
+            out["logits"].append(lg)
+            out["tokens"].append(int(n[0]))
+        out["kv"] = [dec.read_kv(layer) for layer in range(GQA["layers"])]
+        rt.synchronize()
+        if dist is not None:
+            dist.barrier()
+        dec.close()
+        rt.close()
+        queue.put(out)
+    except Exception:
+        queue.put({"rank": rank, "error": traceback.format_exc()})
+    finally:
+        if dist is not None and dist.is_initialized():
+            dist.destroy_process_group()
