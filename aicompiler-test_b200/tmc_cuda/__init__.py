@@ -230,6 +230,110 @@ class Buffer:
                                          byte_offset))
 
 
+# ---- prepared executions and sequences (prepareBuffers / prepareSequence) --------------
+
+_sig("tmc_kernel_count", c_int)
+_sig("tmc_kernel_at", c_int, c_int, POINTER(c_void_p))
+_sig("tmc_kernel_lookup", c_int, c_char_p, POINTER(c_void_p))
+_sig("tmc_kernel_describe", c_int, c_void_p, POINTER(c_char_p), POINTER(c_int), POINTER(c_int), POINTER(c_int),
+     POINTER(c_char_p))
+_sig("tmc_prepare", c_int, c_void_p, c_void_p, POINTER(c_void_p), c_int, POINTER(c_void_p), c_int, c_size_t,
+     c_size_t, POINTER(ctypes.c_uint32), c_int, POINTER(c_void_p))
+_sig("tmc_prepared_destroy", None, c_void_p)
+_sig("tmc_prepared_run", c_int, c_void_p, POINTER(c_float), c_size_t, POINTER(ctypes.c_double),
+     POINTER(ctypes.c_double))
+_sig("tmc_prepared_execute", c_int, c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_double))
+_sig("tmc_sequence_create", c_int, c_void_p, POINTER(c_void_p), c_int, POINTER(c_void_p))
+_sig("tmc_sequence_destroy", None, c_void_p)
+_sig("tmc_sequence_execute", c_int, c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_double))
+_sig("tmc_sequence_launch", c_int, c_void_p, c_int)
+
+
+def float_bits(value: float) -> int:
+    """The uint32 bit pattern of an fp32 value (floating constants of tmc_prepare)."""
+    return int(np.array([value], np.float32).view(np.uint32)[0])
+
+
+def kernels() -> dict:
+    """Built-in kernels: name -> (inputs, outputs, constants, signature)."""
+    out = {}
+    for i in range(lib.tmc_kernel_count()):
+        h = c_void_p()
+        check(lib.tmc_kernel_at(i, ctypes.byref(h)))
+        name, sig = c_char_p(), c_char_p()
+        ni, no, nc = c_int(), c_int(), c_int()
+        check(lib.tmc_kernel_describe(h, ctypes.byref(name), ctypes.byref(ni), ctypes.byref(no), ctypes.byref(nc),
+                                      ctypes.byref(sig)))
+        out[name.value.decode()] = (ni.value, no.value, nc.value, sig.value.decode())
+    return out
+
+
+class Prepared:
+    """A built-in kernel bound to buffers and constants (reference
+    MetalRuntime::prepareBuffers -> PreparedExecution)."""
+
+    def __init__(self, rt: "Runtime", kernel: str, inputs, outputs, constants=(), groups=1, threads=256):
+        k = c_void_p()
+        check(lib.tmc_kernel_lookup(kernel.encode(), ctypes.byref(k)))
+        ins = (c_void_p * max(1, len(inputs)))(*[b.handle for b in inputs])
+        outs = (c_void_p * max(1, len(outputs)))(*[b.handle for b in outputs])
+        consts = (ctypes.c_uint32 * max(1, len(constants)))(*[int(c) & 0xFFFFFFFF for c in constants])
+        h = c_void_p()
+        check(lib.tmc_prepare(rt.handle, k, ins, len(inputs), outs, len(outputs), groups, threads, consts,
+                              len(constants), ctypes.byref(h)))
+        self.handle = h
+        self.first_output_count = outputs[0].count if outputs else 0
+
+    def run(self):
+        """NaN sentinels, execute, read the first output: (values, gpu_us, cpu_us)."""
+        out = np.empty(self.first_output_count, np.float32)
+        g, c = ctypes.c_double(), ctypes.c_double()
+        check(lib.tmc_prepared_run(self.handle, _fptr(out), out.size, ctypes.byref(g), ctypes.byref(c)))
+        return out, g.value, c.value
+
+    def execute(self):
+        g, c = ctypes.c_double(), ctypes.c_double()
+        check(lib.tmc_prepared_execute(self.handle, ctypes.byref(g), ctypes.byref(c)))
+        return g.value, c.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib.tmc_prepared_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
+class Sequence:
+    """Prepared executions in order, captured once as a CUDA graph (reference
+    MetalRuntime::prepareSequence)."""
+
+    def __init__(self, rt: "Runtime", steps):
+        arr = (c_void_p * len(steps))(*[s.handle for s in steps])
+        h = c_void_p()
+        check(lib.tmc_sequence_create(rt.handle, arr, len(steps), ctypes.byref(h)))
+        self.handle = h
+        self.steps = list(steps)
+
+    def execute(self):
+        g, c = ctypes.c_double(), ctypes.c_double()
+        check(lib.tmc_sequence_execute(self.handle, ctypes.byref(g), ctypes.byref(c)))
+        return g.value, c.value
+
+    def launch(self, replays: int = 1):
+        """Enqueue `replays` replays on the runtime stream (no synchronisation)."""
+        check(lib.tmc_sequence_launch(self.handle, replays))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib.tmc_sequence_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
 # ---- kernel wrappers (device pointers) ------------------------------------------------
 
 def rmsnorm_gemv_f32(rt: Runtime, x: Buffer, gamma: Buffer, w: Buffer, y: Buffer, rows: int, k: int,

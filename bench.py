@@ -50,9 +50,11 @@ def parse(argv=None):
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--no-batch", action="store_true", help="skip the batched decode measurement")
     ap.add_argument("--no-c4", action="store_true", help="skip the C4 paged-attention measurement")
-    ap.add_argument("--serving", type=int, default=0,
-                    help="also serve this many requests (C5: Poisson 20 req/s, prompts U[128,2048], "
-                         "outputs U[64,512], max batch 128; 1000 in the full config)")
+    ap.add_argument("--serving", type=int, default=48,
+                    help="serve this many requests (C5: Poisson 20 req/s, prompts U[128,2048], "
+                         "outputs U[64,512], max batch 128; 1000 in the full config; 0 skips)")
+    ap.add_argument("--no-c1", action="store_true", help="skip the C1 RMSNorm -> GEMV measurement")
+    ap.add_argument("--no-c2", action="store_true", help="skip the C2 single-layer measurement")
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="TP reductions: peer exchange fused into the kernels, or NCCL allreduce")
     return ap.parse_args(argv)
@@ -298,6 +300,14 @@ def run_ours(args, world, rank, local):
     if not args.no_c4:
         c4 = guarded("c4", lambda: measure_c4(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind))
 
+    c1 = None
+    if not args.no_c1:
+        c1 = guarded("c1", lambda: measure_c1(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind))
+
+    c2 = None
+    if not args.no_c2:
+        c2 = guarded("c2", lambda: measure_c2(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind))
+
     serving = None
     if args.serving > 0:
         tick_s = batched.get("ms_per_step", 10.0) * 1e-3 if batched else 0.01
@@ -328,6 +338,8 @@ def run_ours(args, world, rank, local):
             "roofline": roofline,
             "kernels": kernels,
             "bs64": batched,
+            "c1": c1,
+            "c2": c2,
             "c4": c4,
             "serving": serving,
             "cpu_baseline": cpu,
@@ -338,6 +350,142 @@ def run_ours(args, world, rank, local):
         dec.close()
         dist.destroy_process_group()
     return 0
+
+
+def events(rt):
+    """CUDA events on the runtime's own stream (torch's events see only the
+    stream they are recorded on)."""
+    import torch
+    stream = torch.cuda.ExternalStream(rt.stream)
+    return stream, torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+
+def measure_c1(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind):
+    """C1: RMSNorm -> GEMV (x fp32 [1, 4096] ~N(0,1), gamma fp32 ~U(0.5,1.5),
+    W fp16 [4096, 4096] ~N(0,0.02), y fp32), through the prepared-execution
+    surface: 10 executions over 10 independent weight copies (335 MB, more
+    than twice the 126 MB L2, so every call streams its weights from HBM),
+    captured as one sequence (CUDA graph) and replayed between CUDA events.
+    value = algorithmic bytes per call (W + x + gamma + y = 33,603,584 B) /
+    device time per call; every rank measures its own copies (the graph path
+    is single-GPU: replicas only). cpu_baseline: the reference's own
+    evaluateGraph on one host core (oracle/_ref)."""
+    import numpy as np
+
+    import tmc_cuda
+    from oracle import workloads  # seeded inputs only (the C1 distributions)
+    copies, reps = 10, 20
+    x, gamma, w = workloads.c1_inputs(seed=0)
+    rt = tmc_cuda.Runtime(local)
+    eps = tmc_cuda.float_bits(1e-5)
+    keep, steps = [], []
+    for c in range(copies):
+        wb = rt.buffer(4096 * 4096, tmc_cuda.F16)
+        tmc_cuda.fill_normal_f16(rt, wb, 100 + c, 0.0, 0.02)
+        xb, gb, yb = rt.upload(x), rt.upload(gamma), rt.buffer(4096, tmc_cuda.F32)
+        keep += [wb, xb, gb, yb]
+        steps.append(tmc_cuda.Prepared(rt, "rmsnorm_gemv_f32", [xb, gb, wb], [yb], [1, 4096, 4096, eps]))
+    seq = tmc_cuda.Sequence(rt, steps)
+    seq.launch(3)
+    rt.synchronize()
+    stream, e0, e1 = events(rt)
+    barrier()
+    e0.record(stream)
+    seq.launch(reps)
+    e1.record(stream)
+    rt.synchronize()
+    us = max_over_ranks(e0.elapsed_time(e1) * 1e3 / (reps * copies))
+    nbytes = 33_603_584
+    single_us = steps[0].execute()[0]  # one call submitted alone (launch latency included)
+    seq.close()
+    for p in steps:
+        p.close()
+    rt.close()
+    cpu = None
+    if rank == 0 and world == 1:
+        try:
+            from oracle import cpu_baseline
+            r = cpu_baseline.c1_gbs(calls=3)
+            cpu = {"value": r["gbs"], "unit": "GB/s", "cores": r["cores"], "kind": r["kind"], "sample": r["sample"],
+                   "us_per_call": r["us_per_call"]}
+        except Exception as e:  # the GPU measurement above stands without it
+            cpu = {"error": f"{type(e).__name__}: {e}"}
+    achieved = nbytes / us / 1e3
+    return {"metric": "RMSNorm -> GEMV HBM GB/s", "value": achieved * world, "unit": "GB/s",
+            "us_per_call": us, "us_single_call_submitted_alone": single_us, "bytes_per_call": nbytes,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+            "cpu_baseline": cpu,
+            "config": {"workload": "C1 RMSNorm -> GEMV 4096 x 4096 (x fp32, W fp16, y fp32), seed 0 inputs",
+                       "api": "tmc_prepare + tmc_sequence_launch (kernel rmsnorm_gemv_f32)",
+                       "l2": f"{copies} weight copies = {copies * 33.55:.0f} MB > 2 x L2, rotated",
+                       "parallelism": f"replicas x{world}"}}
+
+
+def measure_c2(args, world, rank, local, barrier, max_over_ranks, hbm, peak_kind):
+    """C2: one decoder layer (d 1024, 16 x 64 MHA, SwiGLU 2816, fp16 weights
+    ~N(0,0.02), RoPE theta 1e4), a contiguous cache of capacity 2048 with 512
+    N(0,1) positions restored, 64 single-token decode steps (the device greedy
+    loop; step inputs are rows of a 64-row N(0,1) embedding table and the layer
+    output is read through a 64-row head). The layer's 25.7 MB of weights fit
+    in L2, so two numbers: warm = the one-layer decoder's 64 steps; cold = 16
+    independently initialised copies of the layer chained in one step (411 MB
+    of weights per step, more than twice L2), value = its per-layer GB/s.
+    Algorithmic bytes per layer-step: weights + norms + K/V read of the
+    context + K/V append (the 64-row head's 128 KB counted in the step)."""
+    import numpy as np
+
+    import tmc_cuda
+    H, HEADS, INTER, CAP, PREFIX, STEPS = 1024, 16, 2816, 2048, 512, 64
+    D = H // HEADS
+    rng = np.random.default_rng(11)
+    inputs = rng.standard_normal((STEPS, H), dtype=np.float32).astype(np.float16)
+    prefix_k = rng.standard_normal((1, HEADS, PREFIX, D), dtype=np.float32)
+    prefix_v = rng.standard_normal((1, HEADS, PREFIX, D), dtype=np.float32)
+    rt = tmc_cuda.Runtime(local)
+    out = {}
+    for name, layers in (("warm", 1), ("cold", 16)):
+        dec = tmc_cuda.Decoder(rt, H, HEADS, INTER, STEPS, layers, CAP, kv_heads=HEADS, rope_theta=1e4, page_size=0)
+        dec.init_random(seed=11, std=0.02)
+        dec.load_weight("embedding.weight", inputs)
+        dec.restore_kv(0, np.repeat(prefix_k, layers, axis=0), np.repeat(prefix_v, layers, axis=0))
+        dec.generate([0], 4)  # warm-up (builds the step graph); context 516
+        dec.rollback(0, PREFIX)
+        barrier()
+        _, gpu_us = dec.generate([0], STEPS)
+        gpu_us = max_over_ranks(gpu_us)
+        ctx = [PREFIX + STEPS // 2]
+        step_bytes = dec.step_bytes(ctx)
+        per_layer = (step_bytes - 2.0 * (STEPS * H + H)) / layers
+        step_us = gpu_us / STEPS
+        out[name] = {"us_per_step": step_us, "us_per_layer": step_us / layers, "layers_per_step": layers,
+                     "bytes_per_step": step_bytes, "gbs": step_bytes / step_us / 1e3,
+                     "frac_of_peak": step_bytes / step_us / 1e3 / hbm, "bytes_per_layer_step": per_layer}
+        dec.close()
+    rt.close()
+    cpu = None
+    if rank == 0 and world == 1:
+        try:
+            import torch
+
+            from oracle import cpu_baseline
+            torch.set_num_threads(os.cpu_count() or 1)
+            r = cpu_baseline.c2_steps_per_second(steps=STEPS)
+            cpu = {"value": r["gbs"], "unit": "GB/s", "cores": r["threads"], "kind": "port", "sample": r["sample"],
+                   "steps_per_s": r["steps_per_s"]}
+        except Exception as e:
+            cpu = {"error": f"{type(e).__name__}: {e}"}
+    cold = out["cold"]
+    return {"metric": "single decoder layer decode HBM GB/s", "value": cold["gbs"] * world, "unit": "GB/s",
+            "steps_per_s_one_layer_warm": 1e6 / out["warm"]["us_per_step"],
+            "warm": out["warm"], "cold": cold,
+            "roofline": {"bound": "hbm", "achieved": cold["gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": cold["frac_of_peak"], "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)"},
+            "cpu_baseline": cpu,
+            "config": {"workload": "C2 one layer d1024 16x64 MHA FFN 2816, cache 2048 with 512 N(0,1) positions, "
+                                   "64 decode steps",
+                       "l2": "cold: 16 chained copies of the layer (411 MB of weights per step); warm: L2-resident",
+                       "parallelism": f"replicas x{world}"}}
 
 
 def c4_case(world=1, rank=0):

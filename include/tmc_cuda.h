@@ -100,6 +100,56 @@ void *tmc_buffer_device_ptr(tmc_buffer *buf);
 size_t tmc_buffer_count(const tmc_buffer *buf);
 int tmc_buffer_dtype(const tmc_buffer *buf);
 
+/* ---- prepared executions and sequences -----------------------------------
+ * The reference compiles an emitted source into the runtime's current pipeline
+ * (MetalRuntime::createComputePipeline, MetalRuntime.hpp:176-178), binds
+ * buffers and packed uint32 constants to it (prepareBuffers,
+ * MetalRuntime.hpp:199-206, MetalRuntime.mm:594-648), runs it (PreparedExecution
+ * run / execute, MetalRuntime.hpp:101-121, MetalRuntime.mm:197-277) and chains
+ * launches into one submission (prepareSequence, MetalRuntime.mm:751-781).
+ * Here the kernels are this library's precompiled sm_100a functions, looked up
+ * by name (tmc_kernel_lookup; tmc_kernel_describe gives each one's buffer
+ * interface and constants), and a sequence is one CUDA graph.
+ *
+ * tmc_prepare binds inputs, then outputs, then constants, with the reference's
+ * checks: at least one input and one output, at most 31 bindings and 1024
+ * constants, groups and threads non-zero and within the device limits
+ * ("Kernel dispatch exceeds device or pipeline limits."), outputs distinct
+ * and on this runtime, no input aliasing an output; then the kernel's own
+ * interface (element types, sizes against the constants). Floating constants
+ * (eps) are passed as their float bit patterns. Kernels whose launcher sizes
+ * its own grid (the GEMV, GEMM and attention families) take the dispatch only
+ * for the limit check; rmsnorm takes its threads per CTA from it. A prepared
+ * execution retains its buffers (and any workspace it needed) until destroyed.
+ *
+ * tmc_prepared_run fills every output with NaN sentinels (integers with 0),
+ * executes, synchronises and, when `output` is not NULL, copies the first
+ * output as logical floats (count = its element count); tmc_prepared_execute
+ * only executes and synchronises. gpu_us / cpu_us (optional) receive the
+ * CUDA-event time and the host submit-to-completion time.
+ * tmc_sequence_create captures the executions in order into one CUDA graph
+ * (retaining them); tmc_sequence_execute replays it once synchronously;
+ * tmc_sequence_launch enqueues `replays` replays on the runtime stream and
+ * returns (tmc_runtime_synchronize waits). */
+typedef struct tmc_kernel tmc_kernel;
+typedef struct tmc_prepared tmc_prepared;
+typedef struct tmc_sequence tmc_sequence;
+int tmc_kernel_count(void);
+int tmc_kernel_at(int index, const tmc_kernel **out);
+int tmc_kernel_lookup(const char *name, const tmc_kernel **out);
+int tmc_kernel_describe(const tmc_kernel *kernel, const char **name, int *inputs, int *outputs, int *constants,
+                        const char **signature);
+int tmc_prepare(tmc_runtime *rt, const tmc_kernel *kernel, tmc_buffer *const *inputs, int n_inputs,
+                tmc_buffer *const *outputs, int n_outputs, size_t groups, size_t threads, const uint32_t *constants,
+                int n_constants, tmc_prepared **out);
+void tmc_prepared_destroy(tmc_prepared *prepared);
+int tmc_prepared_run(tmc_prepared *prepared, float *output, size_t count, double *gpu_us, double *cpu_us);
+int tmc_prepared_execute(tmc_prepared *prepared, double *gpu_us, double *cpu_us);
+int tmc_sequence_create(tmc_runtime *rt, tmc_prepared *const *steps, int n, tmc_sequence **out);
+void tmc_sequence_destroy(tmc_sequence *sequence);
+int tmc_sequence_execute(tmc_sequence *sequence, double *gpu_us, double *cpu_us);
+int tmc_sequence_launch(tmc_sequence *sequence, int replays);
+
 /* ---- kernels (device pointers; enqueue only) ------------------------------ */
 
 /* Fused RMSNorm -> GEMV, fp32 activations, fp16 weights, fp32 accumulate:

@@ -139,3 +139,63 @@ def paged_attention_gbs(sequences: int = 12, threads: int | None = None, seed: i
                    f"16-token pages; C restatement of the serving kernel (fp64 softmax), once on 1 thread "
                    f"and once with one task per sequence on {workers} threads"),
     }
+
+
+C1_BYTES = 33_603_584  # W fp16 4096x4096 + x, gamma, y fp32 [4096]
+
+
+def c1_gbs(calls: int = 3, seed: int = 0):
+    """C1 RMSNorm -> GEMV on one host core through the reference's OWN
+    evaluateGraph (src/validation/GraphReference.cpp:98, compiled from the
+    reference sources into oracle/_ref by oracle/Makefile) when it was built,
+    else the C restatement (oracle/graph_ref.c); GB/s counts the same
+    algorithmic bytes as the GPU measurement."""
+    from . import oracle, workloads
+    x, gamma, w = workloads.c1_inputs(seed=seed)
+    w32 = w.astype(np.float32)
+    kind = "reference" if oracle.reference_available() else "port"
+    fn = oracle.ref_rmsnorm_matmul if kind == "reference" else oracle.rmsnorm_matmul
+    fn(x, gamma, w32)  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        fn(x, gamma, w32)
+    per_call = (time.perf_counter() - t0) / calls
+    return {"gbs": C1_BYTES / per_call / 1e9, "us_per_call": per_call * 1e6, "cores": 1, "kind": kind,
+            "sample": (f"{calls} calls of the C1 graph (RMSNorm -> Transpose(W) -> MatMul, 4096 x 4096, seed 0) "
+                       + ("through the reference's own evaluateGraph (fp64 accumulation), single-threaded"
+                          if kind == "reference" else "through the C restatement of evaluateGraph, single-threaded"))}
+
+
+def c2_steps_per_second(steps: int = 64, threads: int | None = None, seed: int = 11):
+    """C2 on the host: the oracle port of the reference's decoder_llm.py (one
+    layer, d 1024, 16 x 64 MHA, SwiGLU 2816, fp16 weights, a 512-position
+    N(0,1) KV prefix, capacity 2048) for `steps` decode steps with N(0,1)
+    input embeddings; reports steps/s and GB/s over the C2 algorithmic bytes
+    (weights once + KV read and append per step)."""
+    if threads:
+        torch.set_num_threads(threads)
+    spec = DecoderSpec(hidden=1024, heads=16, kv_heads=16, intermediate=2816, vocab=steps, layers=1,
+                       capacity=2048, epsilon=1e-5, rope_theta=1e4)
+    g = torch.Generator().manual_seed(seed)
+    H, D, I = 1024, 64, 2816
+
+    def mat(r, c, std=0.02):
+        return (torch.randn(r, c, generator=g) * std).to(torch.float16).numpy()
+
+    w = {"embedding.weight": mat(steps, H, 1.0), "final_norm.weight": np.ones(H, np.float16),
+         "lm_head.weight": mat(steps, H), "layer0.input_norm.weight": np.ones(H, np.float16),
+         "layer0.post_norm.weight": np.ones(H, np.float16), "layer0.q.weight": mat(H, H),
+         "layer0.k.weight": mat(H, H), "layer0.v.weight": mat(H, H), "layer0.o.weight": mat(H, H),
+         "layer0.gate.weight": mat(I, H), "layer0.up.weight": mat(I, H), "layer0.down.weight": mat(H, I)}
+    oracle = DecoderOracle(spec, w)
+    k = torch.randn(16, 512, D, generator=g).to(torch.float16)
+    v = torch.randn(16, 512, D, generator=g).to(torch.float16)
+    oracle.caches[0] = [(k, v)]
+    t0 = time.perf_counter()
+    for t in range(steps):
+        oracle.forward(0, [t])
+    dt = time.perf_counter() - t0
+    weights = 2 * (4 * H * H + 3 * H * I + 2 * H) + 2 * steps * H
+    kv = sum(2 * 2 * H * (512 + t + 1) for t in range(steps))
+    return {"steps_per_s": steps / dt, "gbs": (weights * steps + kv) / dt / 1e9, "threads": torch.get_num_threads(),
+            "sample": f"all {steps} C2 decode steps through the oracle port of decoder_llm.py (torch CPU)"}

@@ -91,3 +91,21 @@ def test_noalloc_attention_refuses_requests_beyond_its_fixed_scratch():
     assert code == tmc_cuda.ERR_UNSUPPORTED
     assert f"needs {need} bytes" in tmc_cuda.last_error() and str(limit) in tmc_cuda.last_error()
     assert fn(P, P, P, P, P, 1, P, P, 0, hq, hkv, d, 16, 64, 1024, 1, 64, None, None) == tmc_cuda.ERR_INVALID
+
+
+def test_builtin_kernel_catalog_is_listed_on_the_host():
+    # tmc_kernel_count / tmc_kernel_at / tmc_kernel_lookup / tmc_kernel_describe
+    # need no GPU: the catalog is this library's own table.
+    import tmc_cuda
+    cat = tmc_cuda.kernels()
+    for name, counts in {"rmsnorm": (2, 1, 3), "rmsnorm_gemv_f32": (3, 1, 4), "gemv_f16": (2, 1, 3),
+                         "batched_gemm_f16": (2, 1, 3), "fused_add_rmsnorm": (3, 1, 4),
+                         "fused_add_layernorm": (4, 1, 4), "fused_silu_mul": (2, 1, 3),
+                         "fused_linear_relu": (3, 1, 3), "paged_attention_f16": (6, 1, 10)}.items():
+        assert cat[name][:3] == counts, name
+        assert cat[name][3]
+    import ctypes
+    h = ctypes.c_void_p()
+    assert tmc_cuda.lib.tmc_kernel_lookup(b"missing", ctypes.byref(h)) == tmc_cuda.ERR_UNSUPPORTED
+    assert "no built-in kernel" in tmc_cuda.last_error()
+    assert tmc_cuda.float_bits(1.0) == 0x3F800000

@@ -13,8 +13,10 @@ greedy tokens bit-exact except counted fp16 ties):
 - tensor-core path: the same prompt prefilled in 64-row chunks through the
   tcgen05 GEMMs (all 1024 rows of logits), and a 64-sequence batched decode
   (64 rows, one per sequence, prompts of 8..71 tokens) for 2 steps.
-The oracle's twin with a permuted fp32 summation order gives the noise floor
-printed beside the bs1 numbers.
+The oracle's twin with a permuted fp32 summation order gives the noise floor:
+at this width it is larger than 2e-3 x RMS, so the bound is max(2e-3 x RMS,
+3 x floor) with at most 0.1% of the elements beyond max(2e-3 x RMS, one fp16
+ulp); the measured ratios are printed beside the floor.
 """
 
 import numpy as np
@@ -69,18 +71,21 @@ def model(rt):
     oracle = DecoderOracle(SPEC, weights, cos, sin)
     del weights  # the oracle holds its own fp16 tensors
     ref_logits, ref_tok = oracle.forward(0, prompt)
-    return {"prompt": prompt, "oracle": oracle,
-            "prefill_logits": ref_logits.float().numpy(), "prefill_token": ref_tok}
+    ref_logits = ref_logits.float().numpy()
+    # The noise floor: the same oracle with a permuted fp32 summation order.
+    twin = oracle.fork(summation_order_seed=7)
+    twin_logits, _ = twin.forward(0, prompt)
+    floor = float(np.max(np.abs(twin_logits.float().numpy() - ref_logits)))
+    return {"prompt": prompt, "oracle": oracle, "twin": twin, "floor": floor,
+            "prefill_logits": ref_logits, "prefill_token": ref_tok}
 
 
 def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
-    twin = model["oracle"].fork(summation_order_seed=7)
-    twin_logits, _ = twin.forward(0, model["prompt"])
+    twin = model["twin"].fork(summation_order_seed=7, caches=model["twin"].caches)
     ref = model["prefill_logits"]
-    floor = float(np.max(np.abs(twin_logits.float().numpy() - ref)))
     dec = decoder(rt, max_rows=8)
     logits, tok = dec.prefill(model["prompt"])
-    fp16_close(logits, ref, "C3 width bs1 prefill logits (1024 rows)", floor)
+    fp16_close(logits, ref, "C3 width bs1 prefill logits (1024 rows)", model["floor"])
     tokens = TokenCheck("C3 width bs1")
     tokens.check(tok, model["prefill_token"], ref[-1], logits[-1])
     oracle = model["oracle"].fork(caches=model["oracle"].caches)
@@ -98,15 +103,18 @@ def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
     for layer in range(LAYERS):
         k, v = dec.read_kv(layer)
         rk, rv = oracle.caches[0][layer]
-        fp16_close(k, rk.float().numpy(), f"C3 width layer {layer} key cache ({PROMPT + STEPS} positions)")
-        fp16_close(v, rv.float().numpy(), f"C3 width layer {layer} value cache")
+        tk, tv = twin.caches[0][layer]
+        fk = float((tk.float() - rk.float()).abs().max())
+        fv = float((tv.float() - rv.float()).abs().max())
+        fp16_close(k, rk.float().numpy(), f"C3 width layer {layer} key cache ({PROMPT + STEPS} positions)", fk)
+        fp16_close(v, rv.float().numpy(), f"C3 width layer {layer} value cache", fv)
     dec.close()
 
 
 def test_c3_width_tensor_core_path_matches_oracle(rt, model):
     dec = decoder(rt, max_rows=64, max_slots=64)
     logits, tok = dec.prefill(model["prompt"])  # 16 chunks of 64 rows: tcgen05 GEMMs
-    fp16_close(logits, model["prefill_logits"], "C3 width prefill logits, 64-row tensor-core chunks")
+    fp16_close(logits, model["prefill_logits"], "C3 width prefill logits, 64-row tensor-core chunks", model["floor"])
     tokens = TokenCheck("C3 width 64-row steps")
     tokens.check(tok, model["prefill_token"], model["prefill_logits"][-1], logits[-1])
     dec.release(0)
@@ -130,7 +138,8 @@ def test_c3_width_tensor_core_path_matches_oracle(rt, model):
             ref[s] = lo[0].float().numpy()
             ref_tok.append(to)
         lg, nxt = dec.decode(toks, slots=slots)  # one 64-row step: tensor-core projections
-        fp16_close(lg, ref, f"C3 width 64-sequence decode step {step} logits")
+        # The prefill's noise floor (the same model and weights) bounds these steps.
+        fp16_close(lg, ref, f"C3 width 64-sequence decode step {step} logits", model["floor"])
         for s in range(rows):
             tokens.check(int(nxt[s]), ref_tok[s], ref[s], lg[s])
         toks = ref_tok
