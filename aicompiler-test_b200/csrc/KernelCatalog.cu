@@ -394,13 +394,6 @@ PreparationResult prepareKernel(CudaRuntime &runtime, const KernelEntry &kernel,
     result.errorMessage = "Kernel dispatch exceeds device or pipeline limits.";
     return result;
   }
-  if ((int)inputs.size() != kernel.inputs || (int)outputs.size() != kernel.outputs ||
-      (int)constants.size() != kernel.constants) {
-    result.errorMessage = std::string(kernel.name) + " binds " + std::to_string(kernel.inputs) + " inputs, " +
-                          std::to_string(kernel.outputs) + " outputs and " + std::to_string(kernel.constants) +
-                          " constants: " + kernel.signature;
-    return result;
-  }
   for (std::size_t i = 0; i < outputs.size(); ++i) {
     if (!outputs[i] || std::find(outputs.begin(), outputs.begin() + i, outputs[i]) != outputs.begin() + i) {
       result.errorMessage = "Outputs must be distinct buffers on the current device.";
@@ -412,6 +405,13 @@ PreparationResult prepareKernel(CudaRuntime &runtime, const KernelEntry &kernel,
       result.errorMessage = "Input is missing, on another device, or aliases an output.";
       return result;
     }
+  }
+  if ((int)inputs.size() != kernel.inputs || (int)outputs.size() != kernel.outputs ||
+      (int)constants.size() != kernel.constants) {
+    result.errorMessage = std::string(kernel.name) + " binds " + std::to_string(kernel.inputs) + " inputs, " +
+                          std::to_string(kernel.outputs) + " outputs and " + std::to_string(kernel.constants) +
+                          " constants: " + kernel.signature;
+    return result;
   }
   KernelBinding binding;
   binding.inputs = inputs;

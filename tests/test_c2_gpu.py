@@ -64,8 +64,7 @@ def test_c2_layer_64_steps_match_oracle(rt):
         lt, _ = twin.forward(0, [t])
         lg, nxt = dec.decode([t])
         ref = lo[0].float().numpy()
-        floor = float(np.max(np.abs(lt[0].float().numpy() - ref)))
-        fp16_close(lg[0], ref, f"C2 step {t} (context {PREFIX + t + 1}) head logits", floor)
+        fp16_close(lg[0], ref, f"C2 step {t} (context {PREFIX + t + 1}) head logits", twin=lt[0].float().numpy())
         tokens.check(int(nxt[0]), to, ref, lg[0])
     tokens.report()
     assert dec.length() == PREFIX + STEPS

@@ -13,10 +13,12 @@ greedy tokens bit-exact except counted fp16 ties):
 - tensor-core path: the same prompt prefilled in 64-row chunks through the
   tcgen05 GEMMs (all 1024 rows of logits), and a 64-sequence batched decode
   (64 rows, one per sequence, prompts of 8..71 tokens) for 2 steps.
-The oracle's twin with a permuted fp32 summation order gives the noise floor:
-at this width it is larger than 2e-3 x RMS, so the bound is max(2e-3 x RMS,
-3 x floor) with at most 0.1% of the elements beyond max(2e-3 x RMS, one fp16
-ulp); the measured ratios are printed beside the floor.
+The oracle's twin with a permuted fp32 summation order measures the noise of
+the model itself: at this width a few percent of the twin's own logits lie
+beyond 2e-3 x RMS of the oracle (fp16 rounding of every activation). The GPU
+must be as close to the oracle as the twin is: max |err| <= max(2e-3 x RMS,
+3 x the twin's max |err|), and at most twice the twin's fraction of elements
+beyond max(2e-3 x RMS, one fp16 ulp); both are printed.
 """
 
 import numpy as np
@@ -75,8 +77,10 @@ def model(rt):
     # The noise floor: the same oracle with a permuted fp32 summation order.
     twin = oracle.fork(summation_order_seed=7)
     twin_logits, _ = twin.forward(0, prompt)
-    floor = float(np.max(np.abs(twin_logits.float().numpy() - ref_logits)))
-    return {"prompt": prompt, "oracle": oracle, "twin": twin, "floor": floor,
+    noise = fp16_close(twin_logits.float().numpy(), ref_logits, "C3 width oracle twin prefill logits",
+                       floor=float("inf"), twin_outside_fraction=1.0)
+    return {"prompt": prompt, "oracle": oracle, "twin": twin, "twin_logits": twin_logits.float().numpy(),
+            "floor": noise["max_err"], "twin_outside": noise["outside_elements"] / noise["elements"],
             "prefill_logits": ref_logits, "prefill_token": ref_tok}
 
 
@@ -85,7 +89,7 @@ def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
     ref = model["prefill_logits"]
     dec = decoder(rt, max_rows=8)
     logits, tok = dec.prefill(model["prompt"])
-    fp16_close(logits, ref, "C3 width bs1 prefill logits (1024 rows)", model["floor"])
+    fp16_close(logits, ref, "C3 width bs1 prefill logits (1024 rows)", twin=model["twin_logits"])
     tokens = TokenCheck("C3 width bs1")
     tokens.check(tok, model["prefill_token"], ref[-1], logits[-1])
     oracle = model["oracle"].fork(caches=model["oracle"].caches)
@@ -95,8 +99,7 @@ def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
         lt, _ = twin.forward(0, [t])
         lg, nxt = dec.decode([t])
         ref_step = lo[0].float().numpy()
-        floor = float(np.max(np.abs(lt[0].float().numpy() - ref_step)))
-        fp16_close(lg[0], ref_step, f"C3 width bs1 decode {step} logits", floor)
+        fp16_close(lg[0], ref_step, f"C3 width bs1 decode {step} logits", twin=lt[0].float().numpy())
         tokens.check(int(nxt[0]), to, ref_step, lg[0])
         t = to  # teacher-forced: both continue from the oracle's token
     tokens.report()
@@ -104,17 +107,17 @@ def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
         k, v = dec.read_kv(layer)
         rk, rv = oracle.caches[0][layer]
         tk, tv = twin.caches[0][layer]
-        fk = float((tk.float() - rk.float()).abs().max())
-        fv = float((tv.float() - rv.float()).abs().max())
-        fp16_close(k, rk.float().numpy(), f"C3 width layer {layer} key cache ({PROMPT + STEPS} positions)", fk)
-        fp16_close(v, rv.float().numpy(), f"C3 width layer {layer} value cache", fv)
+        fp16_close(k, rk.float().numpy(), f"C3 width layer {layer} key cache ({PROMPT + STEPS} positions)",
+                   twin=tk.float().numpy())
+        fp16_close(v, rv.float().numpy(), f"C3 width layer {layer} value cache", twin=tv.float().numpy())
     dec.close()
 
 
 def test_c3_width_tensor_core_path_matches_oracle(rt, model):
     dec = decoder(rt, max_rows=64, max_slots=64)
     logits, tok = dec.prefill(model["prompt"])  # 16 chunks of 64 rows: tcgen05 GEMMs
-    fp16_close(logits, model["prefill_logits"], "C3 width prefill logits, 64-row tensor-core chunks", model["floor"])
+    fp16_close(logits, model["prefill_logits"], "C3 width prefill logits, 64-row tensor-core chunks",
+               twin=model["twin_logits"])
     tokens = TokenCheck("C3 width 64-row steps")
     tokens.check(tok, model["prefill_token"], model["prefill_logits"][-1], logits[-1])
     dec.release(0)
@@ -139,7 +142,8 @@ def test_c3_width_tensor_core_path_matches_oracle(rt, model):
             ref_tok.append(to)
         lg, nxt = dec.decode(toks, slots=slots)  # one 64-row step: tensor-core projections
         # The prefill's noise floor (the same model and weights) bounds these steps.
-        fp16_close(lg, ref, f"C3 width 64-sequence decode step {step} logits", model["floor"])
+        fp16_close(lg, ref, f"C3 width 64-sequence decode step {step} logits", floor=model["floor"],
+                   twin_outside_fraction=model["twin_outside"])
         for s in range(rows):
             tokens.check(int(nxt[s]), ref_tok[s], ref[s], lg[s])
         toks = ref_tok
