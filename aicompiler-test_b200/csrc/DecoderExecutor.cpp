@@ -223,6 +223,10 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)R * hkvL_, I32, &attnCounters_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)cfg_.layers * 6 * tmc::kGemvCounterWords, I32, &workCounters_, &activationBytes_)).empty())
     return e;
+  if (!(e = make((size_t)cfg_.layers * tmc::kStreamSyncWords, I32, &streamSync_, &activationBytes_)).empty())
+    return e;
+  streamOk_ = cfg_.useStream && cfg_.tpSize == 1 && tmc::layer_stream_fits(streamParams(0, false)) &&
+              tmc::layer_stream_fits(streamParams(cfg_.layers - 1, false));
   // Zero the state the kernels expect zero (int32 buffers were zero-filled by
   // createBuffer); residual-stream buffers start at zero too.
   cudaStream_t s0 = rt_.stream();
@@ -737,6 +741,7 @@ std::string DecoderExecutor::restoreKV(int slot, std::size_t length,
 // ---- step --------------------------------------------------------------------
 
 int DecoderExecutor::kernelsPerStep(int rows) const {
+  if (streamEligible(rows)) return 1 + 2 * cfg_.layers;
   const bool tp = cfg_.tpSize > 1;
   // Batched steps add a prologue kernel before the QKV, gate/up and LM-head projections.
   const int perLayer = rows > kGemvMaxRows ? 7 : 5;
@@ -797,9 +802,7 @@ std::string DecoderExecutor::launchProjection(const tmc::GemvParams &p, const ch
   return {};
 }
 
-std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bool distinct) {
-  cudaStream_t s = rt_.stream();
-  const bool pdl = cfg_.usePDL;
+tmc::GemvParams DecoderExecutor::projection(int kind, int l, int R, bool feed) const {
   const bool tp = cfg_.tpSize > 1;
   const int H = cfg_.hidden, D = cfg_.headDim;
   auto *io = static_cast<int *>(stepIO_->data());
@@ -808,29 +811,21 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
   // consumer kernel that folds the reduced projection into h also reads h.
   __half *hA = hp(h_), *hB = hp(hB_);
   auto *status = rt_.deviceStatus();
-  // Attention splits per (row, KV head): few pairs -> enough splits to cover
-  // the SMs twice; many pairs (batched decode) -> a power of two that gives
-  // about 8 CTAs per SM (bs64: 2 splits of ~576 positions; 4 splits, ~16 per
-  // SM, cost 86.6 us against 80.7 per layer), so the last partial wave is short.
-  int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
-  if (R * hkvL_ < numSms_) splits = std::min(splits, attnSplitCap_);
-  if (R * hkvL_ >= numSms_) {
-    splits = 1;
-    while (splits < 16 && 2 * splits * R * hkvL_ <= 8 * numSms_) splits *= 2;
-  }
   float *partialF32 = fp(partialF32_);  // [R, H] row-parallel sums (TP with a collective)
   // TP over peer memory: partial-sum phase 2l = O of layer l, 2l + 1 = down.
   const bool xchg = tp && peersAttached_;
-  cudaError_t e;
-  Layer &L = layers_[kind == kKernelLMHead ? 0 : l];
+  const Layer &L = layers_[kind == kKernelLMHead ? 0 : l];
+  tmc::GemvParams p{};
+  p.M = R;
+  p.status = status;
+  p.trace = traceSink(kind == kKernelLMHead ? 0 : l, kind);
+  p.work_counter = workCounter(kind == kKernelLMHead ? 0 : l, kind);
+  p.l2_prefetch_bytes = kL2PrefetchBytes;
   switch (kind) {
-    case kKernelQKV: {
-
-      tmc::GemvParams p{};
+    case kKernelQKV:
       p.W = hp(L.qkv);
       p.N = qkvRows_;
       p.K = H;
-      p.M = R;
       if (l == 0) {
         p.prologue = tmc::kProEmbedNorm;
         p.embedding = hp(embedding_);
@@ -867,14 +862,143 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       p.capacity = cfg_.capacity;
       p.k_pool = hp(L.kPool);
       p.v_pool = hp(L.vPool);
-      p.status = status;
-      p.trace = traceSink(l, kind);
-      p.work_counter = workCounter(l, kind);
-      p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if (auto pe = launchProjection(p, "qkv projection"); !pe.empty()) return pe;
+      break;
+    case kKernelO:
+      p.W = hp(L.o);
+      p.N = H;
+      p.K = hqL_ * D;
+      p.prologue = tmc::kProF16;
+      p.x = hp(ctx_);
+      p.x_stride = (long long)hqL_ * D;
+      p.y_stride = H;
+      if (tp) {
+        p.epilogue = tmc::kEpiF32Partial;
+        p.y_f32 = partialF32;
+        if (xchg) p.xchg = exchange(2 * l);
+      } else {
+        p.epilogue = tmc::kEpiResidual;
+        p.y_f16 = hA;
+        p.residual = hA;
+      }
+      break;
+    case kKernelGateUp:
+      p.W = hp(L.gateUp);
+      p.N = 2 * iL_;
+      p.K = H;
+      if (tp) {
+        p.prologue = tmc::kProResidualNorm;
+        p.x = hA;
+        p.partial = partialF32;
+        p.h_out = hB;
+        if (xchg) p.xchg = exchange(2 * l);
+      } else {
+        p.prologue = tmc::kProF16Norm;
+        p.x = hA;
+      }
+      p.x_stride = H;
+      p.gamma = hp(L.postNorm);
+      p.eps = cfg_.epsilon;
+      p.epilogue = tmc::kEpiSwiGLU;
+      p.y_f16 = hp(act_);
+      p.y_stride = iL_;
+      break;
+    case kKernelDown:
+      p.W = hp(L.down);
+      p.N = H;
+      p.K = iL_;
+      p.prologue = tmc::kProF16;
+      p.x = hp(act_);
+      p.x_stride = iL_;
+      p.y_stride = H;
+      if (tp) {
+        p.epilogue = tmc::kEpiF32Partial;
+        p.y_f32 = partialF32;
+        if (xchg) p.xchg = exchange(2 * l + 1);
+      } else {
+        p.epilogue = tmc::kEpiResidual;
+        p.y_f16 = hA;
+        p.residual = hA;
+      }
+      break;
+    case kKernelLMHead:
+      p.W = hp(lmHead_);
+      p.N = vL_;
+      p.K = H;
+      if (tp) {
+        p.prologue = tmc::kProResidualNorm;
+        p.x = hB;
+        p.partial = partialF32;
+        p.h_out = hA;
+        if (xchg) p.xchg = exchange(2 * (cfg_.layers - 1) + 1);  // also carries the argmax keys
+      } else {
+        p.prologue = tmc::kProF16Norm;
+        p.x = hA;
+      }
+      p.x_stride = H;
+      p.gamma = hp(finalNorm_);
+      p.eps = cfg_.epsilon;
+      p.epilogue = tmc::kEpiArgmax;
+      p.y_f32 = fp(logits_);  // this rank's vocabulary slice
+      p.y_stride = vL_;
+      p.argmax_keys = static_cast<unsigned long long *>(argmaxKeys_->data());
+      p.argmax_counter = static_cast<unsigned int *>(argmaxCounter_->data());
+      p.vocab_offset = cfg_.tpRank * vL_;
+      if (!tp || xchg) {
+        p.next_tokens = static_cast<int *>(nextTokens_->data());
+        if (feed) {
+          p.feed_tokens = tokens;
+          p.feed_positions = positions;
+          p.history = static_cast<int *>(history_->data());
+          p.history_counter = static_cast<unsigned int *>(historyCounter_->data());
+        }
+      }
+      break;
+    default:
+      break;
+  }
+  return p;
+}
 
-      return {};
-    }
+bool DecoderExecutor::streamEligible(int R) const {
+  return streamOk_ && R == 1 && cfg_.tpSize == 1;
+}
+
+tmc::StreamParams DecoderExecutor::streamParams(int l, bool feed) const {
+  tmc::StreamParams s{};
+  s.phase[0] = projection(kKernelO, l, 1, feed);
+  s.phase[1] = projection(kKernelGateUp, l, 1, feed);
+  s.phase[2] = projection(kKernelDown, l, 1, feed);
+  s.phase[3] = l + 1 < cfg_.layers ? projection(kKernelQKV, l + 1, 1, feed) : projection(kKernelLMHead, 0, 1, feed);
+  // One record per CTA, under the O projection's tag (kind 2 of layer l).
+  s.sync = static_cast<unsigned int *>(streamSync_->data()) + (size_t)l * tmc::kStreamSyncWords;
+  return s;
+}
+
+std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bool distinct) {
+  cudaStream_t s = rt_.stream();
+  const bool pdl = cfg_.usePDL;
+  const bool tp = cfg_.tpSize > 1;
+  const int H = cfg_.hidden, D = cfg_.headDim;
+  auto *io = static_cast<int *>(stepIO_->data());
+  int *tokens = io, *positions = io + cfg_.maxRows, *tableRows = io + 2 * cfg_.maxRows;
+  auto *status = rt_.deviceStatus();
+  // Attention splits per (row, KV head): few pairs -> enough splits to cover
+  // the SMs twice; many pairs (batched decode) -> a power of two that gives
+  // about 8 CTAs per SM (bs64: 2 splits of ~576 positions; 4 splits, ~16 per
+  // SM, cost 86.6 us against 80.7 per layer), so the last partial wave is short.
+  int splits = std::max(1, std::min(64, (2 * numSms_ + R * hkvL_ - 1) / (R * hkvL_)));
+  if (R * hkvL_ < numSms_) splits = std::min(splits, attnSplitCap_);
+  if (R * hkvL_ >= numSms_) {
+    splits = 1;
+    while (splits < 16 && 2 * splits * R * hkvL_ <= 8 * numSms_) splits *= 2;
+  }
+  float *partialF32 = fp(partialF32_);
+  const bool xchg = tp && peersAttached_;
+  cudaError_t e;
+  Layer &L = layers_[kind == kKernelLMHead ? 0 : l];
+  switch (kind) {
+    case kKernelQKV:
+      return launchProjection(projection(kind, l, R, feed), "qkv projection");
     case kKernelAttention: {
 
       tmc::AttentionParams a{};
@@ -915,151 +1039,38 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
         if (!a.v_map) return "attention: " + err;
       }
       if ((e = tmc::launch_attention(a, s, pdl)) != cudaSuccess) return cudaText("attention", e);
-
+      (void)H;
       return {};
     }
-    case kKernelO: {
-
-      tmc::GemvParams p{};
-      p.W = hp(L.o);
-      p.N = H;
-      p.K = hqL_ * D;
-      p.M = R;
-      p.prologue = tmc::kProF16;
-      p.x = hp(ctx_);
-      p.x_stride = (long long)hqL_ * D;
-      p.y_stride = H;
-      if (tp) {
-        p.epilogue = tmc::kEpiF32Partial;
-        p.y_f32 = partialF32;
-        if (xchg) p.xchg = exchange(2 * l);
-      } else {
-        p.epilogue = tmc::kEpiResidual;
-        p.y_f16 = hA;
-        p.residual = hA;
-      }
-      p.status = status;
-      p.trace = traceSink(l, kind);
-      p.work_counter = workCounter(l, kind);
-      p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if (auto pe = launchProjection(p, "o projection"); !pe.empty()) return pe;
-      if (tp && !xchg && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
-        return "allreduce (o): " + collective_->lastError();
-
-      return {};
-    }
-    case kKernelGateUp: {
-
-      tmc::GemvParams p{};
-      p.W = hp(L.gateUp);
-      p.N = 2 * iL_;
-      p.K = H;
-      p.M = R;
-      if (tp) {
-        p.prologue = tmc::kProResidualNorm;
-        p.x = hA;
-        p.partial = partialF32;
-        p.h_out = hB;
-        if (xchg) p.xchg = exchange(2 * l);
-      } else {
-        p.prologue = tmc::kProF16Norm;
-        p.x = hA;
-      }
-      p.x_stride = H;
-      p.gamma = hp(L.postNorm);
-      p.eps = cfg_.epsilon;
-      p.epilogue = tmc::kEpiSwiGLU;
-      p.y_f16 = hp(act_);
-      p.y_stride = iL_;
-      p.status = status;
-      p.trace = traceSink(l, kind);
-      p.work_counter = workCounter(l, kind);
-      p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if (auto pe = launchProjection(p, "gate/up projection"); !pe.empty()) return pe;
-
-      return {};
-    }
+    case kKernelO:
     case kKernelDown: {
-
-      tmc::GemvParams p{};
-      p.W = hp(L.down);
-      p.N = H;
-      p.K = iL_;
-      p.M = R;
-      p.prologue = tmc::kProF16;
-      p.x = hp(act_);
-      p.x_stride = iL_;
-      p.y_stride = H;
-      if (tp) {
-        p.epilogue = tmc::kEpiF32Partial;
-        p.y_f32 = partialF32;
-        if (xchg) p.xchg = exchange(2 * l + 1);
-      } else {
-        p.epilogue = tmc::kEpiResidual;
-        p.y_f16 = hA;
-        p.residual = hA;
-      }
-      p.status = status;
-      p.trace = traceSink(l, kind);
-      p.work_counter = workCounter(l, kind);
-      p.l2_prefetch_bytes = kL2PrefetchBytes;
-      if (auto pe = launchProjection(p, "down projection"); !pe.empty()) return pe;
+      if (auto pe = launchProjection(projection(kind, l, R, feed), kind == kKernelO ? "o projection" : "down projection");
+          !pe.empty())
+        return pe;
       if (tp && !xchg && (e = collective_->allReduceSumF32(partialF32, (size_t)R * H, s)) != cudaSuccess)
-        return "allreduce (down): " + collective_->lastError();
-
+        return std::string(kind == kKernelO ? "allreduce (o): " : "allreduce (down): ") + collective_->lastError();
       return {};
     }
+    case kKernelGateUp:
+      return launchProjection(projection(kind, l, R, feed), "gate/up projection");
     case kKernelLMHead: {
-
-    tmc::GemvParams p{};
-    p.W = hp(lmHead_);
-    p.N = vL_;
-    p.K = H;
-    p.M = R;
-    if (tp) {
-      p.prologue = tmc::kProResidualNorm;
-      p.x = hB;
-      p.partial = partialF32;
-      p.h_out = hA;
-      if (xchg) p.xchg = exchange(2 * (cfg_.layers - 1) + 1);  // also carries the argmax keys
-    } else {
-      p.prologue = tmc::kProF16Norm;
-      p.x = hA;
-    }
-    p.x_stride = H;
-    p.gamma = hp(finalNorm_);
-    p.eps = cfg_.epsilon;
-    p.epilogue = tmc::kEpiArgmax;
-    p.y_f32 = fp(logits_);  // this rank's vocabulary slice
-    p.y_stride = vL_;
-    p.argmax_keys = static_cast<unsigned long long *>(argmaxKeys_->data());
-    p.argmax_counter = static_cast<unsigned int *>(argmaxCounter_->data());
-    p.vocab_offset = cfg_.tpRank * vL_;
-    p.status = status;
-    if (!tp || xchg) {
-      p.next_tokens = static_cast<int *>(nextTokens_->data());
-      if (feed) {
-        p.feed_tokens = tokens;
-        p.feed_positions = positions;
-        p.history = static_cast<int *>(history_->data());
-        p.history_counter = static_cast<unsigned int *>(historyCounter_->data());
-      }
-    }
-    p.trace = traceSink(0, kind);
-    p.work_counter = workCounter(0, kind);
-      p.l2_prefetch_bytes = kL2PrefetchBytes;
+      const tmc::GemvParams p = projection(kind, 0, R, feed);
       if (auto pe = launchProjection(p, "lm head projection"); !pe.empty()) return pe;
-    if (tp && !xchg) {
-      if ((e = collective_->allReduceMaxU64(p.argmax_keys, R, s)) != cudaSuccess)
-        return "allreduce (argmax): " + collective_->lastError();
-      if ((e = tmc::launch_argmax_finalize(p.argmax_keys, R, static_cast<int *>(nextTokens_->data()),
-                                           feed ? tokens : nullptr, feed ? positions : nullptr,
-                                           feed ? static_cast<int *>(history_->data()) : nullptr,
-                                           feed ? static_cast<unsigned int *>(historyCounter_->data()) : nullptr,
-                                           s, false)) != cudaSuccess)
-        return cudaText("argmax finalize", e);
+      if (tp && !xchg) {
+        if ((e = collective_->allReduceMaxU64(p.argmax_keys, R, s)) != cudaSuccess)
+          return "allreduce (argmax): " + collective_->lastError();
+        if ((e = tmc::launch_argmax_finalize(p.argmax_keys, R, static_cast<int *>(nextTokens_->data()),
+                                             feed ? tokens : nullptr, feed ? positions : nullptr,
+                                             feed ? static_cast<int *>(history_->data()) : nullptr,
+                                             feed ? static_cast<unsigned int *>(historyCounter_->data()) : nullptr,
+                                             s, false)) != cudaSuccess)
+          return cudaText("argmax finalize", e);
+      }
+      return {};
     }
-
+    case kKernelStream: {
+      const tmc::StreamParams sp = streamParams(l, feed);
+      if ((e = tmc::launch_layer_stream(sp, s, pdl, numSms_)) != cudaSuccess) return cudaText("layer stream", e);
       return {};
     }
     default:
@@ -1071,6 +1082,16 @@ std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct) {
   const bool tp = cfg_.tpSize > 1;
   if (tp && !collective_ && !peersAttached_)
     return "tensor parallelism needs a collective (setCollective) or attached peers (attachPeers).";
+  if (streamEligible(R)) {
+    // Layer 0's QKV, then per layer its attention and one streaming kernel
+    // (O, gate/up, down and the next layer's QKV, or the LM head).
+    auto e = enqueueKernel(kKernelQKV, 0, R, feed, distinct);
+    for (int l = 0; l < cfg_.layers && e.empty(); ++l) {
+      e = enqueueKernel(kKernelAttention, l, R, feed, distinct);
+      if (e.empty()) e = enqueueKernel(kKernelStream, l, R, feed, distinct);
+    }
+    return e;
+  }
   for (int l = 0; l < cfg_.layers; ++l)
     for (int kind = kKernelQKV; kind <= kKernelDown; ++kind) {
       auto e = enqueueKernel(kind, l, R, feed, distinct);
@@ -1131,8 +1152,9 @@ std::string DecoderExecutor::readTrace(std::vector<tmc::TraceRecord> *out) {
 
 std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *avgUs,
                                            double *bytesPerLaunch, int *launchesPerStep) {
-  if (kind < kKernelQKV || kind > kKernelLMHead) return "unknown kernel kind";
+  if (kind < kKernelQKV || kind > kKernelStream) return "unknown kernel kind";
   if (R < 1 || R > cfg_.maxRows || rounds < 1) return "profileKernel: bad rows or rounds";
+  if (kind == kKernelStream && !streamEligible(R)) return "profileKernel: this step does not use the streaming kernel";
   if (cfg_.tpSize > 1 && (kind == kKernelO || kind == kKernelDown))
     return "profileKernel: row-parallel kernels include a collective under TP";
   const double H = cfg_.hidden, D = cfg_.headDim;
@@ -1159,8 +1181,19 @@ std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *
     case kKernelLMHead:
       bytes = 2.0 * vL_ * H + 2.0 * R * H + 2.0 * H + 4.0 * R * vL_;
       break;
+    case kKernelStream: {
+      // One launch per layer: O + gate/up + down + the next layer's QKV (the
+      // last layer's launch: the LM head instead); bytes averaged over layers.
+      const double o = 2.0 * H * hqL_ * D + 2.0 * hqL_ * D + 2.0 * 2.0 * H;
+      const double gu = 2.0 * 2.0 * iL_ * H + 2.0 * H + 2.0 * H + 2.0 * iL_;
+      const double down = 2.0 * H * iL_ + 2.0 * iL_ + 2.0 * 2.0 * H;
+      const double qkv = 2.0 * qkvRows_ * H + 2.0 * H + 2.0 * H + 2.0 * qkvRows_;
+      const double head = 2.0 * vL_ * H + 2.0 * H + 2.0 * H + 4.0 * vL_;
+      bytes = o + gu + down + ((cfg_.layers - 1) * qkv + head) / cfg_.layers;
+      break;
+    }
   }
-  const int perRound = kind == kKernelLMHead ? 1 : cfg_.layers;
+  const int perRound = kind == kKernelLMHead ? 1 : cfg_.layers;  // the stream kind: one launch per layer
   cudaStream_t s = rt_.stream();
   auto sync = rt_.synchronize();
   if (!sync.empty()) return sync;

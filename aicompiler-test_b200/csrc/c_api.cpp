@@ -72,7 +72,7 @@ extern "C" {
 
 const char *tmc_cuda_last_error(void) { return g_last_error.c_str(); }
 
-int tmc_cuda_abi_version(void) { return 1; }
+int tmc_cuda_abi_version(void) { return 2; }
 
 int tmc_cuda_device_count(int *count) {
   if (count == nullptr) return fail(TMC_ERR_INVALID, "count is null");

@@ -76,18 +76,6 @@ __device__ __forceinline__ void store8(__half *dst, const float (&f)[8]) {
   *reinterpret_cast<uint4 *>(dst) = u;
 }
 
-__device__ __forceinline__ float dot8(const uint4 w, const float (&x)[8], float acc) {
-  float2 a = half2_bits_to_float2(w.x);
-  acc = fmaf(a.x, x[0], acc); acc = fmaf(a.y, x[1], acc);
-  a = half2_bits_to_float2(w.y);
-  acc = fmaf(a.x, x[2], acc); acc = fmaf(a.y, x[3], acc);
-  a = half2_bits_to_float2(w.z);
-  acc = fmaf(a.x, x[4], acc); acc = fmaf(a.y, x[5], acc);
-  a = half2_bits_to_float2(w.w);
-  acc = fmaf(a.x, x[6], acc); acc = fmaf(a.y, x[7], acc);
-  return acc;
-}
-
 // Stage the M activation rows (after the fused prologue) into shared memory.
 // K is a multiple of 8 (checked on the host).
 // `writer`: this CTA writes the residual-stream rows back to h_out (one CTA
@@ -400,7 +388,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
             float xv[8];
             XLoad<XS>::get(xs + (size_t)m * p.K, c, xv);
 #pragma unroll
-            for (int r = 0; r < R; ++r) acc[r][m] = dot8(w[r][u], xv, acc[r][m]);
+            for (int r = 0; r < R; ++r) acc[r][m] = gemv_dot8(w[r][u], xv, acc[r][m]);
           }
         }
       }

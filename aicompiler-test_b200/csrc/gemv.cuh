@@ -141,6 +141,21 @@ struct GemvParams {
   PeerExchange xchg;
 };
 
+// One 16-byte chunk (8 fp16 weights) of a row against 8 staged activations,
+// accumulated in element order with fused multiply-adds. Every kernel that
+// computes decode-GEMV rows uses this, so their per-row sums agree bit for bit.
+__device__ __forceinline__ float gemv_dot8(const uint4 w, const float (&x)[8], float acc) {
+  float2 a = half2_bits_to_float2(w.x);
+  acc = fmaf(a.x, x[0], acc); acc = fmaf(a.y, x[1], acc);
+  a = half2_bits_to_float2(w.y);
+  acc = fmaf(a.x, x[2], acc); acc = fmaf(a.y, x[3], acc);
+  a = half2_bits_to_float2(w.z);
+  acc = fmaf(a.x, x[4], acc); acc = fmaf(a.y, x[5], acc);
+  a = half2_bits_to_float2(w.w);
+  acc = fmaf(a.x, x[6], acc); acc = fmaf(a.y, x[7], acc);
+  return acc;
+}
+
 constexpr int kGemvPools = 8;
 constexpr int kGemvPoolStride = 32;
 constexpr int kGemvCounterWords = (kGemvPools + 1) * kGemvPoolStride;

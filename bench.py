@@ -260,7 +260,13 @@ def run_ours(args, world, rank, local):
     kernels = {}
     roofline = None
     if not args.no_kernels:
-        for kind in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head"):
+        # "stream": the layer streaming kernel the bs1 step runs (O + gate/up +
+        # down + next QKV per launch); the GEMV kinds are the same projections
+        # as separate launches (the path of batched steps and of TP).
+        kinds = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head"]
+        if dec.kernels_per_step(1) == 1 + 2 * args.layers:
+            kinds.append("stream")
+        for kind in kinds:
             if world > 1 and kind in ("o_proj", "down"):
                 continue
             us, b, n = dec.profile_kernel(kind, rows=1, rounds=4)
@@ -268,15 +274,17 @@ def run_ours(args, world, rank, local):
                              "gbs": round(b / us / 1e3, 1), "frac_of_peak": round(b / us / 1e3 / hbm, 3)}
         dom = max(kernels, key=lambda k: kernels[k]["us"] * kernels[k]["launches_per_step"])
         d = kernels[dom]
-        # DRAM bytes of one launch of the dominant kernel from the committed ncu
-        # summary (profiles/gemv_gate_up_down_8b_bs1.md), if it covers it.
+        # DRAM bytes of one launch of the dominant kernel from a committed ncu
+        # summary under profiles/ (a "traffic_bytes_per_launch <kind>: N" line).
         traffic = None
-        tpath = os.path.join(ROOT, "profiles", "gemv_gate_up_down_8b_bs1.md")
-        if os.path.exists(tpath) and world == 1:
-            for line in open(tpath):
-                if line.startswith(f"traffic_bytes_per_launch {dom}:"):
-                    traffic = int(line.split(":")[1])
-        roofline = {"kernel": f"gemv {dom}" if dom != "attention" else "attention", "bound": "hbm",
+        if world == 1:
+            import glob
+            for tpath in sorted(glob.glob(os.path.join(ROOT, "profiles", "*.md"))):
+                for line in open(tpath):
+                    if line.startswith(f"traffic_bytes_per_launch {dom}:"):
+                        traffic = int(line.split(":")[1])
+        names = {"attention": "attention", "stream": "layer stream (O + gate/up + down + next QKV or LM head)"}
+        roofline = {"kernel": names.get(dom, f"gemv {dom}"), "bound": "hbm",
                     "achieved": d["gbs"], "peak": hbm, "unit": "GB/s", "frac": d["frac_of_peak"],
                     "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                     "bytes_per_launch": d["bytes"], "launch_us": d["us"]}
