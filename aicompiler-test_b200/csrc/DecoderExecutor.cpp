@@ -969,8 +969,12 @@ tmc::StreamParams DecoderExecutor::streamParams(int l, bool feed) const {
   s.phase[1] = projection(kKernelGateUp, l, 1, feed);
   s.phase[2] = projection(kKernelDown, l, 1, feed);
   s.phase[3] = l + 1 < cfg_.layers ? projection(kKernelQKV, l + 1, 1, feed) : projection(kKernelLMHead, 0, 1, feed);
-  // One record per CTA, under the O projection's tag (kind 2 of layer l).
   s.sync = static_cast<unsigned int *>(streamSync_->data()) + (size_t)l * tmc::kStreamSyncWords;
+  if (l + 1 < cfg_.layers) {
+    s.next_w = hp(layers_[l + 1].o);
+    s.next_rows = cfg_.hidden;
+    s.next_k = hqL_ * cfg_.headDim;
+  }
   return s;
 }
 

@@ -4,22 +4,20 @@
 // KV append) or, after the last layer, the LM head (+ final RMSNorm, argmax).
 //
 // Why: at one token per step every projection is a weight stream (about 1
-// flop per byte), and the step's time goes to the gaps between them -- each
-// kernel boundary costs a dependency hand-off of a few microseconds and each
-// small GEMV a ramp-up and a tail. Here one CTA per SM runs all four phases,
-// separated by bounded grid barriers, and every warp streams its weight rows
-// into a shared-memory ring with 1-D bulk copies (cp.async.bulk) issued ahead
-// of its consumption: the copies for the next phase are in flight while the
-// warp waits at the barrier for the activations the phase needs, so HBM keeps
-// streaming through the dependency. Per step: 1 QKV GEMV, then per layer one
-// attention kernel and one of these (65 launches for 32 layers instead of 161).
+// flop per byte), and a separate kernel per projection pays a launch and a
+// dependency hand-off at every boundary. Here one grid (two CTAs of 8 warps
+// per SM, every CTA resident) runs the four phases of the decode GEMV's own
+// loop (gemv.cu) back to back, separated by bounded grid barriers: before a
+// phase's inputs exist, each warp already holds its first batch of weights in
+// registers and has bulk-prefetched its share into L2 -- what the GEMV does
+// before its programmatic-dependency wait -- so the barrier replaces a kernel
+// boundary. Per step: 1 QKV GEMV, then per layer one attention kernel and one
+// of these (65 launches for 32 layers instead of 161). At the end of a launch
+// the next layer's O weights are prefetched into L2 while attention runs.
 //
-// Arithmetic: every output row is computed exactly as the decode GEMV computes
-// it for one token (gemv.cu): the same RMSNorm prologue (256 threads, same
-// sum order and block reduction), the lane of a warp accumulating the 16-byte
-// chunks lane, lane + 32, ... of the row in order, the same butterfly
-// reduction and the same epilogue functions -- so the two paths give
-// bit-identical results and either may serve any step.
+// Arithmetic: each phase is the GEMV's code for one row (prologue, lane chunk
+// order, reductions, epilogue functions), so the two paths give bit-identical
+// results and either may serve any step.
 #pragma once
 
 #include "gemv.cuh"
@@ -36,10 +34,17 @@ struct StreamParams {
   // head (kProF16Norm, kEpiArgmax). M = 1 in every phase.
   GemvParams phase[kStreamPhases];
   unsigned int *sync;  // kStreamSyncWords words, zero before the launch; left zero
+  // The next launch's first weights (the next layer's O projection, [rows,
+  // k] fp16), pulled into L2 once this launch has issued all of its own
+  // loads, so they stream from HBM while the attention kernel in between
+  // runs; null after the last layer.
+  const __half *next_w;
+  int next_rows, next_k;
 };
 
-// False when the phases' shapes do not fit the kernel (largest K staged in
-// shared memory next to a ring of at least two stages per warp).
+// False when the phases do not fit the kernel (one row, no peer exchange, the
+// O / gate-up / down / QKV-or-LM-head epilogues, staged activations within
+// the GEMV's shared-memory budget).
 bool layer_stream_fits(const StreamParams &p);
 cudaError_t launch_layer_stream(const StreamParams &p, cudaStream_t stream, bool pdl, int num_sms);
 
