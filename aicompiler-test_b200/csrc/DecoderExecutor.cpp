@@ -223,10 +223,6 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)R * hkvL_, I32, &attnCounters_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)cfg_.layers * 6 * tmc::kGemvCounterWords, I32, &workCounters_, &activationBytes_)).empty())
     return e;
-  if (!(e = make((size_t)cfg_.layers * tmc::kStreamSyncWords, I32, &streamSync_, &activationBytes_)).empty())
-    return e;
-  streamOk_ = cfg_.useStream && cfg_.tpSize == 1 && tmc::layer_stream_fits(streamParams(0, false)) &&
-              tmc::layer_stream_fits(streamParams(cfg_.layers - 1, false));
   // Zero the state the kernels expect zero (int32 buffers were zero-filled by
   // createBuffer); residual-stream buffers start at zero too.
   cudaStream_t s0 = rt_.stream();
@@ -741,7 +737,6 @@ std::string DecoderExecutor::restoreKV(int slot, std::size_t length,
 // ---- step --------------------------------------------------------------------
 
 int DecoderExecutor::kernelsPerStep(int rows) const {
-  if (streamEligible(rows)) return 1 + 2 * cfg_.layers;
   const bool tp = cfg_.tpSize > 1;
   // Batched steps add a prologue kernel before the QKV, gate/up and LM-head projections.
   const int perLayer = rows > kGemvMaxRows ? 7 : 5;
@@ -959,25 +954,6 @@ tmc::GemvParams DecoderExecutor::projection(int kind, int l, int R, bool feed) c
   return p;
 }
 
-bool DecoderExecutor::streamEligible(int R) const {
-  return streamOk_ && R == 1 && cfg_.tpSize == 1;
-}
-
-tmc::StreamParams DecoderExecutor::streamParams(int l, bool feed) const {
-  tmc::StreamParams s{};
-  s.phase[0] = projection(kKernelO, l, 1, feed);
-  s.phase[1] = projection(kKernelGateUp, l, 1, feed);
-  s.phase[2] = projection(kKernelDown, l, 1, feed);
-  s.phase[3] = l + 1 < cfg_.layers ? projection(kKernelQKV, l + 1, 1, feed) : projection(kKernelLMHead, 0, 1, feed);
-  s.sync = static_cast<unsigned int *>(streamSync_->data()) + (size_t)l * tmc::kStreamSyncWords;
-  if (l + 1 < cfg_.layers) {
-    s.next_w = hp(layers_[l + 1].o);
-    s.next_rows = cfg_.hidden;
-    s.next_k = hqL_ * cfg_.headDim;
-  }
-  return s;
-}
-
 std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bool distinct) {
   cudaStream_t s = rt_.stream();
   const bool pdl = cfg_.usePDL;
@@ -1072,11 +1048,6 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       }
       return {};
     }
-    case kKernelStream: {
-      const tmc::StreamParams sp = streamParams(l, feed);
-      if ((e = tmc::launch_layer_stream(sp, s, pdl, numSms_)) != cudaSuccess) return cudaText("layer stream", e);
-      return {};
-    }
     default:
       return "unknown kernel kind";
   }
@@ -1086,16 +1057,6 @@ std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct) {
   const bool tp = cfg_.tpSize > 1;
   if (tp && !collective_ && !peersAttached_)
     return "tensor parallelism needs a collective (setCollective) or attached peers (attachPeers).";
-  if (streamEligible(R)) {
-    // Layer 0's QKV, then per layer its attention and one streaming kernel
-    // (O, gate/up, down and the next layer's QKV, or the LM head).
-    auto e = enqueueKernel(kKernelQKV, 0, R, feed, distinct);
-    for (int l = 0; l < cfg_.layers && e.empty(); ++l) {
-      e = enqueueKernel(kKernelAttention, l, R, feed, distinct);
-      if (e.empty()) e = enqueueKernel(kKernelStream, l, R, feed, distinct);
-    }
-    return e;
-  }
   for (int l = 0; l < cfg_.layers; ++l)
     for (int kind = kKernelQKV; kind <= kKernelDown; ++kind) {
       auto e = enqueueKernel(kind, l, R, feed, distinct);
@@ -1156,9 +1117,8 @@ std::string DecoderExecutor::readTrace(std::vector<tmc::TraceRecord> *out) {
 
 std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *avgUs,
                                            double *bytesPerLaunch, int *launchesPerStep) {
-  if (kind < kKernelQKV || kind > kKernelStream) return "unknown kernel kind";
+  if (kind < kKernelQKV || kind > kKernelLMHead) return "unknown kernel kind";
   if (R < 1 || R > cfg_.maxRows || rounds < 1) return "profileKernel: bad rows or rounds";
-  if (kind == kKernelStream && !streamEligible(R)) return "profileKernel: this step does not use the streaming kernel";
   if (cfg_.tpSize > 1 && (kind == kKernelO || kind == kKernelDown))
     return "profileKernel: row-parallel kernels include a collective under TP";
   const double H = cfg_.hidden, D = cfg_.headDim;
@@ -1185,19 +1145,8 @@ std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *
     case kKernelLMHead:
       bytes = 2.0 * vL_ * H + 2.0 * R * H + 2.0 * H + 4.0 * R * vL_;
       break;
-    case kKernelStream: {
-      // One launch per layer: O + gate/up + down + the next layer's QKV (the
-      // last layer's launch: the LM head instead); bytes averaged over layers.
-      const double o = 2.0 * H * hqL_ * D + 2.0 * hqL_ * D + 2.0 * 2.0 * H;
-      const double gu = 2.0 * 2.0 * iL_ * H + 2.0 * H + 2.0 * H + 2.0 * iL_;
-      const double down = 2.0 * H * iL_ + 2.0 * iL_ + 2.0 * 2.0 * H;
-      const double qkv = 2.0 * qkvRows_ * H + 2.0 * H + 2.0 * H + 2.0 * qkvRows_;
-      const double head = 2.0 * vL_ * H + 2.0 * H + 2.0 * H + 4.0 * vL_;
-      bytes = o + gu + down + ((cfg_.layers - 1) * qkv + head) / cfg_.layers;
-      break;
-    }
   }
-  const int perRound = kind == kKernelLMHead ? 1 : cfg_.layers;  // the stream kind: one launch per layer
+  const int perRound = kind == kKernelLMHead ? 1 : cfg_.layers;
   cudaStream_t s = rt_.stream();
   auto sync = rt_.synchronize();
   if (!sync.empty()) return sync;

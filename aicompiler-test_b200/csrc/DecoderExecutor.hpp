@@ -39,7 +39,6 @@
 #include "common.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
-#include "layer_stream.cuh"
 
 namespace tensor::runtime {
 
@@ -62,11 +61,6 @@ struct DecoderConfig {
   int tpSize = 1;
   bool useGraphs = true;
   bool usePDL = true;
-  // Single-token steps (one row) through the layer streaming kernel
-  // (layer_stream.cuh) when the shapes fit and there is no tensor
-  // parallelism; otherwise one GEMV per projection. Both compute every row
-  // identically.
-  bool useStream = true;
 };
 
 // Cross-rank sum/max used by tensor parallelism (implemented over NCCL).
@@ -93,7 +87,6 @@ class DecoderExecutor {
     kKernelGateUp = 3,
     kKernelDown = 4,
     kKernelLMHead = 5,
-    kKernelStream = 6,  // O, gate/up, down and the next QKV (or the LM head) of one layer
   };
   static std::unique_ptr<DecoderExecutor> create(cuda::CudaRuntime &runtime, const DecoderConfig &config,
                                                  std::string *error);
@@ -214,9 +207,6 @@ class DecoderExecutor {
   // The GEMV / GEMM parameters of one projection (kinds QKV, O, gate/up,
   // down, LM head) of layer `layer` for `rows` rows.
   tmc::GemvParams projection(int kind, int layer, int rows, bool feed) const;
-  // Steps of `rows` rows run through the layer streaming kernel.
-  bool streamEligible(int rows) const;
-  tmc::StreamParams streamParams(int layer, bool feed) const;
   std::string launchStep(int rows, bool feed, bool distinct);
   // Step graphs differ by rows, feed-back, distinct rows and the attention
   // split cap the step's contexts need.
@@ -255,8 +245,6 @@ class DecoderExecutor {
   cuda::BufferHandle nextTokens_, argmaxKeys_, argmaxCounter_, history_, historyCounter_;
   cuda::BufferHandle attnWorkspace_, attnCounters_;
   cuda::BufferHandle workCounters_;  // per launch site: tmc::kGemvCounterWords uints
-  cuda::BufferHandle streamSync_;    // per layer: tmc::kStreamSyncWords uints (grid barrier, exit count)
-  bool streamOk_ = false;            // the streaming kernel fits this decoder's shapes
   unsigned int *workCounter(int layer, int kind) const;
   std::int32_t *pinnedIO_ = nullptr;   // host staging [3 * maxRows + maxRows]
   // Page spill / restore: device array of the 2 * layers pool pointers, page-id

@@ -44,7 +44,6 @@ enum : int {
   kWhereMisc = 6,
   kWhereGemm = 7,
   kWhereExchange = 8,  // a peer's flag did not arrive in time (info0 = source rank)
-  kWhereStream = 9,    // the layer streaming kernel (info0 = phase, info1 = CTA)
 };
 
 __device__ __forceinline__ void report_status(TmcDeviceStatus *s, int code, int where,

@@ -76,7 +76,6 @@ int tmc_decoder_create(tmc_runtime *rt, const tmc_decoder_config *c, tmc_decoder
   cfg.tpSize = c->tp_size > 0 ? c->tp_size : 1;
   cfg.useGraphs = c->use_graphs != 0;
   cfg.usePDL = c->use_pdl != 0;
-  cfg.useStream = c->use_stream != 0;
   std::string err;
   auto ex = DecoderExecutor::create(*rt->rt, cfg, &err);
   if (!ex) return fail(err.find("cudaMalloc") != std::string::npos ? TMC_ERR_OUT_OF_MEMORY : TMC_ERR_INVALID, err);

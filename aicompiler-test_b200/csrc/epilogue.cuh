@@ -117,7 +117,7 @@ __device__ __forceinline__ void epilogue_one(const GemvParams &p, int row, int m
   } else if (epi == kEpiF16) {
     p.y_f16[idx] = __float2half_rn(v);
   } else if (epi == kEpiResidual) {
-    p.y_f16[idx] = residual_value(__ldcg(p.residual + idx), v);  // L2-coherent: see stage_x
+    p.y_f16[idx] = residual_value(p.residual[idx], v);
   }
 }
 

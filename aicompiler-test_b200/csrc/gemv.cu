@@ -15,7 +15,6 @@
 //    previous kernel in the decode graph.
 #include "gemv.cuh"
 #include "epilogue.cuh"
-#include "layer_stream.cuh"
 
 #include <mutex>
 #include <unordered_map>
@@ -147,15 +146,7 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
         float ss = 0.0f;
         for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
           float hv[8], f[8], pv[8];
-          {
-            // L2-coherent: within a multi-phase kernel other SMs wrote h.
-            const uint4 u = __ldcg(reinterpret_cast<const uint4 *>(hrow) + v);
-            float2 f2;
-            f2 = half2_bits_to_float2(u.x); hv[0] = f2.x; hv[1] = f2.y;
-            f2 = half2_bits_to_float2(u.y); hv[2] = f2.x; hv[3] = f2.y;
-            f2 = half2_bits_to_float2(u.z); hv[4] = f2.x; hv[5] = f2.y;
-            f2 = half2_bits_to_float2(u.w); hv[6] = f2.x; hv[7] = f2.y;
-          }
+          XLoad<__half>::get(hrow, v, hv);
           if (exchanged) {
             // Rank-ordered sum of the slots (L2 loads: peers wrote them).
 #pragma unroll
@@ -168,8 +159,8 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
               pv[4] += b.x; pv[5] += b.y; pv[6] += b.z; pv[7] += b.w;
             }
           } else {
-            const float4 a = __ldcg(reinterpret_cast<const float4 *>(prow) + 2 * v);
-            const float4 b = __ldcg(reinterpret_cast<const float4 *>(prow) + 2 * v + 1);
+            const float4 a = reinterpret_cast<const float4 *>(prow)[2 * v];
+            const float4 b = reinterpret_cast<const float4 *>(prow)[2 * v + 1];
             pv[0] = a.x; pv[1] = a.y; pv[2] = a.z; pv[3] = a.w;
             pv[4] = b.x; pv[5] = b.y; pv[6] = b.z; pv[7] = b.w;
           }
@@ -216,9 +207,7 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
       float ss = 0.0f;
 #pragma unroll 2
       for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-        // L2-coherent loads: in the layer chain kernel the activations were
-        // written earlier in the same launch by other SMs.
-        const uint4 raw = src != nullptr ? __ldcg(reinterpret_cast<const uint4 *>(src) + v) : make_uint4(0, 0, 0, 0);
+        const uint4 raw = src != nullptr ? reinterpret_cast<const uint4 *>(src)[v] : make_uint4(0, 0, 0, 0);
         if (write_h) reinterpret_cast<uint4 *>(p.h_out + (size_t)m * K)[v] = raw;
         float f[8];
         float2 t;
@@ -556,194 +545,6 @@ __global__ void __launch_bounds__(kThreads) row_prologue_kernel(const GemvParams
   for (int v = threadIdx.x; v < (p.K >> 3); v += blockDim.x) dst[v] = src[v];
 }
 
-// ---- layer chain: the single-token GEMVs of one layer boundary, persistent --
-// (interface and rationale in layer_stream.cuh). The GEMV's own loop for
-// M = 1, R = 2, U = 8, one-warp teams: per phase the first batch of a warp's
-// first row group is loaded into registers and its share of the weights
-// bulk-prefetched into L2 before the phase's inputs are ready, exactly as the
-// GEMV kernel does before its programmatic-dependency wait; here the wait is
-// a grid barrier after the previous phase instead of a kernel boundary.
-constexpr int kChainR = 2, kChainU = 8;
-constexpr unsigned long long kChainBarrierNs = 2ull * 1000 * 1000 * 1000;
-
-__device__ __forceinline__ void chain_load_batch(const GemvParams &p, int g, int c0, int lane,
-                                                 uint4 (&w)[kChainR][kChainU]) {
-  const int row0 = g * kChainR;
-  const int c_hi = p.K >> 3;
-#pragma unroll
-  for (int r = 0; r < kChainR; ++r) {
-    const bool rv = row0 + r < p.N;
-    const uint4 *wr = reinterpret_cast<const uint4 *>(p.W + (size_t)(rv ? row0 + r : row0) * p.K);
-#pragma unroll
-    for (int u = 0; u < kChainU; ++u) {
-      const int c = c0 + u * 32 + lane;
-      w[r][u] = (c < c_hi && rv) ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
-    }
-  }
-}
-
-// Before a phase's inputs exist: the warp's first batch into registers and
-// its static share of the weights into L2 (up to p.l2_prefetch_bytes per
-// phase over the whole grid).
-__device__ __forceinline__ void chain_preload(const GemvParams &p, int gt, int total_teams, int lane,
-                                              uint4 (&w)[kChainR][kChainU]) {
-  const int ngroups = (p.N + kChainR - 1) / kChainR;
-  if (gt < ngroups) chain_load_batch(p, gt, 0, lane, w);
-  if (p.l2_prefetch_bytes > 0 && lane == 0) {
-    const long long per_warp = p.l2_prefetch_bytes / total_teams;
-    const uint32_t slice = static_cast<uint32_t>(p.K >> 3) * 16u;
-    long long budget = per_warp;
-    for (int gg = gt; gg < ngroups && budget > 0; gg += total_teams) {
-#pragma unroll
-      for (int r = 0; r < kChainR; ++r) {
-        const int row = gg * kChainR + r;
-        if (row >= p.N || budget <= 0) continue;
-        prefetch_bulk_l2(p.W + (size_t)row * p.K, slice);
-        budget -= slice;
-      }
-    }
-  }
-}
-
-// One phase: the GEMV main loop over row groups (static first group, then
-// dynamic tickets when the phase is large enough), epilogue per group.
-template <typename XS>
-__device__ __forceinline__ void chain_phase(const GemvParams &p, XS *xs, float *red, int lane, int gt,
-                                            int total_teams, uint4 (&w)[kChainR][kChainU],
-                                            unsigned long long (&best)[1]) {
-  constexpr int R = kChainR, U = kChainU;
-  const int ngroups = (p.N + R - 1) / R;
-  const int c_hi = p.K >> 3;
-  const bool dynamic = p.work_counter != nullptr && total_teams % kGemvPools == 0 && ngroups > 2 * total_teams;
-  const int pool = gt % kGemvPools;
-  const int pool_base = total_teams / kGemvPools;
-  unsigned int *ticket = p.work_counter + pool * kGemvPoolStride;
-  int g = gt, c0 = 0, g_next = gt + total_teams, fetched = 0;
-  if (dynamic && lane == 0) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
-  stage_x<XS, 1>(p, xs, red, blockIdx.x == 0);
-  __syncthreads();
-  float acc[R][1];
-#pragma unroll
-  for (int r = 0; r < R; ++r) acc[r][0] = 0.0f;
-  while (g < ngroups) {
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u * 32 + lane;
-      if (c < c_hi) {
-        float xv[8];
-        XLoad<XS>::get(xs, c, xv);
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[r][0] = gemv_dot8(w[r][u], xv, acc[r][0]);
-      }
-    }
-    int ng = g, nc = c0 + 32 * U;
-    if (nc >= c_hi) {
-      nc = 0;
-      if (dynamic) {
-        ng = __shfl_sync(0xffffffffu, fetched, 0);
-        if (lane == 0 && ng < ngroups) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
-      } else {
-        ng = g_next;
-        g_next += total_teams;
-      }
-    }
-    if (ng < ngroups) chain_load_batch(p, ng, nc, lane, w);
-    if (nc == 0) {
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[r][0] = warp_sum(acc[r][0]);
-      epilogue<R, 1>(p, g * R, acc, lane, best);
-#pragma unroll
-      for (int r = 0; r < R; ++r) acc[r][0] = 0.0f;
-    }
-    g = ng;
-    c0 = nc;
-  }
-}
-
-// Grid barrier after `phase`: the phase's stores, then one arrival per CTA;
-// false if the other CTAs did not arrive within the budget.
-__device__ __forceinline__ bool chain_barrier(const StreamParams &P, int phase, int *flag) {
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(P.sync, 1u);
-    const unsigned int target = static_cast<unsigned int>(phase + 1) * gridDim.x;
-    *flag = wait_count_geq_gpu(P.sync, target, kChainBarrierNs) ? 0 : 1;
-    if (*flag) report_status(P.phase[0].status, kStatusWaitTimeout, kWhereStream, phase, blockIdx.x);
-  }
-  __syncthreads();
-  return *flag == 0;
-}
-
-template <typename XS>
-__global__ void __launch_bounds__(kThreads, 2) layer_chain_kernel(const StreamParams P) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  XS *xs = reinterpret_cast<XS *>(smem_raw);
-  __shared__ float red[32];
-  __shared__ unsigned long long warp_best[kWarps];
-  __shared__ int flag, is_last;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int total_teams = kWarps * gridDim.x;
-  const int gt = warp * gridDim.x + blockIdx.x;
-  uint4 w[kChainR][kChainU];
-  unsigned long long best[1] = {0ull};
-  if (threadIdx.x == 0) flag = 0;
-  chain_preload(P.phase[0], gt, total_teams, lane, w);
-  pdl_wait();
-  pdl_launch_dependents();
-  bool ok = true;
-#pragma unroll
-  for (int ph = 0; ph < kStreamPhases; ++ph) {
-    if (ph > 0 && !chain_barrier(P, ph - 1, &flag)) {
-      ok = false;
-      break;
-    }
-    const bool traced = P.phase[ph].trace.records != nullptr;
-    const unsigned long long t0 = traced ? global_ns() : 0ull;
-    chain_phase<XS>(P.phase[ph], xs, red, lane, gt, total_teams, w, best);
-    if (ph + 1 < kStreamPhases) chain_preload(P.phase[ph + 1], gt, total_teams, lane, w);
-    if (traced) {
-      __syncthreads();
-      trace_emit(P.phase[ph].trace, t0, t0);
-    }
-  }
-  if (ok && P.next_w != nullptr && lane == 0) {
-    // The next launch's O weights into L2 while the attention kernel runs.
-    const uint32_t slice = static_cast<uint32_t>(P.next_k >> 3) * 16u;
-    for (int row = gt; row < P.next_rows; row += total_teams)
-      prefetch_bulk_l2(P.next_w + (size_t)row * P.next_k, slice);
-  }
-  const GemvParams &last = P.phase[kStreamPhases - 1];
-  if (ok && last.epilogue == kEpiArgmax) {
-    if (lane == 0) warp_best[warp] = best[0];
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned long long b = 0ull;
-      for (int k = 0; k < kWarps; ++k) b = warp_best[k] > b ? warp_best[k] : b;
-      if (b != 0ull) atomicMax(last.argmax_keys, b);
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(last.argmax_counter, 1u) == gridDim.x - 1 ? 1 : 0;
-    __syncthreads();
-    if (is_last) {
-      __threadfence();
-      argmax_finalize(last, threadIdx.x, [] { __syncthreads(); });
-    }
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(P.sync + 32, 1u) == gridDim.x - 1) {
-    // The last CTA out resets the barrier and every phase's work tickets.
-    atomicExch(P.sync, 0u);
-    atomicExch(P.sync + 32, 0u);
-    for (int ph = 0; ph < kStreamPhases; ++ph) {
-      unsigned int *wc = P.phase[ph].work_counter;
-      if (wc == nullptr) continue;
-      for (int c = 0; c <= kGemvPools; ++c) atomicExch(wc + c * kGemvPoolStride, 0u);
-    }
-  }
-}
-
 template <typename XS, int M, int R, int U, int KS>
 cudaError_t launch_instance(const GemvParams &p, cudaStream_t stream, bool pdl, int num_sms) {
   auto kernel = gemv_kernel<XS, M, R, U, KS>;
@@ -936,80 +737,6 @@ cudaError_t launch_gemv(const GemvParams &p, cudaStream_t stream, bool pdl, int 
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
-}
-
-namespace {
-
-int chain_max_k(const StreamParams &p) {
-  int k = 0;
-  for (int q = 0; q < kStreamPhases; ++q) k = p.phase[q].K > k ? p.phase[q].K : k;
-  return k;
-}
-
-template <typename XS>
-cudaError_t launch_chain(const StreamParams &p, cudaStream_t stream, bool pdl, int num_sms) {
-  auto kernel = layer_chain_kernel<XS>;
-  const size_t smem = (size_t)chain_max_k(p) * sizeof(XS);
-  static std::mutex mu;
-  static std::unordered_map<long long, int> occ_cache;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  int occ = 0;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    const long long key = (static_cast<long long>(dev) << 40) | static_cast<long long>(smem);
-    auto it = occ_cache.find(key);
-    if (it != occ_cache.end()) {
-      occ = it->second;
-    } else {
-      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-      if (e != cudaSuccess) return e;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kThreads, smem);
-      if (e != cudaSuccess) return e;
-      occ_cache[key] = occ;
-    }
-  }
-  if (occ < 1) return cudaErrorInvalidConfiguration;
-  // Every CTA must be resident at once (grid barriers): one full wave, at
-  // most two CTAs per SM (the GEMV's occupancy).
-  const int per_sm = occ < 2 ? occ : 2;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(per_sm * num_sms);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kernel, p);
-}
-
-}  // namespace
-
-bool layer_stream_fits(const StreamParams &p) {
-  for (int q = 0; q < kStreamPhases; ++q) {
-    const GemvParams &g = p.phase[q];
-    if (g.M != 1 || g.K <= 0 || (g.K & 7) != 0 || g.N <= 0 || g.W == nullptr) return false;
-    if ((g.epilogue == kEpiSwiGLU || g.epilogue == kEpiQKV) && (g.N & 1)) return false;
-    if (g.prologue != kProF16 && g.prologue != kProF16Norm) return false;
-    if (g.xchg.world > 0) return false;
-  }
-  const GemvParams &o = p.phase[0], &d = p.phase[2];
-  if (o.epilogue != kEpiResidual || d.epilogue != kEpiResidual || p.phase[1].epilogue != kEpiSwiGLU) return false;
-  const int last = p.phase[3].epilogue;
-  if (last != kEpiQKV && last != kEpiArgmax) return false;
-  return (size_t)chain_max_k(p) * sizeof(__half) <= 200 * 1024;
-}
-
-cudaError_t launch_layer_stream(const StreamParams &p, cudaStream_t stream, bool pdl, int num_sms) {
-  if (!layer_stream_fits(p) || p.sync == nullptr) return cudaErrorInvalidValue;
-  // fp32 staging while it fits the GEMV's budget (the GEMV's own choice for
-  // one row), else fp16; both hold the same (fp16-rounded) values.
-  if ((size_t)chain_max_k(p) * 4 <= 64 * 1024) return launch_chain<float>(p, stream, pdl, num_sms);
-  return launch_chain<__half>(p, stream, pdl, num_sms);
 }
 
 }  // namespace tmc

@@ -408,7 +408,6 @@ class DecoderConfig(ctypes.Structure):
         ("capacity", c_int), ("epsilon", c_float), ("rope_theta", ctypes.c_double),
         ("max_rows", c_int), ("max_slots", c_int), ("page_size", c_int), ("pool_pages", c_int),
         ("tp_rank", c_int), ("tp_size", c_int), ("use_graphs", c_int), ("use_pdl", c_int),
-        ("use_stream", c_int),
     ]
 
 
@@ -597,12 +596,12 @@ class Decoder:
     def __init__(self, runtime: Runtime, hidden, heads, intermediate, vocab, layers, capacity,
                  kv_heads=None, head_dim=None, epsilon=1e-5, rope_theta=10000.0, max_rows=8,
                  max_slots=1, page_size=0, pool_pages=0, tp_rank=0, tp_size=1, use_graphs=True,
-                 use_pdl=True, use_stream=True):
+                 use_pdl=True):
         self.runtime = runtime
         cfg = DecoderConfig(hidden, heads, kv_heads or heads, head_dim or hidden // heads,
                             intermediate, vocab, layers, capacity, epsilon, rope_theta, max_rows,
                             max_slots, page_size, pool_pages, tp_rank, tp_size, int(use_graphs),
-                            int(use_pdl), int(use_stream))
+                            int(use_pdl))
         self.cfg = cfg
         h = c_void_p()
         check(lib.tmc_decoder_create(runtime.handle, ctypes.byref(cfg), ctypes.byref(h)))
@@ -729,7 +728,7 @@ class Decoder:
         c = _i32(context_lengths)
         return float(lib.tmc_decoder_step_bytes(self.handle, c.size, c.ctypes.data_as(_I32P)))
 
-    KERNELS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head", "stream")
+    KERNELS = ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head")
 
     def profile_kernel(self, kind, rows=1, rounds=4):
         """(mean launch us, algorithmic bytes per launch, launches per step)."""

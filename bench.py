@@ -260,13 +260,7 @@ def run_ours(args, world, rank, local):
     kernels = {}
     roofline = None
     if not args.no_kernels:
-        # "stream": the layer streaming kernel the bs1 step runs (O + gate/up +
-        # down + next QKV per launch); the GEMV kinds are the same projections
-        # as separate launches (the path of batched steps and of TP).
-        kinds = ["qkv", "attention", "o_proj", "gate_up", "down", "lm_head"]
-        if dec.kernels_per_step(1) == 1 + 2 * args.layers:
-            kinds.append("stream")
-        for kind in kinds:
+        for kind in ("qkv", "attention", "o_proj", "gate_up", "down", "lm_head"):
             if world > 1 and kind in ("o_proj", "down"):
                 continue
             us, b, n = dec.profile_kernel(kind, rows=1, rounds=4)
@@ -283,8 +277,7 @@ def run_ours(args, world, rank, local):
                 for line in open(tpath):
                     if line.startswith(f"traffic_bytes_per_launch {dom}:"):
                         traffic = int(line.split(":")[1])
-        names = {"attention": "attention", "stream": "layer stream (O + gate/up + down + next QKV or LM head)"}
-        roofline = {"kernel": names.get(dom, f"gemv {dom}"), "bound": "hbm",
+        roofline = {"kernel": f"gemv {dom}" if dom != "attention" else "attention", "bound": "hbm",
                     "achieved": d["gbs"], "peak": hbm, "unit": "GB/s", "frac": d["frac_of_peak"],
                     "traffic": traffic, "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)",
                     "bytes_per_launch": d["bytes"], "launch_us": d["us"]}

@@ -280,13 +280,6 @@ typedef struct {
   int pool_pages;    /* 0 = max_slots * ceil(capacity / page_size) */
   int tp_rank, tp_size;
   int use_graphs, use_pdl;
-  /* Single-token steps (one row, no tensor parallelism) through the layer
-   * streaming kernel: per layer one persistent kernel runs the O, gate/up and
-   * down projections and the next layer's QKV projection (the LM head after
-   * the last layer), streaming weights through shared memory across its grid
-   * barriers. 0 keeps one GEMV per projection; both give the same results bit
-   * for bit. Zero-initialised configs select the GEMVs. */
-  int use_stream;
 } tmc_decoder_config;
 
 typedef struct tmc_decoder tmc_decoder;
