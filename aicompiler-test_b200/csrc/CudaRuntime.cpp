@@ -299,13 +299,16 @@ SequencePreparationResult CudaRuntime::prepareSequence(
     return result;
   }
   cudaError_t launchError = cudaSuccess;
+  std::vector<const PreparedExecution *> earlier;
   for (const auto *step : steps) {
     if (step == nullptr) {
       launchError = cudaErrorInvalidValue;
       break;
     }
-    launchError = step->enqueue(stream_);
+    launchError = !earlier.empty() && step->canOverlapAfter(earlier) ? step->enqueueOverlapped(stream_)
+                                                                    : step->enqueue(stream_);
     if (launchError != cudaSuccess) break;
+    earlier.push_back(step);
   }
   e = cudaStreamEndCapture(stream_, &graph);
   if (launchError != cudaSuccess || e != cudaSuccess) {
@@ -368,6 +371,15 @@ PreparedExecution::PreparedExecution(CudaRuntime *runtime, Launch launch,
       inputs_(std::move(inputs)),
       outputs_(std::move(outputs)),
       name_(std::move(name)) {}
+
+bool PreparedExecution::canOverlapAfter(const std::vector<const PreparedExecution *> &earlier) const {
+  if (!overlap_) return false;
+  for (const auto *prev : earlier)
+    for (const auto &written : prev->outputs())
+      for (const auto &read : earlyReads_)
+        if (written == read) return false;
+  return true;
+}
 
 ExecutionResult PreparedExecution::execute() const {
   ExecutionResult result;

@@ -102,10 +102,26 @@ class PreparedExecution {
   [[nodiscard]] std::vector<std::vector<float>> readOutputs() const;
   [[nodiscard]] const std::string &name() const { return name_; }
   [[nodiscard]] cudaError_t enqueue(cudaStream_t stream) const { return launch_(stream); }
+  // Programmatic dependent launch inside a sequence: `overlapped` starts the
+  // kernel while its predecessor drains; it waits (griddepcontrol.wait)
+  // before reading anything an earlier launch wrote, except `earlyReads`
+  // (weights), which it may read before that wait.
+  void allowOverlap(Launch overlapped, std::vector<BufferHandle> earlyReads) {
+    overlap_ = std::move(overlapped);
+    earlyReads_ = std::move(earlyReads);
+  }
+  // True when this execution may overlap the end of its predecessor in a
+  // sequence whose earlier steps are `earlier`: it has an overlapped launch
+  // and no buffer it reads early is written by an earlier step.
+  [[nodiscard]] bool canOverlapAfter(const std::vector<const PreparedExecution *> &earlier) const;
+  [[nodiscard]] cudaError_t enqueueOverlapped(cudaStream_t stream) const { return overlap_(stream); }
+  [[nodiscard]] const std::vector<BufferHandle> &outputs() const { return outputs_; }
 
  private:
   CudaRuntime *runtime_;
   Launch launch_;
+  Launch overlap_;
+  std::vector<BufferHandle> earlyReads_;
   std::vector<BufferHandle> inputs_;
   std::vector<BufferHandle> outputs_;
   std::string name_;
@@ -118,6 +134,9 @@ struct PreparationResult {
 
 // A dependency-ordered chain captured once as a CUDA graph and replayed
 // (reference PreparedSequence: one Metal command buffer, MetalRuntime.mm:292-341).
+// Steps that allow it (PreparedExecution::canOverlapAfter) are captured with
+// programmatic dependent launch, so their weight loads overlap the previous
+// kernel's tail.
 class PreparedSequence {
  public:
   ~PreparedSequence();

@@ -10,6 +10,7 @@
 #include "fusion.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
+#include "graph_ops.cuh"
 #include "rmsnorm.cuh"
 
 namespace tensor::cuda {
@@ -98,7 +99,7 @@ std::string bindRmsnormGemv(CudaRuntime &, KernelBinding &b) {
   TMC_CHECK(requireCount(b.outputs[0], rows * n, "rmsnorm_gemv_f32", "y"));
   return {};
 }
-cudaError_t launchRmsnormGemv(const KernelBinding &b, cudaStream_t s) {
+cudaError_t launchRmsnormGemvImpl(const KernelBinding &b, cudaStream_t s, bool pdl) {
   tmc::GemvParams p{};
   p.W = static_cast<const __half *>(b.inputs[2]->data());
   p.M = (int)b.constants[0];
@@ -112,8 +113,10 @@ cudaError_t launchRmsnormGemv(const KernelBinding &b, cudaStream_t s) {
   p.epilogue = tmc::kEpiF32;
   p.y_f32 = static_cast<float *>(b.outputs[0]->data());
   p.y_stride = p.N;
-  return tmc::launch_gemv(p, s, false, b.numSms);
+  return tmc::launch_gemv(p, s, pdl, b.numSms);
 }
+cudaError_t launchRmsnormGemv(const KernelBinding &b, cudaStream_t s) { return launchRmsnormGemvImpl(b, s, false); }
+cudaError_t launchRmsnormGemvPdl(const KernelBinding &b, cudaStream_t s) { return launchRmsnormGemvImpl(b, s, true); }
 
 // ---- gemv_f16: x f16 [rows, k], W f16 [n, k] -> y f16 or f32 [rows, n] ----
 // constants {rows (1..8), k (% 8 == 0), n}
@@ -128,7 +131,7 @@ std::string bindGemv(CudaRuntime &, KernelBinding &b) {
   TMC_CHECK(requireCount(b.outputs[0], rows * n, "gemv_f16", "y"));
   return {};
 }
-cudaError_t launchGemv(const KernelBinding &b, cudaStream_t s) {
+cudaError_t launchGemvImpl(const KernelBinding &b, cudaStream_t s, bool pdl) {
   tmc::GemvParams p{};
   p.W = static_cast<const __half *>(b.inputs[1]->data());
   p.M = (int)b.constants[0];
@@ -145,8 +148,10 @@ cudaError_t launchGemv(const KernelBinding &b, cudaStream_t s) {
     p.y_f32 = static_cast<float *>(b.outputs[0]->data());
   }
   p.y_stride = p.N;
-  return tmc::launch_gemv(p, s, false, b.numSms);
+  return tmc::launch_gemv(p, s, pdl, b.numSms);
 }
+cudaError_t launchGemv(const KernelBinding &b, cudaStream_t s) { return launchGemvImpl(b, s, false); }
+cudaError_t launchGemvPdl(const KernelBinding &b, cudaStream_t s) { return launchGemvImpl(b, s, true); }
 
 // ---- batched_gemm_f16: x f16 [rows, k], W f16 [n, k] -> y f32 [rows, n] (tcgen05) ----
 // constants {rows (1..128), k (% 8 == 0), n}; the split-K workspace and tile
@@ -251,6 +256,68 @@ cudaError_t launchLinearRelu(const KernelBinding &b, cudaStream_t s) {
                                        (int)b.constants[2], b.inputs[0]->elementType() == ElementType::Float16, s);
 }
 
+// ---- generic graph nodes (graph_ops.cuh) ----
+// add / mul: x [rows, width], b [b_rows, width] -> y; constants {rows, width, b_rows}
+std::string bindBinary(const KernelBinding &b, const char *name) {
+  TMC_CHECK(uniformFloat(b, name));
+  const std::size_t rows = b.constants[0], width = b.constants[1], brows = b.constants[2];
+  if (rows < 1 || width < 1 || (brows != 1 && brows != rows)) return std::string(name) + ": b_rows must be 1 or rows.";
+  TMC_CHECK(requireCount(b.inputs[0], rows * width, name, "x"));
+  TMC_CHECK(requireCount(b.inputs[1], brows * width, name, "b"));
+  TMC_CHECK(requireCount(b.outputs[0], rows * width, name, "y"));
+  return {};
+}
+std::string bindAdd(CudaRuntime &, KernelBinding &b) { return bindBinary(b, "add"); }
+std::string bindMul(CudaRuntime &, KernelBinding &b) { return bindBinary(b, "mul"); }
+cudaError_t launchBinary(const KernelBinding &b, cudaStream_t s, bool mul) {
+  return tmc::launch_graph_binary(b.inputs[0]->data(), b.inputs[1]->data(), b.outputs[0]->data(), (int)b.constants[0],
+                                  (int)b.constants[1], (int)b.constants[2], mul,
+                                  b.inputs[0]->elementType() == ElementType::Float16, s);
+}
+cudaError_t launchAdd(const KernelBinding &b, cudaStream_t s) { return launchBinary(b, s, false); }
+cudaError_t launchMul(const KernelBinding &b, cudaStream_t s) { return launchBinary(b, s, true); }
+
+// relu / silu: x -> y; constants {count}
+std::string bindUnary(const KernelBinding &b, const char *name) {
+  TMC_CHECK(uniformFloat(b, name));
+  const std::size_t count = b.constants[0];
+  if (count < 1) return std::string(name) + ": count must be positive.";
+  TMC_CHECK(requireCount(b.inputs[0], count, name, "x"));
+  TMC_CHECK(requireCount(b.outputs[0], count, name, "y"));
+  return {};
+}
+std::string bindRelu(CudaRuntime &, KernelBinding &b) { return bindUnary(b, "relu"); }
+std::string bindSilu(CudaRuntime &, KernelBinding &b) { return bindUnary(b, "silu"); }
+cudaError_t launchRelu(const KernelBinding &b, cudaStream_t s) {
+  return tmc::launch_graph_unary(b.inputs[0]->data(), b.outputs[0]->data(), b.constants[0], false,
+                                 b.inputs[0]->elementType() == ElementType::Float16, s);
+}
+cudaError_t launchSilu(const KernelBinding &b, cudaStream_t s) {
+  return tmc::launch_graph_unary(b.inputs[0]->data(), b.outputs[0]->data(), b.constants[0], true,
+                                 b.inputs[0]->elementType() == ElementType::Float16, s);
+}
+
+// matmul: a [m, k], W ([k, n], or [n, k] read transposed) -> y [m, n];
+// constants {m, k, n, w_transposed}; a and y fp32 or fp16, W as a or fp16.
+std::string bindMatmul(CudaRuntime &, KernelBinding &b) {
+  const ElementType at = b.inputs[0]->elementType(), wt = b.inputs[1]->elementType();
+  if ((at != ElementType::Float32 && at != ElementType::Float16) || (wt != at && wt != ElementType::Float16))
+    return "matmul: a and y fp32 or fp16, W the same type or fp16.";
+  TMC_CHECK(requireTypes(b, {at, wt, at}, "matmul"));
+  const std::size_t m = b.constants[0], k = b.constants[1], n = b.constants[2];
+  if (m < 1 || k < 1 || n < 1 || b.constants[3] > 1) return "matmul: m, k, n positive, w_transposed 0 or 1.";
+  TMC_CHECK(requireCount(b.inputs[0], m * k, "matmul", "a"));
+  TMC_CHECK(requireCount(b.inputs[1], k * n, "matmul", "W"));
+  TMC_CHECK(requireCount(b.outputs[0], m * n, "matmul", "y"));
+  return {};
+}
+cudaError_t launchMatmul(const KernelBinding &b, cudaStream_t s) {
+  return tmc::launch_graph_matmul(b.inputs[0]->data(), b.inputs[1]->data(), b.outputs[0]->data(), (int)b.constants[0],
+                                  (int)b.constants[1], (int)b.constants[2], b.constants[3] != 0,
+                                  b.inputs[0]->elementType() == ElementType::Float16,
+                                  b.inputs[1]->elementType() == ElementType::Float16, s);
+}
+
 // ---- paged_attention_f16 (emitServingPagedKVAttention) ----
 // q f16 [rows, hq, d], k_pool, v_pool f16 [pool_pages, hkv, page, d],
 // block_table i32 [*, table_stride], table_rows i32 [rows], positions i32 [rows]
@@ -336,10 +403,10 @@ const std::vector<KernelEntry> &kernelCatalog() {
       {"rmsnorm_gemv_f32", 3, 1, 4,
        "x fp32 [rows, k], gamma fp32 [k], W fp16 [n, k] -> y fp32 [rows, n]; constants {rows (1..4), k (% 8), n, "
        "eps bits}",
-       bindRmsnormGemv, launchRmsnormGemv},
+       bindRmsnormGemv, launchRmsnormGemv, launchRmsnormGemvPdl, 1u << 2},
       {"gemv_f16", 2, 1, 3,
        "x fp16 [rows, k], W fp16 [n, k] -> y fp16 or fp32 [rows, n]; constants {rows (1..8), k (% 8), n}",
-       bindGemv, launchGemv},
+       bindGemv, launchGemv, launchGemvPdl, 1u << 1},
       {"batched_gemm_f16", 2, 1, 3,
        "x fp16 [rows, k], W fp16 [n, k] -> y fp32 [rows, n] on tcgen05 tensor cores; constants {rows (1..128), "
        "k (% 8), n}",
@@ -358,6 +425,16 @@ const std::vector<KernelEntry> &kernelCatalog() {
       {"fused_linear_relu", 3, 1, 3,
        "a [m, k], w [k, n], bias [n] -> y = relu(a . w + bias) [m, n]; constants {m, k, n}", bindLinearRelu,
        launchLinearRelu},
+      {"add", 2, 1, 3, "x [rows, width], b [b_rows, width] -> y = x + b; constants {rows, width, b_rows}", bindAdd,
+       launchAdd},
+      {"mul", 2, 1, 3, "x [rows, width], b [b_rows, width] -> y = x * b; constants {rows, width, b_rows}", bindMul,
+       launchMul},
+      {"relu", 1, 1, 1, "x -> y = max(x, 0); constants {count}", bindRelu, launchRelu},
+      {"silu", 1, 1, 1, "x -> y = x * sigmoid(x); constants {count}", bindSilu, launchSilu},
+      {"matmul", 2, 1, 4,
+       "a [m, k], W [k, n] (or [n, k] read transposed) -> y [m, n]; a, y fp32 or fp16, W as a or fp16; constants "
+       "{m, k, n, w_transposed}",
+       bindMatmul, launchMatmul},
       {"paged_attention_f16", 6, 1, 10,
        "q fp16 [rows, hq, d], k_pool, v_pool fp16 [pool_pages, hkv, page, d], block_table i32, table_rows i32 "
        "[rows], positions i32 [rows] -> out fp16 [rows, hq, d]; constants {rows, hq, hkv, d, page_size, "
@@ -426,8 +503,17 @@ PreparationResult prepareKernel(CudaRuntime &runtime, const KernelEntry &kernel,
     return result;
   }
   auto launch = kernel.launch;
-  return runtime.prepare([binding, launch](cudaStream_t s) { return launch(binding, s); }, std::move(inputs),
-                         std::move(outputs), kernel.name);
+  std::vector<BufferHandle> early;
+  for (std::size_t i = 0; i < inputs.size(); ++i)
+    if (kernel.earlyInputs & (1u << i)) early.push_back(inputs[i]);
+  result = runtime.prepare([binding, launch](cudaStream_t s) { return launch(binding, s); }, std::move(inputs),
+                           std::move(outputs), kernel.name);
+  if (result.execution && kernel.launchOverlapped) {
+    auto overlapped = kernel.launchOverlapped;
+    result.execution->allowOverlap([binding, overlapped](cudaStream_t s) { return overlapped(binding, s); },
+                                   std::move(early));
+  }
+  return result;
 }
 
 }  // namespace tensor::cuda

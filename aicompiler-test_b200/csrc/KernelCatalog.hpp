@@ -42,6 +42,11 @@ struct KernelEntry {
   // allocates a workspace when the kernel needs one. "" on success.
   std::string (*bind)(CudaRuntime &runtime, KernelBinding &binding);
   cudaError_t (*launch)(const KernelBinding &binding, cudaStream_t stream);
+  // Launch with programmatic dependent launch (null when the kernel does not
+  // wait on its predecessor before reading its inputs), and the inputs it
+  // reads before that wait (a bit per input index: its weights).
+  cudaError_t (*launchOverlapped)(const KernelBinding &binding, cudaStream_t stream) = nullptr;
+  unsigned earlyInputs = 0;
 };
 
 [[nodiscard]] const std::vector<KernelEntry> &kernelCatalog();

@@ -538,6 +538,105 @@ def plan_buffers(input_count: int, nodes, outputs):
     return roles[:values].tolist(), alias[:values].tolist(), launches[:count.value].tolist()
 
 
+# ---- graph compilation (tmc_graph_*; the reference's compileGraph) -----------------------
+
+OPS = ("Add", "Mul", "MatMul", "RMSNorm", "LayerNorm", "ReLU", "SiLU", "Softmax", "RoPE", "ReduceSum",
+       "ReduceMean", "Reshape", "View", "Transpose", "Contiguous", "MaskedFill", "Slice", "Embedding", "Gather")
+
+_sig("tmc_graph_plan", c_int, c_int, _I32P, c_size_t, _I32P, c_size_t, c_int, _I32P, c_int, c_char_p, c_size_t,
+     POINTER(c_size_t))
+_sig("tmc_graph_compile", c_int, c_void_p, c_int, _I32P, c_size_t, _I32P, c_size_t, c_int, _I32P, c_int,
+     POINTER(c_void_p))
+_sig("tmc_graph_destroy", None, c_void_p)
+_sig("tmc_graph_describe", c_int, c_void_p, c_char_p, c_size_t, POINTER(c_size_t))
+_sig("tmc_graph_value_info", c_int, c_void_p, c_int, POINTER(c_int), POINTER(c_int), POINTER(ctypes.c_int64),
+     POINTER(c_size_t))
+_sig("tmc_graph_run", c_int, c_void_p, POINTER(POINTER(c_float)), POINTER(POINTER(c_float)),
+     POINTER(ctypes.c_double), POINTER(ctypes.c_double))
+_sig("tmc_graph_input_buffer", c_int, c_void_p, c_int, POINTER(c_void_p))
+_sig("tmc_graph_launch", c_int, c_void_p, c_int)
+
+
+def encode_typed_graph(inputs, nodes):
+    """(input_types, nodes) int32 arrays of the tmc_graph_* encoding.
+    inputs: [(dtype F16 / F32, shape)]; nodes: [(op name or number, operands,
+    attributes)], attributes a list of ints or floats (floats become their
+    fp32 bit patterns: RMSNorm / LayerNorm epsilon)."""
+    types = []
+    for dtype, shape in inputs:
+        types += [int(dtype), len(shape)] + [int(d) for d in shape]
+    flat = []
+    for op, operands, *rest in nodes:
+        attrs = rest[0] if rest else []
+        op = OPS.index(op) if isinstance(op, str) else int(op)
+        enc = [float_bits(a) if isinstance(a, float) else int(a) for a in attrs]
+        enc = [a - (1 << 32) if a >= (1 << 31) else a for a in enc]
+        flat += [op, len(operands)] + [int(v) for v in operands] + [len(enc)] + enc
+    return np.asarray(types, np.int32), np.asarray(flat, np.int32)
+
+
+def graph_plan(inputs, nodes, outputs) -> list:
+    """Host-only launch plan of a typed graph: one line per kernel launch."""
+    types, flat = encode_typed_graph(inputs, nodes)
+    outs = _i32(outputs)
+    need = c_size_t(0)
+    args = (len(inputs), types.ctypes.data_as(_I32P), types.size, flat.ctypes.data_as(_I32P), flat.size, len(nodes),
+            outs.ctypes.data_as(_I32P), outs.size)
+    check(lib.tmc_graph_plan(*args, None, 0, ctypes.byref(need)))
+    buf = ctypes.create_string_buffer(need.value)
+    check(lib.tmc_graph_plan(*args, buf, need.value, ctypes.byref(need)))
+    return [line for line in buf.value.decode().splitlines() if line]
+
+
+class Graph:
+    """A compiled tensor graph (reference compileGraph -> CompiledGraph)."""
+
+    def __init__(self, rt: "Runtime", inputs, nodes, outputs):
+        types, flat = encode_typed_graph(inputs, nodes)
+        outs = _i32(outputs)
+        h = c_void_p()
+        check(lib.tmc_graph_compile(rt.handle, len(inputs), types.ctypes.data_as(_I32P), types.size,
+                                    flat.ctypes.data_as(_I32P), flat.size, len(nodes), outs.ctypes.data_as(_I32P),
+                                    outs.size, ctypes.byref(h)))
+        self.handle = h
+        self.runtime = rt
+        self.inputs = [(int(d), tuple(int(x) for x in s)) for d, s in inputs]
+        self.outputs = [int(o) for o in outputs]
+
+    def value_shape(self, value: int):
+        dt, rank = c_int(), c_int()
+        dims = (ctypes.c_int64 * 4)()
+        n = c_size_t()
+        check(lib.tmc_graph_value_info(self.handle, value, ctypes.byref(dt), ctypes.byref(rank), dims, ctypes.byref(n)))
+        return tuple(dims[i] for i in range(rank.value))
+
+    def plan(self) -> list:
+        need = c_size_t(0)
+        check(lib.tmc_graph_describe(self.handle, None, 0, ctypes.byref(need)))
+        buf = ctypes.create_string_buffer(need.value)
+        check(lib.tmc_graph_describe(self.handle, buf, need.value, ctypes.byref(need)))
+        return [line for line in buf.value.decode().splitlines() if line]
+
+    def run(self, *arrays):
+        """Logical float outputs (one array per declared output) and the GPU time."""
+        ins = [np.ascontiguousarray(a, dtype=np.float32).reshape(-1) for a in arrays]
+        assert len(ins) == len(self.inputs)
+        outs = [np.empty(self.value_shape(v), np.float32) for v in self.outputs]
+        in_ptrs = (POINTER(c_float) * max(1, len(ins)))(*[_fptr(a) for a in ins])
+        out_ptrs = (POINTER(c_float) * len(outs))(*[_fptr(o) for o in outs])
+        g, c = ctypes.c_double(), ctypes.c_double()
+        check(lib.tmc_graph_run(self.handle, in_ptrs, out_ptrs, ctypes.byref(g), ctypes.byref(c)))
+        return outs, g.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib.tmc_graph_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        self.close()
+
+
 class ManifestInfo(ctypes.Structure):
     _fields_ = [("version", c_int), ("batch", c_int), ("hidden_size", c_int), ("heads", c_int), ("head_dim", c_int),
                 ("intermediate_size", c_int), ("vocab_size", c_int), ("layers", c_int), ("capacity", c_int),

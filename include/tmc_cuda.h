@@ -328,6 +328,53 @@ int tmc_manifest_tensor(const tmc_manifest *m, const char *name, const float **v
 int tmc_plan_regions(int input_count, const int32_t *nodes, size_t nodes_len, int node_count,
                      const int32_t *outputs, int output_count, const int32_t *contiguous, int32_t *order,
                      int32_t *regions, size_t capacity, size_t *written);
+/* ---- graph compilation (replaces compileGraph / CompiledGraph::run,
+ * src/runtime/GraphExecutor.hpp:16-46, GraphExecutor.cpp:346-431) ----
+ * A typed tensor graph is analysed (types inferred, views aliased), split into
+ * regions as formRegions does, and each region bound to one of this library's
+ * kernels (tmc_kernel_lookup names); compile prepares them and captures them
+ * as one CUDA graph. Encoding:
+ *   input_types: per graph input {dtype (TMC_F16 or TMC_F32), rank (1..4),
+ *                dims...}, concatenated;
+ *   nodes:       per node {op, #operands, operands..., #attributes,
+ *                attributes...}, op numbered as the reference's
+ *                tensor::OpType, node i defining value input_count + i;
+ *                attributes: RMSNorm / LayerNorm {epsilon as float bits}
+ *                (none: 1e-5), Transpose {first, second} (a 2-D swap),
+ *                Reshape / View {dims...}.
+ * Supported: Add, Mul (equal shapes or a broadcast last-axis row), MatMul
+ * (2-D; an fp16 right-hand operand is also accepted under an fp32 left-hand
+ * one, an extension over TensorIR's matching-dtype rule so weights can stay
+ * fp16), RMSNorm, LayerNorm (fused behind its residual Add), ReLU, SiLU,
+ * Transpose, Reshape, View; other ops are refused with TMC_ERR_UNSUPPORTED
+ * naming the op. An RMSNorm whose only use is a MatMul against a Transpose
+ * view of an fp16 [N, K] weight, with fp32 rows <= 4, runs inside that GEMV's
+ * prologue (the C1 graph becomes one rmsnorm_gemv_f32 launch).
+ * tmc_graph_plan is host only: it writes the launch plan as text, one line
+ * per launch "kernel(vA, vB, ...) -> vC [region]", and sets *needed to its
+ * size + 1. tmc_graph_run writes every input from logical floats (element
+ * counts from the types), replays the graph synchronously and reads every
+ * declared output as logical floats; tmc_graph_value_info gives any value's
+ * type (dims: 4 int64). tmc_graph_input_buffer returns a new handle on an
+ * input's device storage (release it with tmc_buffer_destroy) and
+ * tmc_graph_launch enqueues replays without synchronising, for device-side
+ * inputs. */
+typedef struct tmc_graph tmc_graph;
+int tmc_graph_plan(int input_count, const int32_t *input_types, size_t input_types_len, const int32_t *nodes,
+                   size_t nodes_len, int node_count, const int32_t *outputs, int output_count, char *text,
+                   size_t size, size_t *needed);
+int tmc_graph_compile(tmc_runtime *rt, int input_count, const int32_t *input_types, size_t input_types_len,
+                      const int32_t *nodes, size_t nodes_len, int node_count, const int32_t *outputs,
+                      int output_count, tmc_graph **out);
+void tmc_graph_destroy(tmc_graph *graph);
+int tmc_graph_describe(const tmc_graph *graph, char *text, size_t size, size_t *needed);
+int tmc_graph_value_info(const tmc_graph *graph, int value, int *dtype, int *rank, int64_t *dims,
+                         size_t *elements);
+int tmc_graph_run(tmc_graph *graph, const float *const *inputs, float *const *outputs, double *gpu_us,
+                  double *cpu_us);
+int tmc_graph_input_buffer(tmc_graph *graph, int input, tmc_buffer **out);
+int tmc_graph_launch(tmc_graph *graph, int replays);
+
 /* planGraph's buffer and launch decisions (KernelPlan.cpp:11-59) for the same
  * graph encoding: roles[v] = 0 graph input, 1 intermediate, 2 declared output
  * (an input that is also an output stays 0); alias_of[v] = the data operand a

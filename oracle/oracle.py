@@ -312,3 +312,30 @@ def ref_plan_buffers(n, squares, vectors, nodes, outputs):
     if k < 0:
         raise ValueError(_ref.ref_last_error().decode())
     return roles.tolist(), alias.tolist(), launches[:k].tolist()
+
+
+def ref_evaluate_graph(inputs, nodes, outputs, values):
+    """The reference's own evaluateGraph (oracle/_ref) on a typed graph in the
+    tmc_graph encoding: inputs [(dtype 0 fp16 / 1 fp32, shape)], nodes [(op
+    name or number, operands, attributes)], values = one array per input.
+    Returns the declared outputs (fp64, flat)."""
+    if _ref is None:
+        raise RuntimeError("oracle/_ref not built (reference sources absent at build time)")
+    import sys as _sys
+    _sys.path.insert(0, __import__("os").path.join(__import__("os").path.dirname(__file__), "..",
+                                                   "aicompiler-test_b200"))
+    from tmc_cuda import encode_typed_graph
+    types, flat = encode_typed_graph(inputs, nodes)
+    data = np.concatenate([np.asarray(v, np.float32).reshape(-1) for v in values]).astype(np.float32)
+    outs = np.asarray(outputs, np.int32)
+    cap = 1 << 24
+    out = np.empty(cap, dtype=np.float64)
+    P = POINTER(c_int32)
+    fn = _ref.ref_evaluate_graph
+    fn.restype = c_long
+    fn.argtypes = [c_int, P, c_int, P, c_int, P, _F, _D, c_long]
+    n = fn(len(inputs), types.ctypes.data_as(P), len(nodes), flat.ctypes.data_as(P), len(outputs),
+           outs.ctypes.data_as(P), _p(data, _F), _p(out, _D), cap)
+    if n < 0:
+        raise RuntimeError(_ref.ref_last_error().decode())
+    return out[:n].copy()

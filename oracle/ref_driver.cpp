@@ -225,4 +225,79 @@ long ref_plan_buffers(long n, long squares, long vectors, const int *nodes, long
   }
 }
 
+// The reference's own evaluateGraph on a typed graph in the encoding of
+// tmc_graph_compile (include/tmc_cuda.h): input types {dtype 0 fp16 / 1 fp32,
+// rank, dims...}, nodes {op, #operands, operands..., #attributes,
+// attributes...} (RMSNorm / LayerNorm: epsilon bits; Transpose: first,
+// second; Reshape / View: dims). `inputs` holds every input's logical values
+// back to back; each declared output's fp64 values are written back to back
+// into `out` (capacity `out_len`). Returns the number written, or -1 with
+// ref_last_error() set.
+long ref_evaluate_graph(int input_count, const int *input_types, int node_count, const int *nodes, int output_count,
+                        const int *outputs, const float *inputs, double *out, long out_len) {
+  try {
+    TensorGraph graph;
+    GraphInputs values;
+    long at = 0, data = 0;
+    for (int i = 0; i < input_count; ++i) {
+      const DType dt = input_types[at] == 0 ? DType::Float16 : DType::Float32;
+      const int rank = input_types[at + 1];
+      at += 2;
+      std::vector<std::size_t> shape;
+      std::size_t count = 1;
+      for (int d = 0; d < rank; ++d) {
+        shape.push_back(std::size_t(input_types[at + d]));
+        count *= std::size_t(input_types[at + d]);
+      }
+      at += rank;
+      const auto id = graph.addInput("in" + std::to_string(i), TensorType{shape, dt});
+      values[id] = std::vector<float>(inputs + data, inputs + data + count);
+      data += long(count);
+    }
+    at = 0;
+    for (int i = 0; i < node_count; ++i) {
+      const auto op = static_cast<OpType>(nodes[at]);
+      const int arity = nodes[at + 1];
+      at += 2;
+      std::vector<ValueId> operands;
+      for (int k = 0; k < arity; ++k) operands.push_back(ValueId(nodes[at + k]));
+      at += arity;
+      const int nattr = nodes[at++];
+      std::vector<int> attrs(nodes + at, nodes + at + nattr);
+      at += nattr;
+      OpAttributes attributes;
+      float eps = 1e-5f;
+      if (!attrs.empty() && (op == OpType::RMSNorm || op == OpType::LayerNorm))
+        std::memcpy(&eps, &attrs[0], 4);
+      if (op == OpType::RMSNorm) attributes = RMSNormAttributes{eps, -1};
+      if (op == OpType::LayerNorm) {
+        LayerNormAttributes a;
+        a.epsilon = eps;
+        attributes = a;
+      }
+      if (op == OpType::Transpose)
+        attributes = TransposeAttributes{attrs.size() >= 2 ? attrs[0] : 0, attrs.size() >= 2 ? attrs[1] : 1};
+      if (op == OpType::Reshape || op == OpType::View) {
+        ReshapeAttributes a;
+        for (int d : attrs) a.shape.push_back(std::size_t(d));
+        attributes = a;
+      }
+      graph.addNode(op, operands, attributes);
+    }
+    for (int i = 0; i < output_count; ++i) graph.outputs.push_back(ValueId(outputs[i]));
+    const auto analyzed = analyzer::analyze(graph);
+    const auto result = validation::evaluateGraph(analyzed, values);
+    long w = 0;
+    for (const auto &o : result.outputs) {
+      if (w + long(o.size()) > out_len) throw std::runtime_error("output buffer too small");
+      std::memcpy(out + w, o.data(), o.size() * sizeof(double));
+      w += long(o.size());
+    }
+    return w;
+  } catch (const std::exception &e) {
+    g_error = e.what();
+    return -1;
+  }
+}
+
 }  // extern "C"

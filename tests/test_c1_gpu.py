@@ -99,3 +99,20 @@ def test_gemv_f16_matches_oracle(rt):
         # fp16 output is the storage rounding of the fp32 result
         got16 = y16.read().reshape(rows, n)
         assert np.max(np.abs(got16 - oracle.round_f16(got32).reshape(rows, n))) <= 2e-3 * rms
+
+
+def test_c1_full_size_through_the_graph_entry(rt):
+    # The C1 TensorGraph (RMSNorm -> Transpose(W) view -> MatMul) compiled by
+    # tmc_graph_compile, the reference's compileGraph path: with W stored fp16
+    # the plan is one rmsnorm_gemv_f32 launch; checked against the reference
+    # exporter's evaluateGraph golden like the direct entry point above.
+    import tmc_cuda
+    x, gamma, w = workloads.c1_inputs(seed=0)
+    g = np.load(os.path.join(GOLDEN, "c1_full.npz"))
+    graph = tmc_cuda.Graph(rt, [(tmc_cuda.F32, (1, 4096)), (tmc_cuda.F32, (4096,)), (tmc_cuda.F16, (4096, 4096))],
+                           [("RMSNorm", [0, 1], [1e-5]), ("Transpose", [2], [0, 1]), ("MatMul", [3, 4])], [5])
+    assert [s.split("(")[0] for s in graph.plan()] == ["rmsnorm_gemv_f32"]
+    (y,), gpu_us = graph.run(x, gamma, w)
+    assert gpu_us > 0
+    assert_close(y, g["y"].reshape(y.shape))
+    graph.close()

@@ -11,7 +11,10 @@ MetalRuntime.mm:594-648), run with NaN sentinels and executed
   interface checks (element types, sizes);
 - a sequence (fp16 RMSNorm, then a GEMV reading its output) equals the two
   executions run one by one, and replays launched without synchronising give
-  the same result;
+  the same result; GEMV steps start before their predecessor ends
+  (programmatic dependent launch) only when no earlier step writes the weights
+  they read early: a sequence whose first step writes the second's weights
+  still equals its steps run one by one;
 - the tensor-core GEMM and the paged attention bound through tmc_prepare equal
   their direct C-ABI entry points bit for bit.
 """
@@ -97,6 +100,30 @@ def test_sequence_equals_its_steps_run_one_by_one(rt):
     seq.launch(5)
     rt.synchronize()
     assert np.array_equal(yb.read(), y_ref)
+
+
+def test_sequence_keeps_weights_written_by_an_earlier_step_ordered(rt):
+    import tmc_cuda
+    rng = np.random.default_rng(4)
+    rows, k, n = 2, 2048, 4096
+    x = rng.standard_normal((rows, k)).astype(np.float16)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float16)
+    xb, wb = rt.upload(x), rt.upload(w)
+    zero = rt.upload(np.zeros(k, np.float16))
+    w2 = rt.buffer(n * k, tmc_cuda.F16)
+    y1 = rt.buffer(rows * n, tmc_cuda.F32)
+    y2 = rt.buffer(rows * n, tmc_cuda.F32)
+    direct = tmc_cuda.Prepared(rt, "gemv_f16", [xb, wb], [y1], [rows, k, n])
+    copy = tmc_cuda.Prepared(rt, "add", [wb, zero], [w2], [n, k, 1])  # w2 = w + 0: writes the next step's weights
+    gemv = tmc_cuda.Prepared(rt, "gemv_f16", [xb, w2], [y2], [rows, k, n])
+    ref, _, _ = direct.run()
+    for _ in range(3):
+        w2.write(np.full(n * k, np.nan, np.float32))
+        y2.write(np.full(rows * n, np.nan, np.float32))
+        seq = tmc_cuda.Sequence(rt, [copy, gemv])
+        seq.execute()
+        assert np.array_equal(y2.read(), ref)
+        seq.close()
 
 
 def test_prepared_gemm_and_attention_equal_their_entry_points(rt):
