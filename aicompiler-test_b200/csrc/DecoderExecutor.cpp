@@ -231,7 +231,9 @@ std::string DecoderExecutor::allocate() {
   TMC_TRY(cudaMemsetAsync(hB_->data(), 0, hB_->byteCount(), s0));
   // Block table: -1 = unmapped.
   TMC_TRY(cudaMemsetAsync(blockTable_->data(), 0xff, blockTable_->byteCount(), s0));
-  TMC_TRY(cudaMallocHost(&pinnedIO_, sizeof(std::int32_t) * 4 * R));
+  prefillChunks_ = (std::size_t)(cfg_.capacity + R - 1) / R;
+  TMC_TRY(cudaMallocHost(&pinnedIO_, sizeof(std::int32_t) * (4 * R + 3 * R * prefillChunks_)));
+  prefillStage_ = pinnedIO_ + 4 * R;
   // Norm weights default to 1 (nn.Parameter(torch.ones), decoder_llm.py:11).
   for (auto &L : layers_) {
     TMC_TRY(tmc::launch_fill_value_f16(hp(L.inputNorm), H, 1.0f, rt_.stream()));
@@ -342,6 +344,54 @@ std::string DecoderExecutor::attachPeers(const void *handles, std::size_t size, 
   if (!err.empty()) return err;
   peersAttached_ = true;
   dropGraphs();
+  return {};
+}
+
+std::string DecoderExecutor::attachLocalPeers(const std::vector<DecoderExecutor *> &ranks, int rank) {
+  if (cfg_.tpSize <= 1 || !xchgWindow_) return "peer exchange needs tensor parallelism (tp_size > 1).";
+  const int world = static_cast<int>(ranks.size());
+  if (world != cfg_.tpSize || rank != cfg_.tpRank)
+    return "peer exchange: world size and rank must equal the decoder's tp_size and tp_rank.";
+  if (world > tmc::kMaxPeers) return "peer exchange: at most 8 ranks.";
+  if (ranks[rank] != this) return "peer exchange: ranks[rank] must be this decoder.";
+  if (peersAttached_) return "peer exchange already attached.";
+  for (int r = 0; r < world; ++r) {
+    const DecoderExecutor *o = ranks[r];
+    if (o == nullptr || !o->xchgWindow_) return "peer exchange: rank " + std::to_string(r) + " has no window.";
+    if (o->cfg_.tpSize != world || o->cfg_.tpRank != r || o->cfg_.hidden != cfg_.hidden ||
+        o->cfg_.maxRows != cfg_.maxRows || o->cfg_.layers != cfg_.layers)
+      return "peer exchange: rank " + std::to_string(r) + " is not a shard of the same model.";
+    auto e = o->rt_.synchronize();  // its window's zero fill has landed
+    if (!e.empty()) return e;
+  }
+  int prev = 0;
+  cudaGetDevice(&prev);
+  cudaSetDevice(rt_.device());
+  std::string err;
+  for (int r = 0; r < world && err.empty(); ++r) {
+    const int dev = ranks[r]->rt_.device();
+    if (dev != rt_.device()) {
+      const cudaError_t ce = cudaDeviceEnablePeerAccess(dev, 0);
+      if (ce != cudaSuccess && ce != cudaErrorPeerAccessAlreadyEnabled)
+        err = "cudaDeviceEnablePeerAccess (rank " + std::to_string(r) + "): " + cudaGetErrorString(ce);
+      cudaGetLastError();
+    }
+    peerWindows_[r] = static_cast<char *>(ranks[r]->xchgWindow_->data());
+  }
+  cudaSetDevice(prev);
+  if (!err.empty()) {
+    for (auto &w : peerWindows_) w = nullptr;
+    return err;
+  }
+  peersAttached_ = true;
+  dropGraphs();
+  return {};
+}
+
+std::string DecoderExecutor::setWaitBudgets(std::uint64_t peerNs, std::uint64_t localNs) {
+  cfg_.peerWaitNs = peerNs;
+  cfg_.localWaitNs = localNs;
+  dropGraphs();  // the budgets are baked into the captured launches
   return {};
 }
 
@@ -816,6 +866,8 @@ tmc::GemvParams DecoderExecutor::projection(int kind, int l, int R, bool feed) c
   p.trace = traceSink(kind == kKernelLMHead ? 0 : l, kind);
   p.work_counter = workCounter(kind == kKernelLMHead ? 0 : l, kind);
   p.l2_prefetch_bytes = kL2PrefetchBytes;
+  p.peer_wait_ns = cfg_.peerWaitNs;
+  p.local_wait_ns = cfg_.localWaitNs;
   switch (kind) {
     case kKernelQKV:
       p.W = hp(L.qkv);
@@ -1220,8 +1272,9 @@ std::string DecoderExecutor::launchStep(int R, bool feed, bool distinct) {
 }
 
 std::string DecoderExecutor::uploadStepInputs(int R, const std::int32_t *tokens, const std::int32_t *positions,
-                                              const std::int32_t *tableRows, int steps) {
+                                              const std::int32_t *tableRows, int steps, std::int32_t *stage) {
   const int M = cfg_.maxRows;
+  std::int32_t *io = stage ? stage : pinnedIO_;
   // The attention chunk policy below (min_chunk 64, max_chunk 128, one
   // 16-CTA cluster filled before a second): splits for the longest context.
   int maxLen = 1;
@@ -1229,14 +1282,14 @@ std::string DecoderExecutor::uploadStepInputs(int R, const std::int32_t *tokens,
   int need = (maxLen + 63) / 64;
   if (need > 16) need = std::max((maxLen + 127) / 128, 16);
   attnSplitCap_ = (need + 15) / 16 * 16;
-  for (int i = 0; i < 3 * M; ++i) pinnedIO_[i] = 0;
+  for (int i = 0; i < 3 * M; ++i) io[i] = 0;
   for (int r = 0; r < M; ++r) lastPositions_[r] = r < R ? positions[r] : 0;
   for (int r = 0; r < R; ++r) {
-    pinnedIO_[r] = tokens[r];
-    pinnedIO_[M + r] = positions[r];
-    pinnedIO_[2 * M + r] = tableRows[r];
+    io[r] = tokens[r];
+    io[M + r] = positions[r];
+    io[2 * M + r] = tableRows[r];
   }
-  TMC_TRY(cudaMemcpyAsync(stepIO_->data(), pinnedIO_, sizeof(std::int32_t) * 3 * M, cudaMemcpyHostToDevice,
+  TMC_TRY(cudaMemcpyAsync(stepIO_->data(), io, sizeof(std::int32_t) * 3 * M, cudaMemcpyHostToDevice,
                           rt_.stream()));
   return {};
 }
@@ -1316,22 +1369,31 @@ std::string DecoderExecutor::prefill(int slot, const std::int32_t *tokens, int c
   const size_t start = st.currentLength();
   auto err = st.stageLength(start + count);
   if (!err.empty()) return err;
+  // Chunks of maxRows rows (the reference's prefillChunked,
+  // DecoderLLMExecutor.cpp:982-1034), queued back to back: each chunk's inputs
+  // come from its own pinned staging block, so the host never waits between
+  // chunks; one synchronisation at the end (per chunk only when logits are
+  // copied to pageable host memory).
   const int M = cfg_.maxRows;
   std::vector<std::int32_t> pos(M), trow(M, slot);
   double gpuUs = 0.0;
   const auto c0 = std::chrono::steady_clock::now();
-  for (int done = 0; done < count && err.empty();) {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  if (timing) {
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, rt_.stream());
+  }
+  int last = 0;
+  for (int done = 0, chunk = 0; done < count && err.empty(); ++chunk) {
     const int R = std::min(M, count - done);
-    for (int r = 0; r < R; ++r) pos[r] = static_cast<std::int32_t>(start + done + r);
-    err = uploadStepInputs(R, tokens + done, pos.data(), trow.data());
-    cudaEvent_t e0 = nullptr, e1 = nullptr;
-    if (timing) {
-      cudaEventCreate(&e0);
-      cudaEventCreate(&e1);
-      cudaEventRecord(e0, rt_.stream());
+    if ((std::size_t)chunk >= prefillChunks_) {
+      err = "prefill: more chunks than the staging holds.";
+      break;
     }
+    for (int r = 0; r < R; ++r) pos[r] = static_cast<std::int32_t>(start + done + r);
+    err = uploadStepInputs(R, tokens + done, pos.data(), trow.data(), 1, prefillStage_ + (std::size_t)chunk * 3 * M);
     if (err.empty()) err = launchStep(R, false, R == 1);
-    if (timing) cudaEventRecord(e1, rt_.stream());
     if (err.empty() && logits) {
       cudaError_t ce = cudaMemcpyAsync(logits + (size_t)done * vL_, logits_->data(), sizeof(float) * R * vL_,
                                        cudaMemcpyDeviceToHost, rt_.stream());
@@ -1342,17 +1404,19 @@ std::string DecoderExecutor::prefill(int slot, const std::int32_t *tokens, int c
                                        cudaMemcpyDeviceToHost, rt_.stream());
       if (ce != cudaSuccess) err = cudaText("prefill token readback", ce);
     }
-    const std::string sync = rt_.synchronize();
-    if (err.empty()) err = sync;
-    if (timing) {
-      float ms = 0.0f;
-      if (err.empty() && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess) gpuUs += ms * 1000.0;
-      cudaEventDestroy(e0);
-      cudaEventDestroy(e1);
-    }
-    if (err.empty() && done + R == count && nextToken) *nextToken = pinnedIO_[3 * M + R - 1];
+    last = R;
     done += R;
   }
+  if (timing) cudaEventRecord(e1, rt_.stream());
+  const std::string sync = rt_.synchronize();
+  if (err.empty()) err = sync;
+  if (timing) {
+    float ms = 0.0f;
+    if (err.empty() && cudaEventElapsedTime(&ms, e0, e1) == cudaSuccess) gpuUs = ms * 1000.0;
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+  }
+  if (err.empty() && nextToken) *nextToken = pinnedIO_[3 * M + last - 1];
   if (timing) {
     timing->gpuUs = gpuUs;
     timing->cpuUs = std::chrono::duration<double, std::micro>(std::chrono::steady_clock::now() - c0).count();

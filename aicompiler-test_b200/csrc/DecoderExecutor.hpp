@@ -61,6 +61,12 @@ struct DecoderConfig {
   int tpSize = 1;
   bool useGraphs = true;
   bool usePDL = true;
+  // Budgets of the kernels' bounded waits in ns (0: the kernel defaults, 10 s
+  // for another rank's exchange flags and 1 s for a GEMM's mbarrier and
+  // split-tile waits). A wait that runs out is reported through the device
+  // status block and the call returns a "device status" error.
+  std::uint64_t peerWaitNs = 0;
+  std::uint64_t localWaitNs = 0;
 };
 
 // Cross-rank sum/max used by tensor parallelism (implemented over NCCL).
@@ -121,7 +127,13 @@ class DecoderExecutor {
   // and switch the row-parallel reductions and the LM-head argmax from the
   // collective to the one-shot peer exchange fused into the GEMV kernels.
   std::string attachPeers(const void *handles, std::size_t size, int world, int rank);
+  // The same over ranks driven by this process (ranks[r] = rank r's
+  // executor, on any device with peer access to this one): their windows are
+  // used directly, without IPC.
+  std::string attachLocalPeers(const std::vector<DecoderExecutor *> &ranks, int rank);
   bool peersAttached() const { return peersAttached_; }
+  // Replace the bounded-wait budgets (DecoderConfig::peerWaitNs/localWaitNs).
+  std::string setWaitBudgets(std::uint64_t peerNs, std::uint64_t localNs);
 
   // ---- execution (CompiledDecoderLLM API) ----
   // Prefill `count` tokens of one sequence in chunks of maxRows rows.
@@ -216,7 +228,7 @@ class DecoderExecutor {
   // Uploads a step's tokens, positions and table rows and sets the attention
   // split cap for contexts up to max(position) + steps.
   std::string uploadStepInputs(int rows, const std::int32_t *tokens, const std::int32_t *positions,
-                               const std::int32_t *tableRows, int steps = 1);
+                               const std::int32_t *tableRows, int steps = 1, std::int32_t *stage = nullptr);
   std::string writeBlockRow(int slot, const std::vector<std::int32_t> &row);
   void computeRope();
 
@@ -246,7 +258,12 @@ class DecoderExecutor {
   cuda::BufferHandle attnWorkspace_, attnCounters_;
   cuda::BufferHandle workCounters_;  // per launch site: tmc::kGemvCounterWords uints
   unsigned int *workCounter(int layer, int kind) const;
-  std::int32_t *pinnedIO_ = nullptr;   // host staging [3 * maxRows + maxRows]
+  // Host staging: [3 * maxRows] step inputs, [maxRows] next tokens, then one
+  // [3 * maxRows] block per prefill chunk (a whole prompt's chunks are queued
+  // without waiting, so each keeps its own staging until its copy runs).
+  std::int32_t *pinnedIO_ = nullptr;
+  std::int32_t *prefillStage_ = nullptr;
+  std::size_t prefillChunks_ = 0;
   // Page spill / restore: device array of the 2 * layers pool pointers, page-id
   // list, packed device staging and pinned host staging (grown on demand).
   cuda::BufferHandle poolPtrs_, spillPages_;

@@ -429,6 +429,7 @@ __global__ void __launch_bounds__(kThreads)
   };
 
   const int first = ntiles < S ? ntiles : S;
+  int issued = first;  // tiles whose copies have been requested (warp 0's count)
   // Boxes (BOX) are all-or-nothing: a box holding any position at or past
   // `fresh` waits for the producer kernel.
   const int early_hi = fresh;
@@ -492,7 +493,8 @@ __global__ void __launch_bounds__(kThreads)
 
   for (int t = 0; t < ntiles && !failed; ++t) {
     const int stage = t % S;
-    if (!mbar_wait(&full[stage], (t / S) & 1)) {
+    // Warp-uniform outcome: the tile step below is warp-synchronous.
+    if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], (t / S) & 1))) {
       if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
       failed = true;
       break;
@@ -507,18 +509,25 @@ __global__ void __launch_bounds__(kThreads)
     if (lane == 0) mbar_arrive(&empty[stage]);
     if (warp == 0 && t + S < ntiles) {
       // Every warp has finished this stage before it is refilled.
-      if (!mbar_wait(&empty[stage], (t / S) & 1)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&empty[stage], (t / S) & 1))) {
         if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, t, row);
         failed = true;
         break;
       }
       arm(t + S);
       copy(t + S, begin, end);
+      issued = t + S + 1;
     }
   }
   // Let the next kernel launch only now: its weight prefetch would otherwise
   // queue ahead of this kernel's latency-critical loads.
   pdl_launch_dependents();
+
+  // After a wait ran out, copies may still be in flight into the ring: wait
+  // (bounded) for the last S requested tiles before the ring is reused for
+  // the merge or the CTA exits.
+  if (__syncthreads_or(failed ? 1 : 0) && warp == 0 && lane == 0)
+    for (int t = issued > S ? issued - S : 0; t < issued; ++t) (void)mbar_wait(&full[t % S], (t / S) & 1);
 
   // Merge the four warps' states (rows gq < G) in shared memory (the K/V ring
   // is free now): per warp [G][D] accumulators, then m and l per head.

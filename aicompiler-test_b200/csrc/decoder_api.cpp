@@ -25,6 +25,7 @@ using namespace tmc_api;
 struct tmc_decoder {
   std::unique_ptr<DecoderExecutor> ex;
   int device = 0;
+  tensor::runtime::StepTiming lastPrefill;  // the last tmc_decoder_prefill call
 };
 
 struct tmc_manifest {
@@ -187,7 +188,15 @@ int tmc_decoder_init_random(tmc_decoder *dec, uint64_t seed, float stddev) {
 int tmc_decoder_prefill(tmc_decoder *dec, int slot, const int32_t *tokens, int count, float *logits,
                         int32_t *next_token) {
   if (!bind(dec) || tokens == nullptr) return fail(TMC_ERR_INVALID, "null argument");
-  return done(dec->ex->prefill(slot, tokens, count, logits, next_token));
+  dec->lastPrefill = {};
+  return done(dec->ex->prefill(slot, tokens, count, logits, next_token, &dec->lastPrefill));
+}
+
+int tmc_decoder_prefill_timing(tmc_decoder *dec, double *gpu_us, double *cpu_us) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  if (gpu_us) *gpu_us = dec->lastPrefill.gpuUs;
+  if (cpu_us) *cpu_us = dec->lastPrefill.cpuUs;
+  return ok();
 }
 
 int tmc_decoder_decode(tmc_decoder *dec, const int32_t *slots, const int32_t *tokens, int rows, float *logits,
@@ -408,6 +417,21 @@ int tmc_decoder_exchange_handle(tmc_decoder *dec, uint8_t *handle, size_t nbytes
   if (!bind(dec) || handle == nullptr) return fail(TMC_ERR_INVALID, "bad argument");
   if (nbytes != TMC_EXCHANGE_HANDLE_BYTES) return fail(TMC_ERR_INVALID, "handle buffer must be TMC_EXCHANGE_HANDLE_BYTES");
   return done(dec->ex->exchangeHandle(handle, nbytes));
+}
+
+int tmc_decoder_attach_local_peers(tmc_decoder *dec, tmc_decoder *const *ranks, int world, int rank) {
+  if (!bind(dec) || ranks == nullptr || world < 1) return fail(TMC_ERR_INVALID, "bad argument");
+  std::vector<DecoderExecutor *> ex(world);
+  for (int r = 0; r < world; ++r) {
+    if (ranks[r] == nullptr || !ranks[r]->ex) return fail(TMC_ERR_INVALID, "null rank decoder");
+    ex[r] = ranks[r]->ex.get();
+  }
+  return done(dec->ex->attachLocalPeers(ex, rank));
+}
+
+int tmc_decoder_set_wait_budgets(tmc_decoder *dec, uint64_t peer_wait_ns, uint64_t local_wait_ns) {
+  if (!bind(dec)) return fail(TMC_ERR_INVALID, "null decoder");
+  return done(dec->ex->setWaitBudgets(peer_wait_ns, local_wait_ns));
 }
 
 int tmc_decoder_attach_peers(tmc_decoder *dec, const uint8_t *handles, size_t nbytes_each, int world,

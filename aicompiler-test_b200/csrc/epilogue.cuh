@@ -15,6 +15,9 @@ namespace tmc {
 
 // ---- peer exchange addressing (layout in gemv.cuh) ----------------------------
 constexpr unsigned long long kPeerWaitNs = 10ull * 1000 * 1000 * 1000;  // 10 s of global time
+__host__ __device__ __forceinline__ unsigned long long peer_wait_budget(const GemvParams &p) {
+  return p.peer_wait_ns ? p.peer_wait_ns : kPeerWaitNs;
+}
 
 __device__ __forceinline__ unsigned int *peer_flag(const PeerExchange &x, int owner, int set, int src) {
   return reinterpret_cast<unsigned int *>(x.window[owner]) + ((size_t)set * kMaxPeers + src) * kPeerFlagStride;
@@ -143,7 +146,7 @@ __device__ __forceinline__ void argmax_finalize(const GemvParams &p, int t, Sync
       for (int q = 0; q < x.world; ++q) *peer_key(x, q, parity, x.rank, x.row0 + t) = key;
     sync();  // the key stores, then one system-scope release per rank (parallel threads)
     if (t < x.world) st_release_sys(peer_flag(x, t, 2 + parity, x.rank), e + 1u);
-    if (t < x.world && !wait_flag_geq(peer_flag(x, x.rank, 2 + parity, t), e + 1u, kPeerWaitNs))
+    if (t < x.world && !wait_flag_geq(peer_flag(x, x.rank, 2 + parity, t), e + 1u, peer_wait_budget(p)))
       report_status(p.status, kStatusWaitTimeout, kWhereExchange, t, -1);
     sync();
     if (t < p.M) {

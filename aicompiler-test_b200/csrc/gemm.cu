@@ -300,6 +300,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ long long tok_slot[kMaxTokens];   // ... and KV element offset of its page row
   __shared__ int s_last, s_fail;
   __shared__ unsigned long long s_ready;
+  __shared__ uint64_t mma_drain;  // tracks the issuer's MMAs on a failure path
+  const unsigned long long local_ns = p.local_wait_ns;
+  const unsigned long long tile_ns = local_ns ? local_ns : kTileWaitNs;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
@@ -314,6 +317,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpiWarps);  // one arrival per epilogue warp
     }
+    mbar_init(&mma_drain, 1);
     fence_barrier_init();
     s_fail = 0;
     s_ready = t_entry;
@@ -333,6 +337,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (lane == 0) {
       // ---- TMA producer ----
       int pending_kb[S];
+      int last_it[S];  // the latest iteration loaded into each stage (-1: none)
+#pragma unroll
+      for (int s = 0; s < S; ++s) last_it[s] = -1;
       int it = 0;
       bool waited = false, ok = true;
       RunCursor run(w);
@@ -350,10 +357,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               tma_load_2d(sB + (size_t)j * C::kBytesB, &x_map, pending_kb[j] * kGemmKBlock, 0, &full[j]);
             waited = true;
           }
-          if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1)) {
+          if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, local_ns)) {
             ok = false;
             break;
           }
+          last_it[st] = it;
           mbar_arrive_expect_tx(&full[st], C::kStageBytes);
           tma_load_2d(sA + (size_t)st * kTileBytesA, &w_map, kb * kGemmKBlock, tile * kGemmTileRows, &full[st]);
           if (waited) {
@@ -372,6 +380,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       pdl_launch_dependents();
       if (!ok) report_status(p.status, kStatusWaitTimeout, kWhereGemm, 0, blockIdx.x);
+      // No copy may still be landing when the CTA exits (on a failure path
+      // the MMA issuer stops consuming): wait, bounded, for each stage's last
+      // load. On the normal path these phases have completed or are about to.
+#pragma unroll 1
+      for (int s = 0; s < S; ++s)
+        if (last_it[s] >= 0) (void)mbar_wait(&full[s], (last_it[s] / S) & 1, local_ns);
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -386,7 +400,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       while (ok && run.get(pc)) {
         const int j = pc.index, kb0 = pc.kb0, kb1 = pc.kb1;
         const int buf = j % C::kAcc;
-        if (j >= C::kAcc && !mbar_wait(&acc_empty[buf], ((j / C::kAcc) - 1) & 1)) {
+        if (j >= C::kAcc && !mbar_wait(&acc_empty[buf], ((j / C::kAcc) - 1) & 1, local_ns)) {
           ok = false;
           break;
         }
@@ -394,7 +408,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t d = tmem + (uint32_t)(buf * TN);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int st = it % S;
-          if (!mbar_wait(&full[st], (it / S) & 1)) {
+          if (!mbar_wait(&full[st], (it / S) & 1, local_ns)) {
             ok = false;
             break;
           }
@@ -408,7 +422,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (ok) umma_commit(&acc_full[buf]);
       }
-      if (!ok) report_status(p.status, kStatusWaitTimeout, kWhereGemm, 1, blockIdx.x);
+      if (!ok) {
+        report_status(p.status, kStatusWaitTimeout, kWhereGemm, 1, blockIdx.x);
+        // Every MMA issued so far completes before TMEM is freed.
+        umma_commit(&mma_drain);
+        (void)mbar_wait(&mma_drain, 0, local_ns);
+      }
     }
   } else {
     // ---- epilogue warps ----
@@ -424,7 +443,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     while (run.get(pc)) {
       const int tile = pc.tile, j = pc.index;
       const int buf = j % C::kAcc;
-      if (!mbar_wait(&acc_full[buf], (j / C::kAcc) & 1)) s_fail = 1;
+      if (!mbar_wait(&acc_full[buf], (j / C::kAcc) & 1, local_ns)) s_fail = 1;
       epi_sync();
       if (s_fail) break;
       tc_fence_after();
@@ -462,7 +481,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         unsigned int *arrived = w.tile_counters + tile;
         if (t == 0) {
           atomic_add_acq_rel_gpu(arrived, 1u);
-          if (ci < closers && !wait_count_geq_gpu(arrived, (unsigned int)(c_last - c_first + 1), kTileWaitNs)) {
+          if (ci < closers && !wait_count_geq_gpu(arrived, (unsigned int)(c_last - c_first + 1), tile_ns)) {
             report_status(p.status, kStatusWaitTimeout, kWhereGemm, 2, tile);
             s_fail = 1;
           }

@@ -90,7 +90,7 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
     // rank's flag on this phase (one thread per source rank).
     if (p.xchg.wait && threadIdx.x < p.xchg.world) {
       const unsigned int value = *p.xchg.epoch * p.xchg.phases + p.xchg.phase + 1u;
-      if (!wait_flag_geq(peer_flag(p.xchg, p.xchg.rank, p.xchg.phase & 1, threadIdx.x), value, kPeerWaitNs))
+      if (!wait_flag_geq(peer_flag(p.xchg, p.xchg.rank, p.xchg.phase & 1, threadIdx.x), value, peer_wait_budget(p)))
         report_status(p.status, kStatusWaitTimeout, kWhereExchange, threadIdx.x, (int)p.xchg.phase);
     }
     __syncthreads();

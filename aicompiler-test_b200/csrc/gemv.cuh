@@ -133,6 +133,11 @@ struct GemvParams {
   // Bytes of W this launch may bulk-prefetch into L2 before its inputs are
   // ready (0: none).
   long long l2_prefetch_bytes;
+  // Budgets of this launch's bounded waits, in ns of global time (0: the
+  // defaults): peer_wait_ns for another rank's exchange flags (10 s),
+  // local_wait_ns for the GEMM's mbarrier and split-tile waits (1 s).
+  unsigned long long peer_wait_ns;
+  unsigned long long local_wait_ns;
   // K-split team size chosen by the decode GEMV tuner (1, 2, 4 or 8); 0: the
   // built-in rule.
   int force_ks;

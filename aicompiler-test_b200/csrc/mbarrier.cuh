@@ -7,6 +7,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace tmc {
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
@@ -24,9 +26,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
                : "memory");
 }
 
-// Bounded wait (about one second of SM clock); false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
+// Bounded wait; false on timeout. budget_ns == 0: about one second of SM
+// clock (2^31 cycles); otherwise budget_ns of global time.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned long long budget_ns = 0) {
   const long long start = clock64();
+  const unsigned long long t0 = budget_ns ? global_ns() : 0ull;
   const uint32_t addr = smem_u32(bar);
   while (true) {
     uint32_t done;
@@ -37,7 +41,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
         : "r"(addr), "r"(parity)
         : "memory");
     if (done) return true;
-    if (clock64() - start > (1ll << 31)) return false;
+    if (budget_ns == 0 ? clock64() - start > (1ll << 31) : global_ns() - t0 > budget_ns) return false;
   }
 }
 

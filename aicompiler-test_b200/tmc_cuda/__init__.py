@@ -419,6 +419,7 @@ _sig("tmc_decoder_load_weight_f16", c_int, c_void_p, c_char_p, c_void_p, c_size_
 _sig("tmc_decoder_read_weight", c_int, c_void_p, c_char_p, POINTER(c_float), c_size_t)
 _sig("tmc_decoder_init_random", c_int, c_void_p, c_uint64, c_float)
 _sig("tmc_decoder_prefill", c_int, c_void_p, c_int, _I32P, c_int, POINTER(c_float), _I32P)
+_sig("tmc_decoder_prefill_timing", c_int, c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_double))
 _sig("tmc_decoder_decode", c_int, c_void_p, _I32P, _I32P, c_int, POINTER(c_float), _I32P)
 _sig("tmc_decoder_generate", c_int, c_void_p, _I32P, _I32P, c_int, c_int, _I32P,
      POINTER(ctypes.c_double))
@@ -446,6 +447,8 @@ _sig("tmc_nccl_unique_id", c_int, ctypes.c_char_p, c_size_t)
 _sig("tmc_decoder_attach_nccl", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_int, c_int)
 _sig("tmc_decoder_exchange_handle", c_int, c_void_p, ctypes.c_char_p, c_size_t)
 _sig("tmc_decoder_attach_peers", c_int, c_void_p, ctypes.c_char_p, c_size_t, c_int, c_int)
+_sig("tmc_decoder_attach_local_peers", c_int, c_void_p, POINTER(c_void_p), c_int, c_int)
+_sig("tmc_decoder_set_wait_budgets", c_int, c_void_p, c_uint64, c_uint64)
 EXCHANGE_HANDLE_BYTES = 64
 
 
@@ -752,6 +755,12 @@ class Decoder:
                                       _fptr(out) if logits else None, nxt.ctypes.data_as(_I32P)))
         return out, int(nxt[0])
 
+    def prefill_timing(self):
+        """(gpu_us, cpu_us) of the last prefill call."""
+        g, c = ctypes.c_double(0.0), ctypes.c_double(0.0)
+        check(lib.tmc_decoder_prefill_timing(self.handle, ctypes.byref(g), ctypes.byref(c)))
+        return g.value, c.value
+
     def decode(self, tokens, slots=None, logits=True):
         t = _i32(tokens)
         s = _i32(slots if slots is not None else range(t.size))
@@ -866,6 +875,16 @@ class Decoder:
         buf = ctypes.create_string_buffer(EXCHANGE_HANDLE_BYTES)
         check(lib.tmc_decoder_exchange_handle(self.handle, buf, EXCHANGE_HANDLE_BYTES))
         return buf.raw
+
+    def attach_local_peers(self, ranks, rank: int):
+        """Attach the windows of decoders driven by this process (ranks[r]
+        is rank r's decoder, ranks[rank] is self)."""
+        arr = (c_void_p * len(ranks))(*[d.handle for d in ranks])
+        check(lib.tmc_decoder_attach_local_peers(self.handle, arr, len(ranks), rank))
+
+    def set_wait_budgets(self, peer_ns: int = 0, local_ns: int = 0):
+        """Budgets of the kernels' bounded waits in ns (0: the defaults)."""
+        check(lib.tmc_decoder_set_wait_budgets(self.handle, peer_ns, local_ns))
 
     def attach_peers(self, handles, rank: int):
         """Map every rank's window (handles in rank order) and switch the

@@ -55,6 +55,7 @@ def parse(argv=None):
                          "outputs U[64,512], max batch 128; 1000 in the full config; 0 skips)")
     ap.add_argument("--no-c1", action="store_true", help="skip the C1 RMSNorm -> GEMV measurement")
     ap.add_argument("--no-c2", action="store_true", help="skip the C2 single-layer measurement")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill / TTFT measurement")
     ap.add_argument("--collective", choices=("p2p", "nccl"), default="p2p",
                     help="TP reductions: peer exchange fused into the kernels, or NCCL allreduce")
     return ap.parse_args(argv)
@@ -213,7 +214,7 @@ def run_ours(args, world, rank, local):
     capacity = ((args.prompt + W + K + E + 32 + 15) // 16) * 16
     dec = tmc_cuda.Decoder(rt, CFG["hidden"], CFG["heads"], CFG["intermediate"], CFG["vocab"], args.layers,
                            capacity, kv_heads=CFG["kv_heads"], epsilon=CFG["epsilon"],
-                           rope_theta=CFG["rope_theta"], max_rows=8, max_slots=1, page_size=16,
+                           rope_theta=CFG["rope_theta"], max_rows=PREFILL_ROWS, max_slots=1, page_size=16,
                            tp_rank=rank, tp_size=world)
     if world > 1 and args.collective == "p2p":
         handles = [None] * world
@@ -225,6 +226,8 @@ def run_ours(args, world, rank, local):
         dec.attach_nccl(uid[0], world, rank)
     dec.init_random(seed=0, std=0.02)
     prompt = np.random.default_rng(0).integers(0, CFG["vocab"], args.prompt).astype(np.int32)
+    # Decode steps run the GEMVs (1 row); the prompt is prefilled in
+    # PREFILL_ROWS-row chunks on the tcgen05 GEMMs.
     _, tok = dec.prefill(prompt, logits=False)
 
     # warm-up (also builds the step graph)
@@ -251,7 +254,7 @@ def run_ours(args, world, rank, local):
         tok = int(n[0])
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0)
-    e2e = {"value": E / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 3 * 8 * 4, "d2h_bytes_per_step": 4,
+    e2e = {"value": E / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 3 * PREFILL_ROWS * 4, "d2h_bytes_per_step": 4,
            "api": "tmc_decoder_decode (token in from pinned host memory, next token out)"}
 
     ctx = args.prompt + W + K + E
@@ -290,6 +293,10 @@ def run_ours(args, world, rank, local):
         except Exception as exc:  # noqa: BLE001
             print(f"[bench] {name} failed on rank {rank}: {exc}", file=sys.stderr, flush=True)
             return {"error": f"{type(exc).__name__}: {exc}"[:400]}
+
+    prefill = None
+    if not args.no_prefill:
+        prefill = guarded("prefill", lambda: measure_prefill(dec, prompt, args, world, barrier, max_over_ranks))
 
     batched = None
     if not args.no_batch:
@@ -338,6 +345,7 @@ def run_ours(args, world, rank, local):
             "gpu_launches": launches,
             "roofline": roofline,
             "kernels": kernels,
+            "prefill": prefill,
             "bs64": batched,
             "c1": c1,
             "c2": c2,
@@ -351,6 +359,71 @@ def run_ours(args, world, rank, local):
         dec.close()
         dist.destroy_process_group()
     return 0
+
+
+PREFILL_ROWS = 128  # prompt rows per prefill chunk (tcgen05 GEMM token columns)
+
+
+def prefill_flops(n, layers=None):
+    """Algorithmic FLOPs of prefilling an n-token prompt and producing its
+    first token: every linear layer for all n rows (2 flops per weight per
+    row), causal attention (QK^T and PV over positions 0..t for row t), and
+    the LM head for the last row only."""
+    L = CFG["layers"] if layers is None else layers
+    H, I, V = CFG["hidden"], CFG["intermediate"], CFG["vocab"]
+    D = H // CFG["heads"]
+    qkv = H * (CFG["heads"] + 2 * CFG["kv_heads"]) * D
+    per_row = 2 * L * (qkv + H * H + 3 * I * H)
+    attn = L * CFG["heads"] * 4 * D * (n * (n + 1) // 2)
+    return per_row * n + attn + 2 * V * H
+
+
+def measure_prefill(dec, prompt, args, world, barrier, max_over_ranks):
+    """TTFT of the headline model: the 1024-token prompt prefilled into an
+    empty slot in PREFILL_ROWS-row chunks on the tcgen05 GEMMs (chunks queued
+    back to back), through tmc_decoder_prefill with the prompt in host memory
+    and the first token read back. 1 untimed + 7 timed prefills; medians.
+    value = prompt tokens / device time; the roofline is tensor-bound
+    (prefill_flops over the measured sustained bf16 dense peak; fp16 and bf16
+    run at the same tensor rate)."""
+    import numpy as np
+    reps = 7
+    gpu, wall = [], []
+    for i in range(reps + 1):
+        dec.release(0)
+        barrier()
+        t0 = time.perf_counter()
+        dec.prefill(prompt, logits=False)
+        barrier()
+        w = max_over_ranks(time.perf_counter() - t0)
+        g = max_over_ranks(dec.prefill_timing()[0])
+        if i:
+            gpu.append(g)
+            wall.append(w)
+    gpu_us = float(np.median(gpu))
+    wall_s = float(np.median(wall))
+    flops = prefill_flops(len(prompt), args.layers)
+    tflops = flops / (gpu_us * 1e-6) / 1e12
+    peak = measured_tensor_peak()
+    return {"metric": "prefill tok/s (TTFT of a 1024-token prompt)", "value": len(prompt) / (gpu_us * 1e-6),
+            "unit": "tok/s", "ttft_ms": wall_s * 1e3, "gpu_ms": gpu_us / 1e3,
+            "ttft_ms_samples": [round(x * 1e3, 3) for x in wall], "chunk_rows": PREFILL_ROWS,
+            "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak[0] * world, "unit": "TFLOP/s",
+                         "frac": tflops / (peak[0] * world), "flops": flops, "peak_source": peak[1]},
+            "e2e": {"value": len(prompt) / wall_s, "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt),
+                    "d2h_bytes_per_step": 4, "api": "tmc_decoder_prefill (prompt from host memory, first token out)"},
+            "config": {"workload": "C3 prefill: 1024-token random prompt, batch 1, empty cache", "reps": reps,
+                       "statistic": "median"}}
+
+
+def measured_tensor_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            m = json.load(f)
+        return float(m["bf16_tflops_sustained"]), "measured bf16_tflops_sustained (MEASURED_PEAKS.json)"
+    except Exception:
+        return 1400.0, "fallback sustained bf16 dense"
 
 
 def events(rt):

@@ -410,6 +410,11 @@ int tmc_decoder_init_random(tmc_decoder *dec, uint64_t seed, float stddev);
  * last position. */
 int tmc_decoder_prefill(tmc_decoder *dec, int slot, const int32_t *tokens, int count,
                         float *logits, int32_t *next_token);
+/* Timing of the last tmc_decoder_prefill (the reference's prefill timing in
+ * DecoderLLMExecutor.cpp:982-1034): gpu_us = device time from the first
+ * chunk's input copy to the last chunk's token readback (CUDA events on the
+ * executor stream); cpu_us = host time of the whole call. */
+int tmc_decoder_prefill_timing(tmc_decoder *dec, double *gpu_us, double *cpu_us);
 /* CompiledDecoderLLM::decode (DecoderLLMExecutor.hpp:59-60) for `rows`
  * sequences at once (distinct slots): stage length+1, run the step graph,
  * commit. logits: NULL or [rows, local_vocab]; next_tokens: [rows]. */
@@ -498,6 +503,17 @@ int tmc_decoder_attach_nccl(tmc_decoder *dec, const uint8_t *id, size_t nbytes, 
 int tmc_decoder_exchange_handle(tmc_decoder *dec, uint8_t *handle, size_t nbytes);
 int tmc_decoder_attach_peers(tmc_decoder *dec, const uint8_t *handles, size_t nbytes_each, int world,
                              int rank);
+/* The same for ranks driven by one process: ranks[r] is rank r's decoder
+ * (ranks[rank] == dec), each on a device with peer access to dec's; their
+ * windows are used directly. Each rank attaches once. */
+int tmc_decoder_attach_local_peers(tmc_decoder *dec, tmc_decoder *const *ranks, int world, int rank);
+/* Budgets of the decoder kernels' bounded waits, in ns of global time (0: the
+ * defaults, 10 s for another rank's exchange flags and 1 s for the tensor-core
+ * GEMM's mbarrier and split-tile waits). A wait that runs out is recorded in
+ * the device status block, the kernel drains its own copies in flight, frees
+ * its tensor memory and returns, and the call returns TMC_ERR_DEVICE_STATUS;
+ * the runtime stays usable. */
+int tmc_decoder_set_wait_budgets(tmc_decoder *dec, uint64_t peer_wait_ns, uint64_t local_wait_ns);
 
 /* ---- continuous batching (replaces runContinuousBatch,
  * src/runtime/ServingRuntime.hpp:73-76, ServingRuntime.cpp:513-930) ----
