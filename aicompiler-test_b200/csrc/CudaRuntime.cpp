@@ -337,11 +337,21 @@ std::string describeDeviceStatus(const tmc::TmcDeviceStatus &s) {
     case tmc::kStatusLengthRange: out << "position " << s.info0 << " outside the cache capacity (row " << s.info1 << ")"; break;
     case tmc::kStatusPageMissing: out << "logical page " << s.info0 << " has no physical page (row " << s.info1 << ")"; break;
     case tmc::kStatusPageRange: out << "physical page " << s.info0 << " outside the page pool (row " << s.info1 << ")"; break;
-    case tmc::kStatusWaitTimeout: out << "bounded wait timed out (tile " << s.info0 << ", row " << s.info1 << ")"; break;
+    case tmc::kStatusWaitTimeout:
+      if (s.where == tmc::kWhereExchange)
+        out << "bounded wait timed out for rank " << s.info0 << "'s exchange flag (phase " << s.info1 << ")";
+      else
+        out << "bounded wait timed out (tile " << s.info0 << ", row " << s.info1 << ")";
+      break;
     case tmc::kStatusShape: out << "shape mismatch (" << s.info0 << ", " << s.info1 << ")"; break;
     default: out << "code " << s.code;
   }
-  out << " [kernel " << s.where << "]";
+  static const char *const kSites[] = {"", "gemv", "attention", "embedding", "lm head", "cache append", "misc",
+                                       "gemm", "peer exchange"};
+  if (s.where > 0 && s.where < (int)(sizeof(kSites) / sizeof(kSites[0])))
+    out << " [" << kSites[s.where] << "]";
+  else
+    out << " [kernel " << s.where << "]";
   return out.str();
 }
 

@@ -1,14 +1,15 @@
 // Batched decode projections on tcgen05 tensor cores (see gemm.cuh).
 //
 // One persistent CTA per SM, 10 warps, warp-specialised:
-//   warp 0    TMA producer: streams 128-row x 64-column weight tiles (A) and
-//             the matching 64-column slice of the token rows (B) into a ring
-//             of shared-memory stages (128-byte swizzle). Weight tiles do not
+//   warp 0    TMA producer: streams 128-row x (64 x atoms)-column weight
+//             tiles (A, one 64-column swizzle atom per TMA box) and the
+//             matching columns of the token rows (B) into a ring of
+//             shared-memory stages (128-byte swizzle). Weight tiles do not
 //             depend on earlier kernels, so the first ring-full is requested
 //             before the programmatic-dependency wait;
 //   warp 1    owns the tensor memory (four TN-column fp32 accumulators) and
-//             issues the MMAs from one thread: 4 x (M=128, N=TN, K=16) per
-//             stage, tcgen05.commit frees the stage, a final commit hands the
+//             issues the MMAs from one thread: 4 x atoms (M=128, N=TN,
+//             K=16) per stage, tcgen05.commit frees the stage, a final commit hands the
 //             accumulator to the epilogue;
 //   warps 2-9 epilogue, two per 32-lane quarter of the accumulator (warp w
 //             reads lanes 32 (w % 4) ..), taking alternate 16-token groups:
@@ -56,9 +57,11 @@ constexpr int kTileBytesA = kGemmTileRows * kGemmKBlock * 2;  // 16 KB
 
 template <int TN>
 struct GemmCfg {
-  static constexpr int kBytesB = TN * kGemmKBlock * 2;
-  static constexpr int kStageBytes = kTileBytesA + kBytesB;
-  static constexpr int kStages = (200 * 1024 / kStageBytes) < 8 ? (200 * 1024 / kStageBytes) : 8;
+  static constexpr int kAtoms = gemm_k_atoms(TN);
+  static constexpr int kBytesB = TN * kGemmKBlock * 2;  // one atom of token rows
+  static constexpr int kStageBytes = kAtoms * (kTileBytesA + kBytesB);
+  static constexpr int kStages = (216 * 1024 / kStageBytes) < 8 ? (216 * 1024 / kStageBytes) : 8;
+  static_assert(kStages >= 2, "a pipeline needs two stages");
   static constexpr int kAcc = 4;  // accumulators in tensor memory (epilogues overlap later MMAs)
   static constexpr int kTmemCols = kAcc * TN < 32 ? 32 : kAcc * TN;  // a power of two, <= 512
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256;
@@ -287,9 +290,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *base = reinterpret_cast<unsigned char *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char *sA = base;
-  unsigned char *sB = base + (size_t)S * kTileBytesA;
-  uint64_t *full = reinterpret_cast<uint64_t *>(sB + (size_t)S * C::kBytesB);
+  constexpr int A = C::kAtoms;
+  unsigned char *sA = base;                                  // [S][A] weight atoms
+  unsigned char *sB = base + (size_t)S * A * kTileBytesA;    // [S][A] token atoms
+  uint64_t *full = reinterpret_cast<uint64_t *>(sB + (size_t)S * A * C::kBytesB);
   uint64_t *empty = full + S;
   uint64_t *acc_full = empty + S;
   uint64_t *acc_empty = acc_full + C::kAcc;
@@ -342,6 +346,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int s = 0; s < S; ++s) last_it[s] = -1;
       int it = 0;
       bool waited = false, ok = true;
+      // The token atoms of stage st, K block kb (A adjacent 64-column boxes).
+      auto load_x = [&](int st, int kb) {
+#pragma unroll
+        for (int a = 0; a < A; ++a)
+          tma_load_2d(sB + ((size_t)st * A + a) * C::kBytesB, &x_map, (kb * A + a) * kGemmKBlock, 0, &full[st]);
+      };
       RunCursor run(w);
       Piece pc;
       while (ok && run.get(pc)) {
@@ -353,8 +363,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // then request the token slices of those stages.
             pdl_wait();
             if (p.trace.records) s_ready = global_ns();
-            for (int j = 0; j < S; ++j)
-              tma_load_2d(sB + (size_t)j * C::kBytesB, &x_map, pending_kb[j] * kGemmKBlock, 0, &full[j]);
+            for (int j = 0; j < S; ++j) load_x(j, pending_kb[j]);
             waited = true;
           }
           if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, local_ns)) {
@@ -362,10 +371,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           last_it[st] = it;
+          // Atoms past K (a ragged last block) read as zeros and add nothing.
           mbar_arrive_expect_tx(&full[st], C::kStageBytes);
-          tma_load_2d(sA + (size_t)st * kTileBytesA, &w_map, kb * kGemmKBlock, tile * kGemmTileRows, &full[st]);
+#pragma unroll
+          for (int a = 0; a < A; ++a)
+            tma_load_2d(sA + ((size_t)st * A + a) * kTileBytesA, &w_map, (kb * A + a) * kGemmKBlock,
+                        tile * kGemmTileRows, &full[st]);
           if (waited) {
-            tma_load_2d(sB + (size_t)st * C::kBytesB, &x_map, kb * kGemmKBlock, 0, &full[st]);
+            load_x(st, kb);
           } else {
             pending_kb[st] = kb;
           }
@@ -375,8 +388,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         pdl_wait();
         if (p.trace.records) s_ready = global_ns();
         const int n = it < S ? it : S;
-        for (int j = 0; j < n; ++j)
-          tma_load_2d(sB + (size_t)j * C::kBytesB, &x_map, pending_kb[j] * kGemmKBlock, 0, &full[j]);
+        for (int j = 0; j < n; ++j) load_x(j, pending_kb[j]);
       }
       pdl_launch_dependents();
       if (!ok) report_status(p.status, kStatusWaitTimeout, kWhereGemm, 0, blockIdx.x);
@@ -413,11 +425,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint64_t da = sw128_desc(sA + (size_t)st * kTileBytesA);
-          const uint64_t db = sw128_desc(sB + (size_t)st * C::kBytesB);
 #pragma unroll
-          for (int k = 0; k < kGemmKBlock / 16; ++k)  // +32 bytes along K per step
-            umma_f16(d, da + 2u * k, db + 2u * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          for (int a = 0; a < A; ++a) {
+            const uint64_t da = sw128_desc(sA + ((size_t)st * A + a) * kTileBytesA);
+            const uint64_t db = sw128_desc(sB + ((size_t)st * A + a) * C::kBytesB);
+#pragma unroll
+            for (int k = 0; k < kGemmKBlock / 16; ++k)  // +32 bytes along K per step
+              umma_f16(d, da + 2u * k, db + 2u * k, idesc, (kb > kb0 || a > 0 || k > 0) ? 1u : 0u);
+          }
           umma_commit(&empty[st]);
         }
         if (ok) umma_commit(&acc_full[buf]);
@@ -672,9 +687,11 @@ GemmPlan plan_gemm(int N, int K, int M, int num_sms) {
   GemmPlan g{};
   g.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   g.tiles = (N + kGemmTileRows - 1) / kGemmTileRows;
-  g.kblocks = (K + kGemmKBlock - 1) / kGemmKBlock;  // a ragged last block reads zeros
+  const int block = kGemmKBlock * gemm_k_atoms(g.tn);
+  g.kblocks = (K + block - 1) / block;  // a ragged last block reads zeros
   const long long iters = (long long)g.tiles * g.kblocks;
-  long long grid = iters / kGemmMinRun;
+  const int min_run = (kGemmMinRun + block - 1) / block;
+  long long grid = iters / min_run;
   if (grid > num_sms) grid = num_sms;
   if (grid < 1) grid = 1;
   g.grid = (int)grid;
@@ -721,7 +738,7 @@ cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUt
                         bool pdl) {
   if (p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 128 ||
       plan.tiles != (p.N + kGemmTileRows - 1) / kGemmTileRows ||
-      plan.kblocks != (p.K + kGemmKBlock - 1) / kGemmKBlock ||
+      plan.kblocks != (p.K + kGemmKBlock * gemm_k_atoms(plan.tn) - 1) / (kGemmKBlock * gemm_k_atoms(plan.tn)) ||
       plan.grid < 1 || plan.grid > (long long)plan.tiles * plan.kblocks ||  // every run non-empty
       tile_counters == nullptr || (gemm_workspace_floats(plan) > 0 && ws == nullptr))
     return cudaErrorInvalidValue;

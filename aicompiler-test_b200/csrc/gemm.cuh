@@ -18,7 +18,12 @@
 namespace tmc {
 
 constexpr int kGemmTileRows = 128;  // weight rows per tile (UMMA M)
-constexpr int kGemmKBlock = 64;     // K elements per pipeline stage: one 128-byte swizzle row
+constexpr int kGemmKBlock = 64;     // K elements of one 128-byte swizzle atom (one TMA box)
+// Swizzle atoms per pipeline stage, adjacent along K: each stage fetches
+// 64 * atoms contiguous weight elements of each of its 128 rows (512 B for
+// up to 64 tokens, 256 B for 128), long enough runs for the DRAM pages (one
+// 128-byte run per row per stage streamed ~20% slower).
+__host__ __device__ constexpr int gemm_k_atoms(int tn) { return tn <= 64 ? 4 : 2; }
 
 // Stream-K work division: the tiles x kblocks (tile, K block) iterations, in
 // tile-major order, are cut into `grid` contiguous equal runs, one per
@@ -29,11 +34,11 @@ constexpr int kGemmKBlock = 64;     // K elements per pipeline stage: one 128-by
 struct GemmPlan {
   int tn;       // token columns per MMA (16, 32, 64 or 128), >= M
   int tiles;    // ceil(N / 128)
-  int kblocks;  // ceil(K / 64)
+  int kblocks;  // ceil(K / (64 * gemm_k_atoms(tn))): K blocks of one pipeline stage
   int grid;     // persistent CTAs (one per SM at most, each with >= kGemmMinRun iterations)
 };
 
-constexpr int kGemmMinRun = 4;  // fewest K blocks a CTA streams (shorter runs cost more in partials)
+constexpr int kGemmMinRun = 256;  // fewest K elements a CTA streams (shorter runs cost more in partials)
 
 GemmPlan plan_gemm(int N, int K, int M, int num_sms);
 // fp32 elements of partial-tile workspace the plan needs (0 when every run is
