@@ -95,6 +95,7 @@ std::string importDecoderManifest(const std::string &path, DecoderManifest *out)
       if (!(in >> m.requestedDtype) || !knownDtype(m.requestedDtype))
         throw std::runtime_error("Unsupported decoder-only dtype.");
       m.effectiveDtype = m.requestedDtype;
+      m.dtypeLine = true;
       if (m.version == 2 && (!(in >> m.effectiveDtype) || !knownDtype(m.effectiveDtype)))
         throw std::runtime_error("Unsupported effective decoder-only dtype.");
       if (!(in >> marker)) throw std::runtime_error("Missing decoder-only tensor section.");

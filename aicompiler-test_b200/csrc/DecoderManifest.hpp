@@ -38,6 +38,7 @@ struct DecoderManifest {
   double ropeTheta = 10000.0;  // RoPE base of the rope.cosine / rope.sine tables
   bool attentionLine = false;
   std::string requestedDtype = "F32", effectiveDtype = "F32";  // F32, F16 or BF16
+  bool dtypeLine = false;  // the manifest carries a DTYPE marker
   std::map<std::string, std::pair<std::size_t, std::size_t>> ranges;  // name -> (offset, count) in floats
   std::vector<float> payload;
 

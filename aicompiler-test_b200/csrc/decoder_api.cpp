@@ -160,6 +160,13 @@ int tmc_decoder_load_manifest(tmc_decoder *dec, const tmc_manifest *m) {
     if (x.second.first != x.second.second)
       return fail(TMC_ERR_INVALID, std::string("decoder ") + x.first + " " + std::to_string(x.second.first) +
                                        " does not match the manifest's " + std::to_string(x.second.second));
+  // The reference resolves fp32, fp16 or bf16 storage (DecoderLLMExecutor.cpp:1218-1240);
+  // this backend's decoder stores and computes in fp16 only, so a manifest
+  // exported for another storage type is refused rather than silently converted.
+  if (d.dtypeLine && d.effectiveDtype != "F16")
+    return fail(TMC_ERR_UNSUPPORTED, "decoder storage dtype is fp16 on this backend; the manifest asks for " +
+                                         d.effectiveDtype + " (requested " + d.requestedDtype +
+                                         "): re-export it with DTYPE F16");
   for (const auto &name : tensor::importer::decoderWeightNames(m->m.layers)) {
     size_t count = 0;
     const float *v = m->m.tensor(name, &count);

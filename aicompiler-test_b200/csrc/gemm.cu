@@ -452,6 +452,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = ew >> 2;  // this warp's 16-token groups: half, half + 2, ...
     const int t = threadIdx.x - 64;
     const int r = q * 32 + lane;
+    if constexpr (EK == kEkQKV) {
+      // One thread per token resolves its position and KV slot (page
+      // lookup, range checks) once for the launch, off the tiles' critical
+      // path (the step inputs are final once the dependency wait returned);
+      // -1 marks a failed check.
+      if (t < p.M) {
+        const int pos = p.positions[t];
+        long long slot = -1;
+        const int ps = p.page_size;
+        if (pos < 0 || pos >= p.capacity) {
+          report_status(p.status, kStatusLengthRange, kWhereAppend, pos, t);
+        } else {
+          const int lp = pos / ps, off = pos % ps;
+          if (lp >= p.table_stride) {
+            report_status(p.status, kStatusLengthRange, kWhereAppend, pos, t);
+          } else {
+            const int page = p.block_table[(size_t)p.table_rows[t] * p.table_stride + lp];
+            if (page < 0 || page >= p.pool_pages) {
+              report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
+                            page < 0 ? lp : page, t);
+            } else {
+              slot = ((long long)page * (p.kv_rows / p.head_dim) * ps + off) * p.head_dim;
+            }
+          }
+        }
+        tok_pos[t] = (pos < 0 || pos >= p.capacity) ? -1 : pos;  // q rows need only the position
+        tok_slot[t] = slot;
+      }
+      epi_sync();
+    }
     const long long iters = (long long)w.tiles * w.kblocks;
     RunCursor run(w);
     Piece pc;
@@ -504,34 +534,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         epi_sync();
         if (ci >= closers) continue;  // not a closer: its run goes on
         if (s_fail) break;
-      }
-      if constexpr (EK == kEkQKV) {
-        // One thread per token resolves its position and KV slot (page
-        // lookup, range checks) once for the tile; -1 marks a failed check.
-        if (t < p.M) {
-          const int pos = p.positions[t];
-          long long slot = -1;
-          const int ps = p.page_size;
-          if (pos < 0 || pos >= p.capacity) {
-            report_status(p.status, kStatusLengthRange, kWhereAppend, pos, t);
-          } else {
-            const int lp = pos / ps, off = pos % ps;
-            if (lp >= p.table_stride) {
-              report_status(p.status, kStatusLengthRange, kWhereAppend, pos, t);
-            } else {
-              const int page = p.block_table[(size_t)p.table_rows[t] * p.table_stride + lp];
-              if (page < 0 || page >= p.pool_pages) {
-                report_status(p.status, page < 0 ? kStatusPageMissing : kStatusPageRange, kWhereAppend,
-                              page < 0 ? lp : page, t);
-              } else {
-                slot = ((long long)page * (p.kv_rows / p.head_dim) * ps + off) * p.head_dim;
-              }
-            }
-          }
-          tok_pos[t] = (pos < 0 || pos >= p.capacity) ? -1 : pos;  // q rows need only the position
-          tok_slot[t] = slot;
-        }
-        epi_sync();
       }
       // Groups this CTA applies: all of a whole tile, or a closer's share.
       const int assigned = whole ? groups : (ci < groups ? (groups - ci + closers - 1) / closers : 0);

@@ -3,6 +3,7 @@
     python -m tmc_cuda.cases gemm --rows 64 --n 28672 --k 4096 [--reps 20]
     python -m tmc_cuda.cases attention --rows 64 --ctx 1152 [--hq 32 --hkv 8 --d 128 --page 16]
     python -m tmc_cuda.cases gemv --rows 1 --n 28672 --k 4096
+    python -m tmc_cuda.cases rmsnorm --rows 16384 --k 4096 [--fp16] [--threads 256]
 
 Each case builds seeded inputs on the device (larger than L2 where the shape
 allows), launches the kernel `--warmup` times, then `--reps` times between
@@ -69,6 +70,25 @@ def case_gemv(rt, a):
             "gbs": nbytes / us / 1e3}
 
 
+def case_rmsnorm(rt, a):
+    """RMSNormOp (emitRMSNorm) over [rows, k]: x, gamma and y all fp32 or all
+    fp16 (--fp16); one CTA per row with --threads threads (0: the baseline)."""
+    import tmc_cuda
+    dt = tmc_cuda.F16 if a.fp16 else tmc_cuda.F32
+    size = 2 if a.fp16 else 4
+    x = rt.buffer(a.rows * a.k, dt)
+    if a.fp16:
+        tmc_cuda.fill_normal_f16(rt, x, 4, 0.0, 1.0)
+    else:
+        x.write(np.random.default_rng(0).standard_normal(a.rows * a.k).astype(np.float32))
+    g = rt.upload(np.random.default_rng(1).uniform(0.5, 1.5, a.k).astype(np.float16 if a.fp16 else np.float32))
+    y = rt.buffer(a.rows * a.k, dt)
+    us = _time(rt, lambda: tmc_cuda.rmsnorm(rt, x, g, y, a.rows, a.k, 1e-5, a.threads), a.warmup, a.reps)
+    nbytes = 2 * size * a.rows * a.k + size * a.k
+    return {"kernel": "rmsnorm_kernel", "rows": a.rows, "width": a.k, "dtype": "f16" if a.fp16 else "f32",
+            "threads": a.threads, "us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
+
+
 def case_attention(rt, a):
     import tmc_cuda
     rng = np.random.default_rng(0)
@@ -113,7 +133,7 @@ def case_attention(rt, a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=("gemm", "gemv", "attention"))
+    ap.add_argument("case", choices=("gemm", "gemv", "attention", "rmsnorm"))
     ap.add_argument("--rows", type=int, default=64)
     ap.add_argument("--n", type=int, default=28672)
     ap.add_argument("--k", type=int, default=4096)
@@ -126,12 +146,14 @@ def main(argv=None):
     ap.add_argument("--splits", type=int, default=0, help="attention max splits (0: the decoder's policy)")
     ap.add_argument("--min-chunk", type=int, default=64, help="attention positions per split at least")
     ap.add_argument("--pool-pages", type=int, default=0, help="attention page pool size (at least what fits)")
+    ap.add_argument("--fp16", action="store_true", help="rmsnorm: fp16 x, gamma and y (default fp32)")
+    ap.add_argument("--threads", type=int, default=256, help="rmsnorm: threads per row (0: the baseline)")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--reps", type=int, default=20)
     a = ap.parse_args(argv)
     import tmc_cuda
     rt = tmc_cuda.Runtime(0)
-    fn = {"gemm": case_gemm, "gemv": case_gemv, "attention": case_attention}[a.case]
+    fn = {"gemm": case_gemm, "gemv": case_gemv, "attention": case_attention, "rmsnorm": case_rmsnorm}[a.case]
     print(json.dumps(fn(rt, a)), flush=True)
     rt.close()
     return 0

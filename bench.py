@@ -40,7 +40,7 @@ CFG = dict(hidden=4096, heads=32, kv_heads=8, intermediate=14336, vocab=128256, 
 def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--steps", type=int, default=256, help="timed decode steps (C3: 256, contexts 1025..1280)")
     ap.add_argument("--warmup", type=int, default=4)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--prompt", type=int, default=1024)
@@ -211,7 +211,8 @@ def run_ours(args, world, rank, local):
     rt = tmc_cuda.Runtime(local)
     W, K = max(3, args.warmup), args.steps
     E = K
-    capacity = ((args.prompt + W + K + E + 32 + 15) // 16) * 16
+    SAMPLES, SAMPLE_STEPS = 31, 8
+    capacity = ((args.prompt + W + K + E + SAMPLES * SAMPLE_STEPS + 32 + 15) // 16) * 16
     dec = tmc_cuda.Decoder(rt, CFG["hidden"], CFG["heads"], CFG["intermediate"], CFG["vocab"], args.layers,
                            capacity, kv_heads=CFG["kv_heads"], epsilon=CFG["epsilon"],
                            rope_theta=CFG["rope_theta"], max_rows=PREFILL_ROWS, max_slots=1, page_size=16,
@@ -246,6 +247,18 @@ def run_ours(args, world, rank, local):
     value = K / (gpu_us * 1e-6)
     launches = dec.kernels_per_step(1) * K
 
+    # Per-sample statistics as the reference's Benchmark reports them
+    # (median / p90 over >= 31 samples): 31 device loops of 8 steps each.
+    per_step = []
+    for _ in range(SAMPLES):
+        o, us = dec.generate([tok], SAMPLE_STEPS)
+        tok = int(o[-1, 0])
+        per_step.append(us / SAMPLE_STEPS / 1e3)
+    samples = {"n": SAMPLES, "steps_each": SAMPLE_STEPS,
+               "ms_per_step_median": max_over_ranks(float(np.median(per_step))),
+               "ms_per_step_p90": max_over_ranks(float(np.percentile(per_step, 90))),
+               "ms_per_step_min": max_over_ranks(float(np.min(per_step)))}
+
     # e2e through the per-step public API with host buffers
     barrier()
     t0 = time.perf_counter()
@@ -257,8 +270,9 @@ def run_ours(args, world, rank, local):
     e2e = {"value": E / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 3 * PREFILL_ROWS * 4, "d2h_bytes_per_step": 4,
            "api": "tmc_decoder_decode (token in from pinned host memory, next token out)"}
 
-    ctx = args.prompt + W + K + E
-    step_bytes = dec.step_bytes([ctx - E // 2])
+    # Bytes of the mean timed step: the KV read grows with the context, which
+    # runs from prompt + W + 1 to prompt + W + K over the timed steps.
+    step_bytes = dec.step_bytes([args.prompt + W + (K + 1) // 2])
     hbm, peak_kind = measured_peaks()
     kernels = {}
     roofline = None
@@ -342,6 +356,8 @@ def run_ours(args, world, rank, local):
                               "aggregate_peak_gbs": hbm * world,
                               "frac": step_bytes / (step_ms * 1e-3) / 1e9 / hbm},
             "e2e": e2e,
+            "samples": samples,
+            "timed_contexts": [args.prompt + W + 1, args.prompt + W + K],
             "gpu_launches": launches,
             "roofline": roofline,
             "kernels": kernels,

@@ -282,6 +282,29 @@ def test_gqa_model_matches_oracle(rt, kv_heads, theta, hidden, heads):
     tokens.report()
 
 
+@pytest.mark.parametrize("dtypes", [("F32", "F32"), ("BF16", "BF16"), ("BF16", "F16")])
+def test_manifest_for_another_storage_dtype(rt, tmp_path, dtypes):
+    # The reference runs fp32, fp16 and bf16 decoders (storage resolved in
+    # DecoderLLMExecutor.cpp:1218-1240); this decoder is fp16 only. A manifest
+    # whose effective dtype is not F16 is refused with a clear error; one
+    # requested as bf16 that fell back to fp16 storage loads.
+    import tmc_cuda
+    from tests.manifest_writer import golden_manifest
+    path, meta, g = golden_manifest(tmp_path, os.path.join(GOLDEN, "decoder_default_fp16.npz"), dtypes=dtypes)
+    m = tmc_cuda.Manifest(path)
+    if dtypes[1] == "F16":
+        dec = m.decoder(rt)
+        _, nxt = dec.prefill(m.tensor("prefill.tokens").astype(np.int32), logits=False)
+        assert int(nxt) == int(m.tensor("prefill.next_tokens")[0])
+        dec.close()
+    else:
+        with pytest.raises(tmc_cuda.TmcError) as err:
+            m.decoder(rt)
+        assert err.value.code == tmc_cuda.ERR_UNSUPPORTED
+        assert "fp16" in err.value.message and dtypes[1] in err.value.message
+    m.close()
+
+
 def test_decoder_from_reference_manifest_matches_exporter(rt, tmp_path):
     # The exporter's manifest format (written from the golden fixture), loaded
     # through the importer into a decoder: greedy tokens bit-exact, logits

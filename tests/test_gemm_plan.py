@@ -8,14 +8,21 @@ workspace slot, and the closers are the pieces whose runs end inside the tile.""
 
 import pytest
 
-TILE_ROWS, KBLOCK, MIN_RUN, SMS = 128, 64, 4, 148
+TILE_ROWS, ATOM, MIN_RUN_K, SMS = 128, 64, 256, 148
+
+
+def k_atoms(tn):
+    """64-column swizzle atoms per pipeline stage (gemm.cuh gemm_k_atoms)."""
+    return 4 if tn <= 64 else 2
 
 
 def plan(n, k, m, sms=SMS):
     tn = 16 if m <= 16 else 32 if m <= 32 else 64 if m <= 64 else 128
-    tiles, kblocks = (n + TILE_ROWS - 1) // TILE_ROWS, (k + KBLOCK - 1) // KBLOCK
+    block = ATOM * k_atoms(tn)  # K elements per pipeline stage
+    tiles, kblocks = (n + TILE_ROWS - 1) // TILE_ROWS, (k + block - 1) // block
     iters = tiles * kblocks
-    grid = max(1, min(sms, iters // MIN_RUN))
+    min_run = (MIN_RUN_K + block - 1) // block
+    grid = max(1, min(sms, iters // min_run))
     return tn, tiles, kblocks, grid
 
 

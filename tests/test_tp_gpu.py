@@ -6,8 +6,12 @@ checks of decoder_llm_main.cpp:122-166).
 
 Every rank's greedy tokens must equal the recorded ones bit for bit; the
 logits slices concatenated in rank order and the KV heads concatenated in rank
-order must meet the north-star tolerance max|err| <= 2e-3 x RMS. Needs >= 2
-GPUs; skipped otherwise."""
+order must meet the north-star tolerance max|err| <= 2e-3 x RMS. The GQA model
+at the C3 head shape (hidden 4096) is checked against the CPU oracle with the
+oracle's own noise floor (a twin with a permuted fp32 summation order; the
+criterion of tests/parity_util.py), since at that width the twin itself has a
+few percent of its logits beyond 2e-3 x RMS. Needs >= 2 GPUs; skipped
+otherwise."""
 
 import json
 import multiprocessing as mp
@@ -199,21 +203,28 @@ def gqa_reference():
     cos = torch.from_numpy(dec.read_weight("rope.cosine", cap * half).reshape(cap, half))
     sin = torch.from_numpy(dec.read_weight("rope.sine", cap * half).reshape(cap, half))
     oracle = DecoderOracle(spec, w, cos, sin)
+    # The noise floor: the same oracle with a permuted fp32 summation order,
+    # teacher-forced with the oracle's tokens (at hidden 4096 a few percent of
+    # its own logits lie beyond 2e-3 x RMS of the oracle's).
+    twin = oracle.fork(summation_order_seed=7)
     prompt = np.random.default_rng(51).integers(0, V, 40).astype(np.int32)
-    logits, tokens = [], []
+    logits, tokens, twin_logits = [], [], []
     lo, to = oracle.forward(0, prompt)
     logits.append(lo.float().numpy())
     tokens.append(to)
+    twin_logits.append(twin.forward(0, prompt)[0].float().numpy())
     for _ in range(8):
+        twin_logits.append(twin.forward(0, [tokens[-1]])[0].float().numpy())
         lo, to = oracle.forward(0, [tokens[-1]])
         logits.append(lo.float().numpy())
         tokens.append(to)
     single = [dec.prefill(prompt)[0]] + [dec.decode([t])[0] for t in tokens[:-1]]
     kv = [tuple(x.float().numpy() for x in oracle.caches[0][layer]) for layer in range(spec.layers)]
+    twin_kv = [tuple(x.float().numpy() for x in twin.caches[0][layer]) for layer in range(spec.layers)]
     dec.close()
     rt.close()
     _GQA_REFERENCE.update({"prompt": prompt, "feed": tokens[:-1], "logits": logits, "tokens": tokens,
-                           "single": single, "kv": kv})
+                           "single": single, "kv": kv, "twin_logits": twin_logits, "twin_kv": twin_kv})
     return _GQA_REFERENCE
 
 
@@ -232,8 +243,10 @@ def test_tensor_parallel_gqa_matches_oracle(world, mode):
     for step in range(len(ref["logits"])):
         got = np.concatenate([r["logits"][step] for r in ranks], axis=-1)
         what = f"TP{world} {mode} GQA {'prefill' if step == 0 else f'decode {step - 1}'} logits"
-        fp16_close(got, ref["logits"][step], what)
-        fp16_close(got, ref["single"][step], what + " vs the single-GPU decoder")
+        noise = fp16_close(got, ref["logits"][step], what, twin=ref["twin_logits"][step])
+        # TP and the single-GPU decoder differ by summation order, as the twin does.
+        fp16_close(got, ref["single"][step], what + " vs the single-GPU decoder", floor=noise["noise_floor"],
+                   twin_outside_fraction=noise["twin_outside_fraction"])
         for r in ranks:
             assert r["tokens"][step] == ranks[0]["tokens"][step]  # every rank finalises the same token
         tokens.check(ranks[0]["tokens"][step], ref["tokens"][step], ref["logits"][step][-1], got[-1])
@@ -241,5 +254,6 @@ def test_tensor_parallel_gqa_matches_oracle(world, mode):
     for layer in range(2):
         k = np.concatenate([r["kv"][layer][0] for r in ranks], axis=0)
         v = np.concatenate([r["kv"][layer][1] for r in ranks], axis=0)
-        fp16_close(k, ref["kv"][layer][0], f"TP{world} {mode} GQA layer {layer} keys")
-        fp16_close(v, ref["kv"][layer][1], f"TP{world} {mode} GQA layer {layer} values")
+        fp16_close(k, ref["kv"][layer][0], f"TP{world} {mode} GQA layer {layer} keys", twin=ref["twin_kv"][layer][0])
+        fp16_close(v, ref["kv"][layer][1], f"TP{world} {mode} GQA layer {layer} values",
+                   twin=ref["twin_kv"][layer][1])
