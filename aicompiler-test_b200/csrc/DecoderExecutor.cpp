@@ -119,8 +119,8 @@ std::unique_ptr<DecoderExecutor> DecoderExecutor::create(cuda::CudaRuntime &runt
     why = "heads, kvHeads, intermediate and vocab must divide by the tensor-parallel size.";
   else if ((c.intermediate / c.tpSize) % 8 != 0 || ((c.heads / c.tpSize) * c.headDim) % 8 != 0)
     why = "Per-rank intermediate and head widths must be multiples of 8.";
-  else if (c.maxRows < 1 || c.maxRows > 128)
-    why = "maxRows must be in [1, 128] (up to 8: GEMV; more: tensor-core projections).";
+  else if (c.maxRows < 1 || c.maxRows > 256)
+    why = "maxRows must be in [1, 256] (up to 8: GEMV; more: tensor-core projections).";
   else if (c.maxSlots < 1) why = "maxSlots must be positive.";
   else if (c.pageSize < 0 || c.pageSize > c.capacity) why = "pageSize must be in [0, capacity].";
   else if (!(c.epsilon > 0.0f) || !std::isfinite(c.epsilon)) why = "epsilon must be finite and positive.";
@@ -1060,6 +1060,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       a.early_mode = distinct ? 1 : 0;
       a.ws_acc = fp(attnWorkspace_);
       a.ws_ml = fp(attnWorkspace_) + (size_t)R * hqL_ * splits * D;
+      a.ws_floats = attnWorkspace_->elementCount();
       a.counters = static_cast<unsigned int *>(attnCounters_->data());
       a.status = status;
       a.trace = traceSink(l, kind);
@@ -1105,7 +1106,7 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
   }
 }
 
-std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct) {
+std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct, bool head) {
   const bool tp = cfg_.tpSize > 1;
   if (tp && !collective_ && !peersAttached_)
     return "tensor parallelism needs a collective (setCollective) or attached peers (attachPeers).";
@@ -1114,7 +1115,7 @@ std::string DecoderExecutor::enqueueStep(int R, bool feed, bool distinct) {
       auto e = enqueueKernel(kind, l, R, feed, distinct);
       if (!e.empty()) return e;
     }
-  return enqueueKernel(kKernelLMHead, 0, R, feed, distinct);
+  return head ? enqueueKernel(kKernelLMHead, 0, R, feed, distinct) : std::string();
 }
 
 unsigned int *DecoderExecutor::workCounter(int layer, int kind) const {
@@ -1242,14 +1243,14 @@ std::string DecoderExecutor::profileKernel(int kind, int R, int rounds, double *
   return {};
 }
 
-std::string DecoderExecutor::launchStep(int R, bool feed, bool distinct) {
-  if (!cfg_.useGraphs) return enqueueStep(R, feed, distinct);
-  const int key = graphKey(R, feed, distinct);
+std::string DecoderExecutor::launchStep(int R, bool feed, bool distinct, bool head) {
+  if (!cfg_.useGraphs) return enqueueStep(R, feed, distinct, head);
+  const int key = graphKey(R, feed, distinct, head);
   auto it = graphs_.find(key);
   if (it == graphs_.end()) {
     cudaStream_t s = rt_.stream();
     TMC_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeRelaxed));
-    const std::string err = enqueueStep(R, feed, distinct);
+    const std::string err = enqueueStep(R, feed, distinct, head);
     cudaGraph_t graph = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (!err.empty() || ce != cudaSuccess) {
@@ -1393,7 +1394,10 @@ std::string DecoderExecutor::prefill(int slot, const std::int32_t *tokens, int c
     }
     for (int r = 0; r < R; ++r) pos[r] = static_cast<std::int32_t>(start + done + r);
     err = uploadStepInputs(R, tokens + done, pos.data(), trow.data(), 1, prefillStage_ + (std::size_t)chunk * 3 * M);
-    if (err.empty()) err = launchStep(R, false, R == 1);
+    // Only the last chunk's LM head is read unless logits are asked for (the
+    // peer exchange's step epoch advances in the head, so it always runs then).
+    const bool head = logits != nullptr || done + R == count || (cfg_.tpSize > 1 && peersAttached_);
+    if (err.empty()) err = launchStep(R, false, R == 1, head);
     if (err.empty() && logits) {
       cudaError_t ce = cudaMemcpyAsync(logits + (size_t)done * vL_, logits_->data(), sizeof(float) * R * vL_,
                                        cudaMemcpyDeviceToHost, rt_.stream());

@@ -214,16 +214,18 @@ class DecoderExecutor {
   std::string allocate();
   // `distinct`: every row belongs to a different sequence (decode); prefill
   // chunks put several rows of one sequence in a step.
-  std::string enqueueStep(int rows, bool feed, bool distinct);
+  // head: the LM head runs (a prefill chunk whose logits and token nobody
+  // reads skips it).
+  std::string enqueueStep(int rows, bool feed, bool distinct, bool head = true);
   std::string enqueueKernel(int kind, int layer, int rows, bool feed, bool distinct);
   // The GEMV / GEMM parameters of one projection (kinds QKV, O, gate/up,
   // down, LM head) of layer `layer` for `rows` rows.
   tmc::GemvParams projection(int kind, int layer, int rows, bool feed) const;
-  std::string launchStep(int rows, bool feed, bool distinct);
+  std::string launchStep(int rows, bool feed, bool distinct, bool head = true);
   // Step graphs differ by rows, feed-back, distinct rows and the attention
   // split cap the step's contexts need.
-  int graphKey(int rows, bool feed, bool distinct) const {
-    return attnSplitCap_ * 1024 + rows * 4 + (feed ? 2 : 0) + (distinct ? 1 : 0);
+  int graphKey(int rows, bool feed, bool distinct, bool head = true) const {
+    return attnSplitCap_ * 8192 + rows * 8 + (head ? 4 : 0) + (feed ? 2 : 0) + (distinct ? 1 : 0);
   }
   // Uploads a step's tokens, positions and table rows and sets the attention
   // split cap for contexts up to max(position) + steps.

@@ -154,13 +154,13 @@ cudaError_t launchGemv(const KernelBinding &b, cudaStream_t s) { return launchGe
 cudaError_t launchGemvPdl(const KernelBinding &b, cudaStream_t s) { return launchGemvImpl(b, s, true); }
 
 // ---- batched_gemm_f16: x f16 [rows, k], W f16 [n, k] -> y f32 [rows, n] (tcgen05) ----
-// constants {rows (1..128), k (% 8 == 0), n}; the split-K workspace and tile
+// constants {rows (1..256), k (% 8 == 0), n}; the split-K workspace and tile
 // tickets are allocated here and retained by the prepared execution.
 std::string bindBatchedGemm(CudaRuntime &rt, KernelBinding &b) {
   TMC_CHECK(requireTypes(b, {ElementType::Float16, ElementType::Float16, ElementType::Float32}, "batched_gemm_f16"));
   const std::size_t rows = b.constants[0], k = b.constants[1], n = b.constants[2];
-  if (rows < 1 || rows > 128 || k < 8 || k % 8 != 0 || n < 1)
-    return "batched_gemm_f16: need 1 <= rows <= 128, k % 8 == 0.";
+  if (rows < 1 || rows > 256 || k < 8 || k % 8 != 0 || n < 1)
+    return "batched_gemm_f16: need 1 <= rows <= 256, k % 8 == 0.";
   TMC_CHECK(requireCount(b.inputs[0], rows * k, "batched_gemm_f16", "x"));
   TMC_CHECK(requireCount(b.inputs[1], n * k, "batched_gemm_f16", "W"));
   TMC_CHECK(requireCount(b.outputs[0], rows * n, "batched_gemm_f16", "y"));
@@ -408,7 +408,7 @@ const std::vector<KernelEntry> &kernelCatalog() {
        "x fp16 [rows, k], W fp16 [n, k] -> y fp16 or fp32 [rows, n]; constants {rows (1..8), k (% 8), n}",
        bindGemv, launchGemv, launchGemvPdl, 1u << 1},
       {"batched_gemm_f16", 2, 1, 3,
-       "x fp16 [rows, k], W fp16 [n, k] -> y fp32 [rows, n] on tcgen05 tensor cores; constants {rows (1..128), "
+       "x fp16 [rows, k], W fp16 [n, k] -> y fp32 [rows, n] on tcgen05 tensor cores; constants {rows (1..256), "
        "k (% 8), n}",
        bindBatchedGemm, launchBatchedGemm},
       {"fused_add_rmsnorm", 3, 1, 4,

@@ -1,16 +1,20 @@
-// GQA split-K decode attention for sm_100a.
+// GQA decode attention for sm_100a, two schedules over one per-tile step.
 //
-// Grid (max_splits, Hkv, rows), 128 threads. A CTA owns one KV head of one
-// query row and a contiguous chunk of key positions, and serves all G = Hq/Hkv
-// query heads of that KV head, so every K/V row is read from HBM once per
-// query row (GQA reuse). K/V rows (D*2 bytes each) are gathered through the
-// block table with 1-D TMA bulk copies (cp.async.bulk) into a two-stage
-// shared-memory ring, completion tracked by mbarriers with bounded waits.
-// Per tile: scores (one thread per (head, position), rotated chunk order so
-// shared-memory reads are conflict-free), an online-softmax update per head,
-// then P.V with each thread owning E output features of one head. Splits write
-// (m, l, acc) partials; the last CTA of a (row, KV head) combines them
-// (atomic ticket), so no second launch is needed.
+// Per tile of 64 key positions of one (query row, KV head) pair: each of four
+// warps takes 16 positions, computes the scores of all G = Hq/Hkv query heads
+// of the KV head with mma.sync (query heads fill rows of the 16-row A tile),
+// updates its online softmax and accumulates P.V; every K/V row is read from
+// HBM once per query row (GQA reuse). K/V arrive through the block table as
+// 16-position page boxes (TMA tensor maps, 128-byte swizzle) or, for other
+// shapes, one bulk copy per position row, into an mbarrier ring with bounded
+// waits.
+// - Split schedule (latency: few pairs, bs1): grid (splits, Hkv, rows); a CTA
+//   owns a chunk of one pair's positions; the CTAs of a pair merge through
+//   distributed shared memory in a cluster, or through a workspace and an
+//   atomic ticket when the pair spans several clusters.
+// - Streaming schedule (throughput: many pairs, batched decode and serving):
+//   one wave of persistent CTAs streams the concatenated tiles of all pairs
+//   with a dedicated producer warp (attention_stream_kernel below).
 #include "attention.cuh"
 #include "gemm.cuh"
 
@@ -772,13 +776,461 @@ cudaError_t dispatch_g(const AttentionParams &p, cudaStream_t stream, bool pdl, 
   }
 }
 
+
+// ---- streaming schedule for batched decode -----------------------------------
+// With many (row, KV head) pairs (batched decode, serving) the split schedule
+// above runs its CTAs in several partial waves and every CTA pays its own
+// prologue and pipeline fill. Here one wave of persistent CTAs streams the
+// concatenated 64-position tiles of all pairs: pair (r, h) owns the tiles
+// [Q[r] + h nt(r), Q[r] + (h + 1) nt(r)) with nt(r) = ceil((pos_r + 1) / 64)
+// and Q[r] = Hkv x (tiles of the rows before r); CTA c streams the run
+// [W c / grid, W (c + 1) / grid) of the W tiles. A producer warp keeps an
+// S-stage TMA ring full across pair boundaries (page lookups included); four
+// consumer warps run the same per-tile step as the split kernel. At the end
+// of a pair's segment the warps merge; a pair wholly inside the run is
+// written out, a pair cut by a run boundary writes (acc, m, l) to its CTA's
+// slot (0 for the run's first segment, 1 for its last) and takes a ticket;
+// the last piece combines the pieces in CTA order (fixed for a given grid).
+// Every wait, the consumer warps' merge barrier included, is a bounded
+// mbarrier wait.
+constexpr int kStreamRowsMax = 1024;
+constexpr int kStreamMaxCtas = 640;  // resident CTAs of the streaming schedule, any device
+template <int D, int G>
+struct StreamCfg {
+  using Tile = Cfg<D, G, true>;
+  static constexpr int T = Tile::T;
+  static constexpr int kStages = G <= 4 ? 3 : 2;
+  static constexpr size_t kStageBytes = Tile::kStageBytes;  // one of K or V
+  static constexpr int kConsumers = 4;
+  static constexpr int kThreadsAll = (kConsumers + 1) * 32;
+  static constexpr size_t kMergeFloats = (size_t)kConsumers * (G * D + 2 * G);
+  __host__ __device__ static constexpr size_t smem_bytes() {
+    return 1024 + (size_t)2 * kStages * kStageBytes + kMergeFloats * 4 + (size_t)kStages * T * 4 +
+           (size_t)(kStreamRowsMax + 1) * 4 + 128;  // + barriers and their 16-byte alignment
+  }
+};
+
+// Workspace floats the streaming schedule needs for `grid` CTAs: two
+// (acc [G][D], m/l [G][2]) slots per CTA.
+__host__ __device__ constexpr size_t stream_ws_floats(int grid, int g, int d) {
+  return (size_t)grid * 2 * g * (d + 2);
+}
+
+// The CTA whose run holds tile i (runs [W c / grid, W (c + 1) / grid)).
+__device__ __forceinline__ int stream_run_of(long long w, int grid, long long i) {
+  return (int)(((i + 1) * grid + w - 1) / w) - 1;
+}
+__device__ __forceinline__ long long stream_run_begin(long long w, int grid, int c) { return w * c / grid; }
+
+// A position in the tile space: row, KV head, tile within the pair.
+struct StreamCursor {
+  int row, h, t, nt;
+  long long pair_start;  // global index of the pair's first tile
+};
+
+// Bounded barrier of the consumer warps (count = consumer warps) on `bar`.
+__device__ __forceinline__ bool consumer_sync(uint64_t *bar, uint32_t &phase, int lane) {
+  __threadfence_block();
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+  const bool ok = __all_sync(0xffffffffu, mbar_wait(bar, phase));
+  phase ^= 1u;
+  return ok;
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
+    attention_stream_kernel(const __grid_constant__ AttentionParams p, const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap) {
+  using C = StreamCfg<D, G>;
+  using Tl = Cfg<D, G, true>;
+  constexpr int T = C::T, S = C::kStages, NC = C::kConsumers;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char *base =
+      reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char *sK = base;
+  unsigned char *sV = base + (size_t)S * C::kStageBytes;
+  float *mrg = reinterpret_cast<float *>(base + (size_t)2 * S * C::kStageBytes);
+  float *mrg_ml = mrg + (size_t)NC * G * D;
+  int *sValid = reinterpret_cast<int *>(mrg + C::kMergeFloats);
+  int *sPrefix = sValid + S * T;  // [rows + 1] tile starts of the rows (Q / Hkv)
+  uint64_t *full = reinterpret_cast<uint64_t *>(
+      (reinterpret_cast<uintptr_t>(sPrefix + kStreamRowsMax + 1) + 15) & ~uintptr_t(15));
+  uint64_t *empty = full + S;
+  uint64_t *merge_bar = empty + S;
+  __shared__ int s_last;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hkv = p.hkv, rows = p.rows;
+  const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
+  unsigned long long t_ready = t_entry;
+
+  // Tile starts of the rows (positions and the block table are final before
+  // the kernel that produces q starts): sPrefix[r] = sum of nt over rows < r.
+  // A row with a position outside the cache has no tiles (and is reported).
+  for (int r = tid; r < rows; r += blockDim.x) {
+    const int pos = p.positions[r];
+    int nt = 0;
+    if (pos < 0 || pos >= p.capacity) {
+      report_status(p.status, kStatusLengthRange, kWhereAttention, pos, r);
+    } else {
+      nt = (pos + T) / T;  // ceil((pos + 1) / T)
+    }
+    sPrefix[r + 1] = nt;
+  }
+  if (tid == 0) {
+    sPrefix[0] = 0;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], NC);
+    }
+    mbar_init(merge_bar, NC);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (warp == 0) {
+    // Inclusive scan in chunks of 32 rows (each lane reads, then writes, its own entry).
+    int carry = 0;
+    for (int r0 = 0; r0 < rows; r0 += 32) {
+      const int r = r0 + lane;
+      int v = r < rows ? sPrefix[r + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+      }
+      if (r < rows) sPrefix[r + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+  }
+  __syncthreads();
+  const long long W = (long long)sPrefix[rows] * hkv;
+  // Runs over min(grid, W) CTAs, so every run is non-empty (the pieces of a
+  // cut pair are then consecutive CTAs); the others have nothing to do.
+  const int grid = (int)(W < (long long)gridDim.x ? W : (long long)gridDim.x);
+  const bool has_run = W > 0 && (int)blockIdx.x < grid;
+  const long long run_a = has_run ? stream_run_begin(W, grid, blockIdx.x) : 0;
+  const long long run_b = has_run ? stream_run_begin(W, grid, blockIdx.x + 1) : 0;
+  const int ntiles = (int)(run_b - run_a);
+
+  // The cursor at global tile i: the last row whose tiles start at or before i
+  // (that row has tiles), then the KV head and the tile within the pair.
+  auto locate = [&](long long i) {
+    int lo = 0, hi = rows - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if ((long long)sPrefix[mid] * hkv <= i) lo = mid; else hi = mid - 1;
+    }
+    StreamCursor c;
+    c.row = lo;
+    c.nt = sPrefix[lo + 1] - sPrefix[lo];
+    const long long off = i - (long long)sPrefix[lo] * hkv;
+    c.h = (int)(off / c.nt);
+    c.t = (int)(off % c.nt);
+    c.pair_start = (long long)sPrefix[lo] * hkv + (long long)c.h * c.nt;
+    return c;
+  };
+  auto advance = [&](StreamCursor &c) {
+    if (++c.t < c.nt) return;
+    c.t = 0;
+    if (++c.h < hkv) {
+      c.pair_start += c.nt;
+      return;
+    }
+    c.h = 0;
+    do {
+      ++c.row;
+    } while (c.row < rows && sPrefix[c.row + 1] == sPrefix[c.row]);
+    if (c.row < rows) {
+      c.nt = sPrefix[c.row + 1] - sPrefix[c.row];
+      c.pair_start = (long long)sPrefix[c.row] * hkv;
+    }
+  };
+
+  if (warp == NC) {
+    // ---- producer warp: the ring, across pairs ----
+    bool waited = false;
+    int issued = 0;
+    if (ntiles > 0) {
+      StreamCursor c = locate(run_a);
+      for (int k = 0; k < ntiles; ++k, advance(c)) {
+        const int stage = k % S;
+        if (k >= S && !__all_sync(0xffffffffu, mbar_wait(&empty[stage], ((k / S) - 1) & 1))) {
+          if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.row);
+          break;
+        }
+        const int pos = p.positions[c.row];
+        const int len = pos + 1, p0 = c.t * T;
+        // Rows the preceding kernel still writes: the row's own newest
+        // position (early_mode 1), every row (0), none (2).
+        const int fresh = p.early_mode == 2 ? len : (p.early_mode == 1 ? pos : 0);
+        if (!waited && p0 + T > fresh) {
+          pdl_wait();
+          waited = true;
+        }
+        const int *table = p.block_table + (size_t)p.table_rows[c.row] * p.table_stride;
+        // Lane w < 4 looks up group w's page (16 positions, one page).
+        int page = -1;
+        if (lane < NC) {
+          const int g0 = p0 + lane * 16;
+          if (g0 < len) {
+            const int logical = g0 / p.page_size;
+            page = logical < p.table_stride ? table[logical] : -1;
+            if (page < 0) {
+              report_status(p.status, kStatusPageMissing, kWhereAttention, logical, c.row);
+            } else if (page >= p.pool_pages) {
+              report_status(p.status, kStatusPageRange, kWhereAttention, page, c.row);
+              page = -1;
+            }
+          }
+        }
+        // Valid rows of the tile (positions before len in a valid page).
+#pragma unroll
+        for (int j = 0; j < T / 32; ++j) {
+          const int lp = lane + 32 * j;
+          const int gp = __shfl_sync(0xffffffffu, page, lp >> 4);
+          sValid[stage * T + lp] = (p0 + lp < len && gp >= 0) ? 1 : 0;
+        }
+        const unsigned boxes = __popc(__ballot_sync(0xffffffffu, lane < NC && page >= 0));
+        __syncwarp();
+        if (lane == 0) mbar_arrive_expect_tx(&full[stage], boxes * 16u * D * 2u * 2u);
+        __syncwarp();
+        if (lane < NC && page >= 0) {
+          const int g0 = p0 + lane * 16;
+          const int y = (page * hkv + c.h) * p.page_size + g0 % p.page_size;
+#pragma unroll
+          for (int hh = 0; hh < D / 64; ++hh) {
+            tma_load_2d(sK + (size_t)stage * C::kStageBytes + hh * T * 128 + lane * 16 * 128, &kmap, hh * 64, y,
+                        &full[stage]);
+            tma_load_2d(sV + (size_t)stage * C::kStageBytes + hh * T * 128 + lane * 16 * 128, &vmap, hh * 64, y,
+                        &full[stage]);
+          }
+        }
+        issued = k + 1;
+      }
+    }
+    if (!waited) pdl_wait();
+    pdl_launch_dependents();
+    // No copy may still be landing when the CTA exits: wait (bounded) for the
+    // last S requested tiles (already consumed ones return at once).
+    for (int k = issued > S ? issued - S : 0; k < issued; ++k) (void)mbar_wait(&full[k % S], (k / S) & 1);
+    trace_emit(p.trace, t_entry, t_ready);
+    return;
+  }
+
+  // ---- consumer warps ----
+  const int gq = lane >> 2, tq = lane & 3;
+  pdl_wait();  // q is written by the preceding kernel
+  if (p.trace.records) t_ready = global_ns();
+  uint32_t merge_phase = 0;
+  bool failed = false;
+  if (ntiles > 0) {
+    StreamCursor c = locate(run_a);
+    uint32_t qa[Tl::kKSteps][4];
+    float m_run = -INFINITY, l_run = 0.0f;
+    float acc[Tl::kDTiles][4];
+    long long seg_first = run_a;  // global index of the segment's first tile
+    for (int k = 0; k < ntiles && !failed; ++k) {
+      const long long gi = run_a + k;
+      if (gi == seg_first) {
+        // A new pair: its query fragments (rows = the G query heads of the KV
+        // head; rows >= G zero) and a fresh online-softmax state.
+        const __half *q = p.q + (size_t)c.row * p.q_stride + (size_t)c.h * G * D;
+#pragma unroll
+        for (int kk = 0; kk < Tl::kKSteps; ++kk) {
+          const int c0 = kk * 16 + 2 * tq;
+          qa[kk][0] = gq < G ? *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0) : 0u;
+          qa[kk][2] = gq < G ? *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0 + 8) : 0u;
+          qa[kk][1] = 0u;
+          qa[kk][3] = 0u;
+        }
+        m_run = -INFINITY;
+        l_run = 0.0f;
+#pragma unroll
+        for (int i = 0; i < Tl::kDTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
+      }
+      const int stage = k % S;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], (k / S) & 1))) {
+        if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.row);
+        failed = true;
+        break;
+      }
+      const int len = p.positions[c.row] + 1;
+      const int r0 = warp * 16;
+      const bool zeroed = tile_step<D, G, true>(sK + (size_t)stage * C::kStageBytes, sV + (size_t)stage * C::kStageBytes,
+                                                r0, c.t * T + r0, len, sValid + stage * T + r0, p.scale, qa, m_run,
+                                                l_run, acc, lane);
+      if (zeroed) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before TMA refills
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+
+      const bool seg_end = c.t == c.nt - 1 || k == ntiles - 1;
+      if (seg_end) {
+        // Merge the warps' states (rows gq < G), then write or hand over.
+        if (gq < G) {
+#pragma unroll
+          for (int dt = 0; dt < Tl::kDTiles; ++dt) {
+            float *dst = mrg + ((size_t)warp * G + gq) * D + dt * 8 + 2 * tq;
+            dst[0] = acc[dt][0];
+            dst[1] = acc[dt][1];
+          }
+          if (tq == 0) {
+            mrg_ml[(warp * G + gq) * 2] = m_run;
+            mrg_ml[(warp * G + gq) * 2 + 1] = l_run;
+          }
+        }
+        if (!consumer_sync(merge_bar, merge_phase, lane)) {
+          failed = true;
+          break;
+        }
+        const bool whole = seg_first == c.pair_start && c.t == c.nt - 1;
+        const int slot = seg_first == run_a ? 0 : 1;
+        const int ct = tid;  // 0 .. 127
+        const size_t pair = (size_t)c.row * hkv + c.h;
+        float *ws_acc = p.ws_acc + ((size_t)blockIdx.x * 2 + slot) * G * D;
+        float *ws_ml = p.ws_ml + ((size_t)blockIdx.x * 2 + slot) * G * 2;
+        for (int i = ct; i < G * D; i += NC * 32) {
+          const int hg = i / D;
+          float m_cta = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < NC; ++w) m_cta = fmaxf(m_cta, mrg_ml[(w * G + hg) * 2]);
+          float l_cta = 0.0f, o = 0.0f;
+#pragma unroll
+          for (int w = 0; w < NC; ++w) {
+            const float mw = mrg_ml[(w * G + hg) * 2];
+            const float f = (mw == -INFINITY) ? 0.0f : expf(mw - m_cta);
+            l_cta += mrg_ml[(w * G + hg) * 2 + 1] * f;
+            o = fmaf(mrg[((size_t)w * G + hg) * D + (i % D)], f, o);
+          }
+          if (whole) {
+            p.out[(size_t)c.row * p.out_stride + (size_t)c.h * G * D + i] = __float2half_rn(o / l_cta);
+          } else {
+            ws_acc[i] = o;
+            if (i % D == 0) {
+              ws_ml[hg * 2] = m_cta;
+              ws_ml[hg * 2 + 1] = l_cta;
+            }
+          }
+        }
+        if (!whole) {
+          __threadfence();
+          if (!consumer_sync(merge_bar, merge_phase, lane)) {
+            failed = true;
+            break;
+          }
+          const long long pair_end = c.pair_start + c.nt;
+          const int c_first = stream_run_of(W, grid, c.pair_start);
+          const int c_last = stream_run_of(W, grid, pair_end - 1);
+          if (ct == 0) {
+            const unsigned int prev = atomicAdd(p.counters + pair, 1u);
+            s_last = prev == (unsigned int)(c_last - c_first) ? 1 : 0;
+          }
+          if (!consumer_sync(merge_bar, merge_phase, lane)) {
+            failed = true;
+            break;
+          }
+          if (s_last) {
+            // The last piece: combine the pieces in CTA order.
+            __threadfence();
+            for (int i = ct; i < G * D; i += NC * 32) {
+              const int hg = i / D;
+              float mmax = -INFINITY;
+              for (int cc = c_first; cc <= c_last; ++cc) {
+                const int sl = stream_run_begin(W, grid, cc) >= c.pair_start ? 0 : 1;
+                mmax = fmaxf(mmax, __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * G * 2 + hg * 2));
+              }
+              float den = 0.0f, num = 0.0f;
+              for (int cc = c_first; cc <= c_last; ++cc) {
+                const int sl = stream_run_begin(W, grid, cc) >= c.pair_start ? 0 : 1;
+                const float mc = __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * G * 2 + hg * 2);
+                const float f = (mc == -INFINITY) ? 0.0f : expf(mc - mmax);
+                den = fmaf(__ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * G * 2 + hg * 2 + 1), f, den);
+                num = fmaf(__ldcg(p.ws_acc + ((size_t)cc * 2 + sl) * G * D + i), f, num);
+              }
+              p.out[(size_t)c.row * p.out_stride + (size_t)c.h * G * D + i] = __float2half_rn(num / den);
+            }
+            if (ct == 0) atomicExch(p.counters + pair, 0u);
+          }
+        }
+        // The merge buffer is free again once every warp has read it.
+        if (!consumer_sync(merge_bar, merge_phase, lane)) {
+          failed = true;
+          break;
+        }
+        seg_first = gi + 1;
+      }
+      advance(c);
+    }
+  }
+  pdl_launch_dependents();
+  trace_emit(p.trace, t_entry, t_ready);
+}
+
+template <int D, int G>
+cudaError_t launch_stream_instance(const AttentionParams &p, cudaStream_t stream, bool pdl, int grid) {
+  auto kernel = attention_stream_kernel<D, G>;
+  const size_t smem = StreamCfg<D, G>::smem_bytes();
+  static std::mutex mu;
+  static std::unordered_map<int, bool> configured;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev]) {
+      e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (e != cudaSuccess) return e;
+      configured[dev] = true;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(StreamCfg<D, G>::kThreadsAll);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, p, *p.k_map, *p.v_map);
+}
+
+// Persistent CTAs the streaming schedule runs for this shape (one wave), or 0
+// when it does not apply.
+template <int D, int G>
+int stream_grid_for(int num_sms) {
+  static std::mutex mu;
+  static std::unordered_map<int, int> per_sm;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = per_sm.find(dev);
+  if (it == per_sm.end()) {
+    auto kernel = attention_stream_kernel<D, G>;
+    const size_t smem = StreamCfg<D, G>::smem_bytes();
+    int blocks = 0;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+            cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, StreamCfg<D, G>::kThreadsAll, smem) !=
+            cudaSuccess)
+      blocks = 0;
+    (void)cudaGetLastError();
+    it = per_sm.emplace(dev, blocks).first;
+  }
+  return it->second * num_sms;
+}
+
 }  // namespace
 
 size_t attention_workspace_bytes(int rows, int hq, int hkv, int head_dim, int max_splits) {
-  (void)hkv;
   const size_t acc = (size_t)rows * hq * max_splits * head_dim * 4;
   const size_t ml = (size_t)rows * hq * max_splits * 2 * 4;
-  return acc + ml;
+  // The streaming schedule's per-CTA slots, for up to kStreamMaxCtas resident
+  // CTAs (a bound for any device: the grid is the occupancy times the SMs).
+  const int g = hkv > 0 && hq % hkv == 0 ? hq / hkv : 1;
+  const size_t stream = stream_ws_floats(kStreamMaxCtas, g, head_dim) * 4;
+  return acc + ml > stream ? acc + ml : stream;
 }
 
 cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool pdl) {
@@ -790,6 +1242,33 @@ cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool
   // Page boxes through tensor maps when the caller built them and the shape
   // allows (64-dim halves, pages of whole 16-position groups).
   const bool box = p.k_map != nullptr && p.v_map != nullptr && p.page_size % 16 == 0;
+  // Many (row, KV head) pairs: the streaming schedule, when the caller's
+  // workspace holds its per-CTA slots.
+  if (box && p.schedule != 1 && p.rows <= kStreamRowsMax && (p.head_dim == 64 || p.head_dim == 128) &&
+      (g == 1 || g == 2 || g == 4 || g == 8)) {
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+                                                   cudaSuccess)
+      return cudaErrorInvalidValue;
+    if (p.schedule == 2 || (long long)p.rows * p.hkv >= sms) {
+      int grid = 0;
+#define TMC_STREAM_GRID(D_, G_) \
+  if (p.head_dim == D_ && g == G_) grid = stream_grid_for<D_, G_>(sms);
+      TMC_STREAM_GRID(64, 1) TMC_STREAM_GRID(64, 2) TMC_STREAM_GRID(64, 4) TMC_STREAM_GRID(64, 8)
+      TMC_STREAM_GRID(128, 1) TMC_STREAM_GRID(128, 2) TMC_STREAM_GRID(128, 4) TMC_STREAM_GRID(128, 8)
+#undef TMC_STREAM_GRID
+      if (grid > 0 && grid <= kStreamMaxCtas && p.ws_floats >= stream_ws_floats(grid, g, p.head_dim)) {
+        AttentionParams q = p;
+        q.ws_ml = q.ws_acc + (size_t)grid * 2 * g * p.head_dim;
+#define TMC_STREAM_LAUNCH(D_, G_) \
+  if (p.head_dim == D_ && g == G_) return launch_stream_instance<D_, G_>(q, stream, pdl, grid);
+        TMC_STREAM_LAUNCH(64, 1) TMC_STREAM_LAUNCH(64, 2) TMC_STREAM_LAUNCH(64, 4) TMC_STREAM_LAUNCH(64, 8)
+        TMC_STREAM_LAUNCH(128, 1) TMC_STREAM_LAUNCH(128, 2) TMC_STREAM_LAUNCH(128, 4) TMC_STREAM_LAUNCH(128, 8)
+#undef TMC_STREAM_LAUNCH
+      }
+      if (p.schedule == 2) return cudaErrorInvalidValue;
+    }
+  }
   switch (p.head_dim) {
     case 16: return dispatch_g<16, false>(p, stream, pdl, g);
     case 32: return dispatch_g<32, false>(p, stream, pdl, g);
@@ -900,6 +1379,7 @@ extern "C" int tmc_k_paged_attention_f16_noalloc(
   p.early_mode = 2;  // standalone call: no kernel produces K/V concurrently
   p.ws_acc = reinterpret_cast<float *>(base);
   p.ws_ml = reinterpret_cast<float *>(base + (size_t)rows * hq * splits * d * sizeof(float));
+  p.ws_floats = partials / sizeof(float);
   p.counters = tickets;
   p.status = static_cast<tmc::TmcDeviceStatus *>(status);
   // Same kernel variant as the allocating entry point: K/V as 16-position page

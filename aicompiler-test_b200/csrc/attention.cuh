@@ -44,6 +44,13 @@ struct AttentionParams {
   int max_chunk;
   float *ws_acc;   // [rows, hkv, <= max_splits cluster slots, G, D] (splits spanning clusters)
   float *ws_ml;    // [rows, hkv, <= max_splits cluster slots, G, 2]
+  // Floats available from ws_acc on (ws_ml included); 0 = unknown. The
+  // streaming schedule runs only when they hold its per-CTA slots.
+  size_t ws_floats;
+  // 0: automatic (streaming for many (row, KV head) pairs with page boxes,
+  // else split); 1: the split schedule; 2: streaming (invalid when it does
+  // not apply).
+  int schedule;
   unsigned int *counters;  // [rows, hkv], zero between launches
   TmcDeviceStatus *status;
   TraceSink trace;         // optional timeline (records == nullptr: off)

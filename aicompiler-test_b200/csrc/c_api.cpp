@@ -293,7 +293,7 @@ int sm_count() {
 }  // namespace
 
 size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows) {
-  if (n <= 0 || k <= 0 || rows <= 0 || rows > 128) return 0;
+  if (n <= 0 || k <= 0 || rows <= 0 || rows > 256) return 0;
   const tmc::GemmPlan plan = tmc::plan_gemm(n, k, rows, sm_count());
   const size_t partial = (tmc::gemm_workspace_floats(plan) * 4 + 255) / 256 * 256;
   return partial + (size_t)plan.tiles * 8;
@@ -302,7 +302,7 @@ size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows) {
 int tmc_k_batched_gemm_f16_f32out(const void *x_f16, const void *w_f16, float *y, int rows, int k, int n,
                                   void *workspace, void *status, void *stream) {
   if (!x_f16 || !w_f16 || !y || !workspace) return fail(TMC_ERR_INVALID, "null pointer");
-  if (rows <= 0 || rows > 128 || n <= 0 || k <= 0 || k % 8 != 0)
+  if (rows <= 0 || rows > 256 || n <= 0 || k <= 0 || k % 8 != 0)
     return fail(TMC_ERR_UNSUPPORTED, "batched gemm: rows in [1, 128], k % 8 == 0");
   const tmc::GemmPlan plan = tmc::plan_gemm(n, k, rows, sm_count());
   const size_t partial = (tmc::gemm_workspace_floats(plan) * 4 + 255) / 256 * 256;
@@ -343,8 +343,19 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
                               int hkv, int d, int page_size, int pool_pages, int capacity,
                               int max_splits, int min_chunk, void *workspace, uint32_t *counters,
                               void *status, void *stream) {
+  return tmc_k_paged_attention_f16_ex(q, out, k_pool, v_pool, block_table, table_stride, table_rows, positions,
+                                      rows, hq, hkv, d, page_size, pool_pages, capacity, max_splits, min_chunk,
+                                      workspace, counters, 0, status, stream);
+}
+
+int tmc_k_paged_attention_f16_ex(const void *q, void *out, const void *k_pool, const void *v_pool,
+                                 const int32_t *block_table, int table_stride, const int32_t *table_rows,
+                                 const int32_t *positions, int rows, int hq, int hkv, int d, int page_size,
+                                 int pool_pages, int capacity, int max_splits, int min_chunk, void *workspace,
+                                 uint32_t *counters, int schedule, void *status, void *stream) {
   if (!q || !out || !k_pool || !v_pool || !block_table || !table_rows || !positions || !counters)
     return fail(TMC_ERR_INVALID, "null pointer");
+  if (schedule < 0 || schedule > 2) return fail(TMC_ERR_INVALID, "schedule must be 0, 1 or 2");
   if (max_splits > 1 && workspace == nullptr) return fail(TMC_ERR_INVALID, "workspace is null");
   tmc::AttentionParams p{};
   p.q = static_cast<const __half *>(q);
@@ -371,6 +382,8 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
   const size_t acc_bytes = (size_t)rows * hq * max_splits * d * 4;
   p.ws_acc = static_cast<float *>(workspace);
   p.ws_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + acc_bytes);
+  p.ws_floats = workspace ? tmc::attention_workspace_bytes(rows, hq, hkv, d, max_splits) / 4 : 0;
+  p.schedule = schedule;
   p.counters = counters;
   p.status = static_cast<tmc::TmcDeviceStatus *>(status);
   CUtensorMap km, vm;

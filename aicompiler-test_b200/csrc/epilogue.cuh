@@ -1,5 +1,5 @@
 // Per-element epilogues shared by the decode GEMV (CUDA cores, M <= 8 rows)
-// and the batched tcgen05 GEMM (tensor cores, up to 128 rows): both kernels
+// and the batched tcgen05 GEMM (tensor cores, up to 256 rows): both kernels
 // hand every finished fp32 sum to these functions, so the two paths round
 // and store identically.
 //

@@ -44,7 +44,7 @@ namespace {
 constexpr int kGemmThreads = 320;
 constexpr int kEpiWarps = 8;
 constexpr int kGroup = 16;      // token columns an epilogue step handles (one tcgen05.ld)
-constexpr int kMaxTokens = 128;  // the largest TN
+constexpr int kMaxTokens = 256;  // the largest TN
 constexpr unsigned long long kTileWaitNs = 1000000000ull;  // a closer waits at most 1 s for the tile's pieces
 
 // Epilogue kinds the kernel is specialised on: each instantiation carries one
@@ -62,7 +62,9 @@ struct GemmCfg {
   static constexpr int kStageBytes = kAtoms * (kTileBytesA + kBytesB);
   static constexpr int kStages = (216 * 1024 / kStageBytes) < 8 ? (216 * 1024 / kStageBytes) : 8;
   static_assert(kStages >= 2, "a pipeline needs two stages");
-  static constexpr int kAcc = 4;  // accumulators in tensor memory (epilogues overlap later MMAs)
+  // Accumulators in tensor memory (epilogues overlap later MMAs): four, two
+  // for 256 tokens (512 columns, all of it).
+  static constexpr int kAcc = TN >= 256 ? 2 : 4;
   static constexpr int kTmemCols = kAcc * TN < 32 ? 32 : kAcc * TN;  // a power of two, <= 512
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + 256;
 };
@@ -675,6 +677,7 @@ cudaError_t launch_ek(const GemvParams &p, const CUtensorMap &w_map, const CUten
     case 32: return launch_tn<32, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
     case 64: return launch_tn<64, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
     case 128: return launch_tn<128, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
+    case 256: return launch_tn<256, EK>(p, w_map, x_map, plan, ws, tile_counters, stream, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -687,7 +690,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_
 
 GemmPlan plan_gemm(int N, int K, int M, int num_sms) {
   GemmPlan g{};
-  g.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
+  g.tn = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
   g.tiles = (N + kGemmTileRows - 1) / kGemmTileRows;
   const int block = kGemmKBlock * gemm_k_atoms(g.tn);
   g.kblocks = (K + block - 1) / block;  // a ragged last block reads zeros
@@ -738,7 +741,7 @@ cudaError_t make_tensor_map_f16(CUtensorMap *map, const void *base, uint64_t row
 cudaError_t launch_gemm(const GemvParams &p, const CUtensorMap &w_map, const CUtensorMap &x_map,
                         const GemmPlan &plan, float *ws, unsigned int *tile_counters, cudaStream_t stream,
                         bool pdl) {
-  if (p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 128 ||
+  if (p.N <= 0 || p.K <= 0 || p.K % 8 != 0 || p.M <= 0 || p.M > plan.tn || plan.tn > 256 ||
       plan.tiles != (p.N + kGemmTileRows - 1) / kGemmTileRows ||
       plan.kblocks != (p.K + kGemmKBlock * gemm_k_atoms(plan.tn) - 1) / (kGemmKBlock * gemm_k_atoms(plan.tn)) ||
       plan.grid < 1 || plan.grid > (long long)plan.tiles * plan.kblocks ||  // every run non-empty

@@ -3,7 +3,7 @@
 // Replaces emitTiledGEMM (DecodeGEMVMetalEmitter.cpp:134-169), the
 // reference's batched/prefill linear layer, for rows > 8: y = epilogue(W x^T)
 // with W [N, K] fp16 row-major (the decoder's weights, unchanged) and x
-// [M <= 128, K] fp16 rows, K % 8 == 0 (the GEMV prologue, written by launch_row_prologue,
+// [M <= 256, K] fp16 rows, K % 8 == 0 (the GEMV prologue, written by launch_row_prologue,
 // or an fp16 activation). The weight tile is the MMA's A operand (128 output
 // features = the UMMA M dimension) and the token rows are its B operand
 // (UMMA N = 16..128), so one weight byte feeds up to 128 tokens; the fp32
@@ -32,7 +32,7 @@ __host__ __device__ constexpr int gemm_k_atoms(int tn) { return tn <= 64 ? 4 : 2
 // and summed in K order by the tile's last-arriving piece, so the result is
 // fixed for a given plan and does not depend on timing.
 struct GemmPlan {
-  int tn;       // token columns per MMA (16, 32, 64 or 128), >= M
+  int tn;       // token columns per MMA (16, 32, 64, 128 or 256), >= M
   int tiles;    // ceil(N / 128)
   int kblocks;  // ceil(K / (64 * gemm_k_atoms(tn))): K blocks of one pipeline stage
   int grid;     // persistent CTAs (one per SM at most, each with >= kGemmMinRun iterations)

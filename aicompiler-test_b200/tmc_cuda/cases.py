@@ -122,12 +122,13 @@ def case_attention(rt, a):
     def launch():
         tmc_cuda.paged_attention_f16(rt, q, out, kp, vp, table, pages_per_seq, trows, pos, a.rows, a.hq,
                                      a.hkv, a.d, a.page, pool_pages, pages_per_seq * a.page, splits,
-                                     a.min_chunk, ws, counters)
+                                     a.min_chunk, ws, counters, a.schedule)
 
     us = _time(rt, launch, a.warmup, a.reps)
     nbytes = 2 * 2 * int(ctx.sum()) * a.hkv * a.d + 2 * 2 * a.rows * a.hq * a.d
     return {"kernel": "attention_kernel", "rows": a.rows, "ctx": a.ctx, "ctx_max": a.ctx_max, "hq": a.hq,
-            "hkv": a.hkv, "d": a.d, "splits": splits, "min_chunk": a.min_chunk, "us": us, "bytes": nbytes,
+            "hkv": a.hkv, "d": a.d, "splits": splits, "min_chunk": a.min_chunk, "schedule": a.schedule,
+            "us": us, "bytes": nbytes,
             "gbs": nbytes / us / 1e3}
 
 
@@ -146,6 +147,8 @@ def main(argv=None):
     ap.add_argument("--splits", type=int, default=0, help="attention max splits (0: the decoder's policy)")
     ap.add_argument("--min-chunk", type=int, default=64, help="attention positions per split at least")
     ap.add_argument("--pool-pages", type=int, default=0, help="attention page pool size (at least what fits)")
+    ap.add_argument("--schedule", type=int, default=0,
+                    help="attention schedule: 0 automatic, 1 split-K with cluster merges, 2 streaming")
     ap.add_argument("--fp16", action="store_true", help="rmsnorm: fp16 x, gamma and y (default fp32)")
     ap.add_argument("--threads", type=int, default=256, help="rmsnorm: threads per row (0: the baseline)")
     ap.add_argument("--warmup", type=int, default=3)

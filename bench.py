@@ -377,7 +377,7 @@ def run_ours(args, world, rank, local):
     return 0
 
 
-PREFILL_ROWS = 128  # prompt rows per prefill chunk (tcgen05 GEMM token columns)
+PREFILL_ROWS = 256  # prompt rows per prefill chunk (tcgen05 GEMM token columns)
 
 
 def prefill_flops(n, layers=None):

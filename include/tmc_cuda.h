@@ -201,7 +201,7 @@ int tmc_k_gemv_f16_f32out(const void *x_f16, const void *w_f16, float *y, int ro
 /* Batched projection on tcgen05 tensor cores, y = x W^T with fp16 x [rows, k]
  * and W [n, k], fp32 accumulation in tensor memory, fp32 y [rows, n]:
  * replaces emitTiledGEMM (DecodeGEMVMetalEmitter.cpp:134-169), the
- * reference's batched linear layer. rows <= 128, k % 8 == 0, x and W 16-byte
+ * reference's batched linear layer. rows <= 256, k % 8 == 0, x and W 16-byte
  * aligned. `workspace` holds tmc_k_batched_gemm_workspace_bytes(n, k, rows)
  * bytes (split-K partials and tile tickets; the call clears the tickets). */
 size_t tmc_k_batched_gemm_workspace_bytes(int n, int k, int rows);
@@ -227,6 +227,20 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
                               int hq, int hkv, int d, int page_size, int pool_pages,
                               int capacity, int max_splits, int min_chunk, void *workspace,
                               uint32_t *counters, void *status, void *stream);
+/* The same with the schedule chosen (tmc_k_paged_attention_f16 passes 0):
+ * 0 automatic; 1 split-K over (splits, kv head, row) CTAs merged through
+ * thread-block clusters (the latency schedule, few (row, kv head) pairs);
+ * 2 streaming: one wave of persistent CTAs streams the 64-position tiles of
+ * all pairs with a producer warp, pairs cut between CTAs merged through the
+ * workspace (the throughput schedule; needs d 64 or 128, page_size % 16 == 0,
+ * rows <= 1024 and a workspace of at least 2 * G * (d + 2) floats per
+ * resident CTA, else TMC_ERR_UNSUPPORTED). Automatic picks 2 when it applies
+ * and rows * hkv >= the SM count. */
+int tmc_k_paged_attention_f16_ex(const void *q, void *out, const void *k_pool, const void *v_pool,
+                                 const int32_t *block_table, int table_stride, const int32_t *table_rows,
+                                 const int32_t *positions, int rows, int hq, int hkv, int d, int page_size,
+                                 int pool_pages, int capacity, int max_splits, int min_chunk, void *workspace,
+                                 uint32_t *counters, int schedule, void *status, void *stream);
 
 /* Allocation-free variant of tmc_k_paged_attention_f16, for callers that cannot
  * allocate device memory at call time (a host that hands all device memory to
@@ -274,7 +288,7 @@ typedef struct {
   int capacity;      /* KVCachePlan::capacity: positions per sequence */
   float epsilon;     /* DecoderLLMPlan::rmsNormEpsilon */
   double rope_theta;
-  int max_rows;      /* tokens per step, 1..128 (> 8: tensor-core projections) */
+  int max_rows;      /* tokens per step, 1..256 (> 8: tensor-core projections) */
   int max_slots;     /* sequences with KV state */
   int page_size;     /* DecoderLLMCompileOptions::kvPageSize; 0 = contiguous */
   int pool_pages;    /* 0 = max_slots * ceil(capacity / page_size) */

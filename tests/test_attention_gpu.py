@@ -35,7 +35,7 @@ def make_case(seed, rows, hq, hkv, d, page_size, lengths, pool_pages=None, share
 
 
 def run_attention(rt, q, k_pool, v_pool, table, table_rows, positions, hkv, page_size, capacity,
-                  max_splits=8, min_chunk=32):
+                  max_splits=8, min_chunk=32, schedule=0):
     import tmc_cuda
     rows, hq, d = q.shape
     ws_bytes = tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, max_splits)
@@ -46,7 +46,7 @@ def run_attention(rt, q, k_pool, v_pool, table, table_rows, positions, hkv, page
     counters = rt.upload(np.zeros(rows * hkv, dtype=np.int32))
     tmc_cuda.paged_attention_f16(rt, qb, out, kb, vb, tb, table.shape[1], trb, pb, rows, hq, hkv, d,
                                  page_size, k_pool.shape[0], capacity, max_splits, min_chunk, ws,
-                                 counters)
+                                 counters, schedule)
     rt.synchronize()
     assert np.all(counters.read_raw() == 0), "split tickets must be left at zero"
     return out.read().reshape(rows, hq, d)
@@ -113,7 +113,8 @@ ROWS_CASES = [
 
 
 @pytest.mark.parametrize("rows,hq,hkv,d,seed,max_len,splits", ROWS_CASES)
-def test_paged_attention_many_waves_matches_oracle(rt, rows, hq, hkv, d, seed, max_len, splits):
+@pytest.mark.parametrize("schedule", [1, 2])  # split-K with cluster merges; streaming
+def test_paged_attention_many_waves_matches_oracle(rt, rows, hq, hkv, d, seed, max_len, splits, schedule):
     rng = np.random.default_rng(seed)
     lengths = [int(x) for x in rng.integers(1, max_len, rows)]
     lengths[0], lengths[1], lengths[2] = 1, 64, 1024 if max_len > 1024 else 48
@@ -121,18 +122,41 @@ def test_paged_attention_many_waves_matches_oracle(rt, rows, hq, hkv, d, seed, m
     capacity = table.shape[1] * 16
     ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
                                  table, trows, pos, hkv, 16)
-    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, 16, capacity, *splits)
+    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, 16, capacity, *splits, schedule=schedule)
     check(got, ref)
 
 
-def test_many_waves_missing_page_reports_device_status(rt):
+# The streaming schedule where it is not picked automatically: few pairs, so
+# the runs are shorter than the pairs and most pairs are cut into several
+# pieces (down to one tile per CTA) merged through the workspace; G = 1, 2, 4, 8.
+STREAM_SMALL = [
+    (3, 32, 8, 128, 16, [17, 16, 300]),
+    (2, 16, 2, 128, 16, [2000, 65]),
+    (2, 4, 2, 64, 16, [64, 1000]),
+    (4, 16, 16, 64, 16, [513, 520, 576, 1]),
+    (1, 32, 8, 128, 16, [8192]),
+]
+
+
+@pytest.mark.parametrize("rows,hq,hkv,d,page,lengths", STREAM_SMALL)
+def test_streaming_schedule_with_cut_pairs_matches_oracle(rt, rows, hq, hkv, d, page, lengths):
+    q, kp, vp, table, trows, pos = make_case(rows * 5 + d, rows, hq, hkv, d, page, lengths)
+    ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
+                                 table, trows, pos, hkv, page)
+    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, page, table.shape[1] * page, 64, 64, schedule=2)
+    check(got, ref)
+
+
+@pytest.mark.parametrize("schedule", [1, 2])
+def test_many_waves_missing_page_reports_device_status(rt, schedule):
     import tmc_cuda
     lengths = [700] * 64
     q, kp, vp, table, trows, pos = make_case(21, 64, 32, 8, 128, 16, lengths)
     table[40, 7] = -1
     with pytest.raises(tmc_cuda.TmcError) as err:
-        run_attention(rt, q, kp, vp, table, trows, pos, 8, 16, table.shape[1] * 16, 8, 64)
+        run_attention(rt, q, kp, vp, table, trows, pos, 8, 16, table.shape[1] * 16, 8, 64, schedule=schedule)
     assert err.value.code == tmc_cuda.ERR_DEVICE_STATUS
+    assert "no physical page" in err.value.message
 
 
 def test_missing_page_reports_device_status(rt):

@@ -12,7 +12,9 @@ greedy tokens bit-exact except counted fp16 ties):
   KV caches after the last step;
 - tensor-core path: the same prompt prefilled in 64-row chunks through the
   tcgen05 GEMMs (all 1024 rows of logits), and a 64-sequence batched decode
-  (64 rows, one per sequence, prompts of 8..71 tokens) for 2 steps.
+  (64 rows, one per sequence, prompts of 8..71 tokens) for 2 steps;
+- the prefill chunks the benchmark's TTFT uses: 256 rows (256-token GEMM
+  tiles, streaming attention), all 1024 rows of logits.
 The oracle's twin with a permuted fp32 summation order measures the noise of
 the model itself: at this width a few percent of the twin's own logits lie
 beyond 2e-3 x RMS of the oracle (fp16 rounding of every activation). The GPU
@@ -110,6 +112,16 @@ def test_c3_width_bs1_gemv_path_matches_oracle(rt, model):
         fp16_close(k, rk.float().numpy(), f"C3 width layer {layer} key cache ({PROMPT + STEPS} positions)",
                    twin=tk.float().numpy())
         fp16_close(v, rv.float().numpy(), f"C3 width layer {layer} value cache", twin=tv.float().numpy())
+    dec.close()
+
+
+def test_c3_width_256_row_prefill_chunks_match_oracle(rt, model):
+    dec = decoder(rt, max_rows=256)
+    logits, tok = dec.prefill(model["prompt"])  # 4 chunks of 256 rows
+    fp16_close(logits, model["prefill_logits"], "C3 width prefill logits, 256-row chunks", twin=model["twin_logits"])
+    tokens = TokenCheck("C3 width 256-row prefill")
+    tokens.check(tok, model["prefill_token"], model["prefill_logits"][-1], logits[-1])
+    tokens.report()
     dec.close()
 
 

@@ -20,6 +20,8 @@ CASES = [
     (64, 14336, 4096),    # bs64 down projection: K split across CTAs
     (100, 2048, 1000),    # 128-token tile, ragged last weight tile
     (128, 512, 384),
+    (200, 4096, 6144),    # 256-token tile (prefill chunks), QKV shape
+    (256, 1024, 2816),    # 256-token tile, C2 FFN shape
     (1, 64, 128),
 ]
 
