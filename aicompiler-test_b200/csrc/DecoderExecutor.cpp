@@ -218,7 +218,8 @@ std::string DecoderExecutor::allocate() {
   if (!(e = make((size_t)historyCapacity_, I32, &history_, &activationBytes_)).empty()) return e;
   if (!(e = make(4, I32, &historyCounter_, &activationBytes_)).empty()) return e;
   const int maxSplits = 64;
-  const size_t wsBytes = tmc::attention_workspace_bytes(R, hqL_, hkvL_, D, maxSplits);
+  const size_t wsBytes = std::max(tmc::attention_workspace_bytes(R, hqL_, hkvL_, D, maxSplits),
+                                  tmc::attention_group_workspace_bytes(D));
   if (!(e = make(wsBytes / 4 + 1, F32, &attnWorkspace_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)R * hkvL_, I32, &attnCounters_, &activationBytes_)).empty()) return e;
   if (!(e = make((size_t)cfg_.layers * 6 * tmc::kGemvCounterWords, I32, &workCounters_, &activationBytes_)).empty())
@@ -1058,6 +1059,9 @@ std::string DecoderExecutor::enqueueKernel(int kind, int l, int R, bool feed, bo
       // One row per sequence: only each row's newest K/V comes from the QKV
       // kernel still running, older rows can be gathered before its completion.
       a.early_mode = distinct ? 1 : 0;
+      // A prefill chunk's rows are consecutive positions of one sequence: the
+      // streaming schedule serves them in groups that share each K/V tile.
+      a.row_group = (!distinct && R > 1) ? 16 / (hqL_ / hkvL_) : 1;
       a.ws_acc = fp(attnWorkspace_);
       a.ws_ml = fp(attnWorkspace_) + (size_t)R * hqL_ * splits * D;
       a.ws_floats = attnWorkspace_->elementCount();

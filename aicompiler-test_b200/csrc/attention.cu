@@ -793,27 +793,37 @@ cudaError_t dispatch_g(const AttentionParams &p, cudaStream_t stream, bool pdl, 
 // the last piece combines the pieces in CTA order (fixed for a given grid).
 // Every wait, the consumer warps' merge barrier included, is a bounded
 // mbarrier wait.
-constexpr int kStreamRowsMax = 1024;
+constexpr int kStreamRowsMax = 512;
 constexpr int kStreamMaxCtas = 640;  // resident CTAs of the streaming schedule, any device
-template <int D, int G>
+
+// QR query rows per pair: 1 for decode (one row per sequence; the G query
+// heads fill G rows of the MMA's A tile), 16 / G for a row group of prefill
+// (QR consecutive positions of one sequence, so all 16 rows are used and
+// every K/V tile is read once for QR query rows).
+template <int D, int G, int QR>
 struct StreamCfg {
   using Tile = Cfg<D, G, true>;
   static constexpr int T = Tile::T;
-  static constexpr int kStages = G <= 4 ? 3 : 2;
+  static constexpr int kRows = QR * G;  // used rows of the MMA's A tile
+  static_assert(kRows <= 16, "a row group fills at most the 16 rows of the A tile");
+  // Decode (QR 1): 3 stages (2 for G = 8), two CTAs per SM. Row groups: the
+  // 16-row tile step's registers leave one CTA per SM (the per-partition
+  // register files), so the ring takes what the merge buffer leaves.
+  static constexpr int kStages = QR == 1 ? (G <= 4 ? 3 : 2) : (D == 128 ? 5 : 4);
   static constexpr size_t kStageBytes = Tile::kStageBytes;  // one of K or V
   static constexpr int kConsumers = 4;
   static constexpr int kThreadsAll = (kConsumers + 1) * 32;
-  static constexpr size_t kMergeFloats = (size_t)kConsumers * (G * D + 2 * G);
+  static constexpr size_t kMergeFloats = (size_t)kConsumers * (kRows * D + 2 * kRows);
   __host__ __device__ static constexpr size_t smem_bytes() {
     return 1024 + (size_t)2 * kStages * kStageBytes + kMergeFloats * 4 + (size_t)kStages * T * 4 +
-           (size_t)(kStreamRowsMax + 1) * 4 + 128;  // + barriers and their 16-byte alignment
+           (size_t)(kStreamRowsMax + 1) * 4 + (size_t)kStreamRowsMax * 4 + 128;  // + barriers, alignment
   }
 };
 
 // Workspace floats the streaming schedule needs for `grid` CTAs: two
-// (acc [G][D], m/l [G][2]) slots per CTA.
-__host__ __device__ constexpr size_t stream_ws_floats(int grid, int g, int d) {
-  return (size_t)grid * 2 * g * (d + 2);
+// (acc [rows][D], m/l [rows][2]) slots per CTA, rows = used A-tile rows.
+__host__ __device__ constexpr size_t stream_ws_floats(int grid, int rows, int d) {
+  return (size_t)grid * 2 * rows * (d + 2);
 }
 
 // The CTA whose run holds tile i (runs [W c / grid, W (c + 1) / grid)).
@@ -822,9 +832,9 @@ __device__ __forceinline__ int stream_run_of(long long w, int grid, long long i)
 }
 __device__ __forceinline__ long long stream_run_begin(long long w, int grid, int c) { return w * c / grid; }
 
-// A position in the tile space: row, KV head, tile within the pair.
+// A position in the tile space: row group, KV head, tile within the pair.
 struct StreamCursor {
-  int row, h, t, nt;
+  int grp, h, t, nt;
   long long pair_start;  // global index of the pair's first tile
 };
 
@@ -838,45 +848,170 @@ __device__ __forceinline__ bool consumer_sync(uint64_t *bar, uint32_t &phase, in
   return ok;
 }
 
+// The per-tile step with all 16 rows of the A tile in use (row groups): row
+// ri = j G + g is query head g of the group's j-th query row. Each row has its
+// own end (the thread's rows gq and gq + 8 end at end0 and end1): positions
+// past it are masked in the scores. V rows past the group's end (end_max) or
+// of a missing page are zeroed, as in tile_step.
 template <int D, int G>
-__global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
+__device__ __forceinline__ bool tile_step_rows16(unsigned char *sKs, unsigned char *sVs, int r0, int p0, int end_max,
+                                                 int end0, int end1, const int *valid, float scale,
+                                                 const uint32_t (&qa)[D / 16][4], float (&m_run)[2],
+                                                 float (&l_run)[2], float (&acc)[D / 8][4], int lane) {
+  using C = Cfg<D, G, true>;
+  constexpr int T = C::T;
+  const int tq = lane & 3;
+  bool zeroed = false;
+  if (p0 >= end_max) return false;
+  {
+    const int lp = lane & 15;
+    const bool bad = !(p0 + lp < end_max && valid[lp]);
+    if (__any_sync(0xffffffffu, bad)) {
+#pragma unroll
+      for (int h = 0; h < D / 64; ++h) {
+        uint4 *dst = reinterpret_cast<uint4 *>(sVs + h * T * 128 + (r0 + lp) * 128 + (lane >> 4) * 64);
+        if (bad) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) dst[c] = make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      __syncwarp();
+      zeroed = true;
+    }
+  }
+  // Scores S[16 rows x 16 positions] as two n-tiles of 8 positions; c0/c1 are
+  // row gq, c2/c3 row gq + 8.
+  float sc[2][4];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+    for (int kk = 0; kk < C::kKSteps; ++kk) {
+      uint32_t b0, b1;
+      const int R = r0 + nt * 8 + (lane & 7), d0 = kk * 16 + ((lane >> 3) & 1) * 8;
+      const __half *addr = reinterpret_cast<const __half *>(sKs + (d0 >> 6) * T * 128 + R * 128 +
+                                                            ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
+      ldmatrix_x2(b0, b1, addr);
+      mma_16816(sc[nt], qa[kk], b0, b1);
+    }
+  }
+  float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int lp = nt * 8 + 2 * tq + j;
+      const bool ok = valid[lp] != 0;
+      sc[nt][j] = (ok && p0 + lp < end0) ? sc[nt][j] * scale : -INFINITY;
+      sc[nt][2 + j] = (ok && p0 + lp < end1) ? sc[nt][2 + j] * scale : -INFINITY;
+      mx[0] = fmaxf(mx[0], sc[nt][j]);
+      mx[1] = fmaxf(mx[1], sc[nt][2 + j]);
+    }
+  }
+  float rescale[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+    mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    const float m_new = fmaxf(m_run[r], mx[r]);
+    rescale[r] = (m_run[r] == -INFINITY) ? 0.0f : expf(m_run[r] - m_new);
+    m_run[r] = m_new;
+  }
+  float pr[2][4], psum[2] = {0.0f, 0.0f};
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int r = c >> 1;
+      pr[nt][c] = (sc[nt][c] == -INFINITY) ? 0.0f : expf(sc[nt][c] - m_run[r]);
+      psum[r] += pr[nt][c];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    psum[r] += __shfl_xor_sync(0xffffffffu, psum[r], 1);
+    psum[r] += __shfl_xor_sync(0xffffffffu, psum[r], 2);
+    l_run[r] = l_run[r] * rescale[r] + psum[r];
+  }
+  // P as the A operand in two fp16 parts, hi + lo: a0 / a2 = row gq for
+  // positions 0-7 / 8-15, a1 / a3 = row gq + 8.
+  uint32_t pa[4], pl[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int nt = i >> 1, c = (i & 1) * 2;  // i: 0 -> (nt 0, row gq), 1 -> (nt 0, gq+8), 2 -> (nt 1, gq), 3 -> (nt 1, gq+8)
+    const __half2 h = __floats2half2_rn(pr[nt][c], pr[nt][c + 1]);
+    const float2 f = __half22float2(h);
+    pa[i] = *reinterpret_cast<const uint32_t *>(&h);
+    pl[i] = pack_half2(pr[nt][c] - f.x, pr[nt][c + 1] - f.y);
+  }
+  // mma_16816's A registers are {a0, a1, a2, a3} = {row gq k0-7, row gq+8 k0-7,
+  // row gq k8-15, row gq+8 k8-15}: reorder (nt, row) -> register.
+  const uint32_t ah[4] = {pa[0], pa[1], pa[2], pa[3]};
+  const uint32_t al[4] = {pl[0], pl[1], pl[2], pl[3]};
+#pragma unroll
+  for (int dt = 0; dt < C::kDTiles; ++dt) {
+    acc[dt][0] *= rescale[0];
+    acc[dt][1] *= rescale[0];
+    acc[dt][2] *= rescale[1];
+    acc[dt][3] *= rescale[1];
+    uint32_t b0, b1;
+    const int R = r0 + (lane & 15), d0 = dt * 8;
+    const __half *addr = reinterpret_cast<const __half *>(sVs + (d0 >> 6) * T * 128 + R * 128 +
+                                                          ((((d0 & 63) >> 3) ^ (R & 7)) << 4));
+    ldmatrix_x2_trans(b0, b1, addr);
+    mma_16816(acc[dt], al, b0, b1);
+    mma_16816(acc[dt], ah, b0, b1);
+  }
+  return zeroed;
+}
+
+template <int D, int G, int QR>
+__global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
     attention_stream_kernel(const __grid_constant__ AttentionParams p, const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap) {
-  using C = StreamCfg<D, G>;
+  using C = StreamCfg<D, G, QR>;
   using Tl = Cfg<D, G, true>;
-  constexpr int T = C::T, S = C::kStages, NC = C::kConsumers;
+  constexpr int T = C::T, S = C::kStages, NC = C::kConsumers, RW = C::kRows;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char *base =
       reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char *sK = base;
   unsigned char *sV = base + (size_t)S * C::kStageBytes;
   float *mrg = reinterpret_cast<float *>(base + (size_t)2 * S * C::kStageBytes);
-  float *mrg_ml = mrg + (size_t)NC * G * D;
+  float *mrg_ml = mrg + (size_t)NC * RW * D;
   int *sValid = reinterpret_cast<int *>(mrg + C::kMergeFloats);
-  int *sPrefix = sValid + S * T;  // [rows + 1] tile starts of the rows (Q / Hkv)
+  int *sPrefix = sValid + S * T;              // [groups + 1] tile starts of the groups (Q / Hkv)
+  int *sEnd = sPrefix + kStreamRowsMax + 1;   // [groups] longest context of the group
   uint64_t *full = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(sPrefix + kStreamRowsMax + 1) + 15) & ~uintptr_t(15));
+      (reinterpret_cast<uintptr_t>(sEnd + kStreamRowsMax) + 15) & ~uintptr_t(15));
   uint64_t *empty = full + S;
   uint64_t *merge_bar = empty + S;
   __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hkv = p.hkv, rows = p.rows;
+  const int groups = (rows + QR - 1) / QR;
   const unsigned long long t_entry = p.trace.records ? global_ns() : 0ull;
   unsigned long long t_ready = t_entry;
 
-  // Tile starts of the rows (positions and the block table are final before
-  // the kernel that produces q starts): sPrefix[r] = sum of nt over rows < r.
-  // A row with a position outside the cache has no tiles (and is reported).
-  for (int r = tid; r < rows; r += blockDim.x) {
-    const int pos = p.positions[r];
-    int nt = 0;
-    if (pos < 0 || pos >= p.capacity) {
-      report_status(p.status, kStatusLengthRange, kWhereAttention, pos, r);
-    } else {
-      nt = (pos + T) / T;  // ceil((pos + 1) / T)
+  // Tiles of the groups (positions and the block table are final before the
+  // kernel that produces q starts): a group's tiles cover its longest context;
+  // a row with a position outside the cache is reported and left out.
+  for (int gi = tid; gi < groups; gi += blockDim.x) {
+    int end = 0;
+#pragma unroll 1
+    for (int j = 0; j < QR; ++j) {
+      const int r = gi * QR + j;
+      if (r >= rows) break;
+      const int pos = p.positions[r];
+      if (pos < 0 || pos >= p.capacity) {
+        report_status(p.status, kStatusLengthRange, kWhereAttention, pos, r);
+      } else {
+        end = max(end, pos + 1);
+      }
     }
-    sPrefix[r + 1] = nt;
+    sEnd[gi] = end;
+    sPrefix[gi + 1] = (end + T - 1) / T;
   }
   if (tid == 0) {
     sPrefix[0] = 0;
@@ -889,22 +1024,22 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
   }
   __syncthreads();
   if (warp == 0) {
-    // Inclusive scan in chunks of 32 rows (each lane reads, then writes, its own entry).
+    // Inclusive scan in chunks of 32 groups (each lane reads, then writes, its own entry).
     int carry = 0;
-    for (int r0 = 0; r0 < rows; r0 += 32) {
-      const int r = r0 + lane;
-      int v = r < rows ? sPrefix[r + 1] : 0;
+    for (int g0 = 0; g0 < groups; g0 += 32) {
+      const int gi = g0 + lane;
+      int v = gi < groups ? sPrefix[gi + 1] : 0;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, v, o);
         if (lane >= o) v += n;
       }
-      if (r < rows) sPrefix[r + 1] = carry + v;
+      if (gi < groups) sPrefix[gi + 1] = carry + v;
       carry += __shfl_sync(0xffffffffu, v, 31);
     }
   }
   __syncthreads();
-  const long long W = (long long)sPrefix[rows] * hkv;
+  const long long W = (long long)sPrefix[groups] * hkv;
   // Runs over min(grid, W) CTAs, so every run is non-empty (the pieces of a
   // cut pair are then consecutive CTAs); the others have nothing to do.
   const int grid = (int)(W < (long long)gridDim.x ? W : (long long)gridDim.x);
@@ -913,16 +1048,16 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
   const long long run_b = has_run ? stream_run_begin(W, grid, blockIdx.x + 1) : 0;
   const int ntiles = (int)(run_b - run_a);
 
-  // The cursor at global tile i: the last row whose tiles start at or before i
-  // (that row has tiles), then the KV head and the tile within the pair.
+  // The cursor at global tile i: the last group whose tiles start at or before
+  // i (that group has tiles), then the KV head and the tile within the pair.
   auto locate = [&](long long i) {
-    int lo = 0, hi = rows - 1;
+    int lo = 0, hi = groups - 1;
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if ((long long)sPrefix[mid] * hkv <= i) lo = mid; else hi = mid - 1;
     }
     StreamCursor c;
-    c.row = lo;
+    c.grp = lo;
     c.nt = sPrefix[lo + 1] - sPrefix[lo];
     const long long off = i - (long long)sPrefix[lo] * hkv;
     c.h = (int)(off / c.nt);
@@ -939,11 +1074,11 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
     }
     c.h = 0;
     do {
-      ++c.row;
-    } while (c.row < rows && sPrefix[c.row + 1] == sPrefix[c.row]);
-    if (c.row < rows) {
-      c.nt = sPrefix[c.row + 1] - sPrefix[c.row];
-      c.pair_start = (long long)sPrefix[c.row] * hkv;
+      ++c.grp;
+    } while (c.grp < groups && sPrefix[c.grp + 1] == sPrefix[c.grp]);
+    if (c.grp < groups) {
+      c.nt = sPrefix[c.grp + 1] - sPrefix[c.grp];
+      c.pair_start = (long long)sPrefix[c.grp] * hkv;
     }
   };
 
@@ -956,19 +1091,19 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
       for (int k = 0; k < ntiles; ++k, advance(c)) {
         const int stage = k % S;
         if (k >= S && !__all_sync(0xffffffffu, mbar_wait(&empty[stage], ((k / S) - 1) & 1))) {
-          if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.row);
+          if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.grp);
           break;
         }
-        const int pos = p.positions[c.row];
-        const int len = pos + 1, p0 = c.t * T;
+        const int len = sEnd[c.grp], p0 = c.t * T;
         // Rows the preceding kernel still writes: the row's own newest
-        // position (early_mode 1), every row (0), none (2).
-        const int fresh = p.early_mode == 2 ? len : (p.early_mode == 1 ? pos : 0);
+        // position (early_mode 1, one row per group), every row (0), none (2).
+        const int fresh = p.early_mode == 2 ? len : (p.early_mode == 1 && QR == 1 ? len - 1 : 0);
         if (!waited && p0 + T > fresh) {
           pdl_wait();
           waited = true;
         }
-        const int *table = p.block_table + (size_t)p.table_rows[c.row] * p.table_stride;
+        // The rows of a group share one block-table row.
+        const int *table = p.block_table + (size_t)p.table_rows[c.grp * QR] * p.table_stride;
         // Lane w < 4 looks up group w's page (16 positions, one page).
         int page = -1;
         if (lane < NC) {
@@ -977,9 +1112,9 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
             const int logical = g0 / p.page_size;
             page = logical < p.table_stride ? table[logical] : -1;
             if (page < 0) {
-              report_status(p.status, kStatusPageMissing, kWhereAttention, logical, c.row);
+              report_status(p.status, kStatusPageMissing, kWhereAttention, logical, c.grp * QR);
             } else if (page >= p.pool_pages) {
-              report_status(p.status, kStatusPageRange, kWhereAttention, page, c.row);
+              report_status(p.status, kStatusPageRange, kWhereAttention, page, c.grp * QR);
               page = -1;
             }
           }
@@ -1024,59 +1159,87 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
   if (p.trace.records) t_ready = global_ns();
   uint32_t merge_phase = 0;
   bool failed = false;
+  // The query row and head of A-tile row ri of group grp (row -1: none).
+  auto row_of = [&](int grp, int ri) { return QR == 1 ? grp : (ri / G < QR ? grp * QR + ri / G : -1); };
+  auto head_of = [&](int ri) { return QR == 1 ? ri : ri % G; };
   if (ntiles > 0) {
     StreamCursor c = locate(run_a);
     uint32_t qa[Tl::kKSteps][4];
-    float m_run = -INFINITY, l_run = 0.0f;
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
     float acc[Tl::kDTiles][4];
+    int end_r[2] = {0, 0};  // QR > 1: ends of the thread's rows gq and gq + 8
     long long seg_first = run_a;  // global index of the segment's first tile
     for (int k = 0; k < ntiles && !failed; ++k) {
       const long long gi = run_a + k;
       if (gi == seg_first) {
-        // A new pair: its query fragments (rows = the G query heads of the KV
-        // head; rows >= G zero) and a fresh online-softmax state.
-        const __half *q = p.q + (size_t)c.row * p.q_stride + (size_t)c.h * G * D;
+        // A new pair: the query fragments of its rows (unused rows zero) and a
+        // fresh online-softmax state.
 #pragma unroll
-        for (int kk = 0; kk < Tl::kKSteps; ++kk) {
-          const int c0 = kk * 16 + 2 * tq;
-          qa[kk][0] = gq < G ? *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0) : 0u;
-          qa[kk][2] = gq < G ? *reinterpret_cast<const uint32_t *>(q + (size_t)gq * D + c0 + 8) : 0u;
-          qa[kk][1] = 0u;
-          qa[kk][3] = 0u;
+        for (int half = 0; half < 2; ++half) {
+          const int ri = gq + 8 * half;
+          int row = -1;
+          if (ri < RW) row = row_of(c.grp, ri);
+          if (row >= rows) row = -1;
+          if (QR > 1) {
+            int e = 0;
+            if (row >= 0) {
+              const int pos = p.positions[row];
+              e = (pos >= 0 && pos < p.capacity) ? pos + 1 : 0;
+            }
+            end_r[half] = e;
+          }
+          const __half *q = row >= 0 ? p.q + (size_t)row * p.q_stride + (size_t)(c.h * G + head_of(ri)) * D : nullptr;
+#pragma unroll
+          for (int kk = 0; kk < Tl::kKSteps; ++kk) {
+            const int c0 = kk * 16 + 2 * tq;
+            qa[kk][half] = q ? *reinterpret_cast<const uint32_t *>(q + c0) : 0u;
+            qa[kk][2 + half] = q ? *reinterpret_cast<const uint32_t *>(q + c0 + 8) : 0u;
+          }
         }
-        m_run = -INFINITY;
-        l_run = 0.0f;
+        m_run[0] = m_run[1] = -INFINITY;
+        l_run[0] = l_run[1] = 0.0f;
 #pragma unroll
         for (int i = 0; i < Tl::kDTiles; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
       }
       const int stage = k % S;
       if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], (k / S) & 1))) {
-        if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.row);
+        if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.grp);
         failed = true;
         break;
       }
-      const int len = p.positions[c.row] + 1;
+      const int len = sEnd[c.grp];
       const int r0 = warp * 16;
-      const bool zeroed = tile_step<D, G, true>(sK + (size_t)stage * C::kStageBytes, sV + (size_t)stage * C::kStageBytes,
-                                                r0, c.t * T + r0, len, sValid + stage * T + r0, p.scale, qa, m_run,
-                                                l_run, acc, lane);
+      bool zeroed;
+      if constexpr (QR == 1) {
+        zeroed = tile_step<D, G, true>(sK + (size_t)stage * C::kStageBytes, sV + (size_t)stage * C::kStageBytes,
+                                       r0, c.t * T + r0, len, sValid + stage * T + r0, p.scale, qa, m_run[0],
+                                       l_run[0], acc, lane);
+      } else {
+        zeroed = tile_step_rows16<D, G>(sK + (size_t)stage * C::kStageBytes, sV + (size_t)stage * C::kStageBytes,
+                                        r0, c.t * T + r0, len, end_r[0], end_r[1], sValid + stage * T + r0, p.scale,
+                                        qa, m_run, l_run, acc, lane);
+      }
       if (zeroed) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // before TMA refills
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
 
       const bool seg_end = c.t == c.nt - 1 || k == ntiles - 1;
       if (seg_end) {
-        // Merge the warps' states (rows gq < G), then write or hand over.
-        if (gq < G) {
+        // Merge the warps' states (used rows), then write or hand over.
 #pragma unroll
-          for (int dt = 0; dt < Tl::kDTiles; ++dt) {
-            float *dst = mrg + ((size_t)warp * G + gq) * D + dt * 8 + 2 * tq;
-            dst[0] = acc[dt][0];
-            dst[1] = acc[dt][1];
-          }
-          if (tq == 0) {
-            mrg_ml[(warp * G + gq) * 2] = m_run;
-            mrg_ml[(warp * G + gq) * 2 + 1] = l_run;
+        for (int half = 0; half < 2; ++half) {
+          const int ri = gq + 8 * half;
+          if (ri < RW && (QR > 1 || half == 0)) {
+#pragma unroll
+            for (int dt = 0; dt < Tl::kDTiles; ++dt) {
+              float *dst = mrg + ((size_t)warp * RW + ri) * D + dt * 8 + 2 * tq;
+              dst[0] = acc[dt][2 * half];
+              dst[1] = acc[dt][2 * half + 1];
+            }
+            if (tq == 0) {
+              mrg_ml[(warp * RW + ri) * 2] = m_run[half];
+              mrg_ml[(warp * RW + ri) * 2 + 1] = l_run[half];
+            }
           }
         }
         if (!consumer_sync(merge_bar, merge_phase, lane)) {
@@ -1086,29 +1249,32 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
         const bool whole = seg_first == c.pair_start && c.t == c.nt - 1;
         const int slot = seg_first == run_a ? 0 : 1;
         const int ct = tid;  // 0 .. 127
-        const size_t pair = (size_t)c.row * hkv + c.h;
-        float *ws_acc = p.ws_acc + ((size_t)blockIdx.x * 2 + slot) * G * D;
-        float *ws_ml = p.ws_ml + ((size_t)blockIdx.x * 2 + slot) * G * 2;
-        for (int i = ct; i < G * D; i += NC * 32) {
-          const int hg = i / D;
+        const size_t pair = (size_t)c.grp * hkv + c.h;
+        float *ws_acc = p.ws_acc + ((size_t)blockIdx.x * 2 + slot) * RW * D;
+        float *ws_ml = p.ws_ml + ((size_t)blockIdx.x * 2 + slot) * RW * 2;
+        for (int i = ct; i < RW * D; i += NC * 32) {
+          const int ri = i / D;
           float m_cta = -INFINITY;
 #pragma unroll
-          for (int w = 0; w < NC; ++w) m_cta = fmaxf(m_cta, mrg_ml[(w * G + hg) * 2]);
+          for (int w = 0; w < NC; ++w) m_cta = fmaxf(m_cta, mrg_ml[(w * RW + ri) * 2]);
           float l_cta = 0.0f, o = 0.0f;
 #pragma unroll
           for (int w = 0; w < NC; ++w) {
-            const float mw = mrg_ml[(w * G + hg) * 2];
+            const float mw = mrg_ml[(w * RW + ri) * 2];
             const float f = (mw == -INFINITY) ? 0.0f : expf(mw - m_cta);
-            l_cta += mrg_ml[(w * G + hg) * 2 + 1] * f;
-            o = fmaf(mrg[((size_t)w * G + hg) * D + (i % D)], f, o);
+            l_cta += mrg_ml[(w * RW + ri) * 2 + 1] * f;
+            o = fmaf(mrg[((size_t)w * RW + ri) * D + (i % D)], f, o);
           }
           if (whole) {
-            p.out[(size_t)c.row * p.out_stride + (size_t)c.h * G * D + i] = __float2half_rn(o / l_cta);
+            const int row = row_of(c.grp, ri);
+            if (row >= 0 && row < rows)
+              p.out[(size_t)row * p.out_stride + (size_t)(c.h * G + head_of(ri)) * D + i % D] =
+                  __float2half_rn(o / l_cta);
           } else {
             ws_acc[i] = o;
             if (i % D == 0) {
-              ws_ml[hg * 2] = m_cta;
-              ws_ml[hg * 2 + 1] = l_cta;
+              ws_ml[ri * 2] = m_cta;
+              ws_ml[ri * 2 + 1] = l_cta;
             }
           }
         }
@@ -1132,22 +1298,25 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
           if (s_last) {
             // The last piece: combine the pieces in CTA order.
             __threadfence();
-            for (int i = ct; i < G * D; i += NC * 32) {
-              const int hg = i / D;
+            for (int i = ct; i < RW * D; i += NC * 32) {
+              const int ri = i / D;
+              const int row = row_of(c.grp, ri);
+              if (row < 0 || row >= rows) continue;
               float mmax = -INFINITY;
               for (int cc = c_first; cc <= c_last; ++cc) {
                 const int sl = stream_run_begin(W, grid, cc) >= c.pair_start ? 0 : 1;
-                mmax = fmaxf(mmax, __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * G * 2 + hg * 2));
+                mmax = fmaxf(mmax, __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * RW * 2 + ri * 2));
               }
               float den = 0.0f, num = 0.0f;
               for (int cc = c_first; cc <= c_last; ++cc) {
                 const int sl = stream_run_begin(W, grid, cc) >= c.pair_start ? 0 : 1;
-                const float mc = __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * G * 2 + hg * 2);
+                const float mc = __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * RW * 2 + ri * 2);
                 const float f = (mc == -INFINITY) ? 0.0f : expf(mc - mmax);
-                den = fmaf(__ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * G * 2 + hg * 2 + 1), f, den);
-                num = fmaf(__ldcg(p.ws_acc + ((size_t)cc * 2 + sl) * G * D + i), f, num);
+                den = fmaf(__ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * RW * 2 + ri * 2 + 1), f, den);
+                num = fmaf(__ldcg(p.ws_acc + ((size_t)cc * 2 + sl) * RW * D + i), f, num);
               }
-              p.out[(size_t)c.row * p.out_stride + (size_t)c.h * G * D + i] = __float2half_rn(num / den);
+              p.out[(size_t)row * p.out_stride + (size_t)(c.h * G + head_of(ri)) * D + i % D] =
+                  __float2half_rn(num / den);
             }
             if (ct == 0) atomicExch(p.counters + pair, 0u);
           }
@@ -1166,10 +1335,10 @@ __global__ void __launch_bounds__(StreamCfg<D, G>::kThreadsAll)
   trace_emit(p.trace, t_entry, t_ready);
 }
 
-template <int D, int G>
+template <int D, int G, int QR>
 cudaError_t launch_stream_instance(const AttentionParams &p, cudaStream_t stream, bool pdl, int grid) {
-  auto kernel = attention_stream_kernel<D, G>;
-  const size_t smem = StreamCfg<D, G>::smem_bytes();
+  auto kernel = attention_stream_kernel<D, G, QR>;
+  const size_t smem = StreamCfg<D, G, QR>::smem_bytes();
   static std::mutex mu;
   static std::unordered_map<int, bool> configured;
   int dev = 0;
@@ -1185,7 +1354,7 @@ cudaError_t launch_stream_instance(const AttentionParams &p, cudaStream_t stream
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(StreamCfg<D, G>::kThreadsAll);
+  cfg.blockDim = dim3(StreamCfg<D, G, QR>::kThreadsAll);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1197,8 +1366,8 @@ cudaError_t launch_stream_instance(const AttentionParams &p, cudaStream_t stream
 }
 
 // Persistent CTAs the streaming schedule runs for this shape (one wave), or 0
-// when it does not apply.
-template <int D, int G>
+// when it does not fit.
+template <int D, int G, int QR>
 int stream_grid_for(int num_sms) {
   static std::mutex mu;
   static std::unordered_map<int, int> per_sm;
@@ -1207,12 +1376,12 @@ int stream_grid_for(int num_sms) {
   std::lock_guard<std::mutex> lock(mu);
   auto it = per_sm.find(dev);
   if (it == per_sm.end()) {
-    auto kernel = attention_stream_kernel<D, G>;
-    const size_t smem = StreamCfg<D, G>::smem_bytes();
+    auto kernel = attention_stream_kernel<D, G, QR>;
+    const size_t smem = StreamCfg<D, G, QR>::smem_bytes();
     int blocks = 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
             cudaSuccess ||
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, StreamCfg<D, G>::kThreadsAll, smem) !=
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, StreamCfg<D, G, QR>::kThreadsAll, smem) !=
             cudaSuccess)
       blocks = 0;
     (void)cudaGetLastError();
@@ -1233,6 +1402,10 @@ size_t attention_workspace_bytes(int rows, int hq, int hkv, int head_dim, int ma
   return acc + ml > stream ? acc + ml : stream;
 }
 
+size_t attention_group_workspace_bytes(int head_dim) {
+  return stream_ws_floats(kStreamMaxCtas, 16, head_dim) * 4;
+}
+
 cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool pdl) {
   if (p.rows <= 0 || p.hkv <= 0 || p.hq <= 0 || p.hq % p.hkv != 0 || p.max_splits <= 0 ||
       p.min_chunk <= 0 || p.page_size <= 0 || p.rows > 65535 || p.hkv > 65535 ||
@@ -1242,26 +1415,33 @@ cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool
   // Page boxes through tensor maps when the caller built them and the shape
   // allows (64-dim halves, pages of whole 16-position groups).
   const bool box = p.k_map != nullptr && p.v_map != nullptr && p.page_size % 16 == 0;
-  // Many (row, KV head) pairs: the streaming schedule, when the caller's
-  // workspace holds its per-CTA slots.
+  // Many (row, KV head) pairs, or row groups: the streaming schedule, when the
+  // caller's workspace holds its per-CTA slots.
+  const bool grouped = p.row_group > 1;
   if (box && p.schedule != 1 && p.rows <= kStreamRowsMax && (p.head_dim == 64 || p.head_dim == 128) &&
       (g == 1 || g == 2 || g == 4 || g == 8)) {
     int dev = 0, sms = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) !=
                                                    cudaSuccess)
       return cudaErrorInvalidValue;
-    if (p.schedule == 2 || (long long)p.rows * p.hkv >= sms) {
+    const int qr = grouped ? 16 / g : 1;
+    const long long pairs = (long long)((p.rows + qr - 1) / qr) * p.hkv;
+    if (p.schedule == 2 || pairs >= sms) {
       int grid = 0;
-#define TMC_STREAM_GRID(D_, G_) \
-  if (p.head_dim == D_ && g == G_) grid = stream_grid_for<D_, G_>(sms);
+#define TMC_STREAM_GRID(D_, G_)                                                          \
+  if (p.head_dim == D_ && g == G_)                                                       \
+    grid = grouped ? stream_grid_for<D_, G_, 16 / G_>(sms) : stream_grid_for<D_, G_, 1>(sms);
       TMC_STREAM_GRID(64, 1) TMC_STREAM_GRID(64, 2) TMC_STREAM_GRID(64, 4) TMC_STREAM_GRID(64, 8)
       TMC_STREAM_GRID(128, 1) TMC_STREAM_GRID(128, 2) TMC_STREAM_GRID(128, 4) TMC_STREAM_GRID(128, 8)
 #undef TMC_STREAM_GRID
-      if (grid > 0 && grid <= kStreamMaxCtas && p.ws_floats >= stream_ws_floats(grid, g, p.head_dim)) {
+      const int used_rows = qr * g;
+      if (grid > 0 && grid <= kStreamMaxCtas && p.ws_floats >= stream_ws_floats(grid, used_rows, p.head_dim)) {
         AttentionParams q = p;
-        q.ws_ml = q.ws_acc + (size_t)grid * 2 * g * p.head_dim;
-#define TMC_STREAM_LAUNCH(D_, G_) \
-  if (p.head_dim == D_ && g == G_) return launch_stream_instance<D_, G_>(q, stream, pdl, grid);
+        q.ws_ml = q.ws_acc + (size_t)grid * 2 * used_rows * p.head_dim;
+#define TMC_STREAM_LAUNCH(D_, G_)                                                                     \
+  if (p.head_dim == D_ && g == G_)                                                                    \
+    return grouped ? launch_stream_instance<D_, G_, 16 / G_>(q, stream, pdl, grid)                    \
+                   : launch_stream_instance<D_, G_, 1>(q, stream, pdl, grid);
         TMC_STREAM_LAUNCH(64, 1) TMC_STREAM_LAUNCH(64, 2) TMC_STREAM_LAUNCH(64, 4) TMC_STREAM_LAUNCH(64, 8)
         TMC_STREAM_LAUNCH(128, 1) TMC_STREAM_LAUNCH(128, 2) TMC_STREAM_LAUNCH(128, 4) TMC_STREAM_LAUNCH(128, 8)
 #undef TMC_STREAM_LAUNCH

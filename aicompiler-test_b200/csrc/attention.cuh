@@ -51,6 +51,11 @@ struct AttentionParams {
   // else split); 1: the split schedule; 2: streaming (invalid when it does
   // not apply).
   int schedule;
+  // > 1: the rows are prefill rows of one sequence at consecutive positions
+  // (one block-table row), served in groups of 16 / G rows by the streaming
+  // schedule so that each K/V tile is read once per group; the split schedule
+  // treats the rows one by one.
+  int row_group;
   unsigned int *counters;  // [rows, hkv], zero between launches
   TmcDeviceStatus *status;
   TraceSink trace;         // optional timeline (records == nullptr: off)
@@ -69,6 +74,8 @@ constexpr int kAttentionMaxSplits = 64;
 
 // Workspace bytes needed for a launch with these dimensions.
 size_t attention_workspace_bytes(int rows, int hq, int hkv, int head_dim, int max_splits);
+// Workspace bytes the streaming schedule needs for row groups (row_group > 1).
+size_t attention_group_workspace_bytes(int head_dim);
 
 cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool pdl);
 

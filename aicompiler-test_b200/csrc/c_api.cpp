@@ -345,17 +345,19 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
                               void *status, void *stream) {
   return tmc_k_paged_attention_f16_ex(q, out, k_pool, v_pool, block_table, table_stride, table_rows, positions,
                                       rows, hq, hkv, d, page_size, pool_pages, capacity, max_splits, min_chunk,
-                                      workspace, counters, 0, status, stream);
+                                      workspace, counters, 0, 1, status, stream);
 }
 
 int tmc_k_paged_attention_f16_ex(const void *q, void *out, const void *k_pool, const void *v_pool,
                                  const int32_t *block_table, int table_stride, const int32_t *table_rows,
                                  const int32_t *positions, int rows, int hq, int hkv, int d, int page_size,
                                  int pool_pages, int capacity, int max_splits, int min_chunk, void *workspace,
-                                 uint32_t *counters, int schedule, void *status, void *stream) {
+                                 uint32_t *counters, int schedule, int row_group, void *status, void *stream) {
   if (!q || !out || !k_pool || !v_pool || !block_table || !table_rows || !positions || !counters)
     return fail(TMC_ERR_INVALID, "null pointer");
   if (schedule < 0 || schedule > 2) return fail(TMC_ERR_INVALID, "schedule must be 0, 1 or 2");
+  if (row_group != 0 && row_group != 1 && row_group != 2)
+    return fail(TMC_ERR_INVALID, "row_group must be 1 (rows one by one) or 2 (prefill row groups)");
   if (max_splits > 1 && workspace == nullptr) return fail(TMC_ERR_INVALID, "workspace is null");
   tmc::AttentionParams p{};
   p.q = static_cast<const __half *>(q);
@@ -384,6 +386,7 @@ int tmc_k_paged_attention_f16_ex(const void *q, void *out, const void *k_pool, c
   p.ws_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + acc_bytes);
   p.ws_floats = workspace ? tmc::attention_workspace_bytes(rows, hq, hkv, d, max_splits) / 4 : 0;
   p.schedule = schedule;
+  p.row_group = row_group == 2 ? 2 : 1;
   p.counters = counters;
   p.status = static_cast<tmc::TmcDeviceStatus *>(status);
   CUtensorMap km, vm;

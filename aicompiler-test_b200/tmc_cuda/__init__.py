@@ -104,7 +104,7 @@ _sig("tmc_k_paged_attention_f16", c_int, c_void_p, c_void_p, c_void_p, c_void_p,
      c_void_p, c_void_p, c_void_p)
 _sig("tmc_k_paged_attention_f16_ex", c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
      c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
-     c_void_p, c_int, c_void_p, c_void_p)
+     c_void_p, c_int, c_int, c_void_p, c_void_p)
 _sig("tmc_k_fill_normal_f16", c_int, c_void_p, c_size_t, c_uint64, c_float, c_float, c_void_p)
 
 
@@ -391,12 +391,14 @@ def paged_attention_f16(rt: Runtime, q: Buffer, out: Buffer, k_pool: Buffer, v_p
                         block_table: Buffer, table_stride: int, table_rows: Buffer,
                         positions: Buffer, rows: int, hq: int, hkv: int, d: int, page_size: int,
                         pool_pages: int, capacity: int, max_splits: int, min_chunk: int,
-                        workspace: Buffer | None, counters: Buffer, schedule: int = 0):
-    """schedule: 0 automatic, 1 split-K with cluster merges, 2 streaming (persistent CTAs)."""
+                        workspace: Buffer | None, counters: Buffer, schedule: int = 0, row_group: int = 1):
+    """schedule: 0 automatic, 1 split-K with cluster merges, 2 streaming (persistent CTAs);
+    row_group 2: prefill rows of one sequence served in groups (streaming schedule)."""
     check(lib.tmc_k_paged_attention_f16_ex(
         q.ptr, out.ptr, k_pool.ptr, v_pool.ptr, block_table.ptr, table_stride, table_rows.ptr,
         positions.ptr, rows, hq, hkv, d, page_size, pool_pages, capacity, max_splits, min_chunk,
-        workspace.ptr if workspace is not None else None, counters.ptr, schedule, rt.status_ptr, rt.stream))
+        workspace.ptr if workspace is not None else None, counters.ptr, schedule, row_group, rt.status_ptr,
+        rt.stream))
 
 
 def fill_normal_f16(rt: Runtime, buf: Buffer, seed: int, mean: float, std: float):

@@ -235,12 +235,16 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
  * workspace (the throughput schedule; needs d 64 or 128, page_size % 16 == 0,
  * rows <= 1024 and a workspace of at least 2 * G * (d + 2) floats per
  * resident CTA, else TMC_ERR_UNSUPPORTED). Automatic picks 2 when it applies
- * and rows * hkv >= the SM count. */
+ * and rows * hkv >= the SM count. row_group 2: the rows are prefill rows of
+ * one sequence at consecutive positions sharing one block-table row (the
+ * decoder's prefill chunks); the streaming schedule then serves them in
+ * groups of 16 / (hq / hkv) rows, reading each K/V tile once per group
+ * (workspace: also 640 * 2 * 16 * (d + 2) floats); 1: rows one by one. */
 int tmc_k_paged_attention_f16_ex(const void *q, void *out, const void *k_pool, const void *v_pool,
                                  const int32_t *block_table, int table_stride, const int32_t *table_rows,
                                  const int32_t *positions, int rows, int hq, int hkv, int d, int page_size,
                                  int pool_pages, int capacity, int max_splits, int min_chunk, void *workspace,
-                                 uint32_t *counters, int schedule, void *status, void *stream);
+                                 uint32_t *counters, int schedule, int row_group, void *status, void *stream);
 
 /* Allocation-free variant of tmc_k_paged_attention_f16, for callers that cannot
  * allocate device memory at call time (a host that hands all device memory to

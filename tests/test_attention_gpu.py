@@ -35,7 +35,7 @@ def make_case(seed, rows, hq, hkv, d, page_size, lengths, pool_pages=None, share
 
 
 def run_attention(rt, q, k_pool, v_pool, table, table_rows, positions, hkv, page_size, capacity,
-                  max_splits=8, min_chunk=32, schedule=0):
+                  max_splits=8, min_chunk=32, schedule=0, row_group=1):
     import tmc_cuda
     rows, hq, d = q.shape
     ws_bytes = tmc_cuda.attention_workspace_bytes(rows, hq, hkv, d, max_splits)
@@ -46,7 +46,7 @@ def run_attention(rt, q, k_pool, v_pool, table, table_rows, positions, hkv, page
     counters = rt.upload(np.zeros(rows * hkv, dtype=np.int32))
     tmc_cuda.paged_attention_f16(rt, qb, out, kb, vb, tb, table.shape[1], trb, pb, rows, hq, hkv, d,
                                  page_size, k_pool.shape[0], capacity, max_splits, min_chunk, ws,
-                                 counters, schedule)
+                                 counters, schedule, row_group)
     rt.synchronize()
     assert np.all(counters.read_raw() == 0), "split tickets must be left at zero"
     return out.read().reshape(rows, hq, d)
@@ -144,6 +144,42 @@ def test_streaming_schedule_with_cut_pairs_matches_oracle(rt, rows, hq, hkv, d, 
     ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
                                  table, trows, pos, hkv, page)
     got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, page, table.shape[1] * page, 64, 64, schedule=2)
+    check(got, ref)
+
+
+# Prefill rows: one sequence, consecutive positions, one block-table row. The
+# streaming schedule serves them in groups of 16 / G rows that share each K/V
+# tile (row_group 2); partial last groups, every G, pairs cut between CTAs.
+PREFILL_CASES = [
+    # (rows, hq, hkv, d, first position)
+    (256, 32, 8, 128, 768),   # the bs1 decoder's last 256-row prefill chunk of a 1024-token prompt
+    (37, 32, 8, 128, 100),    # G = 4: groups of 4, the last one partial
+    (50, 16, 16, 64, 300),    # G = 1: groups of 16
+    (21, 16, 2, 128, 2000),   # G = 8: groups of 2, long contexts
+    (40, 4, 2, 64, 0),        # G = 2: groups of 8 from position 0
+]
+
+
+@pytest.mark.parametrize("rows,hq,hkv,d,first", PREFILL_CASES)
+def test_prefill_row_groups_match_oracle(rt, rows, hq, hkv, d, first):
+    page = 16
+    rng = np.random.default_rng(rows + first)
+    total = first + rows
+    stride = (total + page - 1) // page
+    pool_pages = stride + 5
+    table = rng.permutation(pool_pages)[:stride].astype(np.int32).reshape(1, stride)
+    kp = rng.standard_normal((pool_pages, hkv, page, d)).astype(np.float16)
+    vp = rng.standard_normal((pool_pages, hkv, page, d)).astype(np.float16)
+    q = rng.standard_normal((rows, hq, d)).astype(np.float16)
+    trows = np.zeros(rows, np.int32)
+    pos = (first + np.arange(rows)).astype(np.int32)
+    ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
+                                 table, trows, pos, hkv, page)
+    # The workspace size for these arguments must hold the row groups' slots
+    # (640 x 2 x 16 x (d + 2) floats): pick max_splits accordingly.
+    splits = max(1, -(-640 * 2 * 16 // (rows * hq)))
+    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, page, stride * page, splits, 64, schedule=2,
+                        row_group=2)
     check(got, ref)
 
 
