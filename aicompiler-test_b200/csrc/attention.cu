@@ -816,7 +816,7 @@ struct StreamCfg {
   static constexpr size_t kMergeFloats = (size_t)kConsumers * (kRows * D + 2 * kRows);
   __host__ __device__ static constexpr size_t smem_bytes() {
     return 1024 + (size_t)2 * kStages * kStageBytes + kMergeFloats * 4 + (size_t)kStages * T * 4 +
-           (size_t)(kStreamRowsMax + 1) * 4 + (size_t)kStreamRowsMax * 4 + 128;  // + barriers, alignment
+           (size_t)(kStreamRowsMax + 1) * 4 + (size_t)kStreamRowsMax * 4 * 2 + 128;  // + barriers, alignment
   }
 };
 
@@ -982,8 +982,9 @@ __global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
   int *sValid = reinterpret_cast<int *>(mrg + C::kMergeFloats);
   int *sPrefix = sValid + S * T;              // [groups + 1] tile starts of the groups (Q / Hkv)
   int *sEnd = sPrefix + kStreamRowsMax + 1;   // [groups] longest context of the group
+  int *sTable = sEnd + kStreamRowsMax;        // [groups] block-table row of the group
   uint64_t *full = reinterpret_cast<uint64_t *>(
-      (reinterpret_cast<uintptr_t>(sEnd + kStreamRowsMax) + 15) & ~uintptr_t(15));
+      (reinterpret_cast<uintptr_t>(sTable + kStreamRowsMax) + 15) & ~uintptr_t(15));
   uint64_t *empty = full + S;
   uint64_t *merge_bar = empty + S;
   __shared__ int s_last;
@@ -1011,6 +1012,7 @@ __global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
       }
     }
     sEnd[gi] = end;
+    sTable[gi] = p.table_rows[gi * QR];  // the rows of a group share one block-table row
     sPrefix[gi + 1] = (end + T - 1) / T;
   }
   if (tid == 0) {
@@ -1086,10 +1088,36 @@ __global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
     // ---- producer warp: the ring, across pairs ----
     bool waited = false;
     int issued = 0;
+    // Lane w < 4 looks up box group w's page for tile cursor c (16 positions,
+    // one page); -1 when the group is past the context or its page is bad.
+    auto lookup = [&](const StreamCursor &c) {
+      int page = -1;
+      if (lane < NC) {
+        const int len = sEnd[c.grp], g0 = c.t * T + lane * 16;
+        if (g0 < len) {
+          const int logical = g0 / p.page_size;
+          page = logical < p.table_stride ? p.block_table[(size_t)sTable[c.grp] * p.table_stride + logical] : -1;
+          if (page < 0) {
+            report_status(p.status, kStatusPageMissing, kWhereAttention, logical, c.grp * QR);
+          } else if (page >= p.pool_pages) {
+            report_status(p.status, kStatusPageRange, kWhereAttention, page, c.grp * QR);
+            page = -1;
+          }
+        }
+      }
+      return page;
+    };
     if (ntiles > 0) {
       StreamCursor c = locate(run_a);
-      for (int k = 0; k < ntiles; ++k, advance(c)) {
+      // The next tile's pages are looked up one tile ahead, so the table
+      // load's latency overlaps the wait for a free stage and this tile's issue.
+      int page_next = lookup(c);
+      for (int k = 0; k < ntiles; ++k) {
         const int stage = k % S;
+        const int page = page_next;
+        StreamCursor cn = c;
+        advance(cn);
+        if (k + 1 < ntiles) page_next = lookup(cn);
         if (k >= S && !__all_sync(0xffffffffu, mbar_wait(&empty[stage], ((k / S) - 1) & 1))) {
           if (lane == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, k, c.grp);
           break;
@@ -1101,23 +1129,6 @@ __global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
         if (!waited && p0 + T > fresh) {
           pdl_wait();
           waited = true;
-        }
-        // The rows of a group share one block-table row.
-        const int *table = p.block_table + (size_t)p.table_rows[c.grp * QR] * p.table_stride;
-        // Lane w < 4 looks up group w's page (16 positions, one page).
-        int page = -1;
-        if (lane < NC) {
-          const int g0 = p0 + lane * 16;
-          if (g0 < len) {
-            const int logical = g0 / p.page_size;
-            page = logical < p.table_stride ? table[logical] : -1;
-            if (page < 0) {
-              report_status(p.status, kStatusPageMissing, kWhereAttention, logical, c.grp * QR);
-            } else if (page >= p.pool_pages) {
-              report_status(p.status, kStatusPageRange, kWhereAttention, page, c.grp * QR);
-              page = -1;
-            }
-          }
         }
         // Valid rows of the tile (positions before len in a valid page).
 #pragma unroll
@@ -1142,6 +1153,7 @@ __global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
           }
         }
         issued = k + 1;
+        c = cn;
       }
     }
     if (!waited) pdl_wait();

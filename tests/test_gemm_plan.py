@@ -13,7 +13,7 @@ TILE_ROWS, ATOM, MIN_RUN_K, SMS = 128, 64, 256, 148
 
 def k_atoms(tn):
     """64-column swizzle atoms per pipeline stage (gemm.cuh gemm_k_atoms)."""
-    return 4 if tn <= 64 else 2
+    return 4 if tn <= 64 else 2 if tn <= 128 else 1
 
 
 def plan(n, k, m, sms=SMS):
