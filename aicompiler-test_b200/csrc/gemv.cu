@@ -349,18 +349,23 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   // so equal static shares finish at different times. After its first (static)
   // group a warp takes groups from one of kGemvPools interleaved pools
   // (group = pool + kGemvPools * k), each with its own ticket counter on its
-  // own cache line. Lane 0 takes the next ticket when a group starts and the
-  // warp uses it when the group ends, so the atomic's round trip hides behind
-  // the group's loads. A group's arithmetic does not depend on the warp that
-  // runs it, so results stay deterministic.
+  // own cache line. Lane 0 takes the next ticket when it issues the loads of a
+  // group's last batch and the warp uses it when the group ends, so the
+  // atomic's round trip hides behind that batch, and a warp never holds a
+  // second group when the tickets run out (a ticket taken a whole group ahead
+  // left slow warps with two groups to finish at the end). A group's
+  // arithmetic does not depend on the warp that runs it, so results stay
+  // deterministic.
   const bool dynamic = KS == 1 && p.work_counter != nullptr && total_teams % kGemvPools == 0 &&
                        ngroups > 2 * total_teams;
   const int pool = gt % kGemvPools;
   const int pool_base = total_teams / kGemvPools;
   unsigned int *ticket = p.work_counter + pool * kGemvPoolStride;
   int g_next = gt + total_teams;
-  int fetched = 0;
-  if (dynamic && lane == 0) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
+  int fetched = ngroups;
+  // The first group is one batch long: its last batch is already loaded.
+  if (dynamic && lane == 0 && c_lo + 32 * U >= c_hi)
+    fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
   stage_x<XS, M>(p, xs, red, blockIdx.x == 0);
   __syncthreads();
   pdl_launch_dependents();
@@ -399,12 +404,13 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       nc = c_lo;
       if (dynamic) {
         ng = __shfl_sync(0xffffffffu, fetched, 0);
-        if (lane == 0 && ng < ngroups) fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
       } else {
         ng = g_next;
         g_next += total_teams;
       }
     }
+    if (dynamic && lane == 0 && ng < ngroups && nc + 32 * U >= c_hi)
+      fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
     if (ng < ngroups && c_lo < c_hi) load_batch(ng, nc, w);
     if (nc == c_lo) {
       // Group finished by every warp of the team (all walk the same groups).
