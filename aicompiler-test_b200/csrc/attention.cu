@@ -1438,7 +1438,9 @@ cudaError_t launch_attention(const AttentionParams &p, cudaStream_t stream, bool
       return cudaErrorInvalidValue;
     const int qr = grouped ? 16 / g : 1;
     const long long pairs = (long long)((p.rows + qr - 1) / qr) * p.hkv;
-    if (p.schedule == 2 || pairs >= sms) {
+    // Measured at context 1280, 8 KV heads: streaming 59.7 vs split 16.8 us
+    // at 1 row, equal at 8 rows (64 pairs), 36.7 vs 46.5 us at 16 rows.
+    if (p.schedule == 2 || 2 * pairs >= sms) {
       int grid = 0;
 #define TMC_STREAM_GRID(D_, G_)                                                          \
   if (p.head_dim == D_ && g == G_)                                                       \

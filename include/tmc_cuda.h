@@ -235,7 +235,7 @@ int tmc_k_paged_attention_f16(const void *q, void *out, const void *k_pool, cons
  * workspace (the throughput schedule; needs d 64 or 128, page_size % 16 == 0,
  * rows <= 1024 and a workspace of at least 2 * G * (d + 2) floats per
  * resident CTA, else TMC_ERR_UNSUPPORTED). Automatic picks 2 when it applies
- * and rows * hkv >= the SM count. row_group 2: the rows are prefill rows of
+ * and rows * hkv >= half the SM count. row_group 2: the rows are prefill rows of
  * one sequence at consecutive positions sharing one block-table row (the
  * decoder's prefill chunks); the streaming schedule then serves them in
  * groups of 16 / (hq / hkv) rows, reading each K/V tile once per group
