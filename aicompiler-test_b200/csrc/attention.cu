@@ -806,10 +806,11 @@ struct StreamCfg {
   static constexpr int T = Tile::T;
   static constexpr int kRows = QR * G;  // used rows of the MMA's A tile
   static_assert(kRows <= 16, "a row group fills at most the 16 rows of the A tile");
-  // Decode (QR 1): 3 stages (2 for G = 8), two CTAs per SM. Row groups: the
-  // 16-row tile step's registers leave one CTA per SM (the per-partition
-  // register files), so the ring takes what the merge buffer leaves.
-  static constexpr int kStages = QR == 1 ? (G <= 4 ? 3 : 2) : (D == 128 ? 5 : 4);
+  // Two CTAs per SM in both forms (registers capped at 168 so that three warps
+  // of a partition fit its register file): 3 stages for decode (2 for G = 8),
+  // 2 for row groups, whose merge buffer is four times larger. One CTA per SM
+  // with a 5-stage ring ran the row groups ~20% slower (fewer math warps).
+  static constexpr int kStages = QR == 1 ? (G <= 4 ? 3 : 2) : 2;
   static constexpr size_t kStageBytes = Tile::kStageBytes;  // one of K or V
   static constexpr int kConsumers = 4;
   static constexpr int kThreadsAll = (kConsumers + 1) * 32;
@@ -966,7 +967,7 @@ __device__ __forceinline__ bool tile_step_rows16(unsigned char *sKs, unsigned ch
 }
 
 template <int D, int G, int QR>
-__global__ void __launch_bounds__(StreamCfg<D, G, QR>::kThreadsAll)
+__global__ void __maxnreg__(168)  // two 160-thread CTAs per SM
     attention_stream_kernel(const __grid_constant__ AttentionParams p, const __grid_constant__ CUtensorMap kmap,
                             const __grid_constant__ CUtensorMap vmap) {
   using C = StreamCfg<D, G, QR>;
