@@ -795,6 +795,7 @@ cudaError_t dispatch_g(const AttentionParams &p, cudaStream_t stream, bool pdl, 
 // mbarrier wait.
 constexpr int kStreamRowsMax = 512;
 constexpr int kStreamMaxCtas = 640;  // resident CTAs of the streaming schedule, any device
+constexpr int kMaxPieces = 8;        // pieces of a cut pair combined through per-row weights
 
 // QR query rows per pair: 1 for decode (one row per sequence; the G query
 // heads fill G rows of the MMA's A tile), 16 / G for a row group of prefill
@@ -1309,27 +1310,77 @@ __global__ void __maxnreg__(168)  // two 160-thread CTAs per SM
             break;
           }
           if (s_last) {
-            // The last piece: combine the pieces in CTA order.
+            // The last piece: combine the pieces in CTA order. A piece sits in
+            // slot 0 of a CTA whose run starts inside the pair (every CTA after
+            // the first, and the first when its run starts at the pair), else
+            // in slot 1. First one thread per row turns the pieces' (m, l)
+            // into weights (in the merge buffer, free by now), then every
+            // element sums its pieces' accumulators with all of its loads
+            // independent -- loops of dependent L2 round trips per element
+            // cost tens of microseconds per launch.
             __threadfence();
-            for (int i = ct; i < RW * D; i += NC * 32) {
-              const int ri = i / D;
-              const int row = row_of(c.grp, ri);
-              if (row < 0 || row >= rows) continue;
-              float mmax = -INFINITY;
-              for (int cc = c_first; cc <= c_last; ++cc) {
-                const int sl = stream_run_begin(W, grid, cc) >= c.pair_start ? 0 : 1;
-                mmax = fmaxf(mmax, __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * RW * 2 + ri * 2));
+            const bool first_slot0 = stream_run_begin(W, grid, c_first) >= c.pair_start;
+            const int np = c_last - c_first + 1;
+            auto slot_of = [&](int q) { return (q > 0 || first_slot0) ? 0 : 1; };
+            float *wts = mrg;  // [RW][kMaxPieces] combine weights
+            if (np <= kMaxPieces) {
+              if (ct < RW) {
+                float m[kMaxPieces], mmax = -INFINITY;
+#pragma unroll
+                for (int q = 0; q < kMaxPieces; ++q) {
+                  m[q] = q < np ? __ldcg(p.ws_ml + ((size_t)(c_first + q) * 2 + slot_of(q)) * RW * 2 + ct * 2)
+                               : -INFINITY;
+                  mmax = fmaxf(mmax, m[q]);
+                }
+                float den = 0.0f;
+#pragma unroll
+                for (int q = 0; q < kMaxPieces; ++q) {
+                  const float f = (m[q] == -INFINITY) ? 0.0f : expf(m[q] - mmax);
+                  if (q < np)
+                    den = fmaf(__ldcg(p.ws_ml + ((size_t)(c_first + q) * 2 + slot_of(q)) * RW * 2 + ct * 2 + 1), f,
+                               den);
+                  m[q] = f;
+                }
+#pragma unroll
+                for (int q = 0; q < kMaxPieces; ++q) wts[ct * kMaxPieces + q] = m[q] / den;
               }
-              float den = 0.0f, num = 0.0f;
-              for (int cc = c_first; cc <= c_last; ++cc) {
-                const int sl = stream_run_begin(W, grid, cc) >= c.pair_start ? 0 : 1;
-                const float mc = __ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * RW * 2 + ri * 2);
-                const float f = (mc == -INFINITY) ? 0.0f : expf(mc - mmax);
-                den = fmaf(__ldcg(p.ws_ml + ((size_t)cc * 2 + sl) * RW * 2 + ri * 2 + 1), f, den);
-                num = fmaf(__ldcg(p.ws_acc + ((size_t)cc * 2 + sl) * RW * D + i), f, num);
+              if (!consumer_sync(merge_bar, merge_phase, lane)) {
+                failed = true;
+                break;
               }
-              p.out[(size_t)row * p.out_stride + (size_t)(c.h * G + head_of(ri)) * D + i % D] =
-                  __float2half_rn(num / den);
+#pragma unroll
+              for (int e = 0; e < (RW * D + NC * 32 - 1) / (NC * 32); ++e) {
+                const int i = ct + e * NC * 32;
+                if (i >= RW * D) break;
+                const int ri = i / D;
+                const int row = row_of(c.grp, ri);
+                float num = 0.0f;
+                for (int q = 0; q < np; ++q)
+                  num = fmaf(__ldcg(p.ws_acc + ((size_t)(c_first + q) * 2 + slot_of(q)) * RW * D + i),
+                             wts[ri * kMaxPieces + q], num);
+                if (row >= 0 && row < rows)
+                  p.out[(size_t)row * p.out_stride + (size_t)(c.h * G + head_of(ri)) * D + i % D] =
+                      __float2half_rn(num);
+              }
+            } else {
+              for (int i = ct; i < RW * D; i += NC * 32) {
+                const int ri = i / D;
+                const int row = row_of(c.grp, ri);
+                if (row < 0 || row >= rows) continue;
+                float mmax = -INFINITY;
+                for (int q = 0; q < np; ++q)
+                  mmax = fmaxf(mmax, __ldcg(p.ws_ml + ((size_t)(c_first + q) * 2 + slot_of(q)) * RW * 2 + ri * 2));
+                float den = 0.0f, num = 0.0f;
+                for (int q = 0; q < np; ++q) {
+                  const size_t sl = (size_t)(c_first + q) * 2 + slot_of(q);
+                  const float mc = __ldcg(p.ws_ml + sl * RW * 2 + ri * 2);
+                  const float f = (mc == -INFINITY) ? 0.0f : expf(mc - mmax);
+                  den = fmaf(__ldcg(p.ws_ml + sl * RW * 2 + ri * 2 + 1), f, den);
+                  num = fmaf(__ldcg(p.ws_acc + sl * RW * D + i), f, num);
+                }
+                p.out[(size_t)row * p.out_stride + (size_t)(c.h * G + head_of(ri)) * D + i % D] =
+                    __float2half_rn(num / den);
+              }
             }
             if (ct == 0) atomicExch(p.counters + pair, 0u);
           }
