@@ -1293,7 +1293,10 @@ __global__ void __maxnreg__(168)  // two 160-thread CTAs per SM
           }
         }
         if (!whole) {
-          __threadfence();
+          // Every thread's partial stores, then the consumers' barrier, then
+          // thread 0's GPU-scope acquire-release ticket: the last piece's
+          // acquire (and its barrier) orders the other pieces' stores before
+          // its loads, without a GPU-scope fence in every thread.
           if (!consumer_sync(merge_bar, merge_phase, lane)) {
             failed = true;
             break;
@@ -1302,7 +1305,7 @@ __global__ void __maxnreg__(168)  // two 160-thread CTAs per SM
           const int c_first = stream_run_of(W, grid, c.pair_start);
           const int c_last = stream_run_of(W, grid, pair_end - 1);
           if (ct == 0) {
-            const unsigned int prev = atomicAdd(p.counters + pair, 1u);
+            const unsigned int prev = atomic_add_acq_rel_gpu(p.counters + pair, 1u);
             s_last = prev == (unsigned int)(c_last - c_first) ? 1 : 0;
           }
           if (!consumer_sync(merge_bar, merge_phase, lane)) {
@@ -1318,7 +1321,6 @@ __global__ void __maxnreg__(168)  // two 160-thread CTAs per SM
             // element sums its pieces' accumulators with all of its loads
             // independent -- loops of dependent L2 round trips per element
             // cost tens of microseconds per launch.
-            __threadfence();
             const bool first_slot0 = stream_run_begin(W, grid, c_first) >= c.pair_start;
             const int np = c_last - c_first + 1;
             auto slot_of = [&](int q) { return (q > 0 || first_slot0) ? 0 : 1; };
