@@ -105,15 +105,27 @@ __device__ __forceinline__ uint32_t map_cluster(const void *local, uint32_t rank
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
+// Asynchronous store into cluster CTA shared memory that completes as
+// transaction bytes on an mbarrier of the receiving CTA (the sender does not
+// wait for it to land).
+__device__ __forceinline__ void st_async_f32(uint32_t addr, float v, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr),
+               "r"(__float_as_uint(v)), "r"(remote_bar)
+               : "memory");
 }
-// All threads of all CTAs of the cluster (a hardware barrier, not a spin).
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void st_async_f32x2(uint32_t addr, float a, float b, uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.b32 [%0], {%1, %2}, [%3];" ::"r"(addr),
+               "r"(__float_as_uint(a)), "r"(__float_as_uint(b)), "r"(remote_bar)
+               : "memory");
 }
+// The two halves of a cluster barrier phase (a hardware barrier, not a spin):
+// arriving after the mbarrier initialisation and waiting just before the
+// first remote store proves every CTA of the cluster has started and made its
+// barriers visible, at no cost in between.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
 // One warp's 16 positions [p0, p0 + 16) of a K/V tile held in stage memory
 // (sKs, sVs: the stage's K and V bytes; rows r0 .. r0 + 15 of the tile):
@@ -247,9 +259,11 @@ __device__ __forceinline__ bool tile_step(unsigned char *sKs, unsigned char *sVs
 // of key positions; each warp runs flash-decoding on its own 16 positions of
 // every 64-position tile with tensor-core MMAs (the G query heads of the KV
 // head fill rows of the 16-row A tile; unused rows are zero) and keeps its own
-// online-softmax state; the warps merge in shared memory, then the CTAs of a
-// cluster merge through distributed shared memory. Only when a (row, KV head)
-// spans several clusters do the cluster results meet in the global workspace
+// online-softmax state; the warps merge in shared memory, then every CTA of a
+// cluster pushes its (m, l, o) slices into the receive buffers of the CTAs
+// that own them (remote stores, one cluster barrier) and each owner merges
+// its slice from its own shared memory. Only when a (row, KV head) spans
+// several clusters do the cluster results meet in the global workspace
 // (atomic ticket, last CTA combines).
 template <int D, int G, bool BOX>
 __global__ void __launch_bounds__(kThreads)
@@ -274,7 +288,16 @@ __global__ void __launch_bounds__(kThreads)
   uint64_t *empty = full + S;
   __shared__ int is_last;
   __shared__ int sPages[kPageCache];  // the chunk's physical page ids
-  __shared__ float xml[G * 2];  // this CTA's (m, l) per head, read by the cluster
+  __shared__ float xml[G * 2];  // this CTA's (m, l) per head
+  // Receive buffers of this CTA's slice [crank * per, (crank + 1) * per) of the
+  // G x D outputs: the o values of every CTA of the cluster, and each CTA's
+  // (m, l) per head, written only by the cluster's asynchronous stores, which
+  // complete on recv_bar (never aliasing the ring or the local merge area).
+  __shared__ __align__(16) float recv_o[G * D + kMaxCluster];
+  __shared__ __align__(16) float recv_ml[kMaxCluster * G * 2];
+  __shared__ __align__(8) uint64_t recv_bar;
+  __shared__ float merge_f[kMaxCluster * G];  // exp(m_c - max) per (CTA c, head)
+  __shared__ float merge_md[G * 2];           // (max, denominator) per head
 
   const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -287,6 +310,7 @@ __global__ void __launch_bounds__(kThreads)
   // produces q (and the newest K/V rows) starts: they are read, and the K/V rows
   // of older positions gathered, before the programmatic-dependency wait.
   const int pos = p.positions[row];
+  const int trow = p.table_rows[row];  // loaded alongside pos: one round trip, not two
   if (pos < 0 || pos >= p.capacity) {  // the same for every CTA of the row
     if (split == 0 && kvh == 0 && tid == 0)
       report_status(p.status, kStatusLengthRange, kWhereAttention, pos, row);
@@ -318,7 +342,7 @@ __global__ void __launch_bounds__(kThreads)
   const int begin = idle ? len : split * chunk;
   const int end = idle ? len : min(len, begin + chunk);
   const int ntiles = idle ? 0 : (end - begin + T - 1) / T;
-  const int *table = p.block_table + (size_t)p.table_rows[row] * p.table_stride;
+  const int *table = p.block_table + (size_t)trow * p.table_stride;
   // Positions below `fresh` are never written by the producer kernel.
   const int fresh = p.early_mode == 2 ? end : (p.early_mode == 1 ? pos : begin);
   bool failed = false;
@@ -346,9 +370,18 @@ __global__ void __launch_bounds__(kThreads)
       mbar_init(&full[st], 1);
       mbar_init(&empty[st], C::kWarpsPerCta);
     }
+    // The merge slice's bytes from every CTA of the cluster: its o values and
+    // the (m, l) of every head.
+    const int per = (G * D + (int)csize - 1) / (int)csize;
+    const int lo = (int)crank * per, hi = min(G * D, lo + per);
+    mbar_init(&recv_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    mbar_arrive_expect_tx(&recv_bar, static_cast<uint32_t>(csize) * static_cast<uint32_t>(hi - lo + 2 * G) * 4u);
   }
   __syncthreads();
+  // Phase 0 of the cluster barrier, waited on just before the first remote
+  // store (the clusters that returned above are whole clusters).
+  cluster_arrive_relaxed();
 
   // Warp 0: mark tile t's valid rows and arm its barrier with their bytes.
   auto arm = [&](int t) {
@@ -571,64 +604,79 @@ __global__ void __launch_bounds__(kThreads)
       for (int e = 0; e < E; ++e) o_cta[e] = fmaf(mrg[((size_t)w * G + hg) * D + hd + e], f, o_cta[e]);
     }
   }
-  __syncthreads();
-  // Publish this CTA's (m, l, o) for the cluster (o reuses the merge area).
-  float *xo = mrg;
-  if (own) {
-#pragma unroll
-    for (int e = 0; e < E; ++e) xo[(size_t)hg * D + hd + e] = o_cta[e];
-    if (hd == 0) {
-      xml[hg * 2] = m_cta;
-      xml[hg * 2 + 1] = l_cta;
-    }
+  // Cluster merge: CTA `crank` owns outputs [lo, hi) of G*D. Every CTA sends
+  // its (m, l) per head to all owners and each o value to the owner of its
+  // output as asynchronous stores that complete on the owner's recv_bar; the
+  // owner combines its slice from its own shared memory once all bytes have
+  // landed (one one-way trip, no cluster-wide barrier after the sends).
+  static_assert(kMaxCluster * G <= kThreads, "one (m, l) send per thread");
+  if (own && hd == 0) {
+    xml[hg * 2] = m_cta;
+    xml[hg * 2 + 1] = l_cta;
   }
-  cluster_sync();
-
-  // Cluster merge: CTA `crank` combines outputs [lo, hi) of G*D across the
-  // cluster's CTAs through distributed shared memory.
   const size_t head_base = ((size_t)row * p.hkv + kvh);
   const int nclusters = (active + (int)csize - 1) / (int)csize;
   const int cidx = split / (int)csize;       // this cluster along the splits
   const int stride = gridDim.x / (int)csize;  // cluster slots per (row, KV head)
   const int per = (G * D + (int)csize - 1) / (int)csize;
   const int lo = (int)crank * per, hi = min(G * D, lo + per);
+  __syncthreads();  // xml complete
+  cluster_wait();   // phase 0: every CTA of the cluster has started, its recv_bar armed
+  if (tid < (int)csize * G) {
+    const int q = tid / G, h = tid % G;
+    st_async_f32x2(map_cluster(&recv_ml[((int)crank * G + h) * 2], q), xml[h * 2], xml[h * 2 + 1],
+                   map_cluster(&recv_bar, q));
+  }
+  if (own) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      const int i = hg * D + hd + e, q = i / per;
+      st_async_f32(map_cluster(&recv_o[(int)crank * per + i - q * per], q), o_cta[e], map_cluster(&recv_bar, q));
+    }
+  }
+  if (!mbar_wait(&recv_bar, 0)) {
+    if (tid == 0) report_status(p.status, kStatusWaitTimeout, kWhereAttention, -1, row);
+    // Stores may still be in flight into this CTA: wait once more (bounded)
+    // before its shared memory goes away.
+    (void)mbar_wait(&recv_bar, 0);
+  }
+  // Per head of the slice, lane c of a warp takes CTA c's (m, l): the head's
+  // maximum and denominator come from warp shuffles and CTA c's weight
+  // exp(m - max) goes to shared memory; each output is then one short
+  // weighted sum over the CTAs (a once-per-launch path: little code, few
+  // dependent steps).
+  const int h_lo = lo / D, h_hi = hi > lo ? (hi - 1) / D : h_lo - 1;
+  for (int h = h_lo + warp; h <= h_hi; h += C::kWarpsPerCta) {
+    const bool in = lane < (int)csize;
+    const float m = in ? recv_ml[(lane * G + h) * 2] : -INFINITY;
+    const float l = in ? recv_ml[(lane * G + h) * 2 + 1] : 0.0f;
+    const float mmax = warp_max(m);
+    const float f = (m == -INFINITY) ? 0.0f : expf(m - mmax);
+    const float den = warp_sum(l * f);
+    if (in) merge_f[lane * G + h] = f;
+    if (lane == 0) {
+      merge_md[h * 2] = mmax;
+      merge_md[h * 2 + 1] = den;
+    }
+  }
+  __syncthreads();
   for (int i = lo + tid; i < hi; i += kThreads) {
     const int h = i / D;
-    // Issue every remote load before using any (csize <= kMaxCluster).
-    float mv[kMaxCluster], lv[kMaxCluster], ov[kMaxCluster];
-#pragma unroll
-    for (int c = 0; c < kMaxCluster; ++c) {
-      if (c < (int)csize) {
-        mv[c] = ld_cluster_f32(map_cluster(&xml[h * 2], c));
-        lv[c] = ld_cluster_f32(map_cluster(&xml[h * 2 + 1], c));
-        ov[c] = ld_cluster_f32(map_cluster(&xo[i], c));
-      }
-    }
-    float mmax = -INFINITY;
+    float num = 0.0f;
 #pragma unroll
     for (int c = 0; c < kMaxCluster; ++c)
-      if (c < (int)csize) mmax = fmaxf(mmax, mv[c]);
-    float den = 0.0f, num = 0.0f;
-#pragma unroll
-    for (int c = 0; c < kMaxCluster; ++c) {
-      if (c < (int)csize) {
-        const float f = (mv[c] == -INFINITY) ? 0.0f : expf(mv[c] - mmax);
-        den = fmaf(lv[c], f, den);
-        num = fmaf(ov[c], f, num);
-      }
-    }
+      if (c < (int)csize) num = fmaf(recv_o[c * per + i - lo], merge_f[c * G + h], num);
     if (nclusters == 1) {
-      p.out[(size_t)row * p.out_stride + (size_t)kvh * G * D + i] = __float2half_rn(num / den);
+      p.out[(size_t)row * p.out_stride + (size_t)kvh * G * D + i] = __float2half_rn(num / merge_md[h * 2 + 1]);
     } else {
       p.ws_acc[(head_base * stride + cidx) * G * D + i] = num;
       if (i % D == 0) {
         float *wm = p.ws_ml + ((head_base * stride + cidx) * G + h) * 2;
-        wm[0] = mmax;
-        wm[1] = den;
+        wm[0] = merge_md[h * 2];
+        wm[1] = merge_md[h * 2 + 1];
       }
     }
   }
-  cluster_sync();  // every CTA's shared memory stays valid until all reads are done
   if (nclusters == 1) {
     trace_emit(p.trace, t_entry, t_ready);
     return;

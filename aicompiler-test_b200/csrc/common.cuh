@@ -156,6 +156,23 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
   return v;
 }
 
+// L2 policy for data read once per step (weights): its lines are replaced
+// first, so the lines that are reused -- activations, KV pages, block tables,
+// counters and the kernels' own code -- stay in L2 while gigabytes stream by.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// ldg_stream with an L2 cache policy.
+__device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t pol) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
 __device__ __forceinline__ float2 half2_bits_to_float2(uint32_t bits) {
   __half2 h = *reinterpret_cast<__half2 *>(&bits);
   return __half22float2(h);

@@ -348,6 +348,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int s = 0; s < S; ++s) last_it[s] = -1;
       int it = 0;
       bool waited = false, ok = true;
+      // Weight tiles are read once per launch: evict-first in L2, so the token
+      // slab (read by every CTA) and the step's other reused lines stay.
+      const uint64_t wpol = l2_evict_first_policy();
       // The token atoms of stage st, K block kb (A adjacent 64-column boxes).
       auto load_x = [&](int st, int kb) {
 #pragma unroll
@@ -378,7 +381,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
           for (int a = 0; a < A; ++a)
             tma_load_2d(sA + ((size_t)st * A + a) * kTileBytesA, &w_map, (kb * A + a) * kGemmKBlock,
-                        tile * kGemmTileRows, &full[st]);
+                        tile * kGemmTileRows, &full[st], wpol);
           if (waited) {
             load_x(st, kb);
           } else {

@@ -25,9 +25,11 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 
-// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, size multiple of 16).
-__device__ __forceinline__ void prefetch_bulk_l2(const void *p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+// Bulk prefetch of [p, p + bytes) into L2 (16-byte aligned, size multiple of
+// 16) under the L2 cache policy `pol`.
+__device__ __forceinline__ void prefetch_bulk_l2(const void *p, uint32_t bytes, uint64_t pol) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(p), "r"(bytes), "l"(pol)
+               : "memory");
 }
 
 template <typename XS>
@@ -300,6 +302,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   const int c_lo = (int)(((long long)nchunks * wt) / KS);
   const int c_hi = (int)(((long long)nchunks * (wt + 1)) / KS);
 
+  // Weights are read once per step: evict-first in L2.
+  const uint64_t wpol = l2_evict_first_policy();
   // Load a batch of U 16-byte chunks of each of the R rows of group g,
   // starting at chunk c0 (chunks at or past c_hi read as zero), into registers.
   auto load_batch = [&](int g, int c0, uint4 (&w)[R][U]) {
@@ -311,7 +315,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         const int c = c0 + u * 32 + lane;
-        w[r][u] = (c < c_hi && rv) ? ldg_stream(wr + c) : make_uint4(0, 0, 0, 0);
+        w[r][u] = (c < c_hi && rv) ? ldg_stream(wr + c, wpol) : make_uint4(0, 0, 0, 0);
       }
     }
   };
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
         const int row = gg * R + r;
         if (row >= p.N || budget <= 0) continue;
         const char *src = reinterpret_cast<const char *>(p.W + (size_t)row * p.K) + (size_t)c_lo * 16;
-        prefetch_bulk_l2(src, slice);
+        prefetch_bulk_l2(src, slice, wpol);
         budget -= slice;
       }
     }
