@@ -86,6 +86,22 @@ def test_paged_attention_matches_oracle(rt, rows, hq, hkv, d, page, lengths, spl
     check(got, ref)
 
 
+@pytest.mark.parametrize("rows,hq,hkv,d,lengths,splits", [
+    (1, 32, 8, 128, [5000], (64, 64)),     # 63 active splits: four 16-CTA clusters per head
+    (2, 16, 2, 64, [3000, 40], (48, 64)),  # G = 8, head_dim 64: three clusters for the long
+                                           # row; one active CTA and idle clusters for the short
+])
+def test_split_schedule_across_clusters_matches_oracle(rt, rows, hq, hkv, d, lengths, splits):
+    # A pair wider than one cluster: each cluster merges its CTAs by pushes into
+    # the owners' shared memory, then the last CTA combines the clusters'
+    # results from the workspace.
+    q, kp, vp, table, trows, pos = make_case(sum(lengths) + d, rows, hq, hkv, d, 16, lengths)
+    ref = oracle.paged_attention(q.astype(np.float32), kp.astype(np.float32), vp.astype(np.float32),
+                                 table, trows, pos, hkv, 16)
+    got = run_attention(rt, q, kp, vp, table, trows, pos, hkv, 16, table.shape[1] * 16, *splits, schedule=1)
+    check(got, ref)
+
+
 def test_paged_attention_c4_subset(rt):
     # C4 shapes (32q/8kv x 128, 16-token pages, random pages of a large pool)
     # on 8 sequences with contexts drawn from U[128, 8192].
