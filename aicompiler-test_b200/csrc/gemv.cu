@@ -47,7 +47,9 @@ struct XLoad<float> {
 template <>
 struct XLoad<__half> {
   static __device__ __forceinline__ void get(const __half *row, int c, float (&v)[8]) {
-    const uint4 u = reinterpret_cast<const uint4 *>(row)[c];
+    unpack(reinterpret_cast<const uint4 *>(row)[c], v);
+  }
+  static __device__ __forceinline__ void unpack(const uint4 &u, float (&v)[8]) {
     float2 f;
     f = half2_bits_to_float2(u.x); v[0] = f.x; v[1] = f.y;
     f = half2_bits_to_float2(u.y); v[2] = f.x; v[3] = f.y;
@@ -78,12 +80,44 @@ __device__ __forceinline__ void store8(__half *dst, const float (&f)[8]) {
   *reinterpret_cast<uint4 *>(dst) = u;
 }
 
+// The RMSNorm weights of the fp16-gamma prologues do not depend on the
+// previous kernel: each thread loads the first kGammaPre of the 8-element
+// vectors it will scale (v = threadIdx.x + j blockDim.x) before the
+// programmatic-dependency wait, so the norm's second pass does not wait on L2.
+constexpr int kGammaPre = 2;
+struct GammaPre {
+  uint4 v[kGammaPre];
+  bool ok;
+};
+__device__ __forceinline__ GammaPre load_gamma_pre(const GemvParams &p) {
+  GammaPre g{};
+  const int pro = p.prologue;
+  g.ok = pro == kProF16Norm || pro == kProEmbedNorm || pro == kProResidualNorm;
+  if (g.ok) {
+    const int nvec = p.K >> 3;
+#pragma unroll
+    for (int j = 0; j < kGammaPre; ++j) {
+      const int v = threadIdx.x + j * blockDim.x;
+      g.v[j] = v < nvec ? reinterpret_cast<const uint4 *>(p.gamma)[v] : make_uint4(0, 0, 0, 0);
+    }
+  }
+  return g;
+}
+// gamma[8 v .. 8 v + 7] for the j-th vector of this thread.
+__device__ __forceinline__ void gamma8(const GemvParams &p, const GammaPre &pre, int j, int v, float (&gv)[8]) {
+  if (pre.ok && j < kGammaPre) {
+    XLoad<__half>::unpack(pre.v[j], gv);
+  } else {
+    XLoad<__half>::get(static_cast<const __half *>(p.gamma), v, gv);
+  }
+}
+
 // Stage the M activation rows (after the fused prologue) into shared memory.
 // K is a multiple of 8 (checked on the host).
 // `writer`: this CTA writes the residual-stream rows back to h_out (one CTA
 // of a GEMV launch; every CTA of the row-prologue kernel, one row each).
 template <typename XS, int M>
-__device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
+__device__ __forceinline__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer, const GammaPre &pre) {
   const int K = p.K;
   const int nvec = K >> 3;
   const bool exchanged = p.prologue == kProResidualNorm && p.xchg.world > 0;
@@ -181,10 +215,10 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
         }
         ss = block_sum(ss, red);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
-        const __half *g = static_cast<const __half *>(p.gamma);
-        for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        int j = 0;
+        for (int v = threadIdx.x; v < nvec; v += blockDim.x, ++j) {
           float gv[8], xv[8];
-          XLoad<__half>::get(g, v, gv);
+          gamma8(p, pre, j, v, gv);
           XLoad<XS>::get(dst, v, xv);
 #pragma unroll
           for (int j = 0; j < 8; ++j) xv[j] = round_half(__fmul_rn(__fmul_rn(xv[j], inv), gv[j]));
@@ -224,12 +258,12 @@ __device__ void stage_x(const GemvParams &p, XS *xs, float *red, bool writer) {
       if (norm) {
         ss = block_sum(ss, red);
         const float inv = 1.0f / sqrtf(ss / static_cast<float>(K) + p.eps);
-        const __half *g = static_cast<const __half *>(p.gamma);
         // Pass 2 (same elements per thread): half(x * inv * gamma).
+        int j = 0;
 #pragma unroll 2
-        for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+        for (int v = threadIdx.x; v < nvec; v += blockDim.x, ++j) {
           float gv[8], xv[8];
-          XLoad<__half>::get(g, v, gv);
+          gamma8(p, pre, j, v, gv);
           XLoad<XS>::get(dst, v, xv);
 #pragma unroll
           for (int j = 0; j < 8; ++j) xv[j] = round_half(__fmul_rn(__fmul_rn(xv[j], inv), gv[j]));
@@ -348,6 +382,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
       }
     }
   }
+  // (single-row launches: with more rows the registers are spoken for)
+  const GammaPre gpre = M == 1 ? load_gamma_pre(p) : GammaPre{};
   pdl_wait();
   // Dynamic scheduling (one-warp teams): SMs do not get equal HBM bandwidth,
   // so equal static shares finish at different times. After its first (static)
@@ -370,7 +406,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   // The first group is one batch long: its last batch is already loaded.
   if (dynamic && lane == 0 && c_lo + 32 * U >= c_hi)
     fetched = pool + kGemvPools * (pool_base + (int)atomicAdd(ticket, 1u));
-  stage_x<XS, M>(p, xs, red, blockIdx.x == 0);
+  stage_x<XS, M>(p, xs, red, blockIdx.x == 0, gpre);
   __syncthreads();
   pdl_launch_dependents();
   const unsigned long long t_ready = p.trace.records ? global_ns() : 0ull;
@@ -546,9 +582,10 @@ __global__ void __launch_bounds__(kThreads) row_prologue_kernel(const GemvParams
   if (p.h_out) q.h_out = p.h_out + (size_t)m * p.K;
   if (p.partial) q.partial = p.partial + (size_t)m * p.K;
   q.xchg.row0 = p.xchg.row0 + m;
+  const GammaPre gpre = load_gamma_pre(q);
   pdl_wait();
   pdl_launch_dependents();
-  stage_x<__half, 1>(q, xs, red, true);
+  stage_x<__half, 1>(q, xs, red, true, gpre);
   __syncthreads();
   const uint4 *src = reinterpret_cast<const uint4 *>(xs);
   uint4 *dst = reinterpret_cast<uint4 *>(xn + (size_t)m * p.K);
