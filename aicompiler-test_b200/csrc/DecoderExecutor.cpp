@@ -1004,6 +1004,13 @@ tmc::GemvParams DecoderExecutor::projection(int kind, int l, int R, bool feed) c
     default:
       break;
   }
+  // Every kernel of a step releases its dependents only after its own
+  // dependency wait, so what was written two or more kernels back is final
+  // when a kernel starts: the residual rows that O and down add to (written by
+  // the previous layer's down, three kernels back, and by O, two back).
+  // Single-row GEMVs read them before their own wait. (Reading the QKV
+  // epilogue's positions, pages and RoPE rows early gained nothing.)
+  p.early_epilogue_inputs = !tp && (kind == kKernelO || kind == kKernelDown);
   return p;
 }
 

@@ -52,6 +52,25 @@ __device__ __forceinline__ __half residual_value(__half residual, float acc) {
   return __float2half_rn(__fadd_rn(__half2float(residual), round_half(acc)));
 }
 
+// The residual rows of one row group of token 0, read ahead of the dependency
+// wait (GemvParams::early_epilogue_inputs). ok == false: none.
+struct EpiPre {
+  bool ok;
+  __half res[2];
+};
+
+template <int R>
+__device__ __forceinline__ EpiPre load_epi_pre(const GemvParams &p, int row0) {
+  EpiPre e{};
+  if (p.epilogue == kEpiResidual && R <= 2) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+      if (row0 + r < p.N) e.res[r] = __ldcg(p.residual + row0 + r);
+    e.ok = true;
+  }
+  return e;
+}
+
 // Rows (row0, row0 + 1) of token m, row0 even, with fp32 sums (acc_e, acc_o):
 // kEpiSwiGLU: a (gate_i, up_i) pair, i = row0 / 2 -> y_f16[m, i];
 // kEpiQKV: an interleaved RoPE pair inside one head of [q | k | v]; q goes to
@@ -109,7 +128,9 @@ __device__ __forceinline__ void epilogue_pair(const GemvParams &p, int row0, int
 // One output (row, token m) with fp32 sum v: kEpiF32, kEpiF16, kEpiResidual,
 // kEpiF32Partial (local partial buffer, or this rank's slot of every rank's
 // exchange window).
-__device__ __forceinline__ void epilogue_one(const GemvParams &p, int row, int m, float v) {
+// `has_res`: `res` is the residual read ahead (kEpiResidual, token 0).
+__device__ __forceinline__ void epilogue_one(const GemvParams &p, int row, int m, float v, bool has_res,
+                                             __half res) {
   const int epi = p.epilogue;
   const size_t idx = (size_t)m * p.y_stride + row;
   if (epi == kEpiF32Partial && p.xchg.world > 0) {
@@ -120,7 +141,7 @@ __device__ __forceinline__ void epilogue_one(const GemvParams &p, int row, int m
   } else if (epi == kEpiF16) {
     p.y_f16[idx] = __float2half_rn(v);
   } else if (epi == kEpiResidual) {
-    p.y_f16[idx] = residual_value(p.residual[idx], v);
+    p.y_f16[idx] = residual_value(has_res ? res : p.residual[idx], v);
   }
 }
 

@@ -276,7 +276,7 @@ __device__ __forceinline__ void stage_x(const GemvParams &p, XS *xs, float *red,
 
 template <int R, int M>
 __device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&acc)[R][M],
-                                         int lane, unsigned long long (&best)[M]) {
+                                         int lane, unsigned long long (&best)[M], const EpiPre &pre) {
   const int epi = p.epilogue;
   if (epi == kEpiArgmax) {
     // Every lane holds the full sums; all lanes track the key identically.
@@ -309,7 +309,7 @@ __device__ __forceinline__ void epilogue(const GemvParams &p, int row0, float (&
     if (row >= p.N) continue;
 #pragma unroll
     for (int m = 0; m < M; ++m)
-      if (m < p.M) epilogue_one(p, row, m, acc[r][m]);
+      if (m < p.M) epilogue_one(p, row, m, acc[r][m], m == 0 && pre.ok, pre.res[r < 2 ? r : 0]);
   }
 }
 
@@ -384,6 +384,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
   }
   // (single-row launches: with more rows the registers are spoken for)
   const GammaPre gpre = M == 1 ? load_gamma_pre(p) : GammaPre{};
+  // The first group's residual rows, when the caller marks them final (lane 0
+  // runs the epilogue).
+  EpiPre epre{};
+  if (M == 1 && p.early_epilogue_inputs && lane == 0 && g < ngroups) epre = load_epi_pre<R>(p, g * R);
   pdl_wait();
   // Dynamic scheduling (one-warp teams): SMs do not get equal HBM bandwidth,
   // so equal static shares finish at different times. After its first (static)
@@ -476,16 +480,17 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvParams p) {
               for (int k = 0; k < KS; ++k) t += team_part[team * KS + k][r * M + m];
               acc[r][m] = t;
             }
-          epilogue<R, M>(p, g * R, acc, lane, best);
+          epilogue<R, M>(p, g * R, acc, lane, best, epre);
         }
         asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "r"(KS * 32) : "memory");
       } else {
-        epilogue<R, M>(p, g * R, acc, lane, best);
+        epilogue<R, M>(p, g * R, acc, lane, best, epre);
       }
 #pragma unroll
       for (int r = 0; r < R; ++r)
 #pragma unroll
         for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
+      epre.ok = false;  // the read-ahead inputs were the first group's
     }
     g = ng;
     c0 = nc;

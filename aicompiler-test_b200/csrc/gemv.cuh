@@ -141,6 +141,12 @@ struct GemvParams {
   // K-split team size chosen by the decode GEMV tuner (1, 2, 4 or 8); 0: the
   // built-in rule.
   int force_ks;
+  // Nonzero when the residual rows (kEpiResidual) were final before the
+  // preceding kernel started, i.e. written two or more kernels back in a chain
+  // where every kernel releases its dependents only after its own dependency
+  // wait. Single-row launches then read their first row group's residuals
+  // before their own wait instead of in the epilogue.
+  int early_epilogue_inputs;
   // Tensor parallelism over peer memory (kEpiF32Partial producers,
   // kProResidualNorm consumers, kEpiArgmax key exchange); world 0: off.
   PeerExchange xchg;
