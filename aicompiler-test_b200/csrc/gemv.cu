@@ -239,6 +239,32 @@ __device__ __forceinline__ void stage_x(const GemvParams &p, XS *xs, float *red,
       }
       const bool norm = (pro == kProF16Norm || pro == kProEmbedNorm);
       const bool write_h = (pro == kProEmbedNorm) && writer && p.h_out != nullptr;
+      if (pro == kProF16 && src != nullptr) {
+        // A plain copy: each thread has all of its loads (up to kCopyVecs
+        // 16-byte vectors) in flight before it stores any, one L2 round trip
+        // for rows up to kCopyVecs x 8 x blockDim elements (a long row, e.g.
+        // the down projection's 14336, would otherwise take four).
+        constexpr int kCopyVecs = 8;
+        const uint4 *s4 = reinterpret_cast<const uint4 *>(src);
+        for (int v0 = threadIdx.x; v0 < nvec; v0 += kCopyVecs * blockDim.x) {
+          uint4 buf[kCopyVecs];
+#pragma unroll
+          for (int j = 0; j < kCopyVecs; ++j) {
+            const int v = v0 + j * blockDim.x;
+            buf[j] = v < nvec ? s4[v] : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int j = 0; j < kCopyVecs; ++j) {
+            const int v = v0 + j * blockDim.x;
+            if (v < nvec) {
+              float f[8];
+              XLoad<__half>::unpack(buf[j], f);
+              store8(dst + v * 8, f);
+            }
+          }
+        }
+        continue;
+      }
       // Pass 1: global -> shared (raw values; exact in XS), sum of squares.
       float ss = 0.0f;
 #pragma unroll 2
