@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(kThreads) row_prologue_kernel(const GemvParams
   if (p.h_out) q.h_out = p.h_out + (size_t)m * p.K;
   if (p.partial) q.partial = p.partial + (size_t)m * p.K;
   q.xchg.row0 = p.xchg.row0 + m;
-  const GammaPre gpre = load_gamma_pre(q);
+  const GammaPre gpre{};  // (reading gamma ahead slowed the batched steps' prologue)
   pdl_wait();
   pdl_launch_dependents();
   stage_x<__half, 1>(q, xs, red, true, gpre);
