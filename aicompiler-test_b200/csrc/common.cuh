@@ -147,15 +147,6 @@ __device__ __forceinline__ bool wait_count_geq_gpu(const unsigned int *counter, 
 }
 
 // ---- global loads ----------------------------------------------------------
-// Streaming 16-byte load of immutable data: read-only path, no L1 allocation.
-__device__ __forceinline__ uint4 ldg_stream(const void *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
 // L2 policy for data read once per step (weights): its lines are replaced
 // first, so the lines that are reused -- activations, KV pages, block tables,
 // counters and the kernels' own code -- stay in L2 while gigabytes stream by.
@@ -164,7 +155,8 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
 }
-// ldg_stream with an L2 cache policy.
+// Streaming 16-byte load of immutable data: read-only path, no L1 allocation,
+// under the L2 cache policy `pol`.
 __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t pol) {
   uint4 v;
   asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
